@@ -1,0 +1,176 @@
+/*
+ * rapier_b200.h — C-ABI of the B200-native (sm_100a) decode hot path for the qwen35 hybrid architecture.
+ *
+ * Operator surface: extern "C" twins of the reference engine's strata::kernels calls and of the
+ * in-file kernels of src/qwythos.cpp (paths inside jollyroger1480/rapier). Conventions:
+ *   - device pointers only; `stream` is a cudaStream_t passed as void* (must be non-null, as the
+ *     reference's native_mmvq requires, src/native_mmvq.cu:2323-2325);
+ *   - work is enqueued asynchronously, nothing synchronizes, nothing allocates, so every call can be
+ *     captured into a CUDA graph;
+ *   - every entry validates on the host and returns RK_OK (0) or a negative RK_E* code; the message of
+ *     the last failure on the calling thread is rk_last_error(). Where the reference throws
+ *     std::invalid_argument (src/native_mmvq.cu:2312-2331) or calls exit(1) (src/fused_gdn.cu:169-176),
+ *     this returns RK_EINVAL;
+ *   - weight type ids are ggml's: RK_TYPE_Q6_K = 14, RK_TYPE_Q8_0 = 8.
+ */
+#ifndef RAPIER_B200_H
+#define RAPIER_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define RK_OK 0
+#define RK_EINVAL (-1)       /* bad argument: shape, null or misaligned pointer, null stream */
+#define RK_ECUDA (-2)        /* a CUDA runtime call or kernel launch failed */
+#define RK_ENOMEM (-3)       /* device allocation failed (engine entry points only) */
+#define RK_ERANGE (-4)       /* position / token / context out of range */
+#define RK_EUNSUPPORTED (-5) /* weight type or layout not handled by this entry */
+
+#define RK_TYPE_Q8_0 8
+#define RK_TYPE_Q6_K 14
+
+/* ---------------------------------------------------------------------------------------------- */
+/* diagnostics                                                                                       */
+/* ---------------------------------------------------------------------------------------------- */
+/* Message of the last failed rk_* call on this thread ("" when none). No reference counterpart. */
+const char* rk_last_error(void);
+/* ABI version: (major << 16) | minor. */
+int rk_version(void);
+/* OR of every kernel module's device status word (bit 0: a bulk-copy wait gave up; bit 1: a cluster
+ * handshake gave up; bit 2: an index handed to a kernel was out of range); clear != 0 resets it.
+ * Synchronous. A nonzero value means a kernel returned early instead of hanging. */
+unsigned rk_device_status(int clear);
+
+/* ---------------------------------------------------------------------------------------------- */
+/* Q8_1 activations                                                                                 */
+/* ---------------------------------------------------------------------------------------------- */
+/* Replaces strata::kernels::native_q8_1_bytes (src/native_mmvq.cu:3054): bytes of ncols Q8_1 columns. */
+size_t rk_q8_1_bytes(int n_in, int ncols);
+/* Replaces native_quantize_q8_1 (src/native_mmvq.cu:3059-3071, kernel :158-173): fp32 -> Q8_1 blocks
+ * (36 B per 32 values: half2 {d, sum}, int8[32]); columns contiguous. */
+int rk_quantize_q8_1(const float* x, void* x_q8_1, int n_in, int ncols, void* stream);
+
+/* ---------------------------------------------------------------------------------------------- */
+/* Quantized GEMV, GGUF block layout (drop-in)                                                      */
+/* ---------------------------------------------------------------------------------------------- */
+/* Replaces native_mmvq_weight_bytes (src/native_mmvq.cu:3765-3785) for types 14 and 8. */
+size_t rk_weight_bytes(int type, int n_in, int n_out);
+/* Replaces native_mmvq (src/native_mmvq.cu:3787-3818) / native_q6_k_mmvq (:3627-3660) /
+ * native_q8_0_mmvq (:3732-3736): y[j*n_out + r] = W[r,:] . x[:, j] on GGUF Q6_K / Q8_0 rows,
+ * 1 <= ncols <= 16. */
+int rk_mmvq(int type, const void* weights, const void* x_q8_1, float* y, int n_in, int n_out, int ncols,
+            void* stream);
+/* Replaces native_q6_k_mmvq_res (src/native_mmvq.cu:3187-3200) / native_q8_0_mmvq_res (:3326-3339):
+ * y[r] = W[r,:] . x + res[r]; partials[r/4] = sum of y^2 over rows 4(r/4)..4(r/4)+3 (y == res allowed). */
+int rk_mmvq_res(int type, const void* weights, const void* x_q8_1, float* y, const float* res, float* partials,
+                int n_in, int n_out, void* stream);
+
+/* ---------------------------------------------------------------------------------------------- */
+/* Quantized GEMV, packed tile layout (the fast path)                                               */
+/* ---------------------------------------------------------------------------------------------- */
+/* The load-time step of the reference's upload_mat (src/qwythos.cpp:908-935): a lossless repack of
+ * GGUF rows into 16-byte-aligned tiles of 4 rows x 1024 values (same byte count). Requires
+ * n_in % 1024 == 0 and n_out % 4 == 0; rk_packed_bytes returns 0 for other shapes. */
+size_t rk_packed_bytes(int type, int n_in, int n_out);
+int rk_pack_weights(int type, const void* src, void* dst, int n_in, int n_out, void* stream);
+int rk_unpack_weights(int type, const void* src, void* dst, int n_in, int n_out, void* stream);
+/* Same contract as rk_mmvq on packed weights, 1 <= ncols <= 16. */
+int rk_mmvq_packed(int type, const void* packed, const void* x_q8_1, float* y, int n_in, int n_out, int ncols,
+                   void* stream);
+/* Same contract as rk_mmvq_res on packed weights, per column j: y + j*n_out, res + j*n_out,
+ * partials + j*(n_out/4). 1 <= ncols <= 16. (The reference runs a 2-column GEMV plus add_partials for
+ * this, src/qwythos.cpp:1489-1494.) */
+int rk_mmvq_packed_res(int type, const void* packed, const void* x_q8_1, float* y, const float* res,
+                       float* partials, int n_in, int n_out, int ncols, void* stream);
+/* Parity probe (no reference counterpart): the exact integer sums the packed GEMV accumulates.
+ * out[((j*n_out) + r)*nsub + s]; Q6_K: nsub = n_in/16, s = 16-value sub-block, value
+ * sum((code-32) * x_code) * scale; Q8_0: nsub = n_in/32, value sum(w_code * x_code). */
+int rk_mmvq_isums(int type, const void* packed, const void* x_q8_1, int32_t* out, int n_in, int n_out, int ncols,
+                  void* stream);
+
+/* ---------------------------------------------------------------------------------------------- */
+/* norms and elementwise (src/qwythos.cpp:602-715)                                                  */
+/* ---------------------------------------------------------------------------------------------- */
+/* row_sum_partials_kernel (:616-623): partials[b] = sum of x[4b..4b+3]^2. */
+int rk_row_sumsq_partials(const float* x, float* partials, int n, void* stream);
+/* add_partials_1024_kernel (:602-614): x += o, partials of the new x. */
+int rk_add_partials(float* x, const float* o, float* partials, int n, void* stream);
+/* rms_quant_apply_kernel (:627-655): Q8_1 of x * w * rsqrt(sum(partials)/cols + eps); column j reads
+ * x + j*cols, partials + j*cols/4, writes y + j*rk_q8_1_bytes(cols,1). cols % 32 == 0. */
+int rk_rms_quant_q8_1(const float* x, const float* w, const float* partials, void* y, int cols, int ncols, float eps,
+                      void* stream);
+/* rms_norm_out_kernel (:658-672): out = x * w * rsqrt(sum(partials)/cols + eps). */
+int rk_rms_norm_out(const float* x, const float* w, const float* partials, float* out, int cols, int ncols, float eps,
+                    void* stream);
+/* swiglu_quant_kernel (:676-689): Q8_1 of silu(gate) * up. */
+int rk_swiglu_q8_1(const float* up, const float* gate, void* y, int n, void* stream);
+/* sig_mul_quant_kernel (:692-704): Q8_1 of o * sigmoid(g). */
+int rk_sigmul_q8_1(const float* o, const float* g, void* y, int n, void* stream);
+/* beta_gate_kernel (:707-715): beta = sigmoid(beta) in place; gate = softplus(alpha + dt) * ssm_a. */
+int rk_beta_gate(float* beta, const float* alpha, const float* dt, const float* ssm_a, float* gate, int n,
+                 void* stream);
+/* Strata rms_norm_weighted (called at src/qwythos.cpp:1206-1207): per row x = x * rsqrt(mean(x^2) + eps) * w,
+ * in place. */
+int rk_rms_norm_rows(float* x, const float* w, int rows, int cols, float eps, void* stream);
+/* Greedy argmax of forward_token (src/qwythos.cpp:1803-1811) / argmax_kernel (:70-84): out[j] receives
+ * the index of the largest of x[j*n .. j*n+n) (lowest index on ties). */
+int rk_argmax(const float* x, int n, int ncols, int* out, void* stream);
+
+/* ---------------------------------------------------------------------------------------------- */
+/* Gated DeltaNet (src/fused_gdn.cu)                                                                 */
+/* ---------------------------------------------------------------------------------------------- */
+/* Replaces fused_gdn_conv_l2 (src/fused_gdn.cu:167-176, kernel :113-133). The conv history is a 4-slot
+ * ring per channel, ring[c*4 + (p & 3)] = input at position p (the reference keeps [C][3] and slides);
+ * *pos is read on the device. In-place h == qkv allowed. */
+int rk_gdn_conv_l2(float* ring, const float* qkv, const float* conv_w, float* h, int channels, int qk_heads,
+                   float eps, const int* pos, void* stream);
+/* Replaces fused_gdn_step_norm_silu_q8 (src/fused_gdn.cu:221-225, kernel :39-111): the delta-rule state
+ * step, RMSNorm * gamma * silu(z), and the Q8_1 blocks of y (q8 may be NULL). State fp32
+ * [128][h_v][128]. */
+int rk_gdn_step_norm_silu_q8(float* state, const float* q, const float* k, const float* v, const float* gate,
+                             const float* beta, const float* z, const float* gamma, float eps, float* y, void* q8,
+                             int h_k, int h_v, void* stream);
+
+/* The engine's whole GDN recurrence of one layer for 1-2 tokens in one launch (it fuses
+ * beta_gate_kernel, src/qwythos.cpp:707-715, fused_gdn_conv_l2 and fused_gdn_step_norm_silu_q8,
+ * src/fused_gdn.cu:113-225). Column c (0 <= c < ncols) is the token at position *pos + c; its projection
+ * column proj + c*proj_stride = [q h_k*128 | k h_k*128 | v h_v*128 | z h_v*128 | beta h_v | alpha h_v]
+ * (the reference's qkv||z and beta||alpha GEMV outputs back to back). The state is read from `snap`
+ * instead of `state` when *rollback != 0 (a rejected draft); with ncols == 2 the state after column 0 is
+ * written to `snap`. Writes y + c*h_v*128 and the Q8_1 blocks q8 + c*rk_q8_1_bytes(h_v*128, 1).
+ * Requires h_v == 2*h_k. */
+int rk_gdn_fused(const float* proj, int proj_stride, float* ring, const float* conv_w, const float* dt_bias,
+                 const float* ssm_a, const float* gamma, float* state, float* snap, const int* rollback, float* y,
+                 void* q8, int h_k, int h_v, int ncols, const int* pos, float eps, void* stream);
+
+/* ---------------------------------------------------------------------------------------------- */
+/* Attention (src/qwythos.cpp:320-442)                                                               */
+/* ---------------------------------------------------------------------------------------------- */
+/* split_qg_kernel (:320-327): qg per head [q (hd) | gate (hd)] -> q, g. */
+int rk_split_qg(const float* qg, float* q, float* g, int heads, int hd, void* stream);
+/* Strata native_rope_apply (called at :1210-1211): NEOX rotate-half over the first n_rot dims of each
+ * head, in place, cos/sin from `table` (table[(p*(n_rot/2) + i)*2 + {0,1}] for p < max_pos, built on the
+ * host), at position *pos (device; a position outside the table sets status bit 2 and changes nothing). */
+int rk_rope(float* x, int heads, int hd, int n_rot, const float* table, int max_pos, const int* pos, void* stream);
+/* store_kv2_kernel (:340-345) with fp16 head-major caches [n_kv][max_ctx][hd]:
+ * kcache/vcache[(h*max_ctx + *pos)*hd + d] = k/v[h*hd + d]. */
+int rk_store_kv_f16(uint16_t* kcache, uint16_t* vcache, const float* k, const float* v, const int* pos, int n_kv,
+                    int hd, int max_ctx, void* stream);
+/* gqa_head_kernel (:380-442) with fp16 K/V caches [n_kv][max_ctx][hd], split over token chunks: column c
+ * (0 <= c < ncols) of q [ncols][n_head][hd] attends tokens 0..*pos + c (device) and writes
+ * o [ncols][n_head][hd] = softmax(q . K^T * scale) V. The chunk partials go to `scratch` (caller-owned,
+ * like the reference's `scores` buffer), at least rk_gqa_scratch_bytes(n_head, ncols, max_ctx) bytes,
+ * max_ctx > *pos + ncols - 1. hd == 256, n_head % n_kv == 0, 1 <= ncols <= 2. */
+size_t rk_gqa_scratch_bytes(int n_head, int ncols, int max_ctx);
+int rk_gqa_decode_f16(const float* q, const uint16_t* kcache, const uint16_t* vcache, float* o, int n_head,
+                      int n_kv, int hd, int ncols, const int* pos, int max_ctx, float scale, void* scratch,
+                      size_t scratch_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* RAPIER_B200_H */

@@ -1,0 +1,103 @@
+"""ctypes loader for librapier_b200.so and the raw rk_* C-ABI (include/rapier_b200.h).
+
+The library must exist: there is no CPU fallback. Every wrapper raises RkError (with rk_last_error())
+when an entry point returns a negative RK_E* code.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import re
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(PKG)
+LIB_PATH = os.path.join(PKG, "librapier_b200.so")
+HEADER = os.path.join(ROOT, "include", "rapier_b200.h")
+
+RK_OK, RK_EINVAL, RK_ECUDA, RK_ENOMEM, RK_ERANGE, RK_EUNSUPPORTED = 0, -1, -2, -3, -4, -5
+TYPE_Q8_0, TYPE_Q6_K = 8, 14
+_CODE_NAMES = {RK_EINVAL: "RK_EINVAL", RK_ECUDA: "RK_ECUDA", RK_ENOMEM: "RK_ENOMEM", RK_ERANGE: "RK_ERANGE",
+               RK_EUNSUPPORTED: "RK_EUNSUPPORTED"}
+
+
+class RkError(RuntimeError):
+    def __init__(self, code: int, func: str, msg: str):
+        super().__init__(f"{func} -> {_CODE_NAMES.get(code, code)}: {msg}")
+        self.code = code
+        self.func = func
+
+
+_lib = None
+
+vp, i32, u32, f32, sz, i64 = C.c_void_p, C.c_int, C.c_uint, C.c_float, C.c_size_t, C.c_int64
+
+# name -> (restype, argtypes); every function declared in include/rapier_b200.h appears here.
+SIGNATURES = {
+    "rk_last_error": (C.c_char_p, []),
+    "rk_version": (i32, []),
+    "rk_device_status": (u32, [i32]),
+    "rk_q8_1_bytes": (sz, [i32, i32]),
+    "rk_quantize_q8_1": (i32, [vp, vp, i32, i32, vp]),
+    "rk_weight_bytes": (sz, [i32, i32, i32]),
+    "rk_mmvq": (i32, [i32, vp, vp, vp, i32, i32, i32, vp]),
+    "rk_mmvq_res": (i32, [i32, vp, vp, vp, vp, vp, i32, i32, vp]),
+    "rk_packed_bytes": (sz, [i32, i32, i32]),
+    "rk_pack_weights": (i32, [i32, vp, vp, i32, i32, vp]),
+    "rk_unpack_weights": (i32, [i32, vp, vp, i32, i32, vp]),
+    "rk_mmvq_packed": (i32, [i32, vp, vp, vp, i32, i32, i32, vp]),
+    "rk_mmvq_packed_res": (i32, [i32, vp, vp, vp, vp, vp, i32, i32, i32, vp]),
+    "rk_mmvq_isums": (i32, [i32, vp, vp, vp, i32, i32, i32, vp]),
+    "rk_row_sumsq_partials": (i32, [vp, vp, i32, vp]),
+    "rk_add_partials": (i32, [vp, vp, vp, i32, vp]),
+    "rk_rms_quant_q8_1": (i32, [vp, vp, vp, vp, i32, i32, f32, vp]),
+    "rk_rms_norm_out": (i32, [vp, vp, vp, vp, i32, i32, f32, vp]),
+    "rk_swiglu_q8_1": (i32, [vp, vp, vp, i32, vp]),
+    "rk_sigmul_q8_1": (i32, [vp, vp, vp, i32, vp]),
+    "rk_beta_gate": (i32, [vp, vp, vp, vp, vp, i32, vp]),
+    "rk_rms_norm_rows": (i32, [vp, vp, i32, i32, f32, vp]),
+    "rk_argmax": (i32, [vp, i32, i32, vp, vp]),
+    "rk_gdn_conv_l2": (i32, [vp, vp, vp, vp, i32, i32, f32, vp, vp]),
+    "rk_gdn_step_norm_silu_q8": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, f32, vp, vp, i32, i32, vp]),
+    "rk_split_qg": (i32, [vp, vp, vp, i32, i32, vp]),
+    "rk_gdn_fused": (i32, [vp, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, vp, f32, vp]),
+    "rk_rope": (i32, [vp, i32, i32, i32, vp, i32, vp, vp]),
+    "rk_store_kv_f16": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, vp]),
+    "rk_gqa_scratch_bytes": (sz, [i32, i32, i32]),
+    "rk_gqa_decode_f16": (i32, [vp, vp, vp, vp, i32, i32, i32, i32, vp, i32, f32, vp, sz, vp]),
+}
+
+
+def header_functions() -> list[str]:
+    """Names of every function the public header declares."""
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(rk_[a-z0-9_]+)\s*\(", text)))
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} is missing: build it with `python -m rapier_b200.build` "
+                              "(there is no CPU fallback)")
+        L = C.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name, None)
+            if fn is None:
+                continue
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def last_error() -> str:
+    return lib().rk_last_error().decode()
+
+
+def call(name: str, *args) -> int:
+    """Call an int-returning entry point; raise RkError on a negative code."""
+    rc = getattr(lib(), name)(*args)
+    if rc < 0:
+        raise RkError(rc, name, last_error())
+    return rc

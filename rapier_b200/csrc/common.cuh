@@ -1,0 +1,197 @@
+// common.cuh — shared device helpers for the rapier_b200 sm_100a kernels: block formats, warp
+// reductions, the Q8_1 block rules, PTX wrappers for mbarriers / bulk copies / programmatic dependent
+// launch, bounded waits, and the host-side error plumbing of the C-ABI.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+#include <utility>
+
+#include "../../include/rapier_b200.h"
+
+namespace rk {
+
+constexpr int WARP = 32;
+constexpr int kQ6Tile = 3360;   // packed Q6_K tile: 4 rows x 1024 values
+constexpr int kQ80Tile = 4352;  // packed Q8_0 tile: 4 rows x 1024 values
+
+// ---------------------------------------------------------------------------------------------
+// Error plumbing: every C-ABI entry returns 0 or a negative RK_E* code and records a message that
+// rk_last_error() returns (thread-local). Device-side bounded waits that give up set a bit in a
+// per-module device word that rk_device_status() reads.
+// ---------------------------------------------------------------------------------------------
+int set_error(int code, const char* fmt, ...);
+int check_launch(const char* what);
+void clear_error();
+
+// ---------------------------------------------------------------------------------------------
+// warp reductions (xor butterfly, offsets 16..1: every lane ends with the same value)
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+__device__ __forceinline__ int warp_sum_i(int v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// ---------------------------------------------------------------------------------------------
+// Q8_1 block rules (the reference's q8_1_finite / q8_1_quant / q8_1_ds are out of its tree; this is
+// the written definition the CPU oracle restates):
+//   d = amax / 127, clamped to 65504 when NaN, infinite or above the fp16 maximum;
+//   q = 0 for an all-zero block, else roundf(x / d) clamped to [-127, 127];
+//   stored {half(d), half(sum clamped to +-65504, NaN -> 0)}.
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ float q8_finite_d(float d) { return (d <= 65504.0f) ? d : 65504.0f; }
+__device__ __forceinline__ int q8_quant(float x, float d, float amax) {
+    if (amax == 0.0f) return 0;
+    float q = roundf(__fdiv_rn(x, d));
+    q = fminf(fmaxf(q, -127.0f), 127.0f);
+    return (int) q;
+}
+__device__ __forceinline__ float q8_ds_sum(float s) {
+    if (s != s) return 0.0f;
+    return fminf(fmaxf(s, -65504.0f), 65504.0f);
+}
+// Quantize one value per lane of a full warp as one Q8_1 block (lane l owns value l): returns lane l's
+// int8 code and sets `ds` to the packed half2 {d, sum} word (the same on every lane).
+__device__ __forceinline__ int q8_1_warp_code(float v, uint32_t& ds) {
+    const float amax = warp_max(fabsf(v));
+    const float sum = warp_sum(v);
+    const float d = q8_finite_d(__fdiv_rn(amax, 127.0f));
+    const __half2 h = __halves2half2(__float2half_rn(d), __float2half_rn(q8_ds_sum(sum)));
+    ds = *reinterpret_cast<const uint32_t*>(&h);
+    return q8_quant(v, d, amax);
+}
+// The same block written to global memory in the 36-byte layout (blk = the block's first byte).
+__device__ __forceinline__ void q8_1_warp_store(float v, uint8_t* blk, int lane) {
+    uint32_t ds;
+    const int code = q8_1_warp_code(v, ds);
+    reinterpret_cast<int8_t*>(blk + 4)[lane] = (int8_t) code;
+    if (lane == 0) *reinterpret_cast<uint32_t*>(blk) = ds;
+}
+
+// ---------------------------------------------------------------------------------------------
+// PTX wrappers (sm_90+ forms, valid on sm_100a)
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+// 1-D bulk copy global -> this CTA's shared memory, completion counted on an mbarrier. No multicast.
+// dst, src 16-byte aligned; bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar,
+                                         uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(dst),
+        "l"(src), "r"(bytes), "r"(bar), "l"(policy)
+        : "memory");
+}
+__device__ __forceinline__ uint64_t policy_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ uint64_t policy_evict_normal() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+// Programmatic dependent launch: wait for the upstream grid's memory, and let the downstream grid launch.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Device status word (one per translation unit; rk_device_status() ORs and clears them all):
+// bit 0 = an mbarrier wait gave up (a bulk copy did not land within the bound), bit 1 = a cluster
+// handshake gave up, bit 2 = an index a kernel was handed was out of range.
+static __device__ unsigned int g_rk_status = 0;
+constexpr unsigned kStatusWaitTimeout = 1u;
+constexpr unsigned kStatusClusterTimeout = 2u;
+constexpr unsigned kStatusBadIndex = 4u;
+typedef unsigned (*StatusReader)(bool clear);
+void register_status_reader(StatusReader r);
+namespace {
+unsigned read_status_this_tu(bool clear) {
+    unsigned v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_rk_status, sizeof v) != cudaSuccess) return 0x80000000u;
+    if (clear && v) {
+        const unsigned z = 0;
+        cudaMemcpyToSymbol(g_rk_status, &z, sizeof z);
+    }
+    return v;
+}
+struct StatusRegistrar {
+    StatusRegistrar() { register_status_reader(&read_status_this_tu); }
+};
+static StatusRegistrar g_status_registrar;
+}  // namespace
+// Bounded mbarrier wait: try_wait suspends for a hardware-defined slice per call; 1<<22 calls is far
+// beyond any legal copy latency. On giving up it records the status bit and returns false.
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
+    for (uint32_t it = 0; it < (1u << 22); ++it)
+        if (mbar_try_wait(bar, parity)) return true;
+    atomicOr(&g_rk_status, kStatusWaitTimeout);
+    return false;
+}
+
+__device__ __forceinline__ float half_bits_to_float(uint32_t bits16) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(bits16 & 0xffffu)));
+}
+
+// ---------------------------------------------------------------------------------------------
+// Host-side launch helper: cudaLaunchKernelEx with the programmatic-stream-serialization attribute
+// (the kernel may start while the previous kernel on the stream finishes; it calls pdl_wait() before
+// touching that kernel's outputs).
+// ---------------------------------------------------------------------------------------------
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl,
+                       Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+int num_sms();
+
+}  // namespace rk

@@ -1,0 +1,429 @@
+// mmvq.cuh — the packed-tile Q6_K / Q8_0 x Q8_1 GEMV for sm_100a, shared by the C-ABI (mmvq.cu) and
+// the decode engine (engine.cu), which instantiates its fused prologue / epilogue variants.
+//
+// Weight layout: rk_pack_weights' tiles of 4 rows x 1024 values (3360 B for Q6_K, 4352 B for Q8_0,
+// byte-for-byte the GGUF bytes, reordered so each lane's 32-value group is one 16-byte vector).
+// A "unit" is one row tile over the whole input (n_in/1024 tiles, contiguous in memory). Units are
+// split into contiguous ranges per CTA (balanced per SM) and dealt round-robin to the CTA's warps.
+// Each warp streams its tiles through a private ring of `stages` shared-memory slots filled by 1-D
+// bulk copies (cp.async.bulk, no multicast) that complete on one mbarrier per slot; the warp's lane 0
+// is the producer, so a slot is refilled right after the warp has read it, with no cross-warp sync.
+// Lane g of a warp handles group g of each tile for the tile's 4 rows: the input column's 32 codes
+// and scale stay in registers while 4 rows of weights are decoded against them.
+//
+// Integer arithmetic (bit-exact with the reference's q6_q8_dot_impl / small_q8_dot,
+// src/native_mmvq.cu:642-655, :835-847): for each 16-value sub-block the 6-bit codes (0..63) are
+// dotted with the int8 activations by dp4a with the accumulator seeded at -32 * sum(activations),
+// which equals sum((code - 32) * x) exactly; times the int8 scale. Per group the two sub-block
+// products are added as integers (|sum| < 2^24, so the float conversion is exact) and accumulated
+// in fp32 as fma(float(isum), d8 * d, acc) per lane over the k-chunks, then reduced across the warp
+// by the xor butterfly. The per-row order does not depend on ncols, so every column of a
+// multi-column call is bitwise equal to a single-column call on that column.
+#pragma once
+
+#include "common.cuh"
+
+namespace rk {
+
+constexpr int kMmvqWarps = 8;      // consumer warps per CTA (256 threads)
+constexpr int kMmvqMaxStages = 8;  // ring slots per warp (runtime `stages` <= this)
+constexpr int kMmvqMaxCols = 4;    // columns per launch (more are split into launches over column chunks)
+
+enum MmvqPro { PRO_Q8 = 0, PRO_RMS = 1, PRO_SWIGLU = 2, PRO_SIGMUL = 3 };
+enum MmvqEpi { EPI_STORE = 0, EPI_RES = 1, EPI_ARGMAX = 2 };
+
+struct MmvqParams {
+    const uint8_t* w;  // packed tiles
+    int n_in, n_out;
+    int stages;
+    int prefetch_before_wait;  // 1: weights are static, stream them before waiting on the upstream grid
+    // prologue inputs
+    const uint8_t* xq;  // PRO_Q8: Q8_1 blocks, column stride rk_q8_1_bytes(n_in, 1)
+    const float* xa;    // PRO_RMS: x; PRO_SWIGLU: up; PRO_SIGMUL: o       (column stride xa_stride)
+    const float* xb;    // PRO_RMS: norm weight (shared); PRO_SWIGLU: gate; PRO_SIGMUL: g (stride xb_stride)
+    const float* pin;   // PRO_RMS: partials, column stride n_in/4
+    int xa_stride, xb_stride;
+    float eps;
+    // epilogue
+    float* y;
+    int y_stride;
+    const float* res;   // EPI_RES, column stride res_stride
+    int res_stride;
+    float* pout;        // EPI_RES partials, column stride pout_stride
+    int pout_stride;
+    unsigned long long* amax;  // EPI_ARGMAX: one packed (value, ~row) slot per column
+};
+
+// Smem bytes a launch needs for the activation staging and the rings.
+inline size_t mmvq_smem_bytes(int type, int n_in, int ncols, int stages) {
+    const size_t tile = type == RK_TYPE_Q6_K ? kQ6Tile : kQ80Tile;
+    return (size_t) kMmvqWarps * kMmvqMaxStages * 8 + (size_t) ncols * (n_in / 32) * 48 +
+           (size_t) kMmvqWarps * stages * tile;
+}
+
+// ---------------------------------------------------------------------------------------------------
+// The fixed-order reduction of rms_quant_apply_kernel (src/qwythos.cpp:634-641) over `nslots`
+// partials, for a 256-thread block: thread t sums slots t, t+256, ... in order; shfl_down tree in each
+// warp; red[0] + ... + red[7] in order. Every thread returns the same value. Uses `red` (8 floats).
+// ---------------------------------------------------------------------------------------------------
+__device__ __forceinline__ float block256_partials_sum(const float* partials, int nslots, float* red) {
+    const int t = threadIdx.x;
+    float part = 0.0f;
+    for (int p = t; p < nslots; p += 256) part = __fadd_rn(part, partials[p]);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) part = __fadd_rn(part, __shfl_down_sync(0xffffffffu, part, off));
+    __syncthreads();  // `red` may still be read by a previous call
+    if ((t & 31) == 0) red[t >> 5] = part;
+    __syncthreads();
+    float ss = red[0];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) ss = __fadd_rn(ss, red[w]);
+    return ss;
+}
+__device__ __forceinline__ float rms_inv(float ss, int cols, float eps) {
+    return rsqrtf(__fadd_rn(__fdiv_rn(ss, (float) cols), eps));
+}
+// The fused-quantize producers (one value per lane), shared with the standalone kernels so a fused
+// prologue writes the same bits the standalone kernel writes.
+__device__ __forceinline__ float rms_value(float x, float w, float inv) { return __fmul_rn(__fmul_rn(x, w), inv); }
+__device__ __forceinline__ float swiglu_value(float up, float g) {
+    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), up);
+}
+__device__ __forceinline__ float sigmul_value(float o, float g) {
+    return __fmul_rn(o, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g))));
+}
+
+// Staged activation group in shared memory: codes 0..15 in the lo plane, 16..31 in the hi plane
+// (16 B per group each), and {d8 (the half-rounded Q8_1 scale), 32*sum(codes 0..15), 32*sum(16..31)}.
+struct XStage {
+    int4* lo;
+    int4* hi;
+    float4* meta;
+};
+__device__ __forceinline__ XStage xstage_col(uint8_t* xsm, int ng, int c) {
+    XStage s;
+    s.lo = reinterpret_cast<int4*>(xsm + (size_t) c * ng * 48);
+    s.hi = s.lo + ng;
+    s.meta = reinterpret_cast<float4*>(s.hi + ng);
+    return s;
+}
+
+// One warp stores the Q8_1 block it just quantized (lane l owns code l) as a staged group.
+__device__ __forceinline__ void xstage_put_warp(const XStage& s, int g, int code, uint32_t ds, int lane) {
+    int8_t* lo = reinterpret_cast<int8_t*>(s.lo + g);
+    int8_t* hi = reinterpret_cast<int8_t*>(s.hi + g);
+    if (lane < 16) lo[lane] = (int8_t) code;
+    else hi[lane - 16] = (int8_t) code;
+    const int s0 = __reduce_add_sync(0xffffffffu, lane < 16 ? code : 0);
+    const int s1 = __reduce_add_sync(0xffffffffu, lane < 16 ? 0 : code);
+    if (lane == 0) s.meta[g] = make_float4(half_bits_to_float(ds), __int_as_float(32 * s0), __int_as_float(32 * s1), 0.0f);
+}
+
+// Build every column's staged activations. All 256 threads participate (contains __syncthreads).
+template <int NC, int PRO>
+__device__ __forceinline__ void mmvq_build_x(const MmvqParams& p, uint8_t* xsm, float* red) {
+    const int ng = p.n_in >> 5;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if constexpr (PRO == PRO_Q8) {
+        const size_t col_bytes = (size_t) ng * 36;
+        for (int idx = threadIdx.x; idx < NC * ng; idx += blockDim.x) {
+            const int c = idx / ng, g = idx - c * ng;
+            const int* blk = reinterpret_cast<const int*>(p.xq + (size_t) c * col_bytes + (size_t) g * 36);
+            const uint32_t ds = (uint32_t) blk[0];
+            const int4 a = make_int4(blk[1], blk[2], blk[3], blk[4]);
+            const int4 b = make_int4(blk[5], blk[6], blk[7], blk[8]);
+            const XStage s = xstage_col(xsm, ng, c);
+            s.lo[g] = a;
+            s.hi[g] = b;
+            const int s0 = __dp4a(a.x, 0x01010101, __dp4a(a.y, 0x01010101, __dp4a(a.z, 0x01010101, __dp4a(a.w, 0x01010101, 0))));
+            const int s1 = __dp4a(b.x, 0x01010101, __dp4a(b.y, 0x01010101, __dp4a(b.z, 0x01010101, __dp4a(b.w, 0x01010101, 0))));
+            s.meta[g] = make_float4(half_bits_to_float(ds), __int_as_float(32 * s0), __int_as_float(32 * s1), 0.0f);
+        }
+    } else {
+        float inv[NC];
+        if constexpr (PRO == PRO_RMS) {
+#pragma unroll
+            for (int c = 0; c < NC; ++c)
+                inv[c] = rms_inv(block256_partials_sum(p.pin + (size_t) c * (p.n_in / 4), p.n_in / 4, red), p.n_in,
+                                 p.eps);
+        }
+        for (int idx = warp; idx < NC * ng; idx += blockDim.x >> 5) {
+            const int c = idx / ng, g = idx - c * ng;
+            const int i = (g << 5) + lane;
+            float v;
+            if constexpr (PRO == PRO_RMS) {
+                v = rms_value(p.xa[(size_t) c * p.xa_stride + i], p.xb[i], inv[c]);
+            } else if constexpr (PRO == PRO_SWIGLU) {
+                v = swiglu_value(p.xa[(size_t) c * p.xa_stride + i], p.xb[(size_t) c * p.xb_stride + i]);
+            } else {
+                v = sigmul_value(p.xa[(size_t) c * p.xa_stride + i], p.xb[(size_t) c * p.xb_stride + i]);
+            }
+            uint32_t ds;
+            const int code = q8_1_warp_code(v, ds);
+            xstage_put_warp(xstage_col(xsm, ng, c), g, code, ds, lane);
+        }
+    }
+}
+
+// The 6-bit codes of one row of a group as eight ints (byte b of int T = code of value 4T + b),
+// from the packed ql (16 B) and qh (8 B) of that row.
+__device__ __forceinline__ void q6_decode(const uint4 ql, const uint2 qh, int v[8]) {
+    v[0] = (int) ((ql.x & 0x0f0f0f0fu) | ((qh.x << 4) & 0x30303030u));
+    v[1] = (int) ((ql.y & 0x0f0f0f0fu) | ((qh.x << 2) & 0x30303030u));
+    v[2] = (int) ((ql.z & 0x0f0f0f0fu) | (qh.x & 0x30303030u));
+    v[3] = (int) ((ql.w & 0x0f0f0f0fu) | ((qh.x >> 2) & 0x30303030u));
+    v[4] = (int) (((ql.x >> 4) & 0x0f0f0f0fu) | ((qh.y << 4) & 0x30303030u));
+    v[5] = (int) (((ql.y >> 4) & 0x0f0f0f0fu) | ((qh.y << 2) & 0x30303030u));
+    v[6] = (int) (((ql.z >> 4) & 0x0f0f0f0fu) | (qh.y & 0x30303030u));
+    v[7] = (int) (((ql.w >> 4) & 0x0f0f0f0fu) | ((qh.y >> 2) & 0x30303030u));
+}
+// sum over each 16-value sub-block of (code - 32) * x, exactly.
+__device__ __forceinline__ void q6_subsums(const int v[8], const int4 xa, const int4 xb, int b0, int b1, int& s0,
+                                           int& s1) {
+    s0 = __dp4a(v[0], xa.x, -b0);
+    s0 = __dp4a(v[1], xa.y, s0);
+    s0 = __dp4a(v[2], xa.z, s0);
+    s0 = __dp4a(v[3], xa.w, s0);
+    s1 = __dp4a(v[4], xb.x, -b1);
+    s1 = __dp4a(v[5], xb.y, s1);
+    s1 = __dp4a(v[6], xb.z, s1);
+    s1 = __dp4a(v[7], xb.w, s1);
+}
+__device__ __forceinline__ int sext8(uint32_t w, int byte) { return ((int) (w << (24 - 8 * byte))) >> 24; }
+
+// One Q6_K tile (4 rows x this lane's group) against NC staged columns.
+template <int NC>
+__device__ __forceinline__ void q6_tile(const uint8_t* t, int lane, const int4 (&xa)[NC], const int4 (&xb)[NC],
+                                        const float4 (&xm)[NC], float (&acc)[NC][4]) {
+    const uint2 scw = *reinterpret_cast<const uint2*>(t + 3072 + lane * 8);
+    const uint2 dw = *reinterpret_cast<const uint2*>(t + 3328 + (lane >> 3) * 8);
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+        const uint4 ql = *reinterpret_cast<const uint4*>(t + (r * 32 + lane) * 16);
+        const uint2 qh = *reinterpret_cast<const uint2*>(t + 2048 + (r * 32 + lane) * 8);
+        int v[8];
+        q6_decode(ql, qh, v);
+        const uint32_t sw = r < 2 ? scw.x : scw.y;
+        const int sc0 = sext8(sw, 2 * (r & 1)), sc1 = sext8(sw, 2 * (r & 1) + 1);
+        const float dr = half_bits_to_float((r < 2 ? dw.x : dw.y) >> (16 * (r & 1)));
+#pragma unroll
+        for (int c = 0; c < NC; ++c) {
+            int s0, s1;
+            q6_subsums(v, xa[c], xb[c], __float_as_int(xm[c].y), __float_as_int(xm[c].z), s0, s1);
+            const int isum = s0 * sc0 + s1 * sc1;
+            acc[c][r] = __fmaf_rn((float) isum, __fmul_rn(xm[c].x, dr), acc[c][r]);
+        }
+    }
+}
+
+// One Q8_0 tile.
+template <int NC>
+__device__ __forceinline__ void q80_tile(const uint8_t* t, int lane, const int4 (&xa)[NC], const int4 (&xb)[NC],
+                                         const float4 (&xm)[NC], float (&acc)[NC][4]) {
+    const uint2 dw = *reinterpret_cast<const uint2*>(t + 4096 + lane * 8);
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+        const int4 w0 = *reinterpret_cast<const int4*>(t + ((r * 2 + 0) * 32 + lane) * 16);
+        const int4 w1 = *reinterpret_cast<const int4*>(t + ((r * 2 + 1) * 32 + lane) * 16);
+        const float dr = half_bits_to_float((r < 2 ? dw.x : dw.y) >> (16 * (r & 1)));
+#pragma unroll
+        for (int c = 0; c < NC; ++c) {
+            int s = __dp4a(w0.x, xa[c].x, 0);
+            s = __dp4a(w0.y, xa[c].y, s);
+            s = __dp4a(w0.z, xa[c].z, s);
+            s = __dp4a(w0.w, xa[c].w, s);
+            s = __dp4a(w1.x, xb[c].x, s);
+            s = __dp4a(w1.y, xb[c].y, s);
+            s = __dp4a(w1.z, xb[c].z, s);
+            s = __dp4a(w1.w, xb[c].w, s);
+            acc[c][r] = __fmaf_rn((float) s, __fmul_rn(xm[c].x, dr), acc[c][r]);
+        }
+    }
+}
+
+// Monotonic key for the fused argmax: larger value -> larger key; among equal values the lower row wins.
+__device__ __forceinline__ unsigned long long argmax_key(float v, int row) {
+    uint32_t b = __float_as_uint(v);
+    b ^= (b >> 31) ? 0xffffffffu : 0x80000000u;
+    return ((unsigned long long) b << 32) | (unsigned long long) (0xffffffffu - (uint32_t) row);
+}
+__device__ __forceinline__ int argmax_key_row(unsigned long long k) { return (int) (0xffffffffu - (uint32_t) (k & 0xffffffffu)); }
+
+template <int NC, int EPI>
+__device__ __forceinline__ void mmvq_epilogue(const MmvqParams& p, int unit, int lane, float (&acc)[NC][4]) {
+#pragma unroll
+    for (int c = 0; c < NC; ++c)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) acc[c][r] = warp_sum(acc[c][r]);
+    const int row0 = unit * 4;
+    if constexpr (EPI == EPI_STORE || EPI == EPI_ARGMAX) {
+        if (p.y != nullptr) {
+            float out = 0.0f;
+#pragma unroll
+            for (int c = 0; c < NC; ++c)
+#pragma unroll
+                for (int r = 0; r < 4; ++r)
+                    if (lane == c * 4 + r) out = acc[c][r];
+            if (lane < NC * 4) p.y[(size_t) (lane >> 2) * p.y_stride + row0 + (lane & 3)] = out;
+        }
+        if constexpr (EPI == EPI_ARGMAX) {
+            if (lane < NC) {
+                float best = 0.0f;
+                int br = -1;
+#pragma unroll
+                for (int c = 0; c < NC; ++c)
+                    if (lane == c) {
+#pragma unroll
+                        for (int r = 0; r < 4; ++r)
+                            if (acc[c][r] == acc[c][r] && (br < 0 || acc[c][r] > best)) {
+                                best = acc[c][r];
+                                br = r;
+                            }
+                    }
+                if (br >= 0) atomicMax(p.amax + lane, argmax_key(best, row0 + br));
+            }
+        }
+    } else {  // EPI_RES
+        if (lane < NC) {
+#pragma unroll
+            for (int c = 0; c < NC; ++c)
+                if (lane == c) {
+                    const float* res = p.res + (size_t) c * p.res_stride + row0;
+                    float* y = p.y + (size_t) c * p.y_stride + row0;
+                    float part = 0.0f;
+#pragma unroll
+                    for (int r = 0; r < 4; ++r) {
+                        const float v = __fadd_rn(acc[c][r], res[r]);
+                        y[r] = v;
+                        part = __fmaf_rn(v, v, part);
+                    }
+                    p.pout[(size_t) c * p.pout_stride + unit] = part;
+                }
+        }
+    }
+}
+
+template <int TYPE, int NC, int PRO, int EPI>
+__global__ void __launch_bounds__(kMmvqWarps * 32, 1) mmvq_packed_kernel(const MmvqParams p) {
+    constexpr int TILE = TYPE == RK_TYPE_Q6_K ? kQ6Tile : kQ80Tile;
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ float red[8];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int KC = p.n_in >> 10;
+    const int ng = p.n_in >> 5;
+    const int stages = p.stages;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem) + warp * kMmvqMaxStages;
+    uint8_t* xsm = smem + kMmvqWarps * kMmvqMaxStages * 8;
+    uint8_t* ring = xsm + (size_t) NC * ng * 48 + (size_t) warp * stages * TILE;
+
+    const int units = p.n_out >> 2;
+    const int ubeg = (int) (((long long) blockIdx.x * units) / gridDim.x);
+    const int uend = (int) (((long long) (blockIdx.x + 1) * units) / gridDim.x);
+    const int my_units = (uend - ubeg > warp) ? (uend - ubeg - warp + kMmvqWarps - 1) / kMmvqWarps : 0;
+    const int ntiles = my_units * KC;
+
+    if (lane == 0) {
+        for (int s = 0; s < stages; ++s) mbar_init(smem_u32(bars + s), 1);
+        fence_mbar_init();
+    }
+    __syncwarp();
+    const uint64_t pol = policy_evict_first();
+    auto issue = [&](int i) {
+        const int u = ubeg + warp + (i / KC) * kMmvqWarps;
+        const uint8_t* src = p.w + ((size_t) u * KC + (size_t) (i % KC)) * TILE;
+        const int s = i % stages;
+        mbar_arrive_expect_tx(smem_u32(bars + s), TILE);
+        bulk_g2s(smem_u32(ring + (size_t) s * TILE), src, TILE, smem_u32(bars + s), pol);
+    };
+    const int npre = ntiles < stages ? ntiles : stages;
+    pdl_trigger();
+    if (p.prefetch_before_wait && lane == 0)
+        for (int i = 0; i < npre; ++i) issue(i);
+    pdl_wait();
+    if (!p.prefetch_before_wait && lane == 0)
+        for (int i = 0; i < npre; ++i) issue(i);
+
+    mmvq_build_x<NC, PRO>(p, xsm, red);
+    __syncthreads();
+
+    float acc[NC][4];
+#pragma unroll
+    for (int c = 0; c < NC; ++c)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) acc[c][r] = 0.0f;
+
+    int s = 0, kc = 0, unit = ubeg + warp;
+    uint32_t parity = 0;
+    for (int i = 0; i < ntiles; ++i) {
+        const bool landed = mbar_wait_bounded(smem_u32(bars + s), parity);
+        if (!__all_sync(0xffffffffu, landed)) break;
+        const uint8_t* t = ring + (size_t) s * TILE;
+        int4 xa[NC], xb[NC];
+        float4 xm[NC];
+        const int g = (kc << 5) + lane;
+#pragma unroll
+        for (int c = 0; c < NC; ++c) {
+            const XStage xs = xstage_col(xsm, ng, c);
+            xa[c] = xs.lo[g];
+            xb[c] = xs.hi[g];
+            xm[c] = xs.meta[g];
+        }
+        if constexpr (TYPE == RK_TYPE_Q6_K) q6_tile<NC>(t, lane, xa, xb, xm, acc);
+        else q80_tile<NC>(t, lane, xa, xb, xm, acc);
+        __syncwarp();
+        if (lane == 0 && i + stages < ntiles) {
+            fence_proxy_async_smem();
+            issue(i + stages);
+        }
+        if (++s == stages) {
+            s = 0;
+            parity ^= 1u;
+        }
+        if (++kc == KC) {
+            mmvq_epilogue<NC, EPI>(p, unit, lane, acc);
+#pragma unroll
+            for (int c = 0; c < NC; ++c)
+#pragma unroll
+                for (int r = 0; r < 4; ++r) acc[c][r] = 0.0f;
+            kc = 0;
+            unit += kMmvqWarps;
+        }
+    }
+}
+
+// Host-side launcher for one instantiation: sets the smem attribute once, picks the stage count that
+// keeps two CTAs per SM where possible, grid = one CTA per SM (capped by the unit count).
+template <int TYPE, int NC, int PRO, int EPI>
+cudaError_t mmvq_launch(MmvqParams p, cudaStream_t s, bool pdl) {
+    static int configured_smem = -1;
+    static int max_optin = 0;
+    if (max_optin == 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&max_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+        if (max_optin <= 0) max_optin = 227 * 1024;
+    }
+    const size_t tile = TYPE == RK_TYPE_Q6_K ? kQ6Tile : kQ80Tile;
+    const size_t fixed = mmvq_smem_bytes(TYPE, p.n_in, NC, 0);
+    // two CTAs per SM need <= ~113 KB each; fall back to one CTA with a deeper ring when x is large
+    int stages = (int) ((113 * 1024 - (long long) fixed) / (long long) (kMmvqWarps * tile));
+    if (stages < 3) {
+        stages = (int) (((long long) max_optin - 2048 - (long long) fixed) / (long long) (kMmvqWarps * tile));
+        if (stages > kMmvqMaxStages) stages = kMmvqMaxStages;
+    }
+    if (stages < 2) return cudaErrorInvalidValue;
+    p.stages = stages;
+    const size_t smem = mmvq_smem_bytes(TYPE, p.n_in, NC, stages);
+    if ((int) smem > configured_smem) {
+        cudaError_t e = cudaFuncSetAttribute(mmvq_packed_kernel<TYPE, NC, PRO, EPI>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+        if (e != cudaSuccess) return e;
+        configured_smem = (int) smem;
+    }
+    const int units = p.n_out / 4;
+    int grid = num_sms();
+    if (grid > units) grid = units;
+    return launch_pdl(mmvq_packed_kernel<TYPE, NC, PRO, EPI>, dim3(grid), dim3(kMmvqWarps * 32), smem, s, pdl, p);
+}
+
+}  // namespace rk
