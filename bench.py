@@ -144,7 +144,8 @@ def run_gemv(args, rank, world, local, pg):
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    stream = torch.cuda.current_stream(dev)
+    stream = torch.cuda.Stream(device=dev)  # the C-ABI requires an explicit (non-default) stream
+    torch.cuda.set_stream(stream)
     n_in, n_out, nc = GEMV_N_IN, GEMV_N_OUT, GEMV_NCOLS
     wb = ops.native_mmvq_weight_bytes(14, n_in, n_out)
     # synthetic weights: seeded N(0, 0.02) quantized by the oracle's encoder once, repacked on the device

@@ -28,4 +28,6 @@ def cuda():
     assert torch.cuda.is_available(), "GPU test selected but no CUDA device is visible"
     import rapier_b200  # noqa: F401  (fails loudly when the library is missing)
 
+    # the C-ABI requires an explicit stream (as the reference's native_mmvq does): run every test on one
+    torch.cuda.set_stream(torch.cuda.Stream(device=0))
     return torch.device("cuda:0")
