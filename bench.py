@@ -3,6 +3,11 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl rapier|reference] [--workload gemv|decode]
 
 Workloads (synthetic seeded data, no model file):
+  decode  config 5 (default): the 9B-shaped qwen35 hybrid (24 GDN + 8 GQA layers, MTP block), random-init
+          weights quantized to Q6_K, greedy decode of 400 tokens from a seeded 32-token prompt with exact
+          MTP (--no-mtp: config 4). A step is one 400-token generation; tok/s = generated tokens / device
+          time of the generation (prefill excluded, as the reference's tok_s, src/qwythos.cpp:3243-3247).
+          Weights (6.5 GB) exceed L2, so every token streams them from HBM.
   gemv    config 1: Q6_K x Q8_1 GEMV, W 12288x4096 ~ N(0, 0.02), x 4096 ~ N(0, 1), ncols 2 (the verify's
           shape). A step is one GEMV; weights rotate over 8 packed copies (330 MB > the 126 MB L2), so
           every step streams its weights from HBM.
@@ -241,15 +246,156 @@ def cpu_baseline_gemv(sample_rows=4096):
             "sample": f"{sample_rows}x{n_in} rows of config 1, ncols {nc}, {reps} reps"}
 
 
+# ------------------------------------------------------------------------------------------------------
+# decode workload (configs 4 / 5)
+# ------------------------------------------------------------------------------------------------------
+N_PROMPT, N_GEN = 32, 400
+
+
+def run_decode(args, rank, world, local, pg):
+    import torch
+
+    from rapier_b200.engine import Engine, config_9b
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    cfg = config_9b(max_ctx=args.ctx, seed=1 + rank)
+    eng = Engine(cfg, device=local)
+    prompt = [int(t) for t in np.random.default_rng(1234 + rank).integers(0, cfg.n_vocab, N_PROMPT)]
+    mtp = not args.no_mtp
+    for _ in range(args.warmup):
+        eng.generate(prompt, N_GEN, mtp=mtp)
+    barrier(pg, dev)
+    gen_ms, stats = 0.0, None
+    t0 = time.perf_counter()
+    with ClockSampler(local) as clk:
+        for _ in range(args.steps):
+            ids, st = eng.generate(prompt, N_GEN, mtp=mtp)
+            gen_ms += st["gen_ms"]
+            stats = st
+        barrier(pg, dev)
+    wall_s = time.perf_counter() - t0
+    gen_ms = max_over_ranks(gen_ms, pg, dev)
+    wall_s = max_over_ranks(wall_s, pg, dev)
+    tokens = N_GEN * args.steps * world
+    probe = eng.probe_gemv(ncols=2 if mtp else 1, iters=20)
+    eng.close()
+    peak, peak_kind = measured_peaks()
+    per_launch_s = probe["ms"] / 1e3 / (probe["iters"] * probe["launches"])
+    algo_per_launch = probe["algo_bytes"] / probe["launches"]
+    achieved = algo_per_launch / per_launch_s / 1e9
+    rounds = stats["mtp_steps"]
+    launches_per_gen = (stats["single_steps"] * stats["kernels_per_single_step"] +
+                        rounds * stats["kernels_per_round"])
+    line = {
+        "metric": "greedy decode tok/s (1 B200, exact MTP)" if mtp else "greedy decode tok/s (1 B200, no MTP)",
+        "value": round(tokens / (gen_ms / 1e3), 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(gen_ms / args.steps, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "q6_k x q8_1 int8 dp4a, fp32 accumulate, fp16 KV",
+        "data": "synthetic (random-init weights, seeded prompt)",
+        "config": {"workload": "config5-decode-mtp" if mtp else "config4-decode", "model": "qwen35-9b-shaped",
+                   "layers": "24 GDN + 8 GQA (+1 MTP block)", "n_prompt": N_PROMPT, "n_gen": N_GEN,
+                   "ctx": args.ctx, "parallelism": f"replicas x{world}",
+                   "l2": "6.5 GB of weights per token > 126 MB L2"},
+        "mtp": {"rounds": rounds, "accepted": stats["mtp_accepted"],
+                "acceptance": round(stats["mtp_accepted"] / rounds, 4) if rounds else None,
+                "single_steps": stats["single_steps"]} if mtp else None,
+        "roofline": {"bound": "hbm", "kernel": "mmvq_packed_kernel (all GEMVs of one trunk step, graph replay)",
+                     "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                     "traffic": None, "peak_source": peak_kind, "algorithmic_bytes_per_launch": round(algo_per_launch),
+                     "launches": probe["launches"], "avg_launch_us": round(per_launch_s * 1e6, 3)},
+        "e2e": {"value": round(tokens / wall_s, 2), "unit": "tok/s",
+                "h2d_bytes_per_step": N_PROMPT * 4 + 32 * (N_PROMPT + 2),
+                "d2h_bytes_per_step": N_GEN * 4 + 4 * rounds + 96},
+        "gpu_launches": launches_per_gen * args.steps,
+        "clocks": clk.summary(),
+    }
+    return line
+
+
+def cpu_baseline_decode(budget_s=20.0):
+    """The oracle (C restatement, OpenMP over the host cores) on one GDN layer, one attention layer and the
+    lm_head of the 9B shape; token time extrapolated as 24 x GDN + 8 x attention + head."""
+    from oracle import oracle as O
+    from oracle.model import Model
+    from rapier_b200.engine import config_9b
+
+    cfg = config_9b(max_ctx=64, seed=1)
+    cfg.n_layer, cfg.attn_interval = 4, 4  # layers 0..2 GDN, 3 attention; layers 0 and 3 are timed
+    t_gen = time.perf_counter()
+    m = Model(cfg)
+    t_gen = time.perf_counter() - t_gen
+    H = cfg.n_embd
+    x = O.synth_normal(3, H)
+    timings = {"gdn": [], "attn": [], "head": []}
+    t_end = time.perf_counter() + budget_s
+    pos = 0
+    while (time.perf_counter() < t_end or pos < 2) and pos < cfg.max_ctx:
+        for kind, il in (("gdn", 0), ("attn", 3)):
+            t0 = time.perf_counter()
+            one_layer_forward(m, il, x, pos)
+            timings[kind].append(time.perf_counter() - t0)
+        t0 = time.perf_counter()
+        xq = O.rms_quant_q8_1(x, m.out_norm, O.row_sumsq_partials(x), np.float32(cfg.eps))
+        O.mmvq(O.TYPE_Q6_K, m.lm_head, xq, H, cfg.n_vocab)
+        timings["head"].append(time.perf_counter() - t0)
+        pos += 1
+    med = {k: statistics.median(v) for k, v in timings.items()}
+    t_tok = 24 * med["gdn"] + 8 * med["attn"] + med["head"]
+    return {"value": round(1.0 / t_tok, 4), "unit": "tok/s", "cores": O.num_threads(), "kind": "port",
+            "sample": f"{pos} tokens through 1 GDN + 1 attention layer + lm_head of the 9B shape (no MTP); token "
+                      f"time extrapolated as 24 GDN + 8 attention + head = {t_tok * 1e3:.1f} ms "
+                      f"(weights generated in {t_gen:.1f} s, untimed)"}
+
+
+def one_layer_forward(model, il, x, pos):
+    """Layer il of oracle.model.Model.forward (mixer + FFN) on hidden x at position pos."""
+    from oracle import oracle as O
+
+    H, L, st, eps, Q6 = model.H, model.layers[il], model.state[il], model.eps, O.TYPE_Q6_K
+    xp = O.row_sumsq_partials(x)
+    xq = O.rms_quant_q8_1(x, L["attn_norm"], xp, eps)
+    if L["gdn"]:
+        hk, hv, C, KS = model.hk, model.hv, model.C, 128
+        proj = O.mmvq(Q6, L["in_proj"], xq, H, 2 * hk * KS + 2 * hv * KS + 2 * hv)
+        z = proj[C:C + hv * KS]
+        beta, g = O.beta_gate(proj[C + hv * KS:C + hv * KS + hv], proj[C + hv * KS + hv:], L["dt"], L["ssm_a"])
+        st["ring"], h = O.gdn_conv_l2(st["ring"], proj[:C], L["conv_w"], C, 2 * hk, eps, pos)
+        st["ssm"], _, q8 = O.gdn_step_norm_silu_q8(st["ssm"], h[:hk * KS], h[hk * KS:2 * hk * KS], h[2 * hk * KS:C],
+                                                   g, beta, z, L["ssm_norm"], eps, hk, hv)
+        x2, xp = O.mmvq_res(Q6, L["out_proj"], q8, x, hv * KS, H)
+    else:
+        nh, nkv, HD = model.nh, model.nkv, 256
+        q3 = O.mmvq(Q6, L["in_proj"], xq, H, 2 * nh * HD + 2 * nkv * HD)
+        q, gate = O.split_qg(q3[:2 * nh * HD], nh, HD)
+        k = q3[2 * nh * HD:2 * nh * HD + nkv * HD]
+        v = q3[2 * nh * HD + nkv * HD:]
+        q = O.rope_apply(O.rms_norm_rows(q, L["q_norm"], nh, HD, eps), nh, HD, 64, model.rope, pos)
+        k = O.rope_apply(O.rms_norm_rows(k, L["k_norm"], nkv, HD, eps), nkv, HD, 64, model.rope, pos)
+        st["k"][pos] = O.f32_to_f16(k).reshape(nkv, HD)
+        st["v"][pos] = O.f32_to_f16(v).reshape(nkv, HD)
+        o = O.gqa_decode_f16(q, st["k"].ravel(), st["v"].ravel(), nh, nkv, HD, pos + 1, 0.0625)
+        x2, xp = O.mmvq_res(Q6, L["out_proj"], O.sigmul_q8_1(o, gate), x, nh * HD, H)
+    xq = O.rms_quant_q8_1(x2, L["post_norm"], xp, eps)
+    ug = O.mmvq(Q6, L["upgate"], xq, H, 2 * model.FF)
+    return O.mmvq_res(Q6, L["down"], O.swiglu_q8_1(ug[:model.FF], ug[model.FF:]), x2, model.FF, H)[0]
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
-    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=None)
+    ap.add_argument("--warmup", type=int, default=None)
     ap.add_argument("--impl", default="rapier", choices=["rapier", "reference"])
-    ap.add_argument("--workload", default="gemv", choices=["gemv"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "gemv"])
+    ap.add_argument("--ctx", type=int, default=512, help="decode: KV capacity (512 or 65536)")
+    ap.add_argument("--no-mtp", action="store_true", help="decode: plain greedy (config 4)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
+    if args.steps is None:
+        args.steps = 5 if args.workload == "decode" else 200
+    if args.warmup is None:
+        args.warmup = 3 if args.workload == "decode" else 10
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
 
@@ -257,24 +403,28 @@ def main():
         rank = int(os.environ.get("RANK", "0"))
         if rank != 0:
             return
-        base = cpu_baseline_gemv()
-        line = {"impl": "reference", "metric": "Q6_K x Q8_1 GEMV HBM GB/s (12288x4096, ncols 2)",
-                "value": base["value"], "unit": base["unit"], "n_gpus": args.gpus, "steps": args.steps,
-                "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-                "dtype": "q6_k x q8_1 int8, fp32 accumulate", "data": "synthetic",
-                "config": {"workload": "config1-gemv", "n_in": GEMV_N_IN, "n_out": GEMV_N_OUT,
-                           "ncols": GEMV_NCOLS},
-                "cpu_baseline": base,
-                "e2e": {"value": base["value"], "unit": base["unit"], "h2d_bytes_per_step": 0,
-                        "d2h_bytes_per_step": 0}}
+        if args.workload == "decode":
+            base = cpu_baseline_decode()
+            metric = "greedy decode tok/s (1 B200, exact MTP)" if not args.no_mtp else "greedy decode tok/s (no MTP)"
+            cfgd = {"workload": "config5-decode-mtp" if not args.no_mtp else "config4-decode",
+                    "model": "qwen35-9b-shaped", "n_prompt": N_PROMPT, "n_gen": N_GEN, "ctx": args.ctx}
+        else:
+            base = cpu_baseline_gemv()
+            metric = "Q6_K x Q8_1 GEMV HBM GB/s (12288x4096, ncols 2)"
+            cfgd = {"workload": "config1-gemv", "n_in": GEMV_N_IN, "n_out": GEMV_N_OUT, "ncols": GEMV_NCOLS}
+        line = {"impl": "reference", "metric": metric, "value": base["value"], "unit": base["unit"],
+                "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "q6_k x q8_1 int8, fp32 accumulate",
+                "data": "synthetic", "config": cfgd, "cpu_baseline": base,
+                "e2e": {"value": base["value"], "unit": base["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
         return
 
     rank, world, local, pg = dist_init(args.gpus)
-    line = run_gemv(args, rank, world, local, pg)
+    line = (run_decode if args.workload == "decode" else run_gemv)(args, rank, world, local, pg)
     if rank == 0:
         if world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline_gemv()
+            line["cpu_baseline"] = cpu_baseline_decode() if args.workload == "decode" else cpu_baseline_gemv()
         print(json.dumps(line), flush=True)
     if pg is not None:
         pg.destroy_process_group()

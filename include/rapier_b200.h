@@ -81,6 +81,12 @@ int rk_unpack_weights(int type, const void* src, void* dst, int n_in, int n_out,
 /* Same contract as rk_mmvq on packed weights, 1 <= ncols <= 16. */
 int rk_mmvq_packed(int type, const void* packed, const void* x_q8_1, float* y, int n_in, int n_out, int ncols,
                    void* stream);
+/* rk_mmvq_packed with launch flags. RK_FLAG_STATIC_WEIGHTS: no kernel still in flight on the stream writes
+ * these weights, so the GEMV may start streaming them before the previous kernel on the stream has
+ * finished (programmatic dependent launch); it still waits for that kernel before reading x_q8_1. */
+#define RK_FLAG_STATIC_WEIGHTS 1u
+int rk_mmvq_packed_ex(int type, const void* packed, const void* x_q8_1, float* y, int n_in, int n_out, int ncols,
+                      unsigned flags, void* stream);
 /* Same contract as rk_mmvq_res on packed weights, per column j: y + j*n_out, res + j*n_out,
  * partials + j*(n_out/4). 1 <= ncols <= 16. (The reference runs a 2-column GEMV plus add_partials for
  * this, src/qwythos.cpp:1489-1494.) */
@@ -169,6 +175,83 @@ size_t rk_gqa_scratch_bytes(int n_head, int ncols, int max_ctx);
 int rk_gqa_decode_f16(const float* q, const uint16_t* kcache, const uint16_t* vcache, float* o, int n_head,
                       int n_kv, int hd, int ncols, const int* pos, int max_ctx, float scale, void* scratch,
                       size_t scratch_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------------------------- */
+/* Decode engine (the reference's Engine / load_model / forward_token / draft_predict /              */
+/* launch_token_verify, src/qwythos.cpp:152-281, :1228-1618, :1757-1824, :1978-2134, :2905-3251)      */
+/* ---------------------------------------------------------------------------------------------- */
+/* Model geometry (the reference's compile-time constants, src/qwythos.cpp:33-44, as a runtime struct).
+ * Layer il is full attention when (il + 1) % attn_interval == 0 (src/qwythos.cpp:2016), else Gated
+ * DeltaNet. The weights are synthetic: every tensor is drawn from `seed` by the counter-based generator
+ * and quantized to Q6_K by this library's encoder (no model file is read). */
+typedef struct rk_model_config {
+    int n_layer;       /* trunk layers (32) */
+    int n_embd;        /* hidden (4096) */
+    int n_ff;          /* SwiGLU width (12288) */
+    int n_vocab;       /* 248320 */
+    int ssm_h_k;       /* GDN key heads (16), head size 128 */
+    int ssm_h_v;       /* GDN value heads (32) == 2 * ssm_h_k */
+    int n_head;        /* attention query heads (16), head_dim 256 */
+    int n_head_kv;     /* attention kv heads (4) == n_head / 4 */
+    int n_rot;         /* rotary dims (64) */
+    int attn_interval; /* 4 */
+    int has_mtp;       /* build the nextn draft block (block n_layer) */
+    int max_ctx;       /* KV capacity in positions */
+    float eps;         /* RMSNorm epsilon (1e-6) */
+    double rope_base;  /* 1e7 */
+    uint64_t seed;
+} rk_model_config;
+
+/* Fills `cfg` with the 9B (Qwythos / Qwen3.5-9B) geometry and the given context and seed. */
+void rk_model_config_9b(rk_model_config* cfg, int max_ctx, uint64_t seed);
+
+typedef struct rk_engine rk_engine;
+
+typedef struct rk_gen_stats {
+    double prefill_ms; /* prompt positions 0..P-2 */
+    double gen_ms;     /* from the seed pass (position P-1) to the last generated token, device time */
+    int n_gen;
+    int mtp_steps;     /* verify rounds */
+    int mtp_accepted;  /* accepted drafts */
+    int single_steps;  /* 1-token trunk passes inside the generation */
+    int graph_launches;
+    int kernels_per_single_step;
+    int kernels_per_round;
+} rk_gen_stats;
+
+/* Allocates the engine on `device`, generates the synthetic model and captures the step graphs.
+ * Returns RK_ENOMEM when the device cannot hold it. */
+int rk_engine_create(const rk_model_config* cfg, int device, rk_engine** out);
+int rk_engine_destroy(rk_engine* e);
+/* Clears KV caches, GDN states, conv rings and the draft cache (the reference's op:reset,
+ * src/qwythos.cpp:2533-2549). */
+int rk_engine_reset(rk_engine* e);
+/* Greedy generation (the reference's CLI loop, src/qwythos.cpp:2905-3251): feeds prompt[0..n_prompt-1]
+ * (positions 0..n_prompt-2 as prefill, the last one as the seed pass), then generates n_gen tokens into
+ * out_ids. use_mtp != 0: exact MTP (draft 1 token, 2-column verify, greedy acceptance, rollback); the
+ * token stream is identical to use_mtp == 0. stats may be NULL. */
+int rk_engine_generate(rk_engine* e, const int* prompt, int n_prompt, int n_gen, int use_mtp, int* out_ids,
+                       rk_gen_stats* stats);
+/* One teacher-forced trunk pass (forward_token, src/qwythos.cpp:1773-1824) of ncols (1 or 2) tokens at
+ * positions pos, pos+1: updates the caches and states like a decode step and copies the logits
+ * (ncols x n_vocab floats) and argmax ids to the host (either may be NULL). */
+int rk_engine_step(rk_engine* e, const int* tokens, int ncols, int pos, float* logits, int* argmax);
+/* Copies tensor `tid` (this library's synthetic tensor id) to the host: GGUF Q6_K bytes for quantized
+ * matrices, fp32 values otherwise. bytes == 0 returns the size. Test hook, no reference counterpart. */
+size_t rk_engine_read_tensor(rk_engine* e, int tid, void* host, size_t bytes);
+typedef struct rk_probe_result {
+    double ms;           /* device time of `iters` replays */
+    int launches;        /* GEMV launches per replay */
+    double weight_bytes; /* Q6_K weight bytes streamed per replay */
+    double algo_bytes;   /* weights + activation inputs + outputs (+ residual reads) per replay */
+} rk_probe_result;
+/* The reference's probe_gemv (src/qwythos.cpp:1621-1755): replays the GEMVs of one trunk step (every
+ * layer's four projection groups and the lm_head, ncols columns, the same kernels and launch settings as
+ * the decode graphs) back to back as one graph, `iters` times, timed with CUDA events. It overwrites the
+ * engine's activation buffers (not the caches or states); call rk_engine_reset or generate afterwards. */
+int rk_engine_probe_gemv(rk_engine* e, int ncols, int iters, rk_probe_result* out);
+/* Device bytes the engine holds. */
+size_t rk_engine_device_bytes(const rk_engine* e);
 
 #ifdef __cplusplus
 }

@@ -14,6 +14,7 @@ ROOT = os.path.dirname(PKG)
 LIB_PATH = os.path.join(PKG, "librapier_b200.so")
 HEADER = os.path.join(ROOT, "include", "rapier_b200.h")
 
+RK_FLAG_STATIC_WEIGHTS = 1
 RK_OK, RK_EINVAL, RK_ECUDA, RK_ENOMEM, RK_ERANGE, RK_EUNSUPPORTED = 0, -1, -2, -3, -4, -5
 TYPE_Q8_0, TYPE_Q6_K = 8, 14
 _CODE_NAMES = {RK_EINVAL: "RK_EINVAL", RK_ECUDA: "RK_ECUDA", RK_ENOMEM: "RK_ENOMEM", RK_ERANGE: "RK_ERANGE",
@@ -31,6 +32,26 @@ _lib = None
 
 vp, i32, u32, f32, sz, i64 = C.c_void_p, C.c_int, C.c_uint, C.c_float, C.c_size_t, C.c_int64
 
+class ModelConfig(C.Structure):
+    """rk_model_config (include/rapier_b200.h)."""
+    _fields_ = [("n_layer", C.c_int), ("n_embd", C.c_int), ("n_ff", C.c_int), ("n_vocab", C.c_int),
+                ("ssm_h_k", C.c_int), ("ssm_h_v", C.c_int), ("n_head", C.c_int), ("n_head_kv", C.c_int),
+                ("n_rot", C.c_int), ("attn_interval", C.c_int), ("has_mtp", C.c_int), ("max_ctx", C.c_int),
+                ("eps", C.c_float), ("rope_base", C.c_double), ("seed", C.c_uint64)]
+
+
+class GenStats(C.Structure):
+    """rk_gen_stats (include/rapier_b200.h)."""
+    _fields_ = [("prefill_ms", C.c_double), ("gen_ms", C.c_double), ("n_gen", C.c_int), ("mtp_steps", C.c_int),
+                ("mtp_accepted", C.c_int), ("single_steps", C.c_int), ("graph_launches", C.c_int),
+                ("kernels_per_single_step", C.c_int), ("kernels_per_round", C.c_int)]
+
+
+class ProbeResult(C.Structure):
+    """rk_probe_result (include/rapier_b200.h)."""
+    _fields_ = [("ms", C.c_double), ("launches", C.c_int), ("weight_bytes", C.c_double), ("algo_bytes", C.c_double)]
+
+
 # name -> (restype, argtypes); every function declared in include/rapier_b200.h appears here.
 SIGNATURES = {
     "rk_last_error": (C.c_char_p, []),
@@ -45,6 +66,7 @@ SIGNATURES = {
     "rk_pack_weights": (i32, [i32, vp, vp, i32, i32, vp]),
     "rk_unpack_weights": (i32, [i32, vp, vp, i32, i32, vp]),
     "rk_mmvq_packed": (i32, [i32, vp, vp, vp, i32, i32, i32, vp]),
+    "rk_mmvq_packed_ex": (i32, [i32, vp, vp, vp, i32, i32, i32, u32, vp]),
     "rk_mmvq_packed_res": (i32, [i32, vp, vp, vp, vp, vp, i32, i32, i32, vp]),
     "rk_mmvq_isums": (i32, [i32, vp, vp, vp, i32, i32, i32, vp]),
     "rk_row_sumsq_partials": (i32, [vp, vp, i32, vp]),
@@ -64,6 +86,15 @@ SIGNATURES = {
     "rk_store_kv_f16": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, vp]),
     "rk_gqa_scratch_bytes": (sz, [i32, i32, i32]),
     "rk_gqa_decode_f16": (i32, [vp, vp, vp, vp, i32, i32, i32, i32, vp, i32, f32, vp, sz, vp]),
+    "rk_model_config_9b": (None, [C.POINTER(ModelConfig), i32, C.c_uint64]),
+    "rk_engine_create": (i32, [C.POINTER(ModelConfig), i32, C.POINTER(vp)]),
+    "rk_engine_destroy": (i32, [vp]),
+    "rk_engine_reset": (i32, [vp]),
+    "rk_engine_generate": (i32, [vp, C.POINTER(C.c_int), i32, i32, i32, C.POINTER(C.c_int), C.POINTER(GenStats)]),
+    "rk_engine_step": (i32, [vp, C.POINTER(C.c_int), i32, i32, vp, C.POINTER(C.c_int)]),
+    "rk_engine_read_tensor": (sz, [vp, i32, vp, sz]),
+    "rk_engine_device_bytes": (sz, [vp]),
+    "rk_engine_probe_gemv": (i32, [vp, i32, i32, C.POINTER(ProbeResult)]),
 }
 
 

@@ -1,6 +1,7 @@
 // abi.cu — C-ABI plumbing shared by every module: thread-local error messages, the device status
 // registry, the SM count.
 #include <cstdarg>
+#include <cstdlib>
 #include <cstdio>
 #include <mutex>
 #include <vector>
@@ -36,6 +37,19 @@ int check_launch(const char* what) {
 void register_status_reader(StatusReader r) {
     std::lock_guard<std::mutex> lk(g_status_mu);
     status_readers().push_back(r);
+}
+
+static int env_int(const char* name) {
+    const char* v = std::getenv(name);
+    return v ? std::atoi(v) : 0;
+}
+int mmvq_env_stages() {
+    static const int v = env_int("RK_MMVQ_STAGES");
+    return v;
+}
+int mmvq_env_ctas() {
+    static const int v = env_int("RK_MMVQ_CTAS");
+    return v;
 }
 
 int num_sms() {

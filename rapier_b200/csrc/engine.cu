@@ -1,0 +1,1086 @@
+// engine.cu — the decode engine for the qwen35 hybrid model: the reference's Engine / load_model /
+// forward_token / draft_predict / launch_token_verify (src/qwythos.cpp:152-281, :1228-1618, :1757-1824,
+// :1978-2134, :2905-3251) rebuilt around CUDA graphs and a device-side control block.
+//
+// Per token (1 column) or per MTP round (2 columns), every kernel reads its tokens, positions and the
+// rollback flag from a device Ctrl block, so a non-MTP generation is one graph replayed n times with no
+// host round trip, and an MTP round is one graph: 2-column verify -> accept -> 2-column draft.
+//
+// Kernels per trunk layer (all with programmatic dependent launch; weights stream before the wait):
+//   GDN  : GEMV qkv||z||beta||alpha (RMSNorm+Q8_1 prologue) -> fused conv/L2/delta-rule/norm/Q8_1 ->
+//          GEMV ssm_out (+residual, partials) -> GEMV up||gate (RMSNorm prologue) -> GEMV down (SwiGLU+Q8_1
+//          prologue, +residual, partials)
+//   ATTN : GEMV q||k||v (RMSNorm prologue) -> split/q-k norm/RoPE/fp16 KV store -> flash-decode chunks ->
+//          combine -> GEMV wo (sigmoid-gate+Q8_1 prologue, +residual) -> FFN as above
+// then the lm_head GEMV with the final RMSNorm prologue and a fused argmax epilogue.
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <vector>
+
+#include "mmvq.cuh"
+
+namespace rk {
+
+cudaError_t gdn_fused_launch(const float* proj, int proj_stride, float* ring, const float* conv_w, const float* dt_bias,
+                             const float* ssm_a, const float* gamma, float* state, float* snap, const int* rollback,
+                             float* y, uint8_t* q8, int h_k, int h_v, int ncols, const int* pos, float eps,
+                             cudaStream_t s, bool pdl);
+cudaError_t gqa_launch(const float* q, const __half* kc, const __half* vc, float* o, int n_head, int n_kv, int ncols,
+                       const int* pos, int max_ctx, float scale, float* scratch, cudaStream_t s, bool pdl);
+size_t gqa_scratch_bytes(int n_head, int ncols, int max_ctx);
+
+namespace {
+
+constexpr int kHd = 256;     // attention head dim
+constexpr int kS = 128;      // GDN head size
+constexpr float kAttnScale = 0.0625f;  // 1/sqrt(256)
+
+// ------------------------------------------------------------------------------------------------
+// Synthetic weights: value(i) of tensor t = (sum of the four 16-bit fields of hash(seed_t, i) - 131070)
+// * scale + mean, seed_t = hash(model seed, t). Q6_K tensors are then encoded per 256-value block.
+// ------------------------------------------------------------------------------------------------
+__host__ __device__ __forceinline__ uint64_t hash64(uint64_t seed, uint64_t idx) {
+    uint64_t z = seed * 0x9E3779B97F4A7C15ull + idx + 0x632BE59BD9B4E019ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+__host__ __device__ __forceinline__ int synth_sum(uint64_t seed, uint64_t idx) {
+    const uint64_t h = hash64(seed, idx);
+    return (int) (h & 0xffff) + (int) ((h >> 16) & 0xffff) + (int) ((h >> 32) & 0xffff) + (int) ((h >> 48) & 0xffff) -
+           131070;
+}
+float synth_scale(double std) { return (float) (std * std::sqrt(3.0) / 65536.0); }
+
+// Q6_K encoder (this library's definition, restated by the CPU oracle): per 16-value sub-block amax_j,
+// d = half((max_j amax_j / 31) / 127), scale_j = clamp(roundf((amax_j / 31) / d), 0, 127),
+// code = clamp(roundf(x / (d * scale_j)), -32, 31) + 32.
+__global__ void gen_q6k_kernel(uint64_t seed, float scale, long long n_blocks, uint8_t* __restrict__ out) {
+    const long long b = (long long) blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= n_blocks) return;
+    float x[256];
+    float amax[16];
+    float smax = 0.0f;
+#pragma unroll 4
+    for (int j = 0; j < 16; ++j) {
+        float a = 0.0f;
+        for (int i = 0; i < 16; ++i) {
+            const float v = __fmul_rn((float) synth_sum(seed, (uint64_t) b * 256 + 16 * j + i), scale);
+            x[16 * j + i] = v;
+            a = fmaxf(a, fabsf(v));
+        }
+        amax[j] = a;
+        smax = fmaxf(smax, a);
+    }
+    const __half dh16 = __float2half_rn(__fdiv_rn(__fdiv_rn(smax, 31.0f), 127.0f));
+    const float dh = __half2float(dh16);
+    uint8_t ql[128], qh[64];
+    for (int i = 0; i < 128; ++i) ql[i] = 0;
+    for (int i = 0; i < 64; ++i) qh[i] = 0;
+    uint8_t* blk = out + (size_t) b * 210;
+    for (int j = 0; j < 16; ++j) {
+        int sc = 0;
+        if (dh > 0.0f) {
+            const float s = roundf(__fdiv_rn(__fdiv_rn(amax[j], 31.0f), dh));
+            sc = (int) fminf(fmaxf(s, 0.0f), 127.0f);
+        }
+        blk[192 + j] = (uint8_t) sc;
+        const float eff = __fmul_rn(dh, (float) sc);
+        for (int i = 0; i < 16; ++i) {
+            int q = 0;
+            if (eff > 0.0f) q = (int) fminf(fmaxf(roundf(__fdiv_rn(x[16 * j + i], eff)), -32.0f), 31.0f);
+            const int code = q + 32, v = 16 * j + i;
+            const int h = v >> 7, vv = v & 127, jj = vv >> 5, l = vv & 31;
+            ql[64 * h + l + 32 * (jj & 1)] |= (uint8_t) ((code & 15) << (4 * (jj >> 1)));
+            qh[32 * h + l] |= (uint8_t) (((code >> 4) & 3) << (2 * jj));
+        }
+    }
+    for (int i = 0; i < 128; ++i) blk[i] = ql[i];
+    for (int i = 0; i < 64; ++i) blk[128 + i] = qh[i];
+    const unsigned short dbits = __half_as_ushort(dh16);
+    blk[208] = (uint8_t) (dbits & 0xff);
+    blk[209] = (uint8_t) (dbits >> 8);
+}
+
+// ------------------------------------------------------------------------------------------------
+// Device control block.
+// ------------------------------------------------------------------------------------------------
+struct Ctrl {
+    int pos;       // trunk position of column 0
+    int tok[2];    // trunk input tokens (tok[1] = the draft candidate in a verify round)
+    int dpos;      // draft position of column 0
+    int dtok[2];   // draft input tokens
+    int rollback;  // GDN state from the snapshot (the previous verify's draft was rejected)
+    int accept;    // the last round accepted its draft
+    int n_emitted;
+    int steps, accepted, singles;
+    int bad;       // a token id outside the vocabulary reached a kernel
+    int pad[3];
+    unsigned long long amax[2];   // trunk argmax keys per column
+    unsigned long long damax[2];  // draft argmax keys per column
+};
+constexpr int kCtrlHostFields = 8;  // pos, tok[2], dpos, dtok[2], rollback, accept: written by the host
+
+// ---- token embedding row (GGUF Q6_K, kept on the device) -> x, partials ----
+// dequantize_row_q6_K: y = (d * scale) * (code - 32). Thread t owns 16-value sub-blocks t, t+256, ...
+template <int NC>
+__global__ void __launch_bounds__(256) embed_kernel(const uint8_t* __restrict__ emb, int H, int V, Ctrl* ctrl,
+                                                    int draft, float* __restrict__ x, float* __restrict__ xp) {
+    pdl_trigger();
+    pdl_wait();
+    const int c = blockIdx.x;
+    int tok = draft ? ctrl->dtok[c] : ctrl->tok[c];
+    if (tok < 0 || tok >= V) {
+        if (threadIdx.x == 0) {
+            atomicOr(&g_rk_status, kStatusBadIndex);
+            ctrl->bad = 1;
+        }
+        tok = 0;
+    }
+    if (!draft && c == 0 && threadIdx.x == 0) {
+        ctrl->amax[0] = 0ull;
+        ctrl->amax[1] = 0ull;
+    }
+    const size_t rb = (size_t) (H / 256) * 210;
+    const uint8_t* row = emb + (size_t) tok * rb;
+    for (int sub = threadIdx.x; sub < H / 16; sub += 256) {
+        const uint8_t* blk = row + (size_t) (sub >> 4) * 210;
+        const float d = __half2float(*reinterpret_cast<const __half*>(blk + 208));
+        const float ds = __fmul_rn(d, (float) (int8_t) blk[192 + (sub & 15)]);
+        float part[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const int v = ((sub & 15) << 4) + i;
+            const int h = v >> 7, vv = v & 127, j = vv >> 5, l = vv & 31;
+            const uint8_t qlb = blk[64 * h + l + 32 * (j & 1)];
+            const int code = ((j >> 1) ? (qlb >> 4) : (qlb & 15)) | (((blk[128 + 32 * h + l] >> (2 * j)) & 3) << 4);
+            const float y = __fmul_rn(ds, (float) (code - 32));
+            x[(size_t) c * H + sub * 16 + i] = y;
+            part[i >> 2] = __fmaf_rn(y, y, part[i >> 2]);
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) xp[(size_t) c * (H / 4) + sub * 4 + k] = part[k];
+    }
+}
+
+// ---- attention prologue: split q/gate, per-head RMSNorm, RoPE, fp16 KV store ----
+// q3 column layout: [n_head x (q 256 | gate 256)] [k n_kv x 256] [v n_kv x 256]. Grid (n_head + n_kv, NC).
+__device__ __forceinline__ float block256_sumsq(float v, float* red) {
+    float part = warp_sum(__fmul_rn(v, v));
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = part;
+    __syncthreads();
+    float ss = red[0];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) ss = __fadd_rn(ss, red[w]);
+    return ss;
+}
+template <int NC>
+__global__ void __launch_bounds__(256) attn_prep_kernel(const float* __restrict__ q3, int q3_stride,
+                                                        const float* __restrict__ qn_w, const float* __restrict__ kn_w,
+                                                        const float* __restrict__ rope, int n_rot, const int* posp,
+                                                        int n_head, int n_kv, int max_ctx, float eps,
+                                                        float* __restrict__ q_out, float* __restrict__ gate_out,
+                                                        __half* __restrict__ kc, __half* __restrict__ vc) {
+    __shared__ float red[8];
+    __shared__ float rot[kHd];
+    pdl_trigger();
+    pdl_wait();
+    const int h = blockIdx.x, c = blockIdx.y, d = threadIdx.x;
+    const int pos = *posp + c;
+    const float* col = q3 + (size_t) c * q3_stride;
+    const bool is_q = h < n_head;
+    const int kvh = h - n_head;
+    float x = is_q ? col[h * 2 * kHd + d] : col[n_head * 2 * kHd + kvh * kHd + d];
+    if (is_q) gate_out[(size_t) c * n_head * kHd + h * kHd + d] = col[h * 2 * kHd + kHd + d];
+    const float ss = block256_sumsq(x, red);
+    const float inv = rsqrtf(__fadd_rn(__fdiv_rn(ss, (float) kHd), eps));
+    x = __fmul_rn(__fmul_rn(x, inv), is_q ? qn_w[d] : kn_w[d]);
+    const bool pos_ok = pos >= 0 && pos < max_ctx;
+    if (!pos_ok && d == 0 && h == 0) atomicOr(&g_rk_status, kStatusBadIndex);
+    rot[d] = x;
+    __syncthreads();
+    const int half = n_rot / 2;
+    if (d < n_rot && pos_ok) {
+        const int i = d < half ? d : d - half;
+        const float cs = rope[((size_t) pos * half + i) * 2 + 0], sn = rope[((size_t) pos * half + i) * 2 + 1];
+        const float x0 = rot[i], x1 = rot[i + half];
+        x = d < half ? __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn)) : __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
+    }
+    if (is_q) {
+        q_out[((size_t) c * n_head + h) * kHd + d] = x;
+    } else if (pos_ok) {
+        const size_t dst = ((size_t) kvh * max_ctx + pos) * kHd + d;
+        kc[dst] = __float2half_rn(x);
+        vc[dst] = __float2half_rn(col[n_head * 2 * kHd + n_kv * kHd + kvh * kHd + d]);
+    }
+}
+
+// ---- MTP draft input: Q8_1 of [enorm(emb(dtok)) | hnorm(h)] (src/qwythos.cpp:1316-1334) ----
+// Grid NC, 256 threads, dynamic smem H floats + H/4 partials.
+template <int NC>
+__global__ void __launch_bounds__(256) draft_prep_kernel(const uint8_t* __restrict__ emb, int H, int V, Ctrl* ctrl,
+                                                         const float* __restrict__ enorm, const float* __restrict__ hnorm,
+                                                         const float* __restrict__ hsave, const float* __restrict__ hsave_p,
+                                                         float eps, uint8_t* __restrict__ eh_q8) {
+    extern __shared__ float sm[];
+    float* e = sm;
+    float* ep = sm + H;
+    __shared__ float red[8];
+    pdl_trigger();
+    pdl_wait();
+    const int c = blockIdx.x;
+    if (c == 0 && threadIdx.x == 0) {
+        ctrl->damax[0] = 0ull;
+        ctrl->damax[1] = 0ull;
+    }
+    int tok = ctrl->dtok[c];
+    if (tok < 0 || tok >= V) {
+        if (threadIdx.x == 0) {
+            atomicOr(&g_rk_status, kStatusBadIndex);
+            ctrl->bad = 1;
+        }
+        tok = 0;
+    }
+    const size_t rb = (size_t) (H / 256) * 210;
+    const uint8_t* row = emb + (size_t) tok * rb;
+    for (int sub = threadIdx.x; sub < H / 16; sub += 256) {
+        const uint8_t* blk = row + (size_t) (sub >> 4) * 210;
+        const float d = __half2float(*reinterpret_cast<const __half*>(blk + 208));
+        const float ds = __fmul_rn(d, (float) (int8_t) blk[192 + (sub & 15)]);
+        float part[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const int v = ((sub & 15) << 4) + i;
+            const int h = v >> 7, vv = v & 127, j = vv >> 5, l = vv & 31;
+            const uint8_t qlb = blk[64 * h + l + 32 * (j & 1)];
+            const int code = ((j >> 1) ? (qlb >> 4) : (qlb & 15)) | (((blk[128 + 32 * h + l] >> (2 * j)) & 3) << 4);
+            const float y = __fmul_rn(ds, (float) (code - 32));
+            e[sub * 16 + i] = y;
+            part[i >> 2] = __fmaf_rn(y, y, part[i >> 2]);
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) ep[sub * 4 + k] = part[k];
+    }
+    __syncthreads();
+    const float inv_e = rms_inv(block256_partials_sum(ep, H / 4, red), H, eps);
+    const float inv_h = rms_inv(block256_partials_sum(hsave_p + (size_t) c * (H / 4), H / 4, red), H, eps);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const float* hc = hsave + (size_t) c * H;
+    uint8_t* out = eh_q8 + (size_t) c * (2 * H / 32) * 36;
+    for (int blk = warp; blk < 2 * H / 32; blk += 8) {
+        const int i = blk * 32 + lane;
+        const float v = i < H ? rms_value(e[i], enorm[i], inv_e) : rms_value(hc[i - H], hnorm[i - H], inv_h);
+        q8_1_warp_store(v, out + (size_t) blk * 36, lane);
+    }
+}
+
+// ---- control kernels (one thread) ----
+__global__ void single_finish_kernel(Ctrl* ctrl, int* __restrict__ out, int max_out) {
+    pdl_trigger();
+    pdl_wait();
+    const int id = argmax_key_row(ctrl->amax[0]);
+    if (ctrl->n_emitted < max_out) out[ctrl->n_emitted] = id;
+    ctrl->n_emitted += 1;
+    ctrl->tok[0] = id;
+    ctrl->dtok[0] = id;
+    ctrl->dpos = ctrl->pos + 1;
+    ctrl->pos += 1;
+    ctrl->rollback = 0;
+    ctrl->singles += 1;
+}
+// Greedy acceptance (src/qwythos.cpp:3196-3238): c0 = argmax of column 0; accepted iff c0 == the
+// candidate; then emit c0 (and c1 when accepted); the draft runs on (c0 at pos+1, c1 at pos+2).
+__global__ void accept_kernel(Ctrl* ctrl, int* __restrict__ out, int max_out) {
+    pdl_trigger();
+    pdl_wait();
+    const int c0 = argmax_key_row(ctrl->amax[0]), c1 = argmax_key_row(ctrl->amax[1]);
+    const int acc = c0 == ctrl->tok[1];
+    int n = ctrl->n_emitted;
+    if (n < max_out) out[n] = c0;
+    ++n;
+    if (acc) {
+        if (n < max_out) out[n] = c1;
+        ++n;
+    }
+    ctrl->n_emitted = n;
+    ctrl->dtok[0] = c0;
+    ctrl->dtok[1] = c1;
+    ctrl->dpos = ctrl->pos + 1;
+    ctrl->tok[0] = acc ? c1 : c0;
+    ctrl->pos += 1 + acc;
+    ctrl->rollback = !acc;
+    ctrl->accept = acc;
+    ctrl->steps += 1;
+    ctrl->accepted += acc;
+}
+// The next candidate: the draft column that predicts the position after the last emitted token.
+__global__ void round_finish_kernel(Ctrl* ctrl) {
+    pdl_trigger();
+    pdl_wait();
+    ctrl->tok[1] = argmax_key_row(ctrl->damax[ctrl->accept ? 1 : 0]);
+}
+__global__ void draft1_finish_kernel(Ctrl* ctrl) {
+    pdl_trigger();
+    pdl_wait();
+    ctrl->tok[1] = argmax_key_row(ctrl->damax[0]);
+}
+
+// ------------------------------------------------------------------------------------------------
+// Engine
+// ------------------------------------------------------------------------------------------------
+struct Mat {
+    uint8_t* w = nullptr;  // packed tiles
+    int n_in = 0, n_out = 0;
+};
+struct Layer {
+    bool gdn = true;
+    float* attn_norm = nullptr;
+    float* post_norm = nullptr;
+    Mat in_proj;   // GDN: qkv||z||beta||alpha; ATTN: q||k||v
+    Mat out_proj;  // GDN: ssm_out; ATTN: wo
+    Mat upgate, down;
+    // GDN
+    float *conv_w = nullptr, *dt = nullptr, *ssm_a = nullptr, *ssm_norm = nullptr;
+    float *state = nullptr, *snap = nullptr, *ring = nullptr;
+    // ATTN
+    float *q_norm = nullptr, *k_norm = nullptr;
+    __half *kc = nullptr, *vc = nullptr;
+};
+
+// Tensor ids of the synthetic model (also used by the CPU oracle of the tests).
+enum : int { T_TOK_EMBD = 1, T_OUT_NORM = 2, T_OUTPUT = 3, T_ENORM = 4, T_HNORM = 5, T_EH_PROJ = 6, T_SHNORM = 7 };
+enum : int {
+    L_ATTN_NORM = 0, L_POST_NORM = 1, L_FFN_UP = 2, L_FFN_GATE = 3, L_FFN_DOWN = 4,
+    L_GDN_QKV = 5, L_GDN_Z = 6, L_GDN_BETA = 7, L_GDN_ALPHA = 8, L_GDN_OUT = 9, L_GDN_CONV = 10, L_GDN_A = 11,
+    L_GDN_DT = 12, L_GDN_NORM = 13,
+    L_ATT_Q = 5, L_ATT_K = 6, L_ATT_V = 7, L_ATT_O = 8, L_ATT_QN = 9, L_ATT_KN = 10
+};
+inline int layer_tid(int il, int slot) { return 100 + 32 * il + slot; }
+
+struct TensorRec {
+    int tid;
+    bool q6k;
+    int n_in, n_out;
+    void* dev;        // f32 data, or the packed group buffer
+    size_t row_off;   // first row inside a packed group
+    bool raw;         // stored as GGUF rows (token embedding)
+};
+
+}  // namespace
+
+struct EngineImpl {
+    rk_model_config cfg;
+    int dev = 0;
+    cudaStream_t s = nullptr;
+    int H = 0, FF = 0, V = 0, hk = 0, hv = 0, nh = 0, nkv = 0;
+    int qkvzab_rows = 0, qkv3_rows = 0, max_in_rows = 0;
+    std::vector<Layer> layers;
+    Layer draft;
+    float *enorm = nullptr, *hnorm = nullptr, *shnorm = nullptr, *out_norm = nullptr;
+    Mat eh_proj, lm_head;
+    uint8_t* tok_embd = nullptr;
+    float* rope = nullptr;
+    // activations, 2 columns
+    float *x = nullptr, *xp = nullptr, *proj = nullptr, *gdn_y = nullptr, *ug = nullptr;
+    uint8_t* q8 = nullptr;
+    float *q_attn = nullptr, *g_attn = nullptr, *o_attn = nullptr, *attn_scratch = nullptr;
+    float *hsave = nullptr, *hsave_p = nullptr, *logits = nullptr;
+    float *dx = nullptr, *dxp = nullptr;
+    uint8_t* eh_q8 = nullptr;
+    Ctrl* ctrl = nullptr;
+    int* out = nullptr;
+    int max_out = 0;
+    Ctrl* ctrl_stage = nullptr;  // pinned host staging, one slot per queued host write
+    int stage_slots = 0, stage_next = 0;
+    cudaGraphExec_t g_single = nullptr, g_round = nullptr, g_trunk2 = nullptr, g_draft1 = nullptr, g_draft1_seed = nullptr;
+    cudaGraphExec_t g_probe[2] = {nullptr, nullptr};
+    double probe_weight_bytes = 0, probe_algo_bytes = 0;
+    int probe_launches = 0;
+    int kernels_single = 0, kernels_round = 0;
+    std::vector<void*> allocs;
+    std::vector<TensorRec> tensors;
+    size_t bytes = 0;
+    int launches = 0;  // kernels enqueued by the current capture
+    cudaError_t err = cudaSuccess;
+
+    ~EngineImpl();
+    template <typename T>
+    T* alloc(size_t n) {
+        void* p = nullptr;
+        if (err != cudaSuccess) return nullptr;
+        err = cudaMalloc(&p, n * sizeof(T));
+        if (err != cudaSuccess) return nullptr;
+        allocs.push_back(p);
+        bytes += n * sizeof(T);
+        cudaMemsetAsync(p, 0, n * sizeof(T), s);
+        return static_cast<T*>(p);
+    }
+    int build();
+    void gen_f32(int tid, float* dst, size_t n, double std, double mean, int kind);
+    void gen_q6k_into(int tid, Mat& group, int row_off, int n_in, int n_out, uint8_t* scratch);
+    // launch helpers
+    void ok(cudaError_t e) {
+        if (e != cudaSuccess && err == cudaSuccess) err = e;
+        ++launches;
+    }
+    template <int NC>
+    void trunk(bool pdl);
+    template <int NC>
+    void draft_pass(bool with_head, bool pdl);
+    template <int NC>
+    void gemv_rms(const Mat& m, const float* x_, const float* w, const float* part, float* y, int y_stride, bool pdl,
+                  float* xn_out = nullptr, float* xn_part = nullptr, unsigned long long* amax = nullptr);
+    template <int NC>
+    void gemv_res(int pro, const Mat& m, const void* a, const float* b, int a_stride, int b_stride, float* xres,
+                  float* part, bool pdl);
+    template <int NC>
+    void ffn(const Layer& L, float* xres, float* part, bool pdl);
+    template <int NC>
+    void probe_body();
+    void set_ctrl(const Ctrl& host_fields);
+    int capture(cudaGraphExec_t* exec, int* nk, void (*body)(EngineImpl*));
+};
+
+EngineImpl::~EngineImpl() {
+    if (s) cudaStreamSynchronize(s);
+    cudaGraphExec_t gs[] = {g_single, g_round, g_trunk2, g_draft1, g_draft1_seed, g_probe[0], g_probe[1]};
+    for (cudaGraphExec_t g : gs)
+        if (g) cudaGraphExecDestroy(g);
+    for (void* p : allocs) cudaFree(p);
+    if (ctrl_stage) cudaFreeHost(ctrl_stage);
+    if (s) cudaStreamDestroy(s);
+}
+
+// f32 tensors are generated on the host (they are small) with the same counter-based values the device
+// uses; kind 1: ssm_a = -exp(value) computed in double.
+void EngineImpl::gen_f32(int tid, float* dst, size_t n, double std, double mean, int kind) {
+    std::vector<float> h(n);
+    const uint64_t st = hash64(cfg.seed, (uint64_t) tid);
+    const float scale = synth_scale(std), m = (float) mean;
+    for (size_t i = 0; i < n; ++i) {
+        volatile float v = (float) synth_sum(st, i) * scale;
+        float r = v + m;
+        if (kind == 1) r = (float) -std::exp((double) r);
+        h[i] = r;
+    }
+    if (err == cudaSuccess) err = cudaMemcpyAsync(dst, h.data(), n * sizeof(float), cudaMemcpyHostToDevice, s);
+    if (err == cudaSuccess) err = cudaStreamSynchronize(s);
+    tensors.push_back({tid, false, (int) n, 1, dst, 0, false});
+}
+
+// Q6_K matrix rows [row_off, row_off + n_out) of a packed group: generate GGUF rows, repack in place.
+void EngineImpl::gen_q6k_into(int tid, Mat& group, int row_off, int n_in, int n_out, uint8_t* scratch) {
+    const long long nb = (long long) n_out * (n_in / 256);
+    const uint64_t st = hash64(cfg.seed, (uint64_t) tid);
+    gen_q6k_kernel<<<(unsigned) ((nb + 127) / 128), 128, 0, s>>>(st, synth_scale(0.02), nb, scratch);
+    if (err == cudaSuccess) err = cudaGetLastError();
+    if (err != cudaSuccess) return;
+    uint8_t* dst = group.w + (size_t) (row_off / 4) * (n_in / 1024) * kQ6Tile;
+    const int rc = rk_pack_weights(RK_TYPE_Q6_K, scratch, dst, n_in, n_out, s);
+    if (rc != RK_OK && err == cudaSuccess) err = cudaErrorInvalidValue;
+    tensors.push_back({tid, true, n_in, n_out, group.w, (size_t) row_off, false});
+}
+
+int EngineImpl::build() {
+    const rk_model_config& c = cfg;
+    H = c.n_embd, FF = c.n_ff, V = c.n_vocab, hk = c.ssm_h_k, hv = c.ssm_h_v, nh = c.n_head, nkv = c.n_head_kv;
+    qkvzab_rows = 2 * hk * kS + 2 * hv * kS + 2 * hv;
+    qkv3_rows = 2 * nh * kHd + 2 * nkv * kHd;
+    max_in_rows = qkvzab_rows > qkv3_rows ? qkvzab_rows : qkv3_rows;
+    max_out = c.max_ctx;
+    if ((err = cudaSetDevice(dev)) != cudaSuccess) return RK_ECUDA;
+    if ((err = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking)) != cudaSuccess) return RK_ECUDA;
+    const size_t scratch_bytes = rk_weight_bytes(RK_TYPE_Q6_K, H, V) > rk_weight_bytes(RK_TYPE_Q6_K, FF, H)
+                                     ? rk_weight_bytes(RK_TYPE_Q6_K, H, V)
+                                     : rk_weight_bytes(RK_TYPE_Q6_K, H, 2 * FF);
+    uint8_t* scratch = nullptr;
+    if ((err = cudaMalloc(&scratch, scratch_bytes)) != cudaSuccess) return RK_ENOMEM;
+    auto mat = [&](int n_in, int n_out) {
+        Mat m;
+        m.n_in = n_in;
+        m.n_out = n_out;
+        m.w = alloc<uint8_t>(rk_packed_bytes(RK_TYPE_Q6_K, n_in, n_out));
+        return m;
+    };
+    auto norm = [&](int tid, int n) {
+        float* p = alloc<float>((size_t) n);
+        if (p) gen_f32(tid, p, (size_t) n, 0.02, 1.0, 0);
+        return p;
+    };
+    // globals
+    tok_embd = alloc<uint8_t>(rk_weight_bytes(RK_TYPE_Q6_K, H, V));
+    if (tok_embd) {
+        const long long nb = (long long) V * (H / 256);
+        gen_q6k_kernel<<<(unsigned) ((nb + 127) / 128), 128, 0, s>>>(hash64(c.seed, T_TOK_EMBD), synth_scale(0.02), nb,
+                                                                     tok_embd);
+        tensors.push_back({T_TOK_EMBD, true, H, V, tok_embd, 0, true});
+    }
+    out_norm = norm(T_OUT_NORM, H);
+    lm_head = mat(H, V);
+    if (lm_head.w) gen_q6k_into(T_OUTPUT, lm_head, 0, H, V, scratch);
+    const int n_blocks = c.n_layer + (c.has_mtp ? 1 : 0);
+    layers.resize(c.n_layer);
+    for (int il = 0; il < n_blocks && err == cudaSuccess; ++il) {
+        const bool is_draft = il == c.n_layer;
+        Layer& L = is_draft ? draft : layers[il];
+        L.gdn = !is_draft && ((il + 1) % c.attn_interval) != 0;
+        L.attn_norm = norm(layer_tid(il, L_ATTN_NORM), H);
+        L.post_norm = norm(layer_tid(il, L_POST_NORM), H);
+        L.upgate = mat(H, 2 * FF);
+        if (L.upgate.w) {
+            gen_q6k_into(layer_tid(il, L_FFN_UP), L.upgate, 0, H, FF, scratch);
+            gen_q6k_into(layer_tid(il, L_FFN_GATE), L.upgate, FF, H, FF, scratch);
+        }
+        L.down = mat(FF, H);
+        if (L.down.w) gen_q6k_into(layer_tid(il, L_FFN_DOWN), L.down, 0, FF, H, scratch);
+        if (L.gdn) {
+            L.in_proj = mat(H, qkvzab_rows);
+            if (L.in_proj.w) {
+                gen_q6k_into(layer_tid(il, L_GDN_QKV), L.in_proj, 0, H, 2 * hk * kS + hv * kS, scratch);
+                gen_q6k_into(layer_tid(il, L_GDN_Z), L.in_proj, 2 * hk * kS + hv * kS, H, hv * kS, scratch);
+                gen_q6k_into(layer_tid(il, L_GDN_BETA), L.in_proj, 2 * hk * kS + 2 * hv * kS, H, hv, scratch);
+                gen_q6k_into(layer_tid(il, L_GDN_ALPHA), L.in_proj, 2 * hk * kS + 2 * hv * kS + hv, H, hv, scratch);
+            }
+            L.out_proj = mat(hv * kS, H);
+            if (L.out_proj.w) gen_q6k_into(layer_tid(il, L_GDN_OUT), L.out_proj, 0, hv * kS, H, scratch);
+            const int C = 2 * hk * kS + hv * kS;
+            L.conv_w = alloc<float>((size_t) C * 4);
+            if (L.conv_w) gen_f32(layer_tid(il, L_GDN_CONV), L.conv_w, (size_t) C * 4, 0.3, 0.0, 0);
+            L.ssm_a = alloc<float>(hv);
+            if (L.ssm_a) gen_f32(layer_tid(il, L_GDN_A), L.ssm_a, hv, 0.5, 0.0, 1);
+            L.dt = alloc<float>(hv);
+            if (L.dt) gen_f32(layer_tid(il, L_GDN_DT), L.dt, hv, 0.5, 0.0, 0);
+            L.ssm_norm = norm(layer_tid(il, L_GDN_NORM), kS);
+            L.state = alloc<float>((size_t) kS * hv * kS);
+            L.snap = alloc<float>((size_t) kS * hv * kS);
+            L.ring = alloc<float>((size_t) C * 4);
+        } else {
+            L.in_proj = mat(H, qkv3_rows);
+            if (L.in_proj.w) {
+                gen_q6k_into(layer_tid(il, L_ATT_Q), L.in_proj, 0, H, 2 * nh * kHd, scratch);
+                gen_q6k_into(layer_tid(il, L_ATT_K), L.in_proj, 2 * nh * kHd, H, nkv * kHd, scratch);
+                gen_q6k_into(layer_tid(il, L_ATT_V), L.in_proj, 2 * nh * kHd + nkv * kHd, H, nkv * kHd, scratch);
+            }
+            L.out_proj = mat(nh * kHd, H);
+            if (L.out_proj.w) gen_q6k_into(layer_tid(il, L_ATT_O), L.out_proj, 0, nh * kHd, H, scratch);
+            L.q_norm = norm(layer_tid(il, L_ATT_QN), kHd);
+            L.k_norm = norm(layer_tid(il, L_ATT_KN), kHd);
+            L.kc = alloc<__half>((size_t) nkv * c.max_ctx * kHd);
+            L.vc = alloc<__half>((size_t) nkv * c.max_ctx * kHd);
+        }
+    }
+    if (c.has_mtp && err == cudaSuccess) {
+        enorm = norm(T_ENORM, H);
+        hnorm = norm(T_HNORM, H);
+        shnorm = norm(T_SHNORM, H);
+        eh_proj = mat(2 * H, H);
+        if (eh_proj.w) gen_q6k_into(T_EH_PROJ, eh_proj, 0, 2 * H, H, scratch);
+    }
+    cudaStreamSynchronize(s);
+    cudaFree(scratch);
+    // rope table (double precision on the host, stored as float)
+    {
+        const int half = c.n_rot / 2;
+        std::vector<float> t((size_t) c.max_ctx * half * 2);
+        for (int p = 0; p < c.max_ctx; ++p)
+            for (int i = 0; i < half; ++i) {
+                const double a = (double) p * std::pow(c.rope_base, -2.0 * i / (double) c.n_rot);
+                t[((size_t) p * half + i) * 2 + 0] = (float) std::cos(a);
+                t[((size_t) p * half + i) * 2 + 1] = (float) std::sin(a);
+            }
+        rope = alloc<float>(t.size());
+        if (rope && err == cudaSuccess) err = cudaMemcpy(rope, t.data(), t.size() * sizeof(float), cudaMemcpyHostToDevice);
+    }
+    // activations (2 columns)
+    x = alloc<float>(2 * (size_t) H);
+    xp = alloc<float>(2 * (size_t) H / 4);
+    proj = alloc<float>(2 * (size_t) max_in_rows);
+    gdn_y = alloc<float>(2 * (size_t) hv * kS);
+    ug = alloc<float>(2 * 2 * (size_t) FF);
+    q8 = alloc<uint8_t>(2 * rk_q8_1_bytes(FF > 2 * H ? FF : 2 * H, 1));
+    q_attn = alloc<float>(2 * (size_t) nh * kHd);
+    g_attn = alloc<float>(2 * (size_t) nh * kHd);
+    o_attn = alloc<float>(2 * (size_t) nh * kHd);
+    attn_scratch = alloc<float>(gqa_scratch_bytes(nh, 2, c.max_ctx) / sizeof(float));
+    hsave = alloc<float>(2 * (size_t) H);
+    hsave_p = alloc<float>(2 * (size_t) H / 4);
+    logits = alloc<float>(2 * (size_t) V);
+    dx = alloc<float>(2 * (size_t) H);
+    dxp = alloc<float>(2 * (size_t) H / 4);
+    eh_q8 = alloc<uint8_t>(2 * rk_q8_1_bytes(2 * H, 1));
+    ctrl = alloc<Ctrl>(1);
+    out = alloc<int>((size_t) max_out);
+    stage_slots = 4096;  // plus one slot after them for the emitted-count readback
+    if (err == cudaSuccess) err = cudaMallocHost(&ctrl_stage, sizeof(Ctrl) * (stage_slots + 1));
+    if (err == cudaSuccess) err = cudaStreamSynchronize(s);
+    if (err == cudaErrorMemoryAllocation) return RK_ENOMEM;
+    return err == cudaSuccess ? RK_OK : RK_ECUDA;
+}
+
+// ---------------------------------------------------------------------------------------------------
+// launch sequence
+// ---------------------------------------------------------------------------------------------------
+template <int NC>
+void EngineImpl::gemv_rms(const Mat& m, const float* x_, const float* w, const float* part, float* y, int y_stride,
+                          bool pdl, float* xn_out, float* xn_part, unsigned long long* amax) {
+    MmvqParams p = {};
+    p.w = m.w;
+    p.n_in = m.n_in;
+    p.n_out = m.n_out;
+    p.prefetch_before_wait = 1;
+    p.xa = x_;
+    p.xa_stride = m.n_in;
+    p.xb = w;
+    p.pin = part;
+    p.eps = cfg.eps;
+    p.y = y;
+    p.y_stride = y_stride;
+    p.xn_out = xn_out;
+    p.xn_part = xn_part;
+    p.amax = amax;
+    if (amax) ok(mmvq_launch<RK_TYPE_Q6_K, NC, PRO_RMS, EPI_ARGMAX>(p, s, pdl));
+    else ok(mmvq_launch<RK_TYPE_Q6_K, NC, PRO_RMS, EPI_STORE>(p, s, pdl));
+}
+
+// y = W . prologue(a, b) + xres (in place), partials. pro: PRO_Q8 (a = Q8_1 blocks), PRO_SWIGLU (a = up,
+// b = gate), PRO_SIGMUL (a = o, b = gate).
+template <int NC>
+void EngineImpl::gemv_res(int pro, const Mat& m, const void* a, const float* b, int a_stride, int b_stride, float* xres,
+                          float* part, bool pdl) {
+    MmvqParams p = {};
+    p.w = m.w;
+    p.n_in = m.n_in;
+    p.n_out = m.n_out;
+    p.prefetch_before_wait = 1;
+    p.xq = static_cast<const uint8_t*>(a);
+    p.xa = static_cast<const float*>(a);
+    p.xb = b;
+    p.xa_stride = a_stride;
+    p.xb_stride = b_stride;
+    p.y = xres;
+    p.y_stride = m.n_out;
+    p.res = xres;
+    p.res_stride = m.n_out;
+    p.pout = part;
+    p.pout_stride = m.n_out / 4;
+    if (pro == PRO_Q8) ok(mmvq_launch<RK_TYPE_Q6_K, NC, PRO_Q8, EPI_RES>(p, s, pdl));
+    else if (pro == PRO_SWIGLU) ok(mmvq_launch<RK_TYPE_Q6_K, NC, PRO_SWIGLU, EPI_RES>(p, s, pdl));
+    else ok(mmvq_launch<RK_TYPE_Q6_K, NC, PRO_SIGMUL, EPI_RES>(p, s, pdl));
+}
+
+// FFN (src/qwythos.cpp:1011-1042): RMSNorm(post_norm)+Q8_1 -> up||gate -> silu(gate)*up+Q8_1 -> down + residual.
+template <int NC>
+void EngineImpl::ffn(const Layer& L, float* xres, float* part, bool pdl) {
+    gemv_rms<NC>(L.upgate, xres, L.post_norm, part, ug, 2 * FF, pdl);
+    gemv_res<NC>(PRO_SWIGLU, L.down, ug, ug + FF, 2 * FF, 2 * FF, xres, part, pdl);
+}
+
+template <int NC>
+void EngineImpl::trunk(bool pdl) {
+    const int draft_flag = 0;
+    ok(launch_pdl(embed_kernel<NC>, dim3(NC), dim3(256), 0, s, pdl, (const uint8_t*) tok_embd, H, V, ctrl, draft_flag,
+                  x, xp));
+    const size_t q8col = rk_q8_1_bytes(hv * kS, 1);
+    for (const Layer& L : layers) {
+        gemv_rms<NC>(L.in_proj, x, L.attn_norm, xp, proj, L.in_proj.n_out, pdl);
+        if (L.gdn) {
+            ok(gdn_fused_launch(proj, L.in_proj.n_out, L.ring, L.conv_w, L.dt, L.ssm_a, L.ssm_norm, L.state, L.snap,
+                                &ctrl->rollback, gdn_y, q8, hk, hv, NC, &ctrl->pos, cfg.eps, s, pdl));
+            (void) q8col;
+            gemv_res<NC>(PRO_Q8, L.out_proj, q8, nullptr, 0, 0, x, xp, pdl);
+        } else {
+            ok(launch_pdl(attn_prep_kernel<NC>, dim3(nh + nkv, NC), dim3(256), 0, s, pdl, (const float*) proj,
+                          L.in_proj.n_out, (const float*) L.q_norm, (const float*) L.k_norm, (const float*) rope,
+                          cfg.n_rot, (const int*) &ctrl->pos, nh, nkv, cfg.max_ctx, cfg.eps, q_attn, g_attn, L.kc, L.vc));
+            ok(gqa_launch(q_attn, L.kc, L.vc, o_attn, nh, nkv, NC, &ctrl->pos, cfg.max_ctx, kAttnScale, attn_scratch, s,
+                          pdl));
+            ++launches;  // the combine kernel
+            gemv_res<NC>(PRO_SIGMUL, L.out_proj, o_attn, g_attn, nh * kHd, nh * kHd, x, xp, pdl);
+        }
+        ffn<NC>(L, x, xp, pdl);
+    }
+    // final norm + lm_head + argmax; the normed hidden and its partials feed the draft (src/qwythos.cpp:1234-1237)
+    gemv_rms<NC>(lm_head, x, out_norm, xp, logits, V, pdl, hsave, hsave_p, ctrl->amax);
+}
+
+// The GEMVs of one trunk step only (rk_engine_probe_gemv), with their byte counts.
+template <int NC>
+void EngineImpl::probe_body() {
+    double wb = 0, ab = 0;
+    int n = 0;
+    auto count = [&](const Mat& m, bool fp32_in, bool res) {
+        const double w = (double) rk_weight_bytes(RK_TYPE_Q6_K, m.n_in, m.n_out);
+        const double in = fp32_in ? (double) m.n_in * 4 : (double) rk_q8_1_bytes(m.n_in, 1);
+        wb += w;
+        ab += w + NC * (in + (double) m.n_out * 4 * (res ? 2 : 1));
+        ++n;
+    };
+    for (const Layer& L : layers) {
+        gemv_rms<NC>(L.in_proj, x, L.attn_norm, xp, proj, L.in_proj.n_out, true);
+        count(L.in_proj, true, false);
+        if (L.gdn) gemv_res<NC>(PRO_Q8, L.out_proj, q8, nullptr, 0, 0, x, xp, true);
+        else gemv_res<NC>(PRO_SIGMUL, L.out_proj, o_attn, g_attn, nh * kHd, nh * kHd, x, xp, true);
+        count(L.out_proj, !L.gdn, true);
+        ffn<NC>(L, x, xp, true);
+        count(L.upgate, true, false);
+        count(L.down, true, true);
+    }
+    gemv_rms<NC>(lm_head, x, out_norm, xp, logits, V, true, hsave, hsave_p, ctrl->amax);
+    count(lm_head, true, false);
+    probe_weight_bytes = wb;
+    probe_algo_bytes = ab;
+    probe_launches = n;
+}
+
+template <int NC>
+void EngineImpl::draft_pass(bool with_head, bool pdl) {
+    ok(launch_pdl(draft_prep_kernel<NC>, dim3(NC), dim3(256), (size_t) (H + H / 4) * sizeof(float), s, pdl,
+                  (const uint8_t*) tok_embd, H, V, ctrl, (const float*) enorm, (const float*) hnorm,
+                  (const float*) hsave, (const float*) hsave_p, cfg.eps, eh_q8));
+    // eh_proj (no residual: y = W . x with its partials)
+    {
+        MmvqParams p = {};
+        p.w = eh_proj.w;
+        p.n_in = eh_proj.n_in;
+        p.n_out = eh_proj.n_out;
+        p.prefetch_before_wait = 1;
+        p.xq = eh_q8;
+        p.y = dx;
+        p.y_stride = H;
+        p.pout = dxp;
+        p.pout_stride = H / 4;
+        ok(mmvq_launch<RK_TYPE_Q6_K, NC, PRO_Q8, EPI_STORE_P>(p, s, pdl));
+    }
+    const Layer& D = draft;
+    gemv_rms<NC>(D.in_proj, dx, D.attn_norm, dxp, proj, D.in_proj.n_out, pdl);
+    ok(launch_pdl(attn_prep_kernel<NC>, dim3(nh + nkv, NC), dim3(256), 0, s, pdl, (const float*) proj, D.in_proj.n_out,
+                  (const float*) D.q_norm, (const float*) D.k_norm, (const float*) rope, cfg.n_rot,
+                  (const int*) &ctrl->dpos, nh, nkv, cfg.max_ctx, cfg.eps, q_attn, g_attn, D.kc, D.vc));
+    ok(gqa_launch(q_attn, D.kc, D.vc, o_attn, nh, nkv, NC, &ctrl->dpos, cfg.max_ctx, kAttnScale, attn_scratch, s, pdl));
+    ++launches;
+    gemv_res<NC>(PRO_SIGMUL, D.out_proj, o_attn, g_attn, nh * kHd, nh * kHd, dx, dxp, pdl);
+    ffn<NC>(D, dx, dxp, pdl);
+    if (with_head) gemv_rms<NC>(lm_head, dx, shnorm, dxp, nullptr, V, pdl, nullptr, nullptr, ctrl->damax);
+}
+
+int EngineImpl::capture(cudaGraphExec_t* exec, int* nk, void (*body)(EngineImpl*)) {
+    cudaGraph_t g = nullptr;
+    launches = 0;
+    if ((err = cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal)) != cudaSuccess) return RK_ECUDA;
+    body(this);
+    const cudaError_t e2 = cudaStreamEndCapture(s, &g);
+    if (err == cudaSuccess) err = e2;
+    if (err == cudaSuccess) err = cudaGraphInstantiate(exec, g, 0ull);
+    if (g) cudaGraphDestroy(g);
+    if (nk) *nk = launches;
+    return err == cudaSuccess ? RK_OK : RK_ECUDA;
+}
+
+// Host writes of the control fields go through a ring of pinned slots so that queued copies never
+// read a slot the host is rewriting (one slot per queued write; the ring is drained by syncs).
+void EngineImpl::set_ctrl(const Ctrl& h) {
+    Ctrl* slot = ctrl_stage + stage_next;
+    stage_next = (stage_next + 1) % stage_slots;
+    if (stage_next == 0) cudaStreamSynchronize(s);
+    std::memcpy(slot, &h, sizeof(int) * kCtrlHostFields);
+    const cudaError_t e = cudaMemcpyAsync(ctrl, slot, sizeof(int) * kCtrlHostFields, cudaMemcpyHostToDevice, s);
+    if (e != cudaSuccess && err == cudaSuccess) err = e;
+}
+
+}  // namespace rk
+
+using namespace rk;
+
+struct rk_engine {
+    EngineImpl impl;
+};
+
+extern "C" {
+
+void rk_model_config_9b(rk_model_config* c, int max_ctx, uint64_t seed) {
+    if (!c) return;
+    std::memset(c, 0, sizeof *c);
+    c->n_layer = 32;
+    c->n_embd = 4096;
+    c->n_ff = 12288;
+    c->n_vocab = 248320;
+    c->ssm_h_k = 16;
+    c->ssm_h_v = 32;
+    c->n_head = 16;
+    c->n_head_kv = 4;
+    c->n_rot = 64;
+    c->attn_interval = 4;
+    c->has_mtp = 1;
+    c->max_ctx = max_ctx;
+    c->eps = 1e-6f;
+    c->rope_base = 1e7;
+    c->seed = seed;
+}
+
+int rk_engine_create(const rk_model_config* cfg, int device, rk_engine** out) {
+    const char* what = "rk_engine_create";
+    if (!cfg || !out) return set_error(RK_EINVAL, "%s: null argument", what);
+    const rk_model_config& c = *cfg;
+    if (c.n_layer < 1 || c.n_embd <= 0 || c.n_embd % 1024 || c.n_ff <= 0 || c.n_ff % 1024 || c.n_vocab <= 0 ||
+        c.n_vocab % 4)
+        return set_error(RK_EINVAL, "%s: n_embd and n_ff must be multiples of 1024, n_vocab of 4", what);
+    if (c.ssm_h_k <= 0 || c.ssm_h_v != 2 * c.ssm_h_k || c.ssm_h_v * kS != c.n_embd)
+        return set_error(RK_EINVAL, "%s: requires ssm_h_v == 2*ssm_h_k and ssm_h_v*128 == n_embd", what);
+    if (c.n_head_kv <= 0 || c.n_head != 4 * c.n_head_kv || c.n_head * kHd != c.n_embd)
+        return set_error(RK_EINVAL, "%s: requires n_head == 4*n_head_kv and n_head*256 == n_embd", what);
+    if (c.n_rot <= 0 || c.n_rot > kHd || c.n_rot % 2 || c.attn_interval < 1 || c.max_ctx < 8 || !(c.eps > 0))
+        return set_error(RK_EINVAL, "%s: bad n_rot / attn_interval / max_ctx / eps", what);
+    rk_engine* e = new (std::nothrow) rk_engine;
+    if (!e) return set_error(RK_ENOMEM, "%s: host allocation failed", what);
+    e->impl.cfg = c;
+    e->impl.dev = device;
+    int rc = e->impl.build();
+    if (rc == RK_OK) {
+        EngineImpl& E = e->impl;
+        rc = E.capture(&E.g_single, &E.kernels_single, [](EngineImpl* x) {
+            x->trunk<1>(true);
+            x->ok(launch_pdl(single_finish_kernel, dim3(1), dim3(1), 0, x->s, true, x->ctrl, x->out, x->max_out));
+        });
+        if (rc == RK_OK)
+            rc = E.capture(&E.g_trunk2, nullptr, [](EngineImpl* x) { x->trunk<2>(true); });
+        if (rc == RK_OK && c.has_mtp) {
+            rc = E.capture(&E.g_round, &E.kernels_round, [](EngineImpl* x) {
+                x->trunk<2>(true);
+                x->ok(launch_pdl(accept_kernel, dim3(1), dim3(1), 0, x->s, true, x->ctrl, x->out, x->max_out));
+                x->draft_pass<2>(true, true);
+                x->ok(launch_pdl(round_finish_kernel, dim3(1), dim3(1), 0, x->s, true, x->ctrl));
+            });
+            if (rc == RK_OK)
+                rc = E.capture(&E.g_draft1, nullptr, [](EngineImpl* x) {
+                    x->draft_pass<1>(true, true);
+                    x->ok(launch_pdl(draft1_finish_kernel, dim3(1), dim3(1), 0, x->s, true, x->ctrl));
+                });
+            if (rc == RK_OK)
+                rc = E.capture(&E.g_draft1_seed, nullptr, [](EngineImpl* x) { x->draft_pass<1>(false, true); });
+        }
+    }
+    if (rc != RK_OK) {
+        const cudaError_t ce = e->impl.err;
+        delete e;
+        if (rc == RK_ENOMEM || ce == cudaErrorMemoryAllocation)
+            return set_error(RK_ENOMEM, "%s: out of device memory", what);
+        return set_error(RK_ECUDA, "%s: %s", what, cudaGetErrorString(ce));
+    }
+    *out = e;
+    return RK_OK;
+}
+
+int rk_engine_destroy(rk_engine* e) {
+    delete e;
+    return RK_OK;
+}
+
+int rk_engine_reset(rk_engine* e) {
+    if (!e) return set_error(RK_EINVAL, "rk_engine_reset: null engine");
+    EngineImpl& E = e->impl;
+    cudaStreamSynchronize(E.s);
+    const size_t hvs = (size_t) kS * E.hv * kS;
+    const int C = 2 * E.hk * kS + E.hv * kS;
+    auto clear = [&](Layer& L) {
+        if (L.gdn) {
+            cudaMemsetAsync(L.state, 0, hvs * 4, E.s);
+            cudaMemsetAsync(L.snap, 0, hvs * 4, E.s);
+            cudaMemsetAsync(L.ring, 0, (size_t) C * 16, E.s);
+        } else if (L.kc) {
+            cudaMemsetAsync(L.kc, 0, (size_t) E.nkv * E.cfg.max_ctx * kHd * 2, E.s);
+            cudaMemsetAsync(L.vc, 0, (size_t) E.nkv * E.cfg.max_ctx * kHd * 2, E.s);
+        }
+    };
+    for (Layer& L : E.layers) clear(L);
+    if (E.cfg.has_mtp) clear(E.draft);
+    cudaMemsetAsync(E.ctrl, 0, sizeof(Ctrl), E.s);
+    const cudaError_t ce = cudaStreamSynchronize(E.s);
+    if (ce != cudaSuccess) return set_error(RK_ECUDA, "rk_engine_reset: %s", cudaGetErrorString(ce));
+    return RK_OK;
+}
+
+int rk_engine_step(rk_engine* e, const int* tokens, int ncols, int pos, float* logits, int* argmax) {
+    const char* what = "rk_engine_step";
+    if (!e || !tokens) return set_error(RK_EINVAL, "%s: null argument", what);
+    EngineImpl& E = e->impl;
+    if (ncols < 1 || ncols > 2) return set_error(RK_EINVAL, "%s: ncols must be 1 or 2", what);
+    if (pos < 0 || pos + ncols > E.cfg.max_ctx) return set_error(RK_ERANGE, "%s: position out of range", what);
+    for (int c = 0; c < ncols; ++c)
+        if (tokens[c] < 0 || tokens[c] >= E.V) return set_error(RK_ERANGE, "%s: token out of range", what);
+    Ctrl h = {};
+    h.pos = pos;
+    h.tok[0] = tokens[0];
+    h.tok[1] = ncols > 1 ? tokens[1] : 0;
+    E.set_ctrl(h);
+    cudaError_t ce = cudaGraphLaunch(ncols == 1 ? E.g_single : E.g_trunk2, E.s);
+    if (ce == cudaSuccess && logits)
+        ce = cudaMemcpyAsync(logits, E.logits, sizeof(float) * (size_t) ncols * E.V, cudaMemcpyDeviceToHost, E.s);
+    Ctrl back;
+    if (ce == cudaSuccess) ce = cudaMemcpyAsync(&back, E.ctrl, sizeof(Ctrl), cudaMemcpyDeviceToHost, E.s);
+    if (ce == cudaSuccess) ce = cudaStreamSynchronize(E.s);
+    if (ce != cudaSuccess) return set_error(RK_ECUDA, "%s: %s", what, cudaGetErrorString(ce));
+    if (argmax)
+        for (int c = 0; c < ncols; ++c) argmax[c] = argmax_key_row(back.amax[c]);
+    return RK_OK;
+}
+
+int rk_engine_generate(rk_engine* e, const int* prompt, int n_prompt, int n_gen, int use_mtp, int* out_ids,
+                       rk_gen_stats* stats) {
+    const char* what = "rk_engine_generate";
+    if (!e || !prompt || !out_ids) return set_error(RK_EINVAL, "%s: null argument", what);
+    EngineImpl& E = e->impl;
+    if (n_prompt < 1 || n_gen < 1) return set_error(RK_EINVAL, "%s: needs n_prompt >= 1 and n_gen >= 1", what);
+    if (n_prompt + n_gen + 2 > E.cfg.max_ctx) return set_error(RK_ERANGE, "%s: prompt + generation exceed max_ctx", what);
+    if (use_mtp && !E.cfg.has_mtp) return set_error(RK_EINVAL, "%s: model built without the MTP block", what);
+    for (int i = 0; i < n_prompt; ++i)
+        if (prompt[i] < 0 || prompt[i] >= E.V) return set_error(RK_ERANGE, "%s: prompt token out of range", what);
+    int rc = rk_engine_reset(e);
+    if (rc) return rc;
+    cudaEvent_t ev[3];
+    for (auto& v : ev) cudaEventCreate(&v);
+    int launches = 0;
+    cudaError_t ce = cudaSuccess;
+    // prefill: positions 0..P-2, teacher forced, one trunk pass each (the reference's per-token path)
+    cudaEventRecord(ev[0], E.s);
+    for (int i = 0; i + 1 < n_prompt && ce == cudaSuccess; ++i) {
+        Ctrl h = {};
+        h.pos = i;
+        h.tok[0] = prompt[i];
+        E.set_ctrl(h);
+        ce = cudaGraphLaunch(E.g_single, E.s);
+        ++launches;
+    }
+    if (use_mtp && ce == cudaSuccess) {
+        // seed the draft cache slot 0 with (emb(prompt[0]), h = 0) (src/qwythos.cpp:2955-2958)
+        cudaMemsetAsync(E.hsave, 0, sizeof(float) * E.H, E.s);
+        cudaMemsetAsync(E.hsave_p, 0, sizeof(float) * E.H / 4, E.s);
+        Ctrl h = {};
+        h.dpos = 0;
+        h.dtok[0] = prompt[0];
+        E.set_ctrl(h);
+        ce = cudaGraphLaunch(E.g_draft1_seed, E.s);
+        ++launches;
+    }
+    cudaMemsetAsync(&E.ctrl->n_emitted, 0, sizeof(int) * 4, E.s);  // n_emitted, steps, accepted, singles
+    cudaEventRecord(ev[1], E.s);
+    // seed pass at position P-1 produces the first generated token
+    Ctrl h = {};
+    h.pos = n_prompt - 1;
+    h.tok[0] = prompt[n_prompt - 1];
+    E.set_ctrl(h);
+    if (ce == cudaSuccess) ce = cudaGraphLaunch(E.g_single, E.s);
+    ++launches;
+    if (!use_mtp) {
+        for (int i = 1; i < n_gen && ce == cudaSuccess; ++i) {
+            ce = cudaGraphLaunch(E.g_single, E.s);
+            ++launches;
+        }
+    } else if (ce == cudaSuccess) {
+        // first candidate: draft at (emb(first token), hidden of P-1)
+        ce = cudaGraphLaunch(E.g_draft1, E.s);
+        ++launches;
+        int emitted = 1;
+        int* pinned = reinterpret_cast<int*>(E.ctrl_stage + E.stage_slots);
+        while (ce == cudaSuccess && emitted < n_gen) {
+            const bool single = emitted >= n_gen - 1;
+            ce = cudaGraphLaunch(single ? E.g_single : E.g_round, E.s);
+            ++launches;
+            if (ce != cudaSuccess) break;
+            ce = cudaMemcpyAsync(pinned, &E.ctrl->n_emitted, sizeof(int), cudaMemcpyDeviceToHost, E.s);
+            if (ce == cudaSuccess) ce = cudaStreamSynchronize(E.s);
+            emitted = *pinned;
+        }
+    }
+    cudaEventRecord(ev[2], E.s);
+    Ctrl back = {};
+    if (ce == cudaSuccess) ce = cudaMemcpyAsync(&back, E.ctrl, sizeof(Ctrl), cudaMemcpyDeviceToHost, E.s);
+    if (ce == cudaSuccess)
+        ce = cudaMemcpyAsync(out_ids, E.out, sizeof(int) * (size_t) n_gen, cudaMemcpyDeviceToHost, E.s);
+    if (ce == cudaSuccess) ce = cudaStreamSynchronize(E.s);
+    float pre = 0.0f, gen = 0.0f;
+    if (ce == cudaSuccess) {
+        cudaEventElapsedTime(&pre, ev[0], ev[1]);
+        cudaEventElapsedTime(&gen, ev[1], ev[2]);
+    }
+    for (auto& v : ev) cudaEventDestroy(v);
+    if (ce != cudaSuccess) return set_error(RK_ECUDA, "%s: %s", what, cudaGetErrorString(ce));
+    if (back.bad) return set_error(RK_ERANGE, "%s: a token outside the vocabulary reached the device", what);
+    if (back.n_emitted < n_gen) return set_error(RK_ECUDA, "%s: generation stopped early (%d of %d)", what, back.n_emitted, n_gen);
+    if (stats) {
+        stats->prefill_ms = pre;
+        stats->gen_ms = gen;
+        stats->n_gen = n_gen;
+        stats->mtp_steps = back.steps;
+        stats->mtp_accepted = back.accepted;
+        stats->single_steps = back.singles;
+        stats->graph_launches = launches;
+        stats->kernels_per_single_step = E.kernels_single;
+        stats->kernels_per_round = E.kernels_round;
+    }
+    return RK_OK;
+}
+
+size_t rk_engine_read_tensor(rk_engine* e, int tid, void* host, size_t bytes) {
+    if (!e) return 0;
+    EngineImpl& E = e->impl;
+    for (const TensorRec& t : E.tensors) {
+        if (t.tid != tid) continue;
+        if (!t.q6k) {
+            const size_t need = (size_t) t.n_in * sizeof(float);
+            if (!host || bytes == 0) return need;
+            if (bytes < need) return 0;
+            return cudaMemcpy(host, t.dev, need, cudaMemcpyDeviceToHost) == cudaSuccess ? need : 0;
+        }
+        const size_t need = rk_weight_bytes(RK_TYPE_Q6_K, t.n_in, t.n_out);
+        if (!host || bytes == 0) return need;
+        if (bytes < need) return 0;
+        if (t.raw) return cudaMemcpy(host, t.dev, need, cudaMemcpyDeviceToHost) == cudaSuccess ? need : 0;
+        void* tmp = nullptr;
+        if (cudaMalloc(&tmp, need) != cudaSuccess) return 0;
+        const uint8_t* src = static_cast<const uint8_t*>(t.dev) + (t.row_off / 4) * (size_t) (t.n_in / 1024) * kQ6Tile;
+        int rc = rk_unpack_weights(RK_TYPE_Q6_K, src, tmp, t.n_in, t.n_out, E.s);
+        cudaError_t ce = rc == RK_OK ? cudaStreamSynchronize(E.s) : cudaErrorInvalidValue;
+        if (ce == cudaSuccess) ce = cudaMemcpy(host, tmp, need, cudaMemcpyDeviceToHost);
+        cudaFree(tmp);
+        return ce == cudaSuccess ? need : 0;
+    }
+    return 0;
+}
+
+int rk_engine_probe_gemv(rk_engine* e, int ncols, int iters, rk_probe_result* out) {
+    const char* what = "rk_engine_probe_gemv";
+    if (!e || !out) return set_error(RK_EINVAL, "%s: null argument", what);
+    if (ncols < 1 || ncols > 2 || iters < 1) return set_error(RK_EINVAL, "%s: ncols 1..2, iters >= 1", what);
+    EngineImpl& E = e->impl;
+    cudaGraphExec_t& g = E.g_probe[ncols - 1];
+    if (!g) {
+        int rc = ncols == 1 ? E.capture(&g, nullptr, [](EngineImpl* x) { x->probe_body<1>(); })
+                            : E.capture(&g, nullptr, [](EngineImpl* x) { x->probe_body<2>(); });
+        if (rc != RK_OK) return set_error(RK_ECUDA, "%s: capture failed: %s", what, cudaGetErrorString(E.err));
+    }
+    cudaEvent_t a, b;
+    cudaEventCreate(&a);
+    cudaEventCreate(&b);
+    cudaError_t ce = cudaGraphLaunch(g, E.s);  // warm-up
+    if (ce == cudaSuccess) ce = cudaEventRecord(a, E.s);
+    for (int i = 0; i < iters && ce == cudaSuccess; ++i) ce = cudaGraphLaunch(g, E.s);
+    if (ce == cudaSuccess) ce = cudaEventRecord(b, E.s);
+    if (ce == cudaSuccess) ce = cudaEventSynchronize(b);
+    float ms = 0.0f;
+    if (ce == cudaSuccess) cudaEventElapsedTime(&ms, a, b);
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+    if (ce != cudaSuccess) return set_error(RK_ECUDA, "%s: %s", what, cudaGetErrorString(ce));
+    out->ms = ms;
+    out->launches = E.probe_launches;
+    out->weight_bytes = E.probe_weight_bytes;
+    out->algo_bytes = E.probe_algo_bytes;
+    return RK_OK;
+}
+
+size_t rk_engine_device_bytes(const rk_engine* e) { return e ? e->impl.bytes : 0; }
+
+}  // extern "C"

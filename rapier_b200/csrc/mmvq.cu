@@ -464,14 +464,15 @@ int rk_unpack_weights(int type, const void* src, void* dst, int n_in, int n_out,
     return check_launch(what);
 }
 
-int rk_mmvq_packed(int type, const void* packed, const void* x_q8_1, float* y, int n_in, int n_out, int ncols,
-                   void* stream) {
+int rk_mmvq_packed_ex(int type, const void* packed, const void* x_q8_1, float* y, int n_in, int n_out, int ncols,
+                      unsigned flags, void* stream) {
     const char* what = "rk_mmvq_packed";
     if (int rc = check_packed_shape(type, n_in, n_out, ncols, what)) return rc;
     if (int rc = check_ptr16(packed, what)) return rc;
     if (int rc = check_ptr(x_q8_1, what)) return rc;
     if (int rc = check_ptr(y, what)) return rc;
     if (int rc = check_stream(stream, what)) return rc;
+    if (flags & ~RK_FLAG_STATIC_WEIGHTS) return set_error(RK_EINVAL, "%s: unknown flags 0x%x", what, flags);
     const size_t xcol = (size_t) (n_in / 32) * 36;
     for (int j = 0; j < ncols; j += kMmvqMaxCols) {
         const int nc = ncols - j < kMmvqMaxCols ? ncols - j : kMmvqMaxCols;
@@ -479,7 +480,7 @@ int rk_mmvq_packed(int type, const void* packed, const void* x_q8_1, float* y, i
         p.w = (const uint8_t*) packed;
         p.n_in = n_in;
         p.n_out = n_out;
-        p.prefetch_before_wait = 0;
+        p.prefetch_before_wait = (flags & RK_FLAG_STATIC_WEIGHTS) ? 1 : 0;
         p.xq = (const uint8_t*) x_q8_1 + (size_t) j * xcol;
         p.y = y + (size_t) j * n_out;
         p.y_stride = n_out;
@@ -488,6 +489,11 @@ int rk_mmvq_packed(int type, const void* packed, const void* x_q8_1, float* y, i
         if (e != cudaSuccess) return set_error(RK_ECUDA, "%s: %s", what, cudaGetErrorString(e));
     }
     return check_launch(what);
+}
+
+int rk_mmvq_packed(int type, const void* packed, const void* x_q8_1, float* y, int n_in, int n_out, int ncols,
+                   void* stream) {
+    return rk_mmvq_packed_ex(type, packed, x_q8_1, y, n_in, n_out, ncols, 0u, stream);
 }
 
 int rk_mmvq_packed_res(int type, const void* packed, const void* x_q8_1, float* y, const float* res,

@@ -30,7 +30,7 @@ constexpr int kMmvqMaxStages = 8;  // ring slots per warp (runtime `stages` <= t
 constexpr int kMmvqMaxCols = 4;    // columns per launch (more are split into launches over column chunks)
 
 enum MmvqPro { PRO_Q8 = 0, PRO_RMS = 1, PRO_SWIGLU = 2, PRO_SIGMUL = 3 };
-enum MmvqEpi { EPI_STORE = 0, EPI_RES = 1, EPI_ARGMAX = 2 };
+enum MmvqEpi { EPI_STORE = 0, EPI_RES = 1, EPI_ARGMAX = 2, EPI_STORE_P = 3 };
 
 struct MmvqParams {
     const uint8_t* w;  // packed tiles
@@ -52,6 +52,11 @@ struct MmvqParams {
     float* pout;        // EPI_RES partials, column stride pout_stride
     int pout_stride;
     unsigned long long* amax;  // EPI_ARGMAX: one packed (value, ~row) slot per column
+    // PRO_RMS write-through (optional): CTA 0 stores the normalized fp32 row (x * w * inv) of every
+    // column (stride n_in) and its 4-row sum-of-squares partials (stride n_in/4), the reference's
+    // rms_norm_out + row_sum_partials of the final hidden (src/qwythos.cpp:1236-1237).
+    float* xn_out;
+    float* xn_part;
 };
 
 // Smem bytes a launch needs for the activation staging and the rings.
@@ -160,6 +165,21 @@ __device__ __forceinline__ void mmvq_build_x(const MmvqParams& p, uint8_t* xsm, 
             }
             uint32_t ds;
             const int code = q8_1_warp_code(v, ds);
+            if constexpr (PRO == PRO_RMS) {
+                if (p.xn_out != nullptr && blockIdx.x == 0) {
+                    p.xn_out[(size_t) c * p.n_in + i] = v;
+                    // 4-row partials in row order: lanes 4j..4j+3 form slot j of this block
+                    const float v1 = __shfl_down_sync(0xffffffffu, v, 1), v2 = __shfl_down_sync(0xffffffffu, v, 2),
+                                v3 = __shfl_down_sync(0xffffffffu, v, 3);
+                    if ((lane & 3) == 0) {
+                        float part = __fmul_rn(v, v);
+                        part = __fmaf_rn(v1, v1, part);
+                        part = __fmaf_rn(v2, v2, part);
+                        part = __fmaf_rn(v3, v3, part);
+                        p.xn_part[(size_t) c * (p.n_in / 4) + (i >> 2)] = part;
+                    }
+                }
+            }
             xstage_put_warp(xstage_col(xsm, ng, c), g, code, ds, lane);
         }
     }
@@ -247,7 +267,7 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, int row) {
     b ^= (b >> 31) ? 0xffffffffu : 0x80000000u;
     return ((unsigned long long) b << 32) | (unsigned long long) (0xffffffffu - (uint32_t) row);
 }
-__device__ __forceinline__ int argmax_key_row(unsigned long long k) { return (int) (0xffffffffu - (uint32_t) (k & 0xffffffffu)); }
+__host__ __device__ __forceinline__ int argmax_key_row(unsigned long long k) { return (int) (0xffffffffu - (uint32_t) (k & 0xffffffffu)); }
 
 template <int NC, int EPI>
 __device__ __forceinline__ void mmvq_epilogue(const MmvqParams& p, int unit, int lane, float (&acc)[NC][4]) {
@@ -283,17 +303,17 @@ __device__ __forceinline__ void mmvq_epilogue(const MmvqParams& p, int unit, int
                 if (br >= 0) atomicMax(p.amax + lane, argmax_key(best, row0 + br));
             }
         }
-    } else {  // EPI_RES
+    } else {  // EPI_RES (y = acc + res) / EPI_STORE_P (y = acc), both with the 4-row partials
         if (lane < NC) {
 #pragma unroll
             for (int c = 0; c < NC; ++c)
                 if (lane == c) {
-                    const float* res = p.res + (size_t) c * p.res_stride + row0;
                     float* y = p.y + (size_t) c * p.y_stride + row0;
                     float part = 0.0f;
 #pragma unroll
                     for (int r = 0; r < 4; ++r) {
-                        const float v = __fadd_rn(acc[c][r], res[r]);
+                        const float v =
+                            EPI == EPI_RES ? __fadd_rn(acc[c][r], p.res[(size_t) c * p.res_stride + row0 + r]) : acc[c][r];
                         y[r] = v;
                         part = __fmaf_rn(v, v, part);
                     }
@@ -304,7 +324,7 @@ __device__ __forceinline__ void mmvq_epilogue(const MmvqParams& p, int unit, int
 }
 
 template <int TYPE, int NC, int PRO, int EPI>
-__global__ void __launch_bounds__(kMmvqWarps * 32, 1) mmvq_packed_kernel(const MmvqParams p) {
+__global__ void __launch_bounds__(kMmvqWarps * 32, 2) mmvq_packed_kernel(const MmvqParams p) {
     constexpr int TILE = TYPE == RK_TYPE_Q6_K ? kQ6Tile : kQ80Tile;
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ float red[8];
@@ -393,6 +413,11 @@ __global__ void __launch_bounds__(kMmvqWarps * 32, 1) mmvq_packed_kernel(const M
 
 // Host-side launcher for one instantiation: sets the smem attribute once, picks the stage count that
 // keeps two CTAs per SM where possible, grid = one CTA per SM (capped by the unit count).
+// Tuning knobs read once from the environment (like the reference's QWYTHOS_Q6ROWS sweep knob,
+// src/native_mmvq.cu:3648-3651): RK_MMVQ_STAGES forces the ring depth, RK_MMVQ_CTAS the CTAs per SM.
+int mmvq_env_stages();
+int mmvq_env_ctas();
+
 template <int TYPE, int NC, int PRO, int EPI>
 cudaError_t mmvq_launch(MmvqParams p, cudaStream_t s, bool pdl) {
     static int configured_smem = -1;
@@ -405,13 +430,19 @@ cudaError_t mmvq_launch(MmvqParams p, cudaStream_t s, bool pdl) {
     }
     const size_t tile = TYPE == RK_TYPE_Q6_K ? kQ6Tile : kQ80Tile;
     const size_t fixed = mmvq_smem_bytes(TYPE, p.n_in, NC, 0);
-    // two CTAs per SM need <= ~113 KB each; fall back to one CTA with a deeper ring when x is large
+    // Two CTAs per SM (16 warps; measured best for 1-2 columns) with the deepest ring that fits both in
+    // ~113 KB; when the staged activations leave room for fewer than 2 slots, one CTA with a deeper ring.
+    int ctas = 2;
     int stages = (int) ((113 * 1024 - (long long) fixed) / (long long) (kMmvqWarps * tile));
-    if (stages < 3) {
+    if (stages > 3) stages = 3;
+    if (stages < 2) {
+        ctas = 1;
         stages = (int) (((long long) max_optin - 2048 - (long long) fixed) / (long long) (kMmvqWarps * tile));
-        if (stages > kMmvqMaxStages) stages = kMmvqMaxStages;
+        if (stages > 4) stages = 4;
     }
-    if (stages < 2) return cudaErrorInvalidValue;
+    if (mmvq_env_stages() > 0) stages = mmvq_env_stages();
+    if (mmvq_env_ctas() > 0) ctas = mmvq_env_ctas();
+    if (stages < 2 || stages > kMmvqMaxStages) return cudaErrorInvalidValue;
     p.stages = stages;
     const size_t smem = mmvq_smem_bytes(TYPE, p.n_in, NC, stages);
     if ((int) smem > configured_smem) {
@@ -421,7 +452,7 @@ cudaError_t mmvq_launch(MmvqParams p, cudaStream_t s, bool pdl) {
         configured_smem = (int) smem;
     }
     const int units = p.n_out / 4;
-    int grid = num_sms();
+    int grid = num_sms() * ctas;
     if (grid > units) grid = units;
     return launch_pdl(mmvq_packed_kernel<TYPE, NC, PRO, EPI>, dim3(grid), dim3(kMmvqWarps * 32), smem, s, pdl, p);
 }

@@ -1,0 +1,97 @@
+"""Python wrapper over the C++ decode engine (rk_engine_* in include/rapier_b200.h).
+
+    from rapier_b200.engine import Engine, config_9b
+    eng = Engine(config_9b(max_ctx=512, seed=1))
+    ids, stats = eng.generate(prompt, n_gen=400, mtp=True)
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+from . import _lib
+from ._lib import GenStats, ModelConfig, ProbeResult, RkError
+
+# synthetic tensor ids (engine.cu): globals and per-layer slots, layer il's tensor = 100 + 32*il + slot
+T_TOK_EMBD, T_OUT_NORM, T_OUTPUT, T_ENORM, T_HNORM, T_EH_PROJ, T_SHNORM = 1, 2, 3, 4, 5, 6, 7
+L_ATTN_NORM, L_POST_NORM, L_FFN_UP, L_FFN_GATE, L_FFN_DOWN = 0, 1, 2, 3, 4
+L_GDN_QKV, L_GDN_Z, L_GDN_BETA, L_GDN_ALPHA, L_GDN_OUT, L_GDN_CONV, L_GDN_A, L_GDN_DT, L_GDN_NORM = 5, 6, 7, 8, 9, 10, 11, 12, 13
+L_ATT_Q, L_ATT_K, L_ATT_V, L_ATT_O, L_ATT_QN, L_ATT_KN = 5, 6, 7, 8, 9, 10
+
+
+def layer_tid(il: int, slot: int) -> int:
+    return 100 + 32 * il + slot
+
+
+def config_9b(max_ctx: int = 4096, seed: int = 1) -> ModelConfig:
+    c = ModelConfig()
+    _lib.lib().rk_model_config_9b(C.byref(c), max_ctx, seed)
+    return c
+
+
+def config_tiny(max_ctx: int = 256, seed: int = 7, n_layer: int = 4, vocab: int = 4096) -> ModelConfig:
+    """A small model with the same structure (GDN layers and an attention layer every 4th, MTP block)."""
+    c = config_9b(max_ctx, seed)
+    c.n_layer, c.n_embd, c.n_ff, c.n_vocab = n_layer, 1024, 2048, vocab
+    c.ssm_h_k, c.ssm_h_v, c.n_head, c.n_head_kv = 4, 8, 4, 1
+    return c
+
+
+class Engine:
+    def __init__(self, cfg: ModelConfig, device: int = 0):
+        self.cfg = cfg
+        h = C.c_void_p()
+        _lib.call("rk_engine_create", C.byref(cfg), device, C.byref(h))
+        self._h = h
+
+    def close(self):
+        if self._h:
+            _lib.lib().rk_engine_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def reset(self):
+        _lib.call("rk_engine_reset", self._h)
+
+    def generate(self, prompt, n_gen: int, mtp: bool = False):
+        p = (C.c_int * len(prompt))(*[int(t) for t in prompt])
+        out = (C.c_int * n_gen)()
+        st = GenStats()
+        _lib.call("rk_engine_generate", self._h, p, len(prompt), n_gen, 1 if mtp else 0, out, C.byref(st))
+        stats = {f: getattr(st, f) for f, _ in GenStats._fields_}
+        return np.frombuffer(out, dtype=np.int32).copy(), stats
+
+    def step(self, tokens, pos: int, want_logits: bool = True):
+        n = len(tokens)
+        t = (C.c_int * n)(*[int(x) for x in tokens])
+        am = (C.c_int * n)()
+        logits = np.empty(n * self.cfg.n_vocab, np.float32) if want_logits else None
+        _lib.call("rk_engine_step", self._h, t, n, pos,
+                  logits.ctypes.data_as(C.c_void_p) if want_logits else None, am)
+        return (logits.reshape(n, -1) if want_logits else None), list(am)
+
+    def read_tensor(self, tid: int) -> np.ndarray:
+        L = _lib.lib()
+        n = L.rk_engine_read_tensor(self._h, tid, None, 0)
+        if n == 0:
+            raise RkError(_lib.RK_EINVAL, "rk_engine_read_tensor", f"no tensor {tid}")
+        buf = np.empty(n, np.uint8)
+        got = L.rk_engine_read_tensor(self._h, tid, buf.ctypes.data_as(C.c_void_p), n)
+        if got != n:
+            raise RkError(_lib.RK_ECUDA, "rk_engine_read_tensor", "copy failed")
+        return buf
+
+    def probe_gemv(self, ncols: int = 1, iters: int = 10) -> dict:
+        r = ProbeResult()
+        _lib.call("rk_engine_probe_gemv", self._h, ncols, iters, C.byref(r))
+        return {"ms": r.ms, "iters": iters, "launches": r.launches, "weight_bytes": r.weight_bytes,
+                "algo_bytes": r.algo_bytes}
+
+    def device_bytes(self) -> int:
+        return _lib.lib().rk_engine_device_bytes(self._h)

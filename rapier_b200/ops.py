@@ -19,7 +19,7 @@ __all__ = [
     "TYPE_Q6_K", "TYPE_Q8_0", "RkError",
     "native_q8_1_bytes", "native_quantize_q8_1", "native_mmvq_weight_bytes", "native_mmvq",
     "native_q6_k_mmvq", "native_q8_0_mmvq", "native_q6_k_mmvq_res", "native_q8_0_mmvq_res",
-    "packed_bytes", "pack_weights", "unpack_weights", "mmvq_packed", "mmvq_packed_res", "mmvq_isums",
+    "packed_bytes", "pack_weights", "unpack_weights", "mmvq_packed", "mmvq_packed_ex", "mmvq_packed_res", "mmvq_isums",
     "row_sum_partials", "add_partials", "rms_quant_apply", "rms_norm_out", "swiglu_quant", "sig_mul_quant",
     "beta_gate", "rms_norm_weighted", "argmax", "fused_gdn_conv_l2", "fused_gdn_step_norm_silu_q8",
     "gdn_fused", "split_qg", "rope_apply", "store_kv_f16", "gqa_scratch_bytes", "gqa_decode_f16", "device_status",
@@ -121,6 +121,11 @@ def unpack_weights(ggml_type, src, dst, n_in, n_out, stream=None):
 
 def mmvq_packed(ggml_type, packed, x_q8_1, y, n_in, n_out, ncols, stream=None):
     _call("rk_mmvq_packed", ggml_type, _ptr(packed), _ptr(x_q8_1), _ptr(y), n_in, n_out, ncols, _stream(stream))
+
+
+def mmvq_packed_ex(ggml_type, packed, x_q8_1, y, n_in, n_out, ncols, flags, stream=None):
+    _call("rk_mmvq_packed_ex", ggml_type, _ptr(packed), _ptr(x_q8_1), _ptr(y), n_in, n_out, ncols, flags,
+          _stream(stream))
 
 
 def mmvq_packed_res(ggml_type, packed, x_q8_1, y, res, partials, n_in, n_out, ncols, stream=None):
