@@ -323,7 +323,7 @@ def cpu_baseline_decode(budget_s=20.0):
     cfg = config_9b(max_ctx=64, seed=1)
     cfg.n_layer, cfg.attn_interval = 4, 4  # layers 0..2 GDN, 3 attention; layers 0 and 3 are timed
     t_gen = time.perf_counter()
-    m = Model(cfg)
+    m = Model(cfg, only_layers=(0, 3), with_embed=False)
     t_gen = time.perf_counter() - t_gen
     H = cfg.n_embd
     x = O.synth_normal(3, H)

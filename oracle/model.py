@@ -32,7 +32,9 @@ def gen_q6k(seed: int, tid: int, n_in: int, n_out: int) -> np.ndarray:
 
 
 class Model:
-    def __init__(self, cfg):
+    def __init__(self, cfg, only_layers=None, with_embed=True):
+        """only_layers: generate just these layer indices (the others stay None); with_embed=False skips
+        the token embedding (the CPU baseline times layers and the head only)."""
         from rapier_b200 import engine as E
 
         self.cfg = cfg
@@ -41,13 +43,16 @@ class Model:
         hk, hv, nh, nkv = cfg.ssm_h_k, cfg.ssm_h_v, cfg.n_head, cfg.n_head_kv
         self.H, self.FF, self.V, self.hk, self.hv, self.nh, self.nkv = H, FF, V, hk, hv, nh, nkv
         self.eps = np.float32(cfg.eps)
-        self.tok_embd = gen_q6k(s, E.T_TOK_EMBD, H, V)
+        self.tok_embd = gen_q6k(s, E.T_TOK_EMBD, H, V) if with_embed else None
         self.out_norm = gen_f32(s, E.T_OUT_NORM, H, 0.02, 1.0)
         self.lm_head = gen_q6k(s, E.T_OUTPUT, H, V)
         self.layers = []
         C = 2 * hk * KS + hv * KS
         self.C = C
         for il in range(cfg.n_layer):
+            if only_layers is not None and il not in only_layers:
+                self.layers.append(None)
+                continue
             t = lambda slot: E.layer_tid(il, slot)  # noqa: E731
             L = {"gdn": ((il + 1) % cfg.attn_interval) != 0,
                  "attn_norm": gen_f32(s, t(E.L_ATTN_NORM), H, 0.02, 1.0),
@@ -77,6 +82,8 @@ class Model:
         cfg = self.cfg
         self.state = {}
         for il, L in enumerate(self.layers):
+            if L is None:
+                continue
             if L["gdn"]:
                 self.state[il] = {"ring": np.zeros(self.C * 4, np.float32),
                                   "ssm": np.zeros(KS * self.hv * KS, np.float32)}
