@@ -9,7 +9,7 @@
 // of each (head, column) in chunk order. Column c attends tokens 0..pos+c; its chunk partition and every
 // reduction depend only on its own position, so a 2-column launch gives each column the bits of a
 // 1-column launch at that position.
-#include "common.cuh"
+#include "mmvq.cuh"
 
 namespace rk {
 namespace {
@@ -172,11 +172,14 @@ __global__ void __launch_bounds__(256) gqa_chunk_kernel(const float* __restrict_
     (void) mstat;
 }
 
-// ---- combine: grid (n_head, NC), 256 threads (thread = dim). Chunks merged in order. ----
+// ---- combine: grid (n_head, NC), 256 threads (thread = dim). Chunks merged in order. With gate/q8 set it
+// also writes the Q8_1 blocks of o * sigmoid(gate) (sig_mul_quant_kernel, src/qwythos.cpp:692-704; one
+// warp = one 32-dim block). ----
 template <int NC>
 __global__ void __launch_bounds__(256) gqa_combine_kernel(const float* __restrict__ part_o,
                                                           const float* __restrict__ part_ml, float* __restrict__ o,
-                                                          int n_head, int max_chunks, const int* __restrict__ posp) {
+                                                          int n_head, int max_chunks, const int* __restrict__ posp,
+                                                          const float* __restrict__ gate, uint8_t* __restrict__ q8) {
     pdl_trigger();
     pdl_wait();
     const int h = blockIdx.x, c = blockIdx.y, d = threadIdx.x;
@@ -193,7 +196,11 @@ __global__ void __launch_bounds__(256) gqa_combine_kernel(const float* __restric
         num = __fmaf_rn(w, po[(size_t) k * kHd + d], num);
         den = __fmaf_rn(w, ml[2 * k + 1], den);
     }
-    o[((size_t) c * n_head + h) * kHd + d] = __fdiv_rn(num, den);
+    const float ov = __fdiv_rn(num, den);
+    const size_t oi = ((size_t) c * n_head + h) * kHd + d;
+    o[oi] = ov;
+    if (q8 != nullptr)
+        q8_1_warp_store(sigmul_value(ov, gate[oi]), q8 + (((size_t) c * n_head + h) * (kHd / 32) + (d >> 5)) * 36, d & 31);
 }
 
 int check_ptr(const void* p, const char* what) {
@@ -219,7 +226,8 @@ size_t gqa_scratch_bytes(int n_head, int ncols, int max_ctx) {
 
 // Launch the chunk + combine kernels (the engine calls this directly with PDL).
 cudaError_t gqa_launch(const float* q, const __half* kc, const __half* vc, float* o, int n_head, int n_kv, int ncols,
-                       const int* pos, int max_ctx, float scale, float* scratch, cudaStream_t s, bool pdl) {
+                       const int* pos, int max_ctx, float scale, float* scratch, cudaStream_t s, bool pdl,
+                       const float* gate, uint8_t* q8) {
     const int max_chunks = (max_ctx + kChunk - 1) / kChunk;
     float* part_o = scratch;
     float* part_ml = scratch + (size_t) n_head * ncols * max_chunks * kHd;
@@ -235,9 +243,9 @@ cudaError_t gqa_launch(const float* q, const __half* kc, const __half* vc, float
     if (e != cudaSuccess) return e;
     if (ncols == 1)
         return launch_pdl(gqa_combine_kernel<1>, dim3((unsigned) n_head, 1), dim3(256), 0, s, pdl, part_o, part_ml, o,
-                          n_head, max_chunks, pos);
+                          n_head, max_chunks, pos, gate, q8);
     return launch_pdl(gqa_combine_kernel<2>, dim3((unsigned) n_head, 2), dim3(256), 0, s, pdl, part_o, part_ml, o, n_head,
-                      max_chunks, pos);
+                      max_chunks, pos, gate, q8);
 }
 
 }  // namespace rk
@@ -310,7 +318,7 @@ int rk_gqa_decode_f16(const float* q, const uint16_t* kcache, const uint16_t* vc
     if (int rc = check_ptr(scratch, what)) return rc;
     if (int rc = check_stream(stream, what)) return rc;
     return launched(gqa_launch(q, (const __half*) kcache, (const __half*) vcache, o, n_head, n_kv, ncols, pos, max_ctx,
-                               scale, (float*) scratch, (cudaStream_t) stream, true),
+                               scale, (float*) scratch, (cudaStream_t) stream, true, nullptr, nullptr),
                     what);
 }
 

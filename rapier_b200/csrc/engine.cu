@@ -28,7 +28,8 @@ cudaError_t gdn_fused_launch(const float* proj, int proj_stride, float* ring, co
                              float* y, uint8_t* q8, int h_k, int h_v, int ncols, const int* pos, float eps,
                              cudaStream_t s, bool pdl);
 cudaError_t gqa_launch(const float* q, const __half* kc, const __half* vc, float* o, int n_head, int n_kv, int ncols,
-                       const int* pos, int max_ctx, float scale, float* scratch, cudaStream_t s, bool pdl);
+                       const int* pos, int max_ctx, float scale, float* scratch, cudaStream_t s, bool pdl,
+                       const float* gate, uint8_t* q8);
 size_t gqa_scratch_bytes(int n_head, int ncols, int max_ctx);
 
 namespace {
@@ -387,6 +388,8 @@ struct EngineImpl {
     float *x = nullptr, *xp = nullptr, *proj = nullptr, *gdn_y = nullptr, *ug = nullptr;
     uint8_t* q8 = nullptr;
     float *q_attn = nullptr, *g_attn = nullptr, *o_attn = nullptr, *attn_scratch = nullptr;
+    uint8_t *q8_ff = nullptr, *q8_attn = nullptr;  // Q8_1 inputs of the down and wo GEMVs
+    unsigned* swiglu_cnt = nullptr;                // last-arriver counters of the up||gate epilogue
     float *hsave = nullptr, *hsave_p = nullptr, *logits = nullptr;
     float *dx = nullptr, *dxp = nullptr;
     uint8_t* eh_q8 = nullptr;
@@ -430,12 +433,11 @@ struct EngineImpl {
     void trunk(bool pdl);
     template <int NC>
     void draft_pass(bool with_head, bool pdl);
-    template <int NC>
+    template <int NC, int EPI>
     void gemv_rms(const Mat& m, const float* x_, const float* w, const float* part, float* y, int y_stride, bool pdl,
                   float* xn_out = nullptr, float* xn_part = nullptr, unsigned long long* amax = nullptr);
     template <int NC>
-    void gemv_res(int pro, const Mat& m, const void* a, const float* b, int a_stride, int b_stride, float* xres,
-                  float* part, bool pdl);
+    void gemv_q8_res(const Mat& m, const uint8_t* xq, float* xres, float* part, bool pdl);
     template <int NC>
     void ffn(const Layer& L, float* xres, float* part, bool pdl);
     template <int NC>
@@ -605,6 +607,9 @@ int EngineImpl::build() {
     g_attn = alloc<float>(2 * (size_t) nh * kHd);
     o_attn = alloc<float>(2 * (size_t) nh * kHd);
     attn_scratch = alloc<float>(gqa_scratch_bytes(nh, 2, c.max_ctx) / sizeof(float));
+    q8_ff = alloc<uint8_t>(2 * rk_q8_1_bytes(FF, 1));
+    q8_attn = alloc<uint8_t>(2 * rk_q8_1_bytes(nh * kHd, 1));
+    swiglu_cnt = alloc<unsigned>((size_t) FF / 32);
     hsave = alloc<float>(2 * (size_t) H);
     hsave_p = alloc<float>(2 * (size_t) H / 4);
     logits = alloc<float>(2 * (size_t) V);
@@ -623,7 +628,7 @@ int EngineImpl::build() {
 // ---------------------------------------------------------------------------------------------------
 // launch sequence
 // ---------------------------------------------------------------------------------------------------
-template <int NC>
+template <int NC, int EPI>
 void EngineImpl::gemv_rms(const Mat& m, const float* x_, const float* w, const float* part, float* y, int y_stride,
                           bool pdl, float* xn_out, float* xn_part, unsigned long long* amax) {
     MmvqParams p = {};
@@ -632,7 +637,6 @@ void EngineImpl::gemv_rms(const Mat& m, const float* x_, const float* w, const f
     p.n_out = m.n_out;
     p.prefetch_before_wait = 1;
     p.xa = x_;
-    p.xa_stride = m.n_in;
     p.xb = w;
     p.pin = part;
     p.eps = cfg.eps;
@@ -641,41 +645,35 @@ void EngineImpl::gemv_rms(const Mat& m, const float* x_, const float* w, const f
     p.xn_out = xn_out;
     p.xn_part = xn_part;
     p.amax = amax;
-    if (amax) ok(mmvq_launch<RK_TYPE_Q6_K, NC, PRO_RMS, EPI_ARGMAX>(p, s, pdl));
-    else ok(mmvq_launch<RK_TYPE_Q6_K, NC, PRO_RMS, EPI_STORE>(p, s, pdl));
+    p.q8out = q8_ff;
+    p.cnt = swiglu_cnt;
+    ok(mmvq_launch<RK_TYPE_Q6_K, NC, PRO_RMS, EPI>(p, s, pdl));
 }
 
-// y = W . prologue(a, b) + xres (in place), partials. pro: PRO_Q8 (a = Q8_1 blocks), PRO_SWIGLU (a = up,
-// b = gate), PRO_SIGMUL (a = o, b = gate).
+// xres = W . xq + xres (in place) with the 4-row partials (the reference's residual epilogue).
 template <int NC>
-void EngineImpl::gemv_res(int pro, const Mat& m, const void* a, const float* b, int a_stride, int b_stride, float* xres,
-                          float* part, bool pdl) {
+void EngineImpl::gemv_q8_res(const Mat& m, const uint8_t* xq, float* xres, float* part, bool pdl) {
     MmvqParams p = {};
     p.w = m.w;
     p.n_in = m.n_in;
     p.n_out = m.n_out;
     p.prefetch_before_wait = 1;
-    p.xq = static_cast<const uint8_t*>(a);
-    p.xa = static_cast<const float*>(a);
-    p.xb = b;
-    p.xa_stride = a_stride;
-    p.xb_stride = b_stride;
+    p.xq = xq;
     p.y = xres;
     p.y_stride = m.n_out;
     p.res = xres;
     p.res_stride = m.n_out;
     p.pout = part;
     p.pout_stride = m.n_out / 4;
-    if (pro == PRO_Q8) ok(mmvq_launch<RK_TYPE_Q6_K, NC, PRO_Q8, EPI_RES>(p, s, pdl));
-    else if (pro == PRO_SWIGLU) ok(mmvq_launch<RK_TYPE_Q6_K, NC, PRO_SWIGLU, EPI_RES>(p, s, pdl));
-    else ok(mmvq_launch<RK_TYPE_Q6_K, NC, PRO_SIGMUL, EPI_RES>(p, s, pdl));
+    ok(mmvq_launch<RK_TYPE_Q6_K, NC, PRO_Q8, EPI_RES>(p, s, pdl));
 }
 
-// FFN (src/qwythos.cpp:1011-1042): RMSNorm(post_norm)+Q8_1 -> up||gate -> silu(gate)*up+Q8_1 -> down + residual.
+// FFN (src/qwythos.cpp:1011-1042): RMSNorm(post_norm)+Q8_1 -> up||gate with the SwiGLU+Q8_1 epilogue ->
+// down + residual.
 template <int NC>
 void EngineImpl::ffn(const Layer& L, float* xres, float* part, bool pdl) {
-    gemv_rms<NC>(L.upgate, xres, L.post_norm, part, ug, 2 * FF, pdl);
-    gemv_res<NC>(PRO_SWIGLU, L.down, ug, ug + FF, 2 * FF, 2 * FF, xres, part, pdl);
+    gemv_rms<NC, EPI_SWIGLU>(L.upgate, xres, L.post_norm, part, ug, 2 * FF, pdl);
+    gemv_q8_res<NC>(L.down, q8_ff, xres, part, pdl);
 }
 
 template <int NC>
@@ -685,25 +683,25 @@ void EngineImpl::trunk(bool pdl) {
                   x, xp));
     const size_t q8col = rk_q8_1_bytes(hv * kS, 1);
     for (const Layer& L : layers) {
-        gemv_rms<NC>(L.in_proj, x, L.attn_norm, xp, proj, L.in_proj.n_out, pdl);
+        gemv_rms<NC, EPI_STORE>(L.in_proj, x, L.attn_norm, xp, proj, L.in_proj.n_out, pdl);
         if (L.gdn) {
             ok(gdn_fused_launch(proj, L.in_proj.n_out, L.ring, L.conv_w, L.dt, L.ssm_a, L.ssm_norm, L.state, L.snap,
                                 &ctrl->rollback, gdn_y, q8, hk, hv, NC, &ctrl->pos, cfg.eps, s, pdl));
             (void) q8col;
-            gemv_res<NC>(PRO_Q8, L.out_proj, q8, nullptr, 0, 0, x, xp, pdl);
+            gemv_q8_res<NC>(L.out_proj, q8, x, xp, pdl);
         } else {
             ok(launch_pdl(attn_prep_kernel<NC>, dim3(nh + nkv, NC), dim3(256), 0, s, pdl, (const float*) proj,
                           L.in_proj.n_out, (const float*) L.q_norm, (const float*) L.k_norm, (const float*) rope,
                           cfg.n_rot, (const int*) &ctrl->pos, nh, nkv, cfg.max_ctx, cfg.eps, q_attn, g_attn, L.kc, L.vc));
             ok(gqa_launch(q_attn, L.kc, L.vc, o_attn, nh, nkv, NC, &ctrl->pos, cfg.max_ctx, kAttnScale, attn_scratch, s,
-                          pdl));
+                          pdl, g_attn, q8_attn));
             ++launches;  // the combine kernel
-            gemv_res<NC>(PRO_SIGMUL, L.out_proj, o_attn, g_attn, nh * kHd, nh * kHd, x, xp, pdl);
+            gemv_q8_res<NC>(L.out_proj, q8_attn, x, xp, pdl);
         }
         ffn<NC>(L, x, xp, pdl);
     }
     // final norm + lm_head + argmax; the normed hidden and its partials feed the draft (src/qwythos.cpp:1234-1237)
-    gemv_rms<NC>(lm_head, x, out_norm, xp, logits, V, pdl, hsave, hsave_p, ctrl->amax);
+    gemv_rms<NC, EPI_ARGMAX>(lm_head, x, out_norm, xp, logits, V, pdl, hsave, hsave_p, ctrl->amax);
 }
 
 // The GEMVs of one trunk step only (rk_engine_probe_gemv), with their byte counts.
@@ -719,16 +717,15 @@ void EngineImpl::probe_body() {
         ++n;
     };
     for (const Layer& L : layers) {
-        gemv_rms<NC>(L.in_proj, x, L.attn_norm, xp, proj, L.in_proj.n_out, true);
+        gemv_rms<NC, EPI_STORE>(L.in_proj, x, L.attn_norm, xp, proj, L.in_proj.n_out, true);
         count(L.in_proj, true, false);
-        if (L.gdn) gemv_res<NC>(PRO_Q8, L.out_proj, q8, nullptr, 0, 0, x, xp, true);
-        else gemv_res<NC>(PRO_SIGMUL, L.out_proj, o_attn, g_attn, nh * kHd, nh * kHd, x, xp, true);
-        count(L.out_proj, !L.gdn, true);
+        gemv_q8_res<NC>(L.out_proj, L.gdn ? q8 : q8_attn, x, xp, true);
+        count(L.out_proj, false, true);
         ffn<NC>(L, x, xp, true);
         count(L.upgate, true, false);
-        count(L.down, true, true);
+        count(L.down, false, true);
     }
-    gemv_rms<NC>(lm_head, x, out_norm, xp, logits, V, true, hsave, hsave_p, ctrl->amax);
+    gemv_rms<NC, EPI_ARGMAX>(lm_head, x, out_norm, xp, logits, V, true, hsave, hsave_p, ctrl->amax);
     count(lm_head, true, false);
     probe_weight_bytes = wb;
     probe_algo_bytes = ab;
@@ -755,15 +752,17 @@ void EngineImpl::draft_pass(bool with_head, bool pdl) {
         ok(mmvq_launch<RK_TYPE_Q6_K, NC, PRO_Q8, EPI_STORE_P>(p, s, pdl));
     }
     const Layer& D = draft;
-    gemv_rms<NC>(D.in_proj, dx, D.attn_norm, dxp, proj, D.in_proj.n_out, pdl);
+    gemv_rms<NC, EPI_STORE>(D.in_proj, dx, D.attn_norm, dxp, proj, D.in_proj.n_out, pdl);
     ok(launch_pdl(attn_prep_kernel<NC>, dim3(nh + nkv, NC), dim3(256), 0, s, pdl, (const float*) proj, D.in_proj.n_out,
                   (const float*) D.q_norm, (const float*) D.k_norm, (const float*) rope, cfg.n_rot,
                   (const int*) &ctrl->dpos, nh, nkv, cfg.max_ctx, cfg.eps, q_attn, g_attn, D.kc, D.vc));
-    ok(gqa_launch(q_attn, D.kc, D.vc, o_attn, nh, nkv, NC, &ctrl->dpos, cfg.max_ctx, kAttnScale, attn_scratch, s, pdl));
+    ok(gqa_launch(q_attn, D.kc, D.vc, o_attn, nh, nkv, NC, &ctrl->dpos, cfg.max_ctx, kAttnScale, attn_scratch, s, pdl,
+                  g_attn, q8_attn));
     ++launches;
-    gemv_res<NC>(PRO_SIGMUL, D.out_proj, o_attn, g_attn, nh * kHd, nh * kHd, dx, dxp, pdl);
+    gemv_q8_res<NC>(D.out_proj, q8_attn, dx, dxp, pdl);
     ffn<NC>(D, dx, dxp, pdl);
-    if (with_head) gemv_rms<NC>(lm_head, dx, shnorm, dxp, nullptr, V, pdl, nullptr, nullptr, ctrl->damax);
+    if (with_head)
+        gemv_rms<NC, EPI_ARGMAX>(lm_head, dx, shnorm, dxp, nullptr, V, pdl, nullptr, nullptr, ctrl->damax);
 }
 
 int EngineImpl::capture(cudaGraphExec_t* exec, int* nk, void (*body)(EngineImpl*)) {
@@ -897,6 +896,7 @@ int rk_engine_reset(rk_engine* e) {
     for (Layer& L : E.layers) clear(L);
     if (E.cfg.has_mtp) clear(E.draft);
     cudaMemsetAsync(E.ctrl, 0, sizeof(Ctrl), E.s);
+    cudaMemsetAsync(E.swiglu_cnt, 0, sizeof(unsigned) * (size_t) E.FF / 32, E.s);
     const cudaError_t ce = cudaStreamSynchronize(E.s);
     if (ce != cudaSuccess) return set_error(RK_ECUDA, "rk_engine_reset: %s", cudaGetErrorString(ce));
     return RK_OK;

@@ -29,8 +29,11 @@ constexpr int kMmvqWarps = 8;      // consumer warps per CTA (256 threads)
 constexpr int kMmvqMaxStages = 8;  // ring slots per warp (runtime `stages` <= this)
 constexpr int kMmvqMaxCols = 4;    // columns per launch (more are split into launches over column chunks)
 
-enum MmvqPro { PRO_Q8 = 0, PRO_RMS = 1, PRO_SWIGLU = 2, PRO_SIGMUL = 3 };
-enum MmvqEpi { EPI_STORE = 0, EPI_RES = 1, EPI_ARGMAX = 2, EPI_STORE_P = 3 };
+enum MmvqPro { PRO_Q8 = 0, PRO_RMS = 1 };
+// EPI_SWIGLU: y as EPI_STORE for a [up (n_out/2) | gate (n_out/2)] matrix, and for every 32-position block
+// whose 16 units (8 up + 8 gate) are done, the last warp to finish one of them writes the Q8_1 block of
+// silu(gate) * up (the down GEMV's input; swiglu_quant_kernel, src/qwythos.cpp:676-689).
+enum MmvqEpi { EPI_STORE = 0, EPI_RES = 1, EPI_ARGMAX = 2, EPI_STORE_P = 3, EPI_SWIGLU = 4 };
 
 struct MmvqParams {
     const uint8_t* w;  // packed tiles
@@ -39,10 +42,9 @@ struct MmvqParams {
     int prefetch_before_wait;  // 1: weights are static, stream them before waiting on the upstream grid
     // prologue inputs
     const uint8_t* xq;  // PRO_Q8: Q8_1 blocks, column stride rk_q8_1_bytes(n_in, 1)
-    const float* xa;    // PRO_RMS: x; PRO_SWIGLU: up; PRO_SIGMUL: o       (column stride xa_stride)
-    const float* xb;    // PRO_RMS: norm weight (shared); PRO_SWIGLU: gate; PRO_SIGMUL: g (stride xb_stride)
+    const float* xa;    // PRO_RMS: x (column stride n_in)
+    const float* xb;    // PRO_RMS: norm weight
     const float* pin;   // PRO_RMS: partials, column stride n_in/4
-    int xa_stride, xb_stride;
     float eps;
     // epilogue
     float* y;
@@ -52,6 +54,8 @@ struct MmvqParams {
     float* pout;        // EPI_RES partials, column stride pout_stride
     int pout_stride;
     unsigned long long* amax;  // EPI_ARGMAX: one packed (value, ~row) slot per column
+    uint8_t* q8out;            // EPI_SWIGLU: Q8_1 of silu(gate) * up, column stride rk_q8_1_bytes(n_out/2, 1)
+    unsigned* cnt;             // EPI_SWIGLU: n_out/64 zeroed counters (left zeroed on exit)
     // PRO_RMS write-through (optional): CTA 0 stores the normalized fp32 row (x * w * inv) of every
     // column (stride n_in) and its 4-row sum-of-squares partials (stride n_in/4), the reference's
     // rms_norm_out + row_sum_partials of the final hidden (src/qwythos.cpp:1236-1237).
@@ -125,10 +129,14 @@ __device__ __forceinline__ void xstage_put_warp(const XStage& s, int g, int code
 }
 
 // Build every column's staged activations. All 256 threads participate (contains __syncthreads).
+// PRO_Q8: one thread per Q8_1 block (9 ints) -> planes + meta.
+// PRO_RMS: the reference's rms_quant_apply (inv from the partials, v = x * w * inv, Q8_1 per 32 values)
+// with one thread per 16-value half block: every load is issued before any arithmetic, the two halves of
+// a block meet through one shuffle (amax), and each half's codes go to its plane. The codes and scale are
+// those of the standalone kernel (same q8_* rules on the same fp32 values).
 template <int NC, int PRO>
 __device__ __forceinline__ void mmvq_build_x(const MmvqParams& p, uint8_t* xsm, float* red) {
     const int ng = p.n_in >> 5;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if constexpr (PRO == PRO_Q8) {
         const size_t col_bytes = (size_t) ng * 36;
         for (int idx = threadIdx.x; idx < NC * ng; idx += blockDim.x) {
@@ -146,41 +154,77 @@ __device__ __forceinline__ void mmvq_build_x(const MmvqParams& p, uint8_t* xsm, 
         }
     } else {
         float inv[NC];
-        if constexpr (PRO == PRO_RMS) {
 #pragma unroll
-            for (int c = 0; c < NC; ++c)
-                inv[c] = rms_inv(block256_partials_sum(p.pin + (size_t) c * (p.n_in / 4), p.n_in / 4, red), p.n_in,
-                                 p.eps);
-        }
-        for (int idx = warp; idx < NC * ng; idx += blockDim.x >> 5) {
-            const int c = idx / ng, g = idx - c * ng;
-            const int i = (g << 5) + lane;
-            float v;
-            if constexpr (PRO == PRO_RMS) {
-                v = rms_value(p.xa[(size_t) c * p.xa_stride + i], p.xb[i], inv[c]);
-            } else if constexpr (PRO == PRO_SWIGLU) {
-                v = swiglu_value(p.xa[(size_t) c * p.xa_stride + i], p.xb[(size_t) c * p.xb_stride + i]);
+        for (int c = 0; c < NC; ++c)
+            inv[c] = rms_inv(block256_partials_sum(p.pin + (size_t) c * (p.n_in / 4), p.n_in / 4, red), p.n_in, p.eps);
+        const int items = NC * ng * 2;  // half blocks; the two halves of a block sit on adjacent lanes
+        for (int base = 0; base < items; base += 256) {
+            const int it = base + (int) threadIdx.x;
+            const bool live = it < items;
+            const int c = live ? it / (2 * ng) : 0;
+            const int rem = it - c * 2 * ng;
+            const int g = rem >> 1, h = rem & 1;
+            const int i0 = (g << 5) + (h << 4);
+            float v[16];
+            if (live) {
+                const float4* xp4 = reinterpret_cast<const float4*>(p.xa + (size_t) c * p.n_in + i0);
+                const float4* wp4 = reinterpret_cast<const float4*>(p.xb + i0);
+                float4 xv[4], wv[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    xv[k] = xp4[k];
+                    wv[k] = wp4[k];
+                }
+                float invc = inv[0];
+#pragma unroll
+                for (int cc = 1; cc < NC; ++cc)
+                    if (c == cc) invc = inv[cc];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    v[4 * k + 0] = rms_value(xv[k].x, wv[k].x, invc);
+                    v[4 * k + 1] = rms_value(xv[k].y, wv[k].y, invc);
+                    v[4 * k + 2] = rms_value(xv[k].z, wv[k].z, invc);
+                    v[4 * k + 3] = rms_value(xv[k].w, wv[k].w, invc);
+                }
             } else {
-                v = sigmul_value(p.xa[(size_t) c * p.xa_stride + i], p.xb[(size_t) c * p.xb_stride + i]);
+#pragma unroll
+                for (int k = 0; k < 16; ++k) v[k] = 0.0f;
             }
-            uint32_t ds;
-            const int code = q8_1_warp_code(v, ds);
-            if constexpr (PRO == PRO_RMS) {
-                if (p.xn_out != nullptr && blockIdx.x == 0) {
-                    p.xn_out[(size_t) c * p.n_in + i] = v;
-                    // 4-row partials in row order: lanes 4j..4j+3 form slot j of this block
-                    const float v1 = __shfl_down_sync(0xffffffffu, v, 1), v2 = __shfl_down_sync(0xffffffffu, v, 2),
-                                v3 = __shfl_down_sync(0xffffffffu, v, 3);
-                    if ((lane & 3) == 0) {
-                        float part = __fmul_rn(v, v);
-                        part = __fmaf_rn(v1, v1, part);
-                        part = __fmaf_rn(v2, v2, part);
-                        part = __fmaf_rn(v3, v3, part);
-                        p.xn_part[(size_t) c * (p.n_in / 4) + (i >> 2)] = part;
-                    }
+            float amax = 0.0f;
+#pragma unroll
+            for (int k = 0; k < 16; ++k) amax = fmaxf(amax, fabsf(v[k]));
+            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+            const float d = q8_finite_d(__fdiv_rn(amax, 127.0f));
+            int packed[4] = {0, 0, 0, 0};
+            int csum = 0;
+#pragma unroll
+            for (int k = 0; k < 16; ++k) {
+                const int q = q8_quant(v[k], d, amax);
+                csum += q;
+                packed[k >> 2] |= (q & 0xff) << (8 * (k & 3));
+            }
+            const int other = __shfl_xor_sync(0xffffffffu, csum, 1);
+            if (live) {
+                const XStage s = xstage_col(xsm, ng, c);
+                (h ? s.hi : s.lo)[g] = make_int4(packed[0], packed[1], packed[2], packed[3]);
+                if (h == 0)
+                    s.meta[g] = make_float4(__half2float(__float2half_rn(d)), __int_as_float(32 * csum),
+                                            __int_as_float(32 * other), 0.0f);
+            }
+            // PRO_RMS write-through of the normalized row and its partials (CTA 0 only)
+            if (p.xn_out != nullptr && blockIdx.x == 0 && live) {
+                float* xo = p.xn_out + (size_t) c * p.n_in + i0;
+#pragma unroll
+                for (int k = 0; k < 16; ++k) xo[k] = v[k];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    float part = __fmul_rn(v[4 * k], v[4 * k]);
+                    part = __fmaf_rn(v[4 * k + 1], v[4 * k + 1], part);
+                    part = __fmaf_rn(v[4 * k + 2], v[4 * k + 2], part);
+                    part = __fmaf_rn(v[4 * k + 3], v[4 * k + 3], part);
+                    p.xn_part[(size_t) c * (p.n_in / 4) + (i0 >> 2) + k] = part;
                 }
             }
-            xstage_put_warp(xstage_col(xsm, ng, c), g, code, ds, lane);
         }
     }
 }
@@ -276,7 +320,7 @@ __device__ __forceinline__ void mmvq_epilogue(const MmvqParams& p, int unit, int
 #pragma unroll
         for (int r = 0; r < 4; ++r) acc[c][r] = warp_sum(acc[c][r]);
     const int row0 = unit * 4;
-    if constexpr (EPI == EPI_STORE || EPI == EPI_ARGMAX) {
+    if constexpr (EPI == EPI_STORE || EPI == EPI_ARGMAX || EPI == EPI_SWIGLU) {
         if (p.y != nullptr) {
             float out = 0.0f;
 #pragma unroll
@@ -301,6 +345,28 @@ __device__ __forceinline__ void mmvq_epilogue(const MmvqParams& p, int unit, int
                             }
                     }
                 if (br >= 0) atomicMax(p.amax + lane, argmax_key(best, row0 + br));
+            }
+        }
+        if constexpr (EPI == EPI_SWIGLU) {
+            // units [0, half/4) are up rows, [half/4, half/2) gate rows; block group = 8 units of each
+            const int half = p.n_out >> 1;
+            const int u_half = unit < (half >> 2) ? unit : unit - (half >> 2);
+            const int grp = u_half >> 3;
+            __threadfence();  // every lane's y stores, before the count that publishes them
+            __syncwarp();
+            unsigned last = 0;
+            if (lane == 0) last = atomicAdd(p.cnt + grp, 1u) == 15u;
+            last = __shfl_sync(0xffffffffu, last, 0);
+            if (last) {
+                __threadfence();
+                const int i = (grp << 5) + lane;
+#pragma unroll
+                for (int c = 0; c < NC; ++c) {
+                    const float up = __ldcg(p.y + (size_t) c * p.y_stride + i);
+                    const float g = __ldcg(p.y + (size_t) c * p.y_stride + half + i);
+                    q8_1_warp_store(swiglu_value(up, g), p.q8out + ((size_t) c * (half >> 5) + grp) * 36, lane);
+                }
+                if (lane == 0) p.cnt[grp] = 0u;
             }
         }
     } else {  // EPI_RES (y = acc + res) / EPI_STORE_P (y = acc), both with the 4-row partials
