@@ -313,8 +313,12 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, int row) {
 }
 __host__ __device__ __forceinline__ int argmax_key_row(unsigned long long k) { return (int) (0xffffffffu - (uint32_t) (k & 0xffffffffu)); }
 
+// best[c] (EPI_ARGMAX): the warp's running packed (value, ~row) maximum of column c; the caller issues one
+// atomicMax per warp and column after its last unit (the reference's atomicMax on (monotonic bits, n-1-idx),
+// src/qwythos.cpp:70-84, with the lowest-index tie rule).
 template <int NC, int EPI>
-__device__ __forceinline__ void mmvq_epilogue(const MmvqParams& p, int unit, int lane, float (&acc)[NC][4]) {
+__device__ __forceinline__ void mmvq_epilogue(const MmvqParams& p, int unit, int lane, float (&acc)[NC][4],
+                                              unsigned long long (&best)[NC]) {
 #pragma unroll
     for (int c = 0; c < NC; ++c)
 #pragma unroll
@@ -331,21 +335,14 @@ __device__ __forceinline__ void mmvq_epilogue(const MmvqParams& p, int unit, int
             if (lane < NC * 4) p.y[(size_t) (lane >> 2) * p.y_stride + row0 + (lane & 3)] = out;
         }
         if constexpr (EPI == EPI_ARGMAX) {
-            if (lane < NC) {
-                float best = 0.0f;
-                int br = -1;
 #pragma unroll
-                for (int c = 0; c < NC; ++c)
-                    if (lane == c) {
+            for (int c = 0; c < NC; ++c)
 #pragma unroll
-                        for (int r = 0; r < 4; ++r)
-                            if (acc[c][r] == acc[c][r] && (br < 0 || acc[c][r] > best)) {
-                                best = acc[c][r];
-                                br = r;
-                            }
+                for (int r = 0; r < 4; ++r)
+                    if (acc[c][r] == acc[c][r]) {  // NaN never wins
+                        const unsigned long long k = argmax_key(acc[c][r], row0 + r);
+                        best[c] = k > best[c] ? k : best[c];
                     }
-                if (br >= 0) atomicMax(p.amax + lane, argmax_key(best, row0 + br));
-            }
         }
         if constexpr (EPI == EPI_SWIGLU) {
             // units [0, half/4) are up rows, [half/4, half/2) gate rows; block group = 8 units of each
@@ -433,10 +430,13 @@ __global__ void __launch_bounds__(kMmvqWarps * 32, 2) mmvq_packed_kernel(const M
     __syncthreads();
 
     float acc[NC][4];
+    unsigned long long best[NC];
 #pragma unroll
-    for (int c = 0; c < NC; ++c)
+    for (int c = 0; c < NC; ++c) {
+        best[c] = 0ull;
 #pragma unroll
         for (int r = 0; r < 4; ++r) acc[c][r] = 0.0f;
+    }
 
     int s = 0, kc = 0, unit = ubeg + warp;
     uint32_t parity = 0;
@@ -466,7 +466,7 @@ __global__ void __launch_bounds__(kMmvqWarps * 32, 2) mmvq_packed_kernel(const M
             parity ^= 1u;
         }
         if (++kc == KC) {
-            mmvq_epilogue<NC, EPI>(p, unit, lane, acc);
+            mmvq_epilogue<NC, EPI>(p, unit, lane, acc, best);
 #pragma unroll
             for (int c = 0; c < NC; ++c)
 #pragma unroll
@@ -474,6 +474,11 @@ __global__ void __launch_bounds__(kMmvqWarps * 32, 2) mmvq_packed_kernel(const M
             kc = 0;
             unit += kMmvqWarps;
         }
+    }
+    if constexpr (EPI == EPI_ARGMAX) {
+#pragma unroll
+        for (int c = 0; c < NC; ++c)
+            if (lane == c && best[c] != 0ull) atomicMax(p.amax + c, best[c]);
     }
 }
 
