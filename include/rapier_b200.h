@@ -175,6 +175,15 @@ size_t rk_gqa_scratch_bytes(int n_head, int ncols, int max_ctx);
 int rk_gqa_decode_f16(const float* q, const uint16_t* kcache, const uint16_t* vcache, float* o, int n_head,
                       int n_kv, int hd, int ncols, const int* pos, int max_ctx, float scale, void* scratch,
                       size_t scratch_bytes, void* stream);
+/* No counterpart in the reference. rk_gqa_decode_f16 for callers that cannot allocate device memory (an
+ * application that owns all device memory through its own pool, a loop that cannot afford cudaMalloc's
+ * device synchronization): the chunk partials go to an array built into the library (16 MiB per device,
+ * held until exit) and nothing is allocated. Same arguments minus the scratch buffer; rejects shapes
+ * whose partials exceed 16 MiB (rk_gqa_scratch_bytes > 16 MiB; e.g. n_head 16, 2 columns fits up to
+ * max_ctx 126976) with RK_EINVAL. The first call on each device looks up the array's address; make it
+ * before any stream capture. All calls on a device share the array: calls that overlap on the GPU race. */
+int rk_gqa_decode_f16_noalloc(const float* q, const uint16_t* kcache, const uint16_t* vcache, float* o, int n_head,
+                              int n_kv, int hd, int ncols, const int* pos, int max_ctx, float scale, void* stream);
 
 /* ---------------------------------------------------------------------------------------------- */
 /* Decode engine (the reference's Engine / load_model / forward_token / draft_predict /              */

@@ -86,6 +86,7 @@ SIGNATURES = {
     "rk_store_kv_f16": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, vp]),
     "rk_gqa_scratch_bytes": (sz, [i32, i32, i32]),
     "rk_gqa_decode_f16": (i32, [vp, vp, vp, vp, i32, i32, i32, i32, vp, i32, f32, vp, sz, vp]),
+    "rk_gqa_decode_f16_noalloc": (i32, [vp, vp, vp, vp, i32, i32, i32, i32, vp, i32, f32, vp]),
     "rk_model_config_9b": (None, [C.POINTER(ModelConfig), i32, C.c_uint64]),
     "rk_engine_create": (i32, [C.POINTER(ModelConfig), i32, C.POINTER(vp)]),
     "rk_engine_destroy": (i32, [vp]),

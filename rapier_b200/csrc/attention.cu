@@ -9,6 +9,8 @@
 // of each (head, column) in chunk order. Column c attends tokens 0..pos+c; its chunk partition and every
 // reduction depend only on its own position, so a 2-column launch gives each column the bits of a
 // 1-column launch at that position.
+#include <mutex>
+
 #include "mmvq.cuh"
 
 namespace rk {
@@ -323,3 +325,71 @@ int rk_gqa_decode_f16(const float* q, const uint16_t* kcache, const uint16_t* vc
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------------------------
+// Allocation-free attention for callers that cannot allocate device memory themselves: for example a
+// plugin loaded into an application that hands all device memory to its own pool and forbids raw
+// cudaMalloc, or a decode loop that cannot afford the device-wide synchronization cudaMalloc / cudaFree
+// imply. The chunk partials live in the file-scope array below instead of a caller buffer. Every GPU that
+// loads this library holds the array (16 MiB) until the process exits.
+//
+// Set-up: the first call on each device looks up the array's device address with cudaGetSymbolAddress
+// (with that device current) and caches it; make that first call before any stream capture. Host code
+// never hands the symbol itself to a kernel: on the host it is only a stand-in, not a device address.
+//
+// Sharing: all calls on a device use the same array and it keeps the last call's contents. Nothing in it
+// has to start at zero (the chunk kernel writes every partial the combine reads in the same call), but
+// calls whose kernels overlap on the GPU (other streams, other host threads) race on the array and must
+// be serialized by the caller.
+// ---------------------------------------------------------------------------------------------------
+namespace rk {
+namespace {
+constexpr size_t kNoAllocScratchBytes = (size_t) 16 << 20;
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+}  // namespace
+}  // namespace rk
+
+static __device__ __align__(256) float g_gqa_noalloc_scratch[rk::kNoAllocScratchBytes / sizeof(float)];
+
+extern "C" int rk_gqa_decode_f16_noalloc(const float* q, const uint16_t* kcache, const uint16_t* vcache, float* o,
+                                         int n_head, int n_kv, int hd, int ncols, const int* pos, int max_ctx,
+                                         float scale, void* stream) {
+    const char* what = "rk_gqa_decode_f16_noalloc";
+    if (hd != kHd) return set_error(RK_EINVAL, "%s: requires hd == 256", what);
+    if (n_kv <= 0 || n_head != 4 * n_kv) return set_error(RK_EINVAL, "%s: requires n_head == 4 * n_kv", what);
+    if (ncols < 1 || ncols > 2) return set_error(RK_EINVAL, "%s: requires 1 <= ncols <= 2", what);
+    if (max_ctx <= 0) return set_error(RK_EINVAL, "%s: requires max_ctx > 0", what);
+    const size_t need = gqa_scratch_bytes(n_head, ncols, max_ctx);
+    if (need > kNoAllocScratchBytes)
+        return set_error(RK_EINVAL,
+                         "%s: n_head %d x ncols %d x max_ctx %d needs %zu bytes of partials, above the built-in %zu "
+                         "(use rk_gqa_decode_f16 with a caller buffer)",
+                         what, n_head, ncols, max_ctx, need, kNoAllocScratchBytes);
+    if (!q || (reinterpret_cast<uintptr_t>(q) & 15u)) return set_error(RK_EINVAL, "%s: q must be 16-byte aligned", what);
+    if (!kcache || !vcache || (reinterpret_cast<uintptr_t>(kcache) & 15u) || (reinterpret_cast<uintptr_t>(vcache) & 15u))
+        return set_error(RK_EINVAL, "%s: caches must be 16-byte aligned", what);
+    if (int rc = check_ptr(o, what)) return rc;
+    if (int rc = check_ptr(pos, what)) return rc;
+    if (int rc = check_stream(stream, what)) return rc;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return set_error(RK_ECUDA, "%s: cudaGetDevice: %s", what, cudaGetErrorString(e));
+    if (dev < 0 || dev >= kNoAllocMaxDevices) return set_error(RK_EINVAL, "%s: device %d out of range", what, dev);
+    void* scratch = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_noalloc_mu);
+        if (!g_noalloc_ptr[dev]) {
+            void* p = nullptr;
+            e = cudaGetSymbolAddress(&p, g_gqa_noalloc_scratch);
+            if (e != cudaSuccess || !p)
+                return set_error(RK_ECUDA, "%s: cudaGetSymbolAddress: %s", what, cudaGetErrorString(e));
+            g_noalloc_ptr[dev] = p;
+        }
+        scratch = g_noalloc_ptr[dev];
+    }
+    return launched(gqa_launch(q, (const __half*) kcache, (const __half*) vcache, o, n_head, n_kv, ncols, pos, max_ctx,
+                               scale, static_cast<float*>(scratch), (cudaStream_t) stream, true, nullptr, nullptr),
+                    what);
+}

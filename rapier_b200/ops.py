@@ -22,7 +22,7 @@ __all__ = [
     "packed_bytes", "pack_weights", "unpack_weights", "mmvq_packed", "mmvq_packed_ex", "mmvq_packed_res", "mmvq_isums",
     "row_sum_partials", "add_partials", "rms_quant_apply", "rms_norm_out", "swiglu_quant", "sig_mul_quant",
     "beta_gate", "rms_norm_weighted", "argmax", "fused_gdn_conv_l2", "fused_gdn_step_norm_silu_q8",
-    "gdn_fused", "split_qg", "rope_apply", "store_kv_f16", "gqa_scratch_bytes", "gqa_decode_f16", "device_status",
+    "gdn_fused", "split_qg", "rope_apply", "store_kv_f16", "gqa_scratch_bytes", "gqa_decode_f16", "gqa_decode_f16_noalloc", "device_status",
 ]
 
 
@@ -213,6 +213,14 @@ def gqa_decode_f16(q, kcache, vcache, o, n_head, n_kv, hd, ncols, pos, max_ctx, 
                    stream=None):
     _call("rk_gqa_decode_f16", _ptr(q), _ptr(kcache), _ptr(vcache), _ptr(o), n_head, n_kv, hd, ncols, _ptr(pos),
           max_ctx, scale, _ptr(scratch), scratch_bytes, _stream(stream))
+
+
+def gqa_decode_f16_noalloc(q, kcache, vcache, o, n_head, n_kv, hd, ncols, pos, max_ctx, scale, stream=None):
+    """gqa_decode_f16 without a scratch buffer, for callers that cannot allocate device memory: the chunk
+    partials use an array built into the library (16 MiB per device). Calls that overlap on the GPU race
+    on that array; the first call on a device should come before any stream capture."""
+    _call("rk_gqa_decode_f16_noalloc", _ptr(q), _ptr(kcache), _ptr(vcache), _ptr(o), n_head, n_kv, hd, ncols,
+          _ptr(pos), max_ctx, scale, _stream(stream))
 
 
 def device_status(clear: bool = True) -> int:
