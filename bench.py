@@ -263,21 +263,22 @@ def run_decode(args, rank, world, local, pg):
     eng = Engine(cfg, device=local)
     prompt = [int(t) for t in np.random.default_rng(1234 + rank).integers(0, cfg.n_vocab, N_PROMPT)]
     mtp = not args.no_mtp
+    n_gen = args.gen
     for _ in range(args.warmup):
-        eng.generate(prompt, N_GEN, mtp=mtp)
+        eng.generate(prompt, n_gen, mtp=mtp)
     barrier(pg, dev)
     gen_ms, stats = 0.0, None
     t0 = time.perf_counter()
     with ClockSampler(local) as clk:
         for _ in range(args.steps):
-            ids, st = eng.generate(prompt, N_GEN, mtp=mtp)
+            ids, st = eng.generate(prompt, n_gen, mtp=mtp)
             gen_ms += st["gen_ms"]
             stats = st
         barrier(pg, dev)
     wall_s = time.perf_counter() - t0
     gen_ms = max_over_ranks(gen_ms, pg, dev)
     wall_s = max_over_ranks(wall_s, pg, dev)
-    tokens = N_GEN * args.steps * world
+    tokens = n_gen * args.steps * world
     probe = eng.probe_gemv(ncols=2 if mtp else 1, iters=20)
     eng.close()
     peak, peak_kind = measured_peaks()
@@ -294,7 +295,7 @@ def run_decode(args, rank, world, local, pg):
         "scaling": "weak", "vs_baseline": None, "dtype": "q6_k x q8_1 int8 dp4a, fp32 accumulate, fp16 KV",
         "data": "synthetic (random-init weights, seeded prompt)",
         "config": {"workload": "config5-decode-mtp" if mtp else "config4-decode", "model": "qwen35-9b-shaped",
-                   "layers": "24 GDN + 8 GQA (+1 MTP block)", "n_prompt": N_PROMPT, "n_gen": N_GEN,
+                   "layers": "24 GDN + 8 GQA (+1 MTP block)", "n_prompt": N_PROMPT, "n_gen": n_gen,
                    "ctx": args.ctx, "parallelism": f"replicas x{world}",
                    "l2": "6.5 GB of weights per token > 126 MB L2"},
         "mtp": {"rounds": rounds, "accepted": stats["mtp_accepted"],
@@ -306,7 +307,7 @@ def run_decode(args, rank, world, local, pg):
                      "launches": probe["launches"], "avg_launch_us": round(per_launch_s * 1e6, 3)},
         "e2e": {"value": round(tokens / wall_s, 2), "unit": "tok/s",
                 "h2d_bytes_per_step": N_PROMPT * 4 + 32 * (N_PROMPT + 2),
-                "d2h_bytes_per_step": N_GEN * 4 + 4 * rounds + 96},
+                "d2h_bytes_per_step": n_gen * 4 + 4 * rounds + 96},
         "gpu_launches": launches_per_gen * args.steps,
         "clocks": clk.summary(),
     }
@@ -390,6 +391,7 @@ def main():
     ap.add_argument("--workload", default="decode", choices=["decode", "gemv"])
     ap.add_argument("--ctx", type=int, default=512, help="decode: KV capacity (512 or 65536)")
     ap.add_argument("--no-mtp", action="store_true", help="decode: plain greedy (config 4)")
+    ap.add_argument("--gen", type=int, default=N_GEN, help="decode: tokens per generation (400; fewer for profiling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.steps is None:
