@@ -2,14 +2,15 @@
 
 The product is librapier_b200.so (C-ABI in include/rapier_b200.h): hand-written CUDA kernels and the
 C++ decode engine. This package is the host-side mirror of the reference's operator surface (ops) and
-a thin wrapper over the engine (engine). Importing it loads the library and fails loudly if it is
-missing: there is no CPU fallback.
+a thin wrapper over the engine (engine). The library is loaded on first use; every entry point raises
+ImportError if it is missing: there is no CPU fallback.
 """
-from . import _lib
+from . import _lib, ops  # noqa: F401
 
-_lib.lib()
-
-from . import ops  # noqa: E402
-
-__all__ = ["ops"]
+__all__ = ["ops", "load"]
 __version__ = "0.1.0"
+
+
+def load():
+    """Load librapier_b200.so now (raises ImportError when it has not been built)."""
+    return _lib.lib()

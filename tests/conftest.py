@@ -26,7 +26,9 @@ def cuda():
     import torch
 
     assert torch.cuda.is_available(), "GPU test selected but no CUDA device is visible"
-    import rapier_b200  # noqa: F401  (fails loudly when the library is missing)
+    import rapier_b200
+
+    rapier_b200.load()  # fails loudly when the library is missing
 
     # the C-ABI requires an explicit stream (as the reference's native_mmvq does): run every test on one
     torch.cuda.set_stream(torch.cuda.Stream(device=0))
