@@ -223,12 +223,12 @@ typedef struct rk_gen_stats {
     int mtp_steps;     /* verify rounds */
     int mtp_accepted;  /* accepted drafts */
     int single_steps;  /* 1-token trunk passes inside the generation */
-    int graph_launches;
-    int kernels_per_single_step;
-    int kernels_per_round;
+    int graph_launches;          /* step-program runs enqueued (graph replays or persistent launches) */
+    int kernels_per_single_step; /* kernels one single-token program run launches (1 when persistent) */
+    int kernels_per_round;       /* kernels one MTP-round program run launches (1 when persistent) */
 } rk_gen_stats;
 
-/* Allocates the engine on `device`, generates the synthetic model and captures the step graphs.
+/* Allocates the engine on `device`, generates the synthetic model and builds the step programs.
  * Returns RK_ENOMEM when the device cannot hold it. */
 int rk_engine_create(const rk_model_config* cfg, int device, rk_engine** out);
 int rk_engine_destroy(rk_engine* e);
@@ -254,13 +254,21 @@ typedef struct rk_probe_result {
     double weight_bytes; /* Q6_K weight bytes streamed per replay */
     double algo_bytes;   /* weights + activation inputs + outputs (+ residual reads) per replay */
 } rk_probe_result;
-/* The reference's probe_gemv (src/qwythos.cpp:1621-1755): replays the GEMVs of one trunk step (every
- * layer's four projection groups and the lm_head, ncols columns, the same kernels and launch settings as
- * the decode graphs) back to back as one graph, `iters` times, timed with CUDA events. It overwrites the
- * engine's activation buffers (not the caches or states); call rk_engine_reset or generate afterwards. */
+/* The reference's probe_gemv (src/qwythos.cpp:1621-1755): runs the GEMVs of one trunk step (every
+ * layer's four projection groups and the lm_head, ncols columns) back to back through the engine's
+ * executor (one persistent launch, or one graph of GEMV launches), `iters` times, timed with CUDA events.
+ * It overwrites the engine's activation buffers (not the caches or states); call rk_engine_reset or
+ * generate afterwards. */
 int rk_engine_probe_gemv(rk_engine* e, int ncols, int iters, rk_probe_result* out);
 /* Device bytes the engine holds. */
 size_t rk_engine_device_bytes(const rk_engine* e);
+/* The executor the engine runs its step programs with: RK_ENGINE_PERSISTENT (one cooperative kernel per
+ * program, a whole generation in one launch; the default) or RK_ENGINE_GRAPH (one kernel per op, replayed
+ * from CUDA graphs; chosen by the environment variable RK_ENGINE_MODE=graph at rk_engine_create). Both
+ * produce the same bits. No reference counterpart (the reference replays a CUDA graph). */
+#define RK_ENGINE_GRAPH 0
+#define RK_ENGINE_PERSISTENT 1
+int rk_engine_mode(const rk_engine* e);
 
 #ifdef __cplusplus
 }

@@ -95,6 +95,7 @@ SIGNATURES = {
     "rk_engine_step": (i32, [vp, C.POINTER(C.c_int), i32, i32, vp, C.POINTER(C.c_int)]),
     "rk_engine_read_tensor": (sz, [vp, i32, vp, sz]),
     "rk_engine_device_bytes": (sz, [vp]),
+    "rk_engine_mode": (i32, [vp]),
     "rk_engine_probe_gemv": (i32, [vp, i32, i32, C.POINTER(ProbeResult)]),
 }
 

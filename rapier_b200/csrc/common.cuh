@@ -136,11 +136,13 @@ __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.lau
 
 // Device status word (one per translation unit; rk_device_status() ORs and clears them all):
 // bit 0 = an mbarrier wait gave up (a bulk copy did not land within the bound), bit 1 = a cluster
-// handshake gave up, bit 2 = an index a kernel was handed was out of range.
+// handshake gave up, bit 2 = an index a kernel was handed was out of range, bit 3 = a grid barrier of
+// the persistent decode kernel gave up.
 static __device__ unsigned int g_rk_status = 0;
 constexpr unsigned kStatusWaitTimeout = 1u;
 constexpr unsigned kStatusClusterTimeout = 2u;
 constexpr unsigned kStatusBadIndex = 4u;
+constexpr unsigned kStatusGridTimeout = 8u;
 typedef unsigned (*StatusReader)(bool clear);
 void register_status_reader(StatusReader r);
 namespace {

@@ -1,41 +1,33 @@
 // engine.cu — the decode engine for the qwen35 hybrid model: the reference's Engine / load_model /
 // forward_token / draft_predict / launch_token_verify (src/qwythos.cpp:152-281, :1228-1618, :1757-1824,
-// :1978-2134, :2905-3251) rebuilt around CUDA graphs and a device-side control block.
+// :1978-2134, :2905-3251) rebuilt around op programs and a device-side control block.
 //
-// Per token (1 column) or per MTP round (2 columns), every kernel reads its tokens, positions and the
-// rollback flag from a device Ctrl block, so a non-MTP generation is one graph replayed n times with no
-// host round trip, and an MTP round is one graph: 2-column verify -> accept -> 2-column draft.
+// Every step kind is an op program (decode_ops.cuh): one token; the trunk over 2 columns; an MTP round
+// (2-column verify -> accept -> 2-column draft -> next candidate); the first draft; the draft seed. Every
+// op reads its tokens, positions and the rollback flag from the device Ctrl block, so no step needs a
+// host round trip. Two executors (persistent.cuh) run a program: by default one persistent cooperative
+// kernel (a whole generation in one launch); with RK_ENGINE_MODE=graph one kernel per op, replayed from
+// a CUDA graph. Both write the same bits.
 //
-// Kernels per trunk layer (all with programmatic dependent launch; weights stream before the wait):
-//   GDN  : GEMV qkv||z||beta||alpha (RMSNorm+Q8_1 prologue) -> fused conv/L2/delta-rule/norm/Q8_1 ->
-//          GEMV ssm_out (+residual, partials) -> GEMV up||gate (RMSNorm prologue) -> GEMV down (SwiGLU+Q8_1
-//          prologue, +residual, partials)
-//   ATTN : GEMV q||k||v (RMSNorm prologue) -> split/q-k norm/RoPE/fp16 KV store -> flash-decode chunks ->
-//          combine -> GEMV wo (sigmoid-gate+Q8_1 prologue, +residual) -> FFN as above
+// Ops per trunk layer:
+//   GDN  : GEMV qkv||z||beta||alpha (RMSNorm+Q8_1 prologue) -> GDN (conv / L2 / delta rule / gated norm /
+//          Q8_1) -> GEMV ssm_out (+residual, partials) -> GEMV up||gate (RMSNorm prologue, SwiGLU+Q8_1
+//          epilogue) -> GEMV down (+residual, partials)
+//   ATTN : GEMV q||k||v (RMSNorm prologue) -> attention chunks (q/k norm, RoPE and the fp16 KV store
+//          folded in) -> combine (sigmoid gate + Q8_1) -> GEMV wo (+residual) -> FFN as above
 // then the lm_head GEMV with the final RMSNorm prologue and a fused argmax epilogue.
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <new>
 #include <vector>
 
-#include "mmvq.cuh"
+#include "persistent.cuh"
 
 namespace rk {
-
-cudaError_t gdn_fused_launch(const float* proj, int proj_stride, float* ring, const float* conv_w, const float* dt_bias,
-                             const float* ssm_a, const float* gamma, float* state, float* snap, const int* rollback,
-                             float* y, uint8_t* q8, int h_k, int h_v, int ncols, const int* pos, float eps,
-                             cudaStream_t s, bool pdl);
-cudaError_t gqa_launch(const float* q, const __half* kc, const __half* vc, float* o, int n_head, int n_kv, int ncols,
-                       const int* pos, int max_ctx, float scale, float* scratch, cudaStream_t s, bool pdl,
-                       const float* gate, uint8_t* q8);
-size_t gqa_scratch_bytes(int n_head, int ncols, int max_ctx);
-
 namespace {
 
-constexpr int kHd = 256;     // attention head dim
-constexpr int kS = 128;      // GDN head size
 constexpr float kAttnScale = 0.0625f;  // 1/sqrt(256)
 
 // ------------------------------------------------------------------------------------------------
@@ -106,230 +98,6 @@ __global__ void gen_q6k_kernel(uint64_t seed, float scale, long long n_blocks, u
 }
 
 // ------------------------------------------------------------------------------------------------
-// Device control block.
-// ------------------------------------------------------------------------------------------------
-struct Ctrl {
-    int pos;       // trunk position of column 0
-    int tok[2];    // trunk input tokens (tok[1] = the draft candidate in a verify round)
-    int dpos;      // draft position of column 0
-    int dtok[2];   // draft input tokens
-    int rollback;  // GDN state from the snapshot (the previous verify's draft was rejected)
-    int accept;    // the last round accepted its draft
-    int n_emitted;
-    int steps, accepted, singles;
-    int bad;       // a token id outside the vocabulary reached a kernel
-    int pad[3];
-    unsigned long long amax[2];   // trunk argmax keys per column
-    unsigned long long damax[2];  // draft argmax keys per column
-};
-constexpr int kCtrlHostFields = 8;  // pos, tok[2], dpos, dtok[2], rollback, accept: written by the host
-
-// ---- token embedding row (GGUF Q6_K, kept on the device) -> x, partials ----
-// dequantize_row_q6_K: y = (d * scale) * (code - 32). Thread t owns 16-value sub-blocks t, t+256, ...
-template <int NC>
-__global__ void __launch_bounds__(256) embed_kernel(const uint8_t* __restrict__ emb, int H, int V, Ctrl* ctrl,
-                                                    int draft, float* __restrict__ x, float* __restrict__ xp) {
-    pdl_trigger();
-    pdl_wait();
-    const int c = blockIdx.x;
-    int tok = draft ? ctrl->dtok[c] : ctrl->tok[c];
-    if (tok < 0 || tok >= V) {
-        if (threadIdx.x == 0) {
-            atomicOr(&g_rk_status, kStatusBadIndex);
-            ctrl->bad = 1;
-        }
-        tok = 0;
-    }
-    if (!draft && c == 0 && threadIdx.x == 0) {
-        ctrl->amax[0] = 0ull;
-        ctrl->amax[1] = 0ull;
-    }
-    const size_t rb = (size_t) (H / 256) * 210;
-    const uint8_t* row = emb + (size_t) tok * rb;
-    for (int sub = threadIdx.x; sub < H / 16; sub += 256) {
-        const uint8_t* blk = row + (size_t) (sub >> 4) * 210;
-        const float d = __half2float(*reinterpret_cast<const __half*>(blk + 208));
-        const float ds = __fmul_rn(d, (float) (int8_t) blk[192 + (sub & 15)]);
-        float part[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-            const int v = ((sub & 15) << 4) + i;
-            const int h = v >> 7, vv = v & 127, j = vv >> 5, l = vv & 31;
-            const uint8_t qlb = blk[64 * h + l + 32 * (j & 1)];
-            const int code = ((j >> 1) ? (qlb >> 4) : (qlb & 15)) | (((blk[128 + 32 * h + l] >> (2 * j)) & 3) << 4);
-            const float y = __fmul_rn(ds, (float) (code - 32));
-            x[(size_t) c * H + sub * 16 + i] = y;
-            part[i >> 2] = __fmaf_rn(y, y, part[i >> 2]);
-        }
-#pragma unroll
-        for (int k = 0; k < 4; ++k) xp[(size_t) c * (H / 4) + sub * 4 + k] = part[k];
-    }
-}
-
-// ---- attention prologue: split q/gate, per-head RMSNorm, RoPE, fp16 KV store ----
-// q3 column layout: [n_head x (q 256 | gate 256)] [k n_kv x 256] [v n_kv x 256]. Grid (n_head + n_kv, NC).
-__device__ __forceinline__ float block256_sumsq(float v, float* red) {
-    float part = warp_sum(__fmul_rn(v, v));
-    __syncthreads();
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = part;
-    __syncthreads();
-    float ss = red[0];
-#pragma unroll
-    for (int w = 1; w < 8; ++w) ss = __fadd_rn(ss, red[w]);
-    return ss;
-}
-template <int NC>
-__global__ void __launch_bounds__(256) attn_prep_kernel(const float* __restrict__ q3, int q3_stride,
-                                                        const float* __restrict__ qn_w, const float* __restrict__ kn_w,
-                                                        const float* __restrict__ rope, int n_rot, const int* posp,
-                                                        int n_head, int n_kv, int max_ctx, float eps,
-                                                        float* __restrict__ q_out, float* __restrict__ gate_out,
-                                                        __half* __restrict__ kc, __half* __restrict__ vc) {
-    __shared__ float red[8];
-    __shared__ float rot[kHd];
-    pdl_trigger();
-    pdl_wait();
-    const int h = blockIdx.x, c = blockIdx.y, d = threadIdx.x;
-    const int pos = *posp + c;
-    const float* col = q3 + (size_t) c * q3_stride;
-    const bool is_q = h < n_head;
-    const int kvh = h - n_head;
-    float x = is_q ? col[h * 2 * kHd + d] : col[n_head * 2 * kHd + kvh * kHd + d];
-    if (is_q) gate_out[(size_t) c * n_head * kHd + h * kHd + d] = col[h * 2 * kHd + kHd + d];
-    const float ss = block256_sumsq(x, red);
-    const float inv = rsqrtf(__fadd_rn(__fdiv_rn(ss, (float) kHd), eps));
-    x = __fmul_rn(__fmul_rn(x, inv), is_q ? qn_w[d] : kn_w[d]);
-    const bool pos_ok = pos >= 0 && pos < max_ctx;
-    if (!pos_ok && d == 0 && h == 0) atomicOr(&g_rk_status, kStatusBadIndex);
-    rot[d] = x;
-    __syncthreads();
-    const int half = n_rot / 2;
-    if (d < n_rot && pos_ok) {
-        const int i = d < half ? d : d - half;
-        const float cs = rope[((size_t) pos * half + i) * 2 + 0], sn = rope[((size_t) pos * half + i) * 2 + 1];
-        const float x0 = rot[i], x1 = rot[i + half];
-        x = d < half ? __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn)) : __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
-    }
-    if (is_q) {
-        q_out[((size_t) c * n_head + h) * kHd + d] = x;
-    } else if (pos_ok) {
-        const size_t dst = ((size_t) kvh * max_ctx + pos) * kHd + d;
-        kc[dst] = __float2half_rn(x);
-        vc[dst] = __float2half_rn(col[n_head * 2 * kHd + n_kv * kHd + kvh * kHd + d]);
-    }
-}
-
-// ---- MTP draft input: Q8_1 of [enorm(emb(dtok)) | hnorm(h)] (src/qwythos.cpp:1316-1334) ----
-// Grid NC, 256 threads, dynamic smem H floats + H/4 partials.
-template <int NC>
-__global__ void __launch_bounds__(256) draft_prep_kernel(const uint8_t* __restrict__ emb, int H, int V, Ctrl* ctrl,
-                                                         const float* __restrict__ enorm, const float* __restrict__ hnorm,
-                                                         const float* __restrict__ hsave, const float* __restrict__ hsave_p,
-                                                         float eps, uint8_t* __restrict__ eh_q8) {
-    extern __shared__ float sm[];
-    float* e = sm;
-    float* ep = sm + H;
-    __shared__ float red[8];
-    pdl_trigger();
-    pdl_wait();
-    const int c = blockIdx.x;
-    if (c == 0 && threadIdx.x == 0) {
-        ctrl->damax[0] = 0ull;
-        ctrl->damax[1] = 0ull;
-    }
-    int tok = ctrl->dtok[c];
-    if (tok < 0 || tok >= V) {
-        if (threadIdx.x == 0) {
-            atomicOr(&g_rk_status, kStatusBadIndex);
-            ctrl->bad = 1;
-        }
-        tok = 0;
-    }
-    const size_t rb = (size_t) (H / 256) * 210;
-    const uint8_t* row = emb + (size_t) tok * rb;
-    for (int sub = threadIdx.x; sub < H / 16; sub += 256) {
-        const uint8_t* blk = row + (size_t) (sub >> 4) * 210;
-        const float d = __half2float(*reinterpret_cast<const __half*>(blk + 208));
-        const float ds = __fmul_rn(d, (float) (int8_t) blk[192 + (sub & 15)]);
-        float part[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-            const int v = ((sub & 15) << 4) + i;
-            const int h = v >> 7, vv = v & 127, j = vv >> 5, l = vv & 31;
-            const uint8_t qlb = blk[64 * h + l + 32 * (j & 1)];
-            const int code = ((j >> 1) ? (qlb >> 4) : (qlb & 15)) | (((blk[128 + 32 * h + l] >> (2 * j)) & 3) << 4);
-            const float y = __fmul_rn(ds, (float) (code - 32));
-            e[sub * 16 + i] = y;
-            part[i >> 2] = __fmaf_rn(y, y, part[i >> 2]);
-        }
-#pragma unroll
-        for (int k = 0; k < 4; ++k) ep[sub * 4 + k] = part[k];
-    }
-    __syncthreads();
-    const float inv_e = rms_inv(block256_partials_sum(ep, H / 4, red), H, eps);
-    const float inv_h = rms_inv(block256_partials_sum(hsave_p + (size_t) c * (H / 4), H / 4, red), H, eps);
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const float* hc = hsave + (size_t) c * H;
-    uint8_t* out = eh_q8 + (size_t) c * (2 * H / 32) * 36;
-    for (int blk = warp; blk < 2 * H / 32; blk += 8) {
-        const int i = blk * 32 + lane;
-        const float v = i < H ? rms_value(e[i], enorm[i], inv_e) : rms_value(hc[i - H], hnorm[i - H], inv_h);
-        q8_1_warp_store(v, out + (size_t) blk * 36, lane);
-    }
-}
-
-// ---- control kernels (one thread) ----
-__global__ void single_finish_kernel(Ctrl* ctrl, int* __restrict__ out, int max_out) {
-    pdl_trigger();
-    pdl_wait();
-    const int id = argmax_key_row(ctrl->amax[0]);
-    if (ctrl->n_emitted < max_out) out[ctrl->n_emitted] = id;
-    ctrl->n_emitted += 1;
-    ctrl->tok[0] = id;
-    ctrl->dtok[0] = id;
-    ctrl->dpos = ctrl->pos + 1;
-    ctrl->pos += 1;
-    ctrl->rollback = 0;
-    ctrl->singles += 1;
-}
-// Greedy acceptance (src/qwythos.cpp:3196-3238): c0 = argmax of column 0; accepted iff c0 == the
-// candidate; then emit c0 (and c1 when accepted); the draft runs on (c0 at pos+1, c1 at pos+2).
-__global__ void accept_kernel(Ctrl* ctrl, int* __restrict__ out, int max_out) {
-    pdl_trigger();
-    pdl_wait();
-    const int c0 = argmax_key_row(ctrl->amax[0]), c1 = argmax_key_row(ctrl->amax[1]);
-    const int acc = c0 == ctrl->tok[1];
-    int n = ctrl->n_emitted;
-    if (n < max_out) out[n] = c0;
-    ++n;
-    if (acc) {
-        if (n < max_out) out[n] = c1;
-        ++n;
-    }
-    ctrl->n_emitted = n;
-    ctrl->dtok[0] = c0;
-    ctrl->dtok[1] = c1;
-    ctrl->dpos = ctrl->pos + 1;
-    ctrl->tok[0] = acc ? c1 : c0;
-    ctrl->pos += 1 + acc;
-    ctrl->rollback = !acc;
-    ctrl->accept = acc;
-    ctrl->steps += 1;
-    ctrl->accepted += acc;
-}
-// The next candidate: the draft column that predicts the position after the last emitted token.
-__global__ void round_finish_kernel(Ctrl* ctrl) {
-    pdl_trigger();
-    pdl_wait();
-    ctrl->tok[1] = argmax_key_row(ctrl->damax[ctrl->accept ? 1 : 0]);
-}
-__global__ void draft1_finish_kernel(Ctrl* ctrl) {
-    pdl_trigger();
-    pdl_wait();
-    ctrl->tok[1] = argmax_key_row(ctrl->damax[0]);
-}
-
-// ------------------------------------------------------------------------------------------------
 // Engine
 // ------------------------------------------------------------------------------------------------
 struct Mat {
@@ -370,6 +138,23 @@ struct TensorRec {
     bool raw;         // stored as GGUF rows (token embedding)
 };
 
+// A step program: its ops on the host and the device, its column count, and its graph (graph mode).
+struct Program {
+    std::vector<POp> ops;
+    POp* dev = nullptr;
+    int nc = 1;
+    cudaGraphExec_t graph = nullptr;
+    int kernels = 0;  // kernels one run launches
+};
+enum : int { P_SINGLE = 0, P_TRUNK2, P_ROUND, P_DRAFT1, P_SEED, P_PROBE1, P_PROBE2, P_COUNT };
+
+POp make_op(int kind) {
+    POp op;
+    std::memset(&op, 0, sizeof op);
+    op.kind = kind;
+    return op;
+}
+
 }  // namespace
 
 struct EngineImpl {
@@ -377,7 +162,7 @@ struct EngineImpl {
     int dev = 0;
     cudaStream_t s = nullptr;
     int H = 0, FF = 0, V = 0, hk = 0, hv = 0, nh = 0, nkv = 0;
-    int qkvzab_rows = 0, qkv3_rows = 0, max_in_rows = 0;
+    int qkvzab_rows = 0, qkv3_rows = 0, max_in_rows = 0, max_chunks = 0;
     std::vector<Layer> layers;
     Layer draft;
     float *enorm = nullptr, *hnorm = nullptr, *shnorm = nullptr, *out_norm = nullptr;
@@ -385,11 +170,13 @@ struct EngineImpl {
     uint8_t* tok_embd = nullptr;
     float* rope = nullptr;
     // activations, 2 columns
-    float *x = nullptr, *xp = nullptr, *proj = nullptr, *gdn_y = nullptr, *ug = nullptr;
-    uint8_t* q8 = nullptr;
-    float *q_attn = nullptr, *g_attn = nullptr, *o_attn = nullptr, *attn_scratch = nullptr;
-    uint8_t *q8_ff = nullptr, *q8_attn = nullptr;  // Q8_1 inputs of the down and wo GEMVs
-    unsigned* swiglu_cnt = nullptr;                // last-arriver counters of the up||gate epilogue
+    float *x = nullptr, *xp = nullptr, *proj = nullptr, *ug = nullptr;
+    uint8_t* q8 = nullptr;                        // Q8_1 input of ssm_out (the GDN output)
+    float *gdn_o = nullptr, *gdn_ss = nullptr;    // GDN read-outs / per-quarter sums of squares
+    unsigned* gdn_cnt = nullptr;                  // GDN last-quarter counters
+    float* attn_scratch = nullptr;                // flash-decode partials
+    uint8_t *q8_ff = nullptr, *q8_attn = nullptr; // Q8_1 inputs of the down and wo GEMVs
+    unsigned* swiglu_cnt = nullptr;               // last-arriver counters of the up||gate epilogue
     float *hsave = nullptr, *hsave_p = nullptr, *logits = nullptr;
     float *dx = nullptr, *dxp = nullptr;
     uint8_t* eh_q8 = nullptr;
@@ -398,15 +185,17 @@ struct EngineImpl {
     int max_out = 0;
     Ctrl* ctrl_stage = nullptr;  // pinned host staging, one slot per queued host write
     int stage_slots = 0, stage_next = 0;
-    cudaGraphExec_t g_single = nullptr, g_round = nullptr, g_trunk2 = nullptr, g_draft1 = nullptr, g_draft1_seed = nullptr;
-    cudaGraphExec_t g_probe[2] = {nullptr, nullptr};
-    double probe_weight_bytes = 0, probe_algo_bytes = 0;
-    int probe_launches = 0;
-    int kernels_single = 0, kernels_round = 0;
+    // programs and executors
+    Program progs[P_COUNT];
+    bool persistent = false;
+    PSync* psync = nullptr;
+    int p_grid = 0, p_stages = 0, p_region = 0;
+    size_t p_smem = 0;
+    double probe_weight_bytes[2] = {0, 0}, probe_algo_bytes[2] = {0, 0};
+    int probe_gemvs = 0;
     std::vector<void*> allocs;
     std::vector<TensorRec> tensors;
     size_t bytes = 0;
-    int launches = 0;  // kernels enqueued by the current capture
     cudaError_t err = cudaSuccess;
 
     ~EngineImpl();
@@ -424,33 +213,29 @@ struct EngineImpl {
     int build();
     void gen_f32(int tid, float* dst, size_t n, double std, double mean, int kind);
     void gen_q6k_into(int tid, Mat& group, int row_off, int n_in, int n_out, uint8_t* scratch);
-    // launch helpers
-    void ok(cudaError_t e) {
-        if (e != cudaSuccess && err == cudaSuccess) err = e;
-        ++launches;
-    }
+    // programs
+    MmvqParams rms_params(const Mat& m, const float* x_, const float* w, const float* part, float* y, int y_stride);
+    MmvqParams q8_params(const Mat& m, const uint8_t* xq, float* y, const float* res, float* part);
+    void add_gemv(std::vector<POp>& v, int pro, int epi, const MmvqParams& p);
+    void add_ffn(std::vector<POp>& v, const Layer& L, float* xres, float* part);
+    POp attn_op(int kind, const Layer& L, int draft_flag);
+    void add_trunk(std::vector<POp>& v);
+    void add_draft(std::vector<POp>& v, bool head);
+    void add_ctrl(std::vector<POp>& v, int kind);
+    void add_probe(std::vector<POp>& v, int nc);
+    int setup_executor();
+    int finalize(Program& P, int nc);
     template <int NC>
-    void trunk(bool pdl);
-    template <int NC>
-    void draft_pass(bool with_head, bool pdl);
-    template <int NC, int EPI>
-    void gemv_rms(const Mat& m, const float* x_, const float* w, const float* part, float* y, int y_stride, bool pdl,
-                  float* xn_out = nullptr, float* xn_part = nullptr, unsigned long long* amax = nullptr);
-    template <int NC>
-    void gemv_q8_res(const Mat& m, const uint8_t* xq, float* xres, float* part, bool pdl);
-    template <int NC>
-    void ffn(const Layer& L, float* xres, float* part, bool pdl);
-    template <int NC>
-    void probe_body();
+    cudaError_t launch_op(const POp& op);
+    cudaError_t run(const Program& P, int until = 0, int max_iters = 1);
     void set_ctrl(const Ctrl& host_fields);
-    int capture(cudaGraphExec_t* exec, int* nk, void (*body)(EngineImpl*));
+    int check_abort(const char* what);
 };
 
 EngineImpl::~EngineImpl() {
     if (s) cudaStreamSynchronize(s);
-    cudaGraphExec_t gs[] = {g_single, g_round, g_trunk2, g_draft1, g_draft1_seed, g_probe[0], g_probe[1]};
-    for (cudaGraphExec_t g : gs)
-        if (g) cudaGraphExecDestroy(g);
+    for (Program& P : progs)
+        if (P.graph) cudaGraphExecDestroy(P.graph);
     for (void* p : allocs) cudaFree(p);
     if (ctrl_stage) cudaFreeHost(ctrl_stage);
     if (s) cudaStreamDestroy(s);
@@ -489,9 +274,10 @@ void EngineImpl::gen_q6k_into(int tid, Mat& group, int row_off, int n_in, int n_
 int EngineImpl::build() {
     const rk_model_config& c = cfg;
     H = c.n_embd, FF = c.n_ff, V = c.n_vocab, hk = c.ssm_h_k, hv = c.ssm_h_v, nh = c.n_head, nkv = c.n_head_kv;
-    qkvzab_rows = 2 * hk * kS + 2 * hv * kS + 2 * hv;
-    qkv3_rows = 2 * nh * kHd + 2 * nkv * kHd;
+    qkvzab_rows = 2 * hk * kSsm + 2 * hv * kSsm + 2 * hv;
+    qkv3_rows = 2 * nh * kHdA + 2 * nkv * kHdA;
     max_in_rows = qkvzab_rows > qkv3_rows ? qkvzab_rows : qkv3_rows;
+    max_chunks = (c.max_ctx + kChunkA - 1) / kChunkA;
     max_out = c.max_ctx;
     if ((err = cudaSetDevice(dev)) != cudaSuccess) return RK_ECUDA;
     if ((err = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking)) != cudaSuccess) return RK_ECUDA;
@@ -541,37 +327,37 @@ int EngineImpl::build() {
         if (L.gdn) {
             L.in_proj = mat(H, qkvzab_rows);
             if (L.in_proj.w) {
-                gen_q6k_into(layer_tid(il, L_GDN_QKV), L.in_proj, 0, H, 2 * hk * kS + hv * kS, scratch);
-                gen_q6k_into(layer_tid(il, L_GDN_Z), L.in_proj, 2 * hk * kS + hv * kS, H, hv * kS, scratch);
-                gen_q6k_into(layer_tid(il, L_GDN_BETA), L.in_proj, 2 * hk * kS + 2 * hv * kS, H, hv, scratch);
-                gen_q6k_into(layer_tid(il, L_GDN_ALPHA), L.in_proj, 2 * hk * kS + 2 * hv * kS + hv, H, hv, scratch);
+                gen_q6k_into(layer_tid(il, L_GDN_QKV), L.in_proj, 0, H, 2 * hk * kSsm + hv * kSsm, scratch);
+                gen_q6k_into(layer_tid(il, L_GDN_Z), L.in_proj, 2 * hk * kSsm + hv * kSsm, H, hv * kSsm, scratch);
+                gen_q6k_into(layer_tid(il, L_GDN_BETA), L.in_proj, 2 * hk * kSsm + 2 * hv * kSsm, H, hv, scratch);
+                gen_q6k_into(layer_tid(il, L_GDN_ALPHA), L.in_proj, 2 * hk * kSsm + 2 * hv * kSsm + hv, H, hv, scratch);
             }
-            L.out_proj = mat(hv * kS, H);
-            if (L.out_proj.w) gen_q6k_into(layer_tid(il, L_GDN_OUT), L.out_proj, 0, hv * kS, H, scratch);
-            const int C = 2 * hk * kS + hv * kS;
+            L.out_proj = mat(hv * kSsm, H);
+            if (L.out_proj.w) gen_q6k_into(layer_tid(il, L_GDN_OUT), L.out_proj, 0, hv * kSsm, H, scratch);
+            const int C = 2 * hk * kSsm + hv * kSsm;
             L.conv_w = alloc<float>((size_t) C * 4);
             if (L.conv_w) gen_f32(layer_tid(il, L_GDN_CONV), L.conv_w, (size_t) C * 4, 0.3, 0.0, 0);
             L.ssm_a = alloc<float>(hv);
             if (L.ssm_a) gen_f32(layer_tid(il, L_GDN_A), L.ssm_a, hv, 0.5, 0.0, 1);
             L.dt = alloc<float>(hv);
             if (L.dt) gen_f32(layer_tid(il, L_GDN_DT), L.dt, hv, 0.5, 0.0, 0);
-            L.ssm_norm = norm(layer_tid(il, L_GDN_NORM), kS);
-            L.state = alloc<float>((size_t) kS * hv * kS);
-            L.snap = alloc<float>((size_t) kS * hv * kS);
-            L.ring = alloc<float>((size_t) C * 4);
+            L.ssm_norm = norm(layer_tid(il, L_GDN_NORM), kSsm);
+            L.state = alloc<float>((size_t) kSsm * hv * kSsm);
+            L.snap = alloc<float>((size_t) kSsm * hv * kSsm);
+            L.ring = alloc<float>((size_t) C * kRingSlots);
         } else {
             L.in_proj = mat(H, qkv3_rows);
             if (L.in_proj.w) {
-                gen_q6k_into(layer_tid(il, L_ATT_Q), L.in_proj, 0, H, 2 * nh * kHd, scratch);
-                gen_q6k_into(layer_tid(il, L_ATT_K), L.in_proj, 2 * nh * kHd, H, nkv * kHd, scratch);
-                gen_q6k_into(layer_tid(il, L_ATT_V), L.in_proj, 2 * nh * kHd + nkv * kHd, H, nkv * kHd, scratch);
+                gen_q6k_into(layer_tid(il, L_ATT_Q), L.in_proj, 0, H, 2 * nh * kHdA, scratch);
+                gen_q6k_into(layer_tid(il, L_ATT_K), L.in_proj, 2 * nh * kHdA, H, nkv * kHdA, scratch);
+                gen_q6k_into(layer_tid(il, L_ATT_V), L.in_proj, 2 * nh * kHdA + nkv * kHdA, H, nkv * kHdA, scratch);
             }
-            L.out_proj = mat(nh * kHd, H);
-            if (L.out_proj.w) gen_q6k_into(layer_tid(il, L_ATT_O), L.out_proj, 0, nh * kHd, H, scratch);
-            L.q_norm = norm(layer_tid(il, L_ATT_QN), kHd);
-            L.k_norm = norm(layer_tid(il, L_ATT_KN), kHd);
-            L.kc = alloc<__half>((size_t) nkv * c.max_ctx * kHd);
-            L.vc = alloc<__half>((size_t) nkv * c.max_ctx * kHd);
+            L.out_proj = mat(nh * kHdA, H);
+            if (L.out_proj.w) gen_q6k_into(layer_tid(il, L_ATT_O), L.out_proj, 0, nh * kHdA, H, scratch);
+            L.q_norm = norm(layer_tid(il, L_ATT_QN), kHdA);
+            L.k_norm = norm(layer_tid(il, L_ATT_KN), kHdA);
+            L.kc = alloc<__half>((size_t) nkv * c.max_ctx * kHdA);
+            L.vc = alloc<__half>((size_t) nkv * c.max_ctx * kHdA);
         }
     }
     if (c.has_mtp && err == cudaSuccess) {
@@ -594,21 +380,22 @@ int EngineImpl::build() {
                 t[((size_t) p * half + i) * 2 + 1] = (float) std::sin(a);
             }
         rope = alloc<float>(t.size());
-        if (rope && err == cudaSuccess) err = cudaMemcpy(rope, t.data(), t.size() * sizeof(float), cudaMemcpyHostToDevice);
+        if (rope && err == cudaSuccess)
+            err = cudaMemcpyAsync(rope, t.data(), t.size() * sizeof(float), cudaMemcpyHostToDevice, s);
+        if (err == cudaSuccess) err = cudaStreamSynchronize(s);
     }
     // activations (2 columns)
     x = alloc<float>(2 * (size_t) H);
     xp = alloc<float>(2 * (size_t) H / 4);
     proj = alloc<float>(2 * (size_t) max_in_rows);
-    gdn_y = alloc<float>(2 * (size_t) hv * kS);
     ug = alloc<float>(2 * 2 * (size_t) FF);
-    q8 = alloc<uint8_t>(2 * rk_q8_1_bytes(FF > 2 * H ? FF : 2 * H, 1));
-    q_attn = alloc<float>(2 * (size_t) nh * kHd);
-    g_attn = alloc<float>(2 * (size_t) nh * kHd);
-    o_attn = alloc<float>(2 * (size_t) nh * kHd);
-    attn_scratch = alloc<float>(gqa_scratch_bytes(nh, 2, c.max_ctx) / sizeof(float));
+    q8 = alloc<uint8_t>(2 * rk_q8_1_bytes(hv * kSsm, 1));
+    gdn_o = alloc<float>(2 * (size_t) hv * kSsm);
+    gdn_ss = alloc<float>(2 * (size_t) hv * 4);
+    gdn_cnt = alloc<unsigned>((size_t) hv);
+    attn_scratch = alloc<float>((size_t) nh * 2 * max_chunks * (kHdA + 2));
     q8_ff = alloc<uint8_t>(2 * rk_q8_1_bytes(FF, 1));
-    q8_attn = alloc<uint8_t>(2 * rk_q8_1_bytes(nh * kHd, 1));
+    q8_attn = alloc<uint8_t>(2 * rk_q8_1_bytes(nh * kHdA, 1));
     swiglu_cnt = alloc<unsigned>((size_t) FF / 32);
     hsave = alloc<float>(2 * (size_t) H);
     hsave_p = alloc<float>(2 * (size_t) H / 4);
@@ -618,6 +405,7 @@ int EngineImpl::build() {
     eh_q8 = alloc<uint8_t>(2 * rk_q8_1_bytes(2 * H, 1));
     ctrl = alloc<Ctrl>(1);
     out = alloc<int>((size_t) max_out);
+    psync = alloc<PSync>(1);
     stage_slots = 4096;  // plus one slot after them for the emitted-count readback
     if (err == cudaSuccess) err = cudaMallocHost(&ctrl_stage, sizeof(Ctrl) * (stage_slots + 1));
     if (err == cudaSuccess) err = cudaStreamSynchronize(s);
@@ -626,11 +414,10 @@ int EngineImpl::build() {
 }
 
 // ---------------------------------------------------------------------------------------------------
-// launch sequence
+// Step programs
 // ---------------------------------------------------------------------------------------------------
-template <int NC, int EPI>
-void EngineImpl::gemv_rms(const Mat& m, const float* x_, const float* w, const float* part, float* y, int y_stride,
-                          bool pdl, float* xn_out, float* xn_part, unsigned long long* amax) {
+MmvqParams EngineImpl::rms_params(const Mat& m, const float* x_, const float* w, const float* part, float* y,
+                                  int y_stride) {
     MmvqParams p = {};
     p.w = m.w;
     p.n_in = m.n_in;
@@ -642,140 +429,303 @@ void EngineImpl::gemv_rms(const Mat& m, const float* x_, const float* w, const f
     p.eps = cfg.eps;
     p.y = y;
     p.y_stride = y_stride;
-    p.xn_out = xn_out;
-    p.xn_part = xn_part;
-    p.amax = amax;
     p.q8out = q8_ff;
     p.cnt = swiglu_cnt;
-    ok(mmvq_launch<RK_TYPE_Q6_K, NC, PRO_RMS, EPI>(p, s, pdl));
+    return p;
 }
 
-// xres = W . xq + xres (in place) with the 4-row partials (the reference's residual epilogue).
-template <int NC>
-void EngineImpl::gemv_q8_res(const Mat& m, const uint8_t* xq, float* xres, float* part, bool pdl) {
+// y = W . xq (+ res) with the 4-row partials (the reference's residual epilogue; y == res in place).
+MmvqParams EngineImpl::q8_params(const Mat& m, const uint8_t* xq, float* y, const float* res, float* part) {
     MmvqParams p = {};
     p.w = m.w;
     p.n_in = m.n_in;
     p.n_out = m.n_out;
     p.prefetch_before_wait = 1;
     p.xq = xq;
-    p.y = xres;
+    p.y = y;
     p.y_stride = m.n_out;
-    p.res = xres;
+    p.res = res;
     p.res_stride = m.n_out;
     p.pout = part;
     p.pout_stride = m.n_out / 4;
-    ok(mmvq_launch<RK_TYPE_Q6_K, NC, PRO_Q8, EPI_RES>(p, s, pdl));
+    return p;
+}
+
+void EngineImpl::add_gemv(std::vector<POp>& v, int pro, int epi, const MmvqParams& p) {
+    POp op = make_op(POP_GEMV);
+    op.pro = pro;
+    op.epi = epi;
+    op.g = p;
+    v.push_back(op);
 }
 
 // FFN (src/qwythos.cpp:1011-1042): RMSNorm(post_norm)+Q8_1 -> up||gate with the SwiGLU+Q8_1 epilogue ->
 // down + residual.
-template <int NC>
-void EngineImpl::ffn(const Layer& L, float* xres, float* part, bool pdl) {
-    gemv_rms<NC, EPI_SWIGLU>(L.upgate, xres, L.post_norm, part, ug, 2 * FF, pdl);
-    gemv_q8_res<NC>(L.down, q8_ff, xres, part, pdl);
+void EngineImpl::add_ffn(std::vector<POp>& v, const Layer& L, float* xres, float* part) {
+    add_gemv(v, PRO_RMS, EPI_SWIGLU, rms_params(L.upgate, xres, L.post_norm, part, ug, 2 * FF));
+    add_gemv(v, PRO_Q8, EPI_RES, q8_params(L.down, q8_ff, xres, xres, part));
 }
 
-template <int NC>
-void EngineImpl::trunk(bool pdl) {
-    const int draft_flag = 0;
-    ok(launch_pdl(embed_kernel<NC>, dim3(NC), dim3(256), 0, s, pdl, (const uint8_t*) tok_embd, H, V, ctrl, draft_flag,
-                  x, xp));
-    const size_t q8col = rk_q8_1_bytes(hv * kS, 1);
+POp EngineImpl::attn_op(int kind, const Layer& L, int draft_flag) {
+    POp op = make_op(kind);
+    op.draft = draft_flag;
+    AttnArgs& a = op.at;
+    a.proj = proj;
+    a.proj_stride = L.in_proj.n_out;
+    a.qn = L.q_norm;
+    a.kn = L.k_norm;
+    a.rope = rope;
+    a.n_rot = cfg.n_rot;
+    a.n_head = nh;
+    a.n_kv = nkv;
+    a.max_ctx = cfg.max_ctx;
+    a.max_chunks = max_chunks;
+    a.eps = cfg.eps;
+    a.scale = kAttnScale;
+    a.kc = L.kc;
+    a.vc = L.vc;
+    a.part_o = attn_scratch;
+    a.part_ml = attn_scratch + (size_t) nh * 2 * max_chunks * kHdA;
+    a.o = nullptr;
+    a.q8 = q8_attn;
+    return op;
+}
+
+void EngineImpl::add_trunk(std::vector<POp>& v) {
+    POp e = make_op(POP_EMBED);
+    e.em.emb = tok_embd;
+    e.em.H = H;
+    e.em.V = V;
+    e.em.x = x;
+    e.em.xp = xp;
+    v.push_back(e);
     for (const Layer& L : layers) {
-        gemv_rms<NC, EPI_STORE>(L.in_proj, x, L.attn_norm, xp, proj, L.in_proj.n_out, pdl);
+        add_gemv(v, PRO_RMS, EPI_STORE, rms_params(L.in_proj, x, L.attn_norm, xp, proj, L.in_proj.n_out));
         if (L.gdn) {
-            ok(gdn_fused_launch(proj, L.in_proj.n_out, L.ring, L.conv_w, L.dt, L.ssm_a, L.ssm_norm, L.state, L.snap,
-                                &ctrl->rollback, gdn_y, q8, hk, hv, NC, &ctrl->pos, cfg.eps, s, pdl));
-            (void) q8col;
-            gemv_q8_res<NC>(L.out_proj, q8, x, xp, pdl);
+            POp g = make_op(POP_GDN);
+            GdnArgs& a = g.gd;
+            a.proj = proj;
+            a.proj_stride = L.in_proj.n_out;
+            a.ring = L.ring;
+            a.conv_w = L.conv_w;
+            a.dt = L.dt;
+            a.ssm_a = L.ssm_a;
+            a.gamma = L.ssm_norm;
+            a.state = L.state;
+            a.snap = L.snap;
+            a.o_scr = gdn_o;
+            a.ss_scr = gdn_ss;
+            a.cnt = gdn_cnt;
+            a.y = nullptr;
+            a.q8 = q8;
+            a.hk = hk;
+            a.hv = hv;
+            a.eps = cfg.eps;
+            v.push_back(g);
+            add_gemv(v, PRO_Q8, EPI_RES, q8_params(L.out_proj, q8, x, x, xp));
         } else {
-            ok(launch_pdl(attn_prep_kernel<NC>, dim3(nh + nkv, NC), dim3(256), 0, s, pdl, (const float*) proj,
-                          L.in_proj.n_out, (const float*) L.q_norm, (const float*) L.k_norm, (const float*) rope,
-                          cfg.n_rot, (const int*) &ctrl->pos, nh, nkv, cfg.max_ctx, cfg.eps, q_attn, g_attn, L.kc, L.vc));
-            ok(gqa_launch(q_attn, L.kc, L.vc, o_attn, nh, nkv, NC, &ctrl->pos, cfg.max_ctx, kAttnScale, attn_scratch, s,
-                          pdl, g_attn, q8_attn));
-            ++launches;  // the combine kernel
-            gemv_q8_res<NC>(L.out_proj, q8_attn, x, xp, pdl);
+            v.push_back(attn_op(POP_ATTN, L, 0));
+            v.push_back(attn_op(POP_COMBINE, L, 0));
+            add_gemv(v, PRO_Q8, EPI_RES, q8_params(L.out_proj, q8_attn, x, x, xp));
         }
-        ffn<NC>(L, x, xp, pdl);
+        add_ffn(v, L, x, xp);
     }
     // final norm + lm_head + argmax; the normed hidden and its partials feed the draft (src/qwythos.cpp:1234-1237)
-    gemv_rms<NC, EPI_ARGMAX>(lm_head, x, out_norm, xp, logits, V, pdl, hsave, hsave_p, ctrl->amax);
+    MmvqParams p = rms_params(lm_head, x, out_norm, xp, logits, V);
+    p.xn_out = hsave;
+    p.xn_part = hsave_p;
+    p.amax = &ctrl->amax[0];
+    add_gemv(v, PRO_RMS, EPI_ARGMAX, p);
+}
+
+// The MTP draft (draft_predict, src/qwythos.cpp:1316-1406): [enorm(emb) | hnorm(h)] -> eh_proj -> the
+// nextn attention block -> (with_head) shnorm + the shared lm_head + argmax.
+void EngineImpl::add_draft(std::vector<POp>& v, bool head) {
+    POp d = make_op(POP_DRAFT_PREP);
+    d.draft = 1;
+    d.dp.emb = tok_embd;
+    d.dp.H = H;
+    d.dp.V = V;
+    d.dp.enorm = enorm;
+    d.dp.hnorm = hnorm;
+    d.dp.hsave = hsave;
+    d.dp.hsave_p = hsave_p;
+    d.dp.eps = cfg.eps;
+    d.dp.eh_q8 = eh_q8;
+    v.push_back(d);
+    add_gemv(v, PRO_Q8, EPI_STORE_P, q8_params(eh_proj, eh_q8, dx, nullptr, dxp));  // no residual
+    const Layer& D = draft;
+    add_gemv(v, PRO_RMS, EPI_STORE, rms_params(D.in_proj, dx, D.attn_norm, dxp, proj, D.in_proj.n_out));
+    v.push_back(attn_op(POP_ATTN, D, 1));
+    v.push_back(attn_op(POP_COMBINE, D, 1));
+    add_gemv(v, PRO_Q8, EPI_RES, q8_params(D.out_proj, q8_attn, dx, dx, dxp));
+    add_ffn(v, D, dx, dxp);
+    if (head) {
+        MmvqParams p = rms_params(lm_head, dx, shnorm, dxp, nullptr, V);
+        p.amax = &ctrl->damax[0];
+        add_gemv(v, PRO_RMS, EPI_ARGMAX, p);
+    }
+}
+
+void EngineImpl::add_ctrl(std::vector<POp>& v, int kind) {
+    POp c = make_op(POP_CTRL);
+    c.ct.kind = kind;
+    c.ct.out = out;
+    c.ct.max_out = max_out;
+    v.push_back(c);
 }
 
 // The GEMVs of one trunk step only (rk_engine_probe_gemv), with their byte counts.
-template <int NC>
-void EngineImpl::probe_body() {
+void EngineImpl::add_probe(std::vector<POp>& v, int nc) {
     double wb = 0, ab = 0;
     int n = 0;
     auto count = [&](const Mat& m, bool fp32_in, bool res) {
         const double w = (double) rk_weight_bytes(RK_TYPE_Q6_K, m.n_in, m.n_out);
         const double in = fp32_in ? (double) m.n_in * 4 : (double) rk_q8_1_bytes(m.n_in, 1);
         wb += w;
-        ab += w + NC * (in + (double) m.n_out * 4 * (res ? 2 : 1));
+        ab += w + nc * (in + (double) m.n_out * 4 * (res ? 2 : 1));
         ++n;
     };
     for (const Layer& L : layers) {
-        gemv_rms<NC, EPI_STORE>(L.in_proj, x, L.attn_norm, xp, proj, L.in_proj.n_out, true);
+        add_gemv(v, PRO_RMS, EPI_STORE, rms_params(L.in_proj, x, L.attn_norm, xp, proj, L.in_proj.n_out));
         count(L.in_proj, true, false);
-        gemv_q8_res<NC>(L.out_proj, L.gdn ? q8 : q8_attn, x, xp, true);
+        add_gemv(v, PRO_Q8, EPI_RES, q8_params(L.out_proj, L.gdn ? q8 : q8_attn, x, x, xp));
         count(L.out_proj, false, true);
-        ffn<NC>(L, x, xp, true);
+        add_ffn(v, L, x, xp);
         count(L.upgate, true, false);
         count(L.down, false, true);
     }
-    gemv_rms<NC, EPI_ARGMAX>(lm_head, x, out_norm, xp, logits, V, true, hsave, hsave_p, ctrl->amax);
+    MmvqParams p = rms_params(lm_head, x, out_norm, xp, logits, V);
+    p.xn_out = hsave;
+    p.xn_part = hsave_p;
+    p.amax = &ctrl->amax[0];
+    add_gemv(v, PRO_RMS, EPI_ARGMAX, p);
     count(lm_head, true, false);
-    probe_weight_bytes = wb;
-    probe_algo_bytes = ab;
-    probe_launches = n;
+    probe_weight_bytes[nc - 1] = wb;
+    probe_algo_bytes[nc - 1] = ab;
+    probe_gemvs = n;
+}
+
+// The executor: persistent unless RK_ENGINE_MODE=graph, or unless the device cannot hold one CTA per SM
+// with at least two ring slots per warp. RK_PERSIST_STAGES forces the ring depth (a tuning knob, like the
+// reference's QWYTHOS_Q6ROWS sweep knob, src/native_mmvq.cu:3648-3651).
+int EngineImpl::setup_executor() {
+    const char* mode = std::getenv("RK_ENGINE_MODE");
+    persistent = !(mode && std::strcmp(mode, "graph") == 0);
+    if (!persistent) return RK_OK;
+    int optin = 0, sms = 0;
+    if ((err = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) != cudaSuccess) return RK_ECUDA;
+    if ((err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return RK_ECUDA;
+    const int max_in = FF > 2 * H ? FF : 2 * H;
+    size_t region = (size_t) 2 * (max_in / 32) * 48;
+    if (op_scratch_bytes(2, H) > region) region = op_scratch_bytes(2, H);
+    region = (region + 127) & ~(size_t) 127;
+    cudaFuncAttributes fa1 = {}, fa2 = {};
+    if ((err = cudaFuncGetAttributes(&fa1, persistent_kernel<1>)) != cudaSuccess) return RK_ECUDA;
+    if ((err = cudaFuncGetAttributes(&fa2, persistent_kernel<2>)) != cudaSuccess) return RK_ECUDA;
+    const long long stat = (long long) (fa1.sharedSizeBytes > fa2.sharedSizeBytes ? fa1.sharedSizeBytes : fa2.sharedSizeBytes);
+    const long long avail = (long long) optin - stat - (long long) persistent_smem_bytes((int) region, 0);
+    int stages = (int) (avail / ((long long) kMmvqWarps * kQ6Tile));
+    if (stages > kMmvqMaxStages) stages = kMmvqMaxStages;
+    if (const char* st = std::getenv("RK_PERSIST_STAGES")) {
+        const int v = std::atoi(st);
+        if (v >= 2 && v <= stages) stages = v;
+    }
+    if (stages < 2) {
+        persistent = false;
+        return RK_OK;
+    }
+    p_smem = persistent_smem_bytes((int) region, stages);
+    if ((err = cudaFuncSetAttribute(persistent_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) p_smem)) != cudaSuccess)
+        return RK_ECUDA;
+    if ((err = cudaFuncSetAttribute(persistent_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) p_smem)) != cudaSuccess)
+        return RK_ECUDA;
+    int occ1 = 0, occ2 = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ1, persistent_kernel<1>, 256, p_smem);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ2, persistent_kernel<2>, 256, p_smem);
+    if (occ1 < 1 || occ2 < 1) {
+        persistent = false;
+        return RK_OK;
+    }
+    p_grid = sms;
+    p_stages = stages;
+    p_region = (int) region;
+    return RK_OK;
 }
 
 template <int NC>
-void EngineImpl::draft_pass(bool with_head, bool pdl) {
-    ok(launch_pdl(draft_prep_kernel<NC>, dim3(NC), dim3(256), (size_t) (H + H / 4) * sizeof(float), s, pdl,
-                  (const uint8_t*) tok_embd, H, V, ctrl, (const float*) enorm, (const float*) hnorm,
-                  (const float*) hsave, (const float*) hsave_p, cfg.eps, eh_q8));
-    // eh_proj (no residual: y = W . x with its partials)
-    {
-        MmvqParams p = {};
-        p.w = eh_proj.w;
-        p.n_in = eh_proj.n_in;
-        p.n_out = eh_proj.n_out;
-        p.prefetch_before_wait = 1;
-        p.xq = eh_q8;
-        p.y = dx;
-        p.y_stride = H;
-        p.pout = dxp;
-        p.pout_stride = H / 4;
-        ok(mmvq_launch<RK_TYPE_Q6_K, NC, PRO_Q8, EPI_STORE_P>(p, s, pdl));
+cudaError_t EngineImpl::launch_op(const POp& op) {
+    if (op.kind == POP_GEMV) {
+        const MmvqParams& p = op.g;
+        if (op.pro == PRO_RMS) {
+            if (op.epi == EPI_STORE) return mmvq_launch<RK_TYPE_Q6_K, NC, PRO_RMS, EPI_STORE>(p, s, true);
+            if (op.epi == EPI_SWIGLU) return mmvq_launch<RK_TYPE_Q6_K, NC, PRO_RMS, EPI_SWIGLU>(p, s, true);
+            return mmvq_launch<RK_TYPE_Q6_K, NC, PRO_RMS, EPI_ARGMAX>(p, s, true);
+        }
+        if (op.epi == EPI_RES) return mmvq_launch<RK_TYPE_Q6_K, NC, PRO_Q8, EPI_RES>(p, s, true);
+        return mmvq_launch<RK_TYPE_Q6_K, NC, PRO_Q8, EPI_STORE_P>(p, s, true);
     }
-    const Layer& D = draft;
-    gemv_rms<NC, EPI_STORE>(D.in_proj, dx, D.attn_norm, dxp, proj, D.in_proj.n_out, pdl);
-    ok(launch_pdl(attn_prep_kernel<NC>, dim3(nh + nkv, NC), dim3(256), 0, s, pdl, (const float*) proj, D.in_proj.n_out,
-                  (const float*) D.q_norm, (const float*) D.k_norm, (const float*) rope, cfg.n_rot,
-                  (const int*) &ctrl->dpos, nh, nkv, cfg.max_ctx, cfg.eps, q_attn, g_attn, D.kc, D.vc));
-    ok(gqa_launch(q_attn, D.kc, D.vc, o_attn, nh, nkv, NC, &ctrl->dpos, cfg.max_ctx, kAttnScale, attn_scratch, s, pdl,
-                  g_attn, q8_attn));
-    ++launches;
-    gemv_q8_res<NC>(D.out_proj, q8_attn, dx, dxp, pdl);
-    ffn<NC>(D, dx, dxp, pdl);
-    if (with_head)
-        gemv_rms<NC, EPI_ARGMAX>(lm_head, dx, shnorm, dxp, nullptr, V, pdl, nullptr, nullptr, ctrl->damax);
+    // grid: the op's largest item count (positions up to the end of the cache)
+    const int grid = pop_items<NC>(op, cfg.max_ctx - NC);
+    const size_t smem = op_scratch_bytes(NC, H);
+    static bool attr_set[2] = {false, false};
+    if (smem > 48 * 1024 && !attr_set[NC - 1]) {
+        const cudaError_t e = cudaFuncSetAttribute(op_kernel<NC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+        if (e != cudaSuccess) return e;
+        attr_set[NC - 1] = true;
+    }
+    return launch_pdl(op_kernel<NC>, dim3((unsigned) grid), dim3(256), smem, s, true, op, ctrl);
 }
 
-int EngineImpl::capture(cudaGraphExec_t* exec, int* nk, void (*body)(EngineImpl*)) {
+// Upload a program; in graph mode also capture its launches.
+int EngineImpl::finalize(Program& P, int nc) {
+    P.nc = nc;
+    for (const POp& op : P.ops)
+        if (op.kind == POP_GEMV && !gemv_combo_supported(op.pro, op.epi)) return RK_EINVAL;
+    P.dev = alloc<POp>(P.ops.size());
+    if (err == cudaSuccess)
+        err = cudaMemcpyAsync(P.dev, P.ops.data(), sizeof(POp) * P.ops.size(), cudaMemcpyHostToDevice, s);
+    if (err == cudaSuccess) err = cudaStreamSynchronize(s);
+    if (err != cudaSuccess) return RK_ECUDA;
+    if (persistent) {
+        P.kernels = 1;
+        return RK_OK;
+    }
     cudaGraph_t g = nullptr;
-    launches = 0;
     if ((err = cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal)) != cudaSuccess) return RK_ECUDA;
-    body(this);
+    int launches = 0;
+    for (const POp& op : P.ops) {
+        const cudaError_t e = nc == 1 ? launch_op<1>(op) : launch_op<2>(op);
+        if (e != cudaSuccess && err == cudaSuccess) err = e;
+        ++launches;
+    }
     const cudaError_t e2 = cudaStreamEndCapture(s, &g);
     if (err == cudaSuccess) err = e2;
-    if (err == cudaSuccess) err = cudaGraphInstantiate(exec, g, 0ull);
+    if (err == cudaSuccess) err = cudaGraphInstantiate(&P.graph, g, 0ull);
     if (g) cudaGraphDestroy(g);
-    if (nk) *nk = launches;
+    P.kernels = launches;
     return err == cudaSuccess ? RK_OK : RK_ECUDA;
+}
+
+// Enqueue one run of a program. Persistent: until > 0 repeats it while ctrl->n_emitted < until, at most
+// max_iters times. Graph mode runs it once (the caller loops).
+cudaError_t EngineImpl::run(const Program& P, int until, int max_iters) {
+    if (!persistent) return cudaGraphLaunch(P.graph, s);
+    cudaLaunchConfig_t c = {};
+    c.gridDim = dim3((unsigned) p_grid);
+    c.blockDim = dim3(256);
+    c.dynamicSmemBytes = p_smem;
+    c.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeCooperative;
+    at[0].val.cooperative = 1;
+    c.attrs = at;
+    c.numAttrs = 1;
+    const POp* prog = P.dev;
+    const int nops = (int) P.ops.size();
+    if (P.nc == 1)
+        return cudaLaunchKernelEx(&c, persistent_kernel<1>, prog, nops, ctrl, psync, p_stages, p_region, until, max_iters);
+    return cudaLaunchKernelEx(&c, persistent_kernel<2>, prog, nops, ctrl, psync, p_stages, p_region, until, max_iters);
 }
 
 // Host writes of the control fields go through a ring of pinned slots so that queued copies never
@@ -787,6 +737,16 @@ void EngineImpl::set_ctrl(const Ctrl& h) {
     std::memcpy(slot, &h, sizeof(int) * kCtrlHostFields);
     const cudaError_t e = cudaMemcpyAsync(ctrl, slot, sizeof(int) * kCtrlHostFields, cudaMemcpyHostToDevice, s);
     if (e != cudaSuccess && err == cudaSuccess) err = e;
+}
+
+// After a synchronized run: a persistent launch that gave up on a wait leaves the sticky abort word.
+int EngineImpl::check_abort(const char* what) {
+    if (!persistent) return RK_OK;
+    PSync h = {};
+    if (cudaMemcpy(&h, psync, sizeof h, cudaMemcpyDeviceToHost) != cudaSuccess)
+        return set_error(RK_ECUDA, "%s: reading the executor state failed", what);
+    if (h.abort) return set_error(RK_ECUDA, "%s: a device wait timed out; the step was abandoned (rk_engine_reset clears it)", what);
+    return RK_OK;
 }
 
 }  // namespace rk
@@ -826,46 +786,59 @@ int rk_engine_create(const rk_model_config* cfg, int device, rk_engine** out) {
     if (c.n_layer < 1 || c.n_embd <= 0 || c.n_embd % 1024 || c.n_ff <= 0 || c.n_ff % 1024 || c.n_vocab <= 0 ||
         c.n_vocab % 4)
         return set_error(RK_EINVAL, "%s: n_embd and n_ff must be multiples of 1024, n_vocab of 4", what);
-    if (c.ssm_h_k <= 0 || c.ssm_h_v != 2 * c.ssm_h_k || c.ssm_h_v * kS != c.n_embd)
+    if (c.ssm_h_k <= 0 || c.ssm_h_v != 2 * c.ssm_h_k || c.ssm_h_v * kSsm != c.n_embd)
         return set_error(RK_EINVAL, "%s: requires ssm_h_v == 2*ssm_h_k and ssm_h_v*128 == n_embd", what);
-    if (c.n_head_kv <= 0 || c.n_head != 4 * c.n_head_kv || c.n_head * kHd != c.n_embd)
+    if (c.n_head_kv <= 0 || c.n_head != 4 * c.n_head_kv || c.n_head * kHdA != c.n_embd)
         return set_error(RK_EINVAL, "%s: requires n_head == 4*n_head_kv and n_head*256 == n_embd", what);
-    if (c.n_rot <= 0 || c.n_rot > kHd || c.n_rot % 2 || c.attn_interval < 1 || c.max_ctx < 8 || !(c.eps > 0))
+    if (c.n_rot <= 0 || c.n_rot > kHdA || c.n_rot % 2 || c.attn_interval < 1 || c.max_ctx < 8 || !(c.eps > 0))
         return set_error(RK_EINVAL, "%s: bad n_rot / attn_interval / max_ctx / eps", what);
     rk_engine* e = new (std::nothrow) rk_engine;
     if (!e) return set_error(RK_ENOMEM, "%s: host allocation failed", what);
     e->impl.cfg = c;
     e->impl.dev = device;
-    int rc = e->impl.build();
+    EngineImpl& E = e->impl;
+    int rc = E.build();
+    if (rc == RK_OK) rc = E.setup_executor();
     if (rc == RK_OK) {
-        EngineImpl& E = e->impl;
-        rc = E.capture(&E.g_single, &E.kernels_single, [](EngineImpl* x) {
-            x->trunk<1>(true);
-            x->ok(launch_pdl(single_finish_kernel, dim3(1), dim3(1), 0, x->s, true, x->ctrl, x->out, x->max_out));
-        });
-        if (rc == RK_OK)
-            rc = E.capture(&E.g_trunk2, nullptr, [](EngineImpl* x) { x->trunk<2>(true); });
-        if (rc == RK_OK && c.has_mtp) {
-            rc = E.capture(&E.g_round, &E.kernels_round, [](EngineImpl* x) {
-                x->trunk<2>(true);
-                x->ok(launch_pdl(accept_kernel, dim3(1), dim3(1), 0, x->s, true, x->ctrl, x->out, x->max_out));
-                x->draft_pass<2>(true, true);
-                x->ok(launch_pdl(round_finish_kernel, dim3(1), dim3(1), 0, x->s, true, x->ctrl));
-            });
-            if (rc == RK_OK)
-                rc = E.capture(&E.g_draft1, nullptr, [](EngineImpl* x) {
-                    x->draft_pass<1>(true, true);
-                    x->ok(launch_pdl(draft1_finish_kernel, dim3(1), dim3(1), 0, x->s, true, x->ctrl));
-                });
-            if (rc == RK_OK)
-                rc = E.capture(&E.g_draft1_seed, nullptr, [](EngineImpl* x) { x->draft_pass<1>(false, true); });
+        E.add_trunk(E.progs[P_SINGLE].ops);
+        E.add_ctrl(E.progs[P_SINGLE].ops, CTRL_SINGLE);
+        rc = E.finalize(E.progs[P_SINGLE], 1);
+    }
+    if (rc == RK_OK) {
+        E.add_trunk(E.progs[P_TRUNK2].ops);
+        rc = E.finalize(E.progs[P_TRUNK2], 2);
+    }
+    if (rc == RK_OK && c.has_mtp) {
+        std::vector<POp>& r = E.progs[P_ROUND].ops;
+        E.add_trunk(r);
+        E.add_ctrl(r, CTRL_ACCEPT);
+        E.add_draft(r, true);
+        E.add_ctrl(r, CTRL_ROUND);
+        rc = E.finalize(E.progs[P_ROUND], 2);
+        if (rc == RK_OK) {
+            E.add_draft(E.progs[P_DRAFT1].ops, true);
+            E.add_ctrl(E.progs[P_DRAFT1].ops, CTRL_DRAFT1);
+            rc = E.finalize(E.progs[P_DRAFT1], 1);
+        }
+        if (rc == RK_OK) {
+            E.add_draft(E.progs[P_SEED].ops, false);
+            rc = E.finalize(E.progs[P_SEED], 1);
         }
     }
+    if (rc == RK_OK) {
+        E.add_probe(E.progs[P_PROBE1].ops, 1);
+        rc = E.finalize(E.progs[P_PROBE1], 1);
+    }
+    if (rc == RK_OK) {
+        E.add_probe(E.progs[P_PROBE2].ops, 2);
+        rc = E.finalize(E.progs[P_PROBE2], 2);
+    }
     if (rc != RK_OK) {
-        const cudaError_t ce = e->impl.err;
+        const cudaError_t ce = E.err;
         delete e;
         if (rc == RK_ENOMEM || ce == cudaErrorMemoryAllocation)
             return set_error(RK_ENOMEM, "%s: out of device memory", what);
+        if (rc == RK_EINVAL) return set_error(RK_EINVAL, "%s: unsupported GEMV prologue/epilogue pair", what);
         return set_error(RK_ECUDA, "%s: %s", what, cudaGetErrorString(ce));
     }
     *out = e;
@@ -877,26 +850,30 @@ int rk_engine_destroy(rk_engine* e) {
     return RK_OK;
 }
 
+int rk_engine_mode(const rk_engine* e) { return e && e->impl.persistent ? RK_ENGINE_PERSISTENT : RK_ENGINE_GRAPH; }
+
 int rk_engine_reset(rk_engine* e) {
     if (!e) return set_error(RK_EINVAL, "rk_engine_reset: null engine");
     EngineImpl& E = e->impl;
     cudaStreamSynchronize(E.s);
-    const size_t hvs = (size_t) kS * E.hv * kS;
-    const int C = 2 * E.hk * kS + E.hv * kS;
+    const size_t hvs = (size_t) kSsm * E.hv * kSsm;
+    const int C = 2 * E.hk * kSsm + E.hv * kSsm;
     auto clear = [&](Layer& L) {
         if (L.gdn) {
             cudaMemsetAsync(L.state, 0, hvs * 4, E.s);
             cudaMemsetAsync(L.snap, 0, hvs * 4, E.s);
-            cudaMemsetAsync(L.ring, 0, (size_t) C * 16, E.s);
+            cudaMemsetAsync(L.ring, 0, (size_t) C * kRingSlots * 4, E.s);
         } else if (L.kc) {
-            cudaMemsetAsync(L.kc, 0, (size_t) E.nkv * E.cfg.max_ctx * kHd * 2, E.s);
-            cudaMemsetAsync(L.vc, 0, (size_t) E.nkv * E.cfg.max_ctx * kHd * 2, E.s);
+            cudaMemsetAsync(L.kc, 0, (size_t) E.nkv * E.cfg.max_ctx * kHdA * 2, E.s);
+            cudaMemsetAsync(L.vc, 0, (size_t) E.nkv * E.cfg.max_ctx * kHdA * 2, E.s);
         }
     };
     for (Layer& L : E.layers) clear(L);
     if (E.cfg.has_mtp) clear(E.draft);
     cudaMemsetAsync(E.ctrl, 0, sizeof(Ctrl), E.s);
     cudaMemsetAsync(E.swiglu_cnt, 0, sizeof(unsigned) * (size_t) E.FF / 32, E.s);
+    cudaMemsetAsync(E.gdn_cnt, 0, sizeof(unsigned) * (size_t) E.hv, E.s);
+    cudaMemsetAsync(E.psync, 0, sizeof(PSync), E.s);
     const cudaError_t ce = cudaStreamSynchronize(E.s);
     if (ce != cudaSuccess) return set_error(RK_ECUDA, "rk_engine_reset: %s", cudaGetErrorString(ce));
     return RK_OK;
@@ -915,13 +892,14 @@ int rk_engine_step(rk_engine* e, const int* tokens, int ncols, int pos, float* l
     h.tok[0] = tokens[0];
     h.tok[1] = ncols > 1 ? tokens[1] : 0;
     E.set_ctrl(h);
-    cudaError_t ce = cudaGraphLaunch(ncols == 1 ? E.g_single : E.g_trunk2, E.s);
+    cudaError_t ce = E.run(E.progs[ncols == 1 ? P_SINGLE : P_TRUNK2], 0);
     if (ce == cudaSuccess && logits)
         ce = cudaMemcpyAsync(logits, E.logits, sizeof(float) * (size_t) ncols * E.V, cudaMemcpyDeviceToHost, E.s);
     Ctrl back;
     if (ce == cudaSuccess) ce = cudaMemcpyAsync(&back, E.ctrl, sizeof(Ctrl), cudaMemcpyDeviceToHost, E.s);
     if (ce == cudaSuccess) ce = cudaStreamSynchronize(E.s);
     if (ce != cudaSuccess) return set_error(RK_ECUDA, "%s: %s", what, cudaGetErrorString(ce));
+    if (int rc = E.check_abort(what)) return rc;
     if (argmax)
         for (int c = 0; c < ncols; ++c) argmax[c] = argmax_key_row(back.amax[c]);
     return RK_OK;
@@ -943,6 +921,12 @@ int rk_engine_generate(rk_engine* e, const int* prompt, int n_prompt, int n_gen,
     for (auto& v : ev) cudaEventCreate(&v);
     int launches = 0;
     cudaError_t ce = cudaSuccess;
+    int* pinned = reinterpret_cast<int*>(E.ctrl_stage + E.stage_slots);
+    auto read_emitted = [&]() {
+        if (ce == cudaSuccess) ce = cudaMemcpyAsync(pinned, &E.ctrl->n_emitted, sizeof(int), cudaMemcpyDeviceToHost, E.s);
+        if (ce == cudaSuccess) ce = cudaStreamSynchronize(E.s);
+        return ce == cudaSuccess ? *pinned : -1;
+    };
     // prefill: positions 0..P-2, teacher forced, one trunk pass each (the reference's per-token path)
     cudaEventRecord(ev[0], E.s);
     for (int i = 0; i + 1 < n_prompt && ce == cudaSuccess; ++i) {
@@ -950,7 +934,7 @@ int rk_engine_generate(rk_engine* e, const int* prompt, int n_prompt, int n_gen,
         h.pos = i;
         h.tok[0] = prompt[i];
         E.set_ctrl(h);
-        ce = cudaGraphLaunch(E.g_single, E.s);
+        ce = E.run(E.progs[P_SINGLE], 0);
         ++launches;
     }
     if (use_mtp && ce == cudaSuccess) {
@@ -961,37 +945,50 @@ int rk_engine_generate(rk_engine* e, const int* prompt, int n_prompt, int n_gen,
         h.dpos = 0;
         h.dtok[0] = prompt[0];
         E.set_ctrl(h);
-        ce = cudaGraphLaunch(E.g_draft1_seed, E.s);
+        ce = E.run(E.progs[P_SEED], 0);
         ++launches;
     }
     cudaMemsetAsync(&E.ctrl->n_emitted, 0, sizeof(int) * 4, E.s);  // n_emitted, steps, accepted, singles
     cudaEventRecord(ev[1], E.s);
-    // seed pass at position P-1 produces the first generated token
+    // the seed pass at position P-1 produces the first generated token
     Ctrl h = {};
     h.pos = n_prompt - 1;
     h.tok[0] = prompt[n_prompt - 1];
     E.set_ctrl(h);
-    if (ce == cudaSuccess) ce = cudaGraphLaunch(E.g_single, E.s);
-    ++launches;
     if (!use_mtp) {
-        for (int i = 1; i < n_gen && ce == cudaSuccess; ++i) {
-            ce = cudaGraphLaunch(E.g_single, E.s);
+        if (E.persistent) {
+            if (ce == cudaSuccess) ce = E.run(E.progs[P_SINGLE], n_gen, n_gen);  // the whole generation
             ++launches;
+        } else {
+            for (int i = 0; i < n_gen && ce == cudaSuccess; ++i) {
+                ce = E.run(E.progs[P_SINGLE], 0);
+                ++launches;
+            }
         }
     } else if (ce == cudaSuccess) {
+        ce = E.run(E.progs[P_SINGLE], 0);
+        ++launches;
         // first candidate: draft at (emb(first token), hidden of P-1)
-        ce = cudaGraphLaunch(E.g_draft1, E.s);
+        if (ce == cudaSuccess) ce = E.run(E.progs[P_DRAFT1], 0);
         ++launches;
         int emitted = 1;
-        int* pinned = reinterpret_cast<int*>(E.ctrl_stage + E.stage_slots);
-        while (ce == cudaSuccess && emitted < n_gen) {
-            const bool single = emitted >= n_gen - 1;
-            ce = cudaGraphLaunch(single ? E.g_single : E.g_round, E.s);
-            ++launches;
-            if (ce != cudaSuccess) break;
-            ce = cudaMemcpyAsync(pinned, &E.ctrl->n_emitted, sizeof(int), cudaMemcpyDeviceToHost, E.s);
-            if (ce == cudaSuccess) ce = cudaStreamSynchronize(E.s);
-            emitted = *pinned;
+        if (E.persistent) {
+            if (emitted < n_gen - 1 && ce == cudaSuccess) {
+                ce = E.run(E.progs[P_ROUND], n_gen - 1, n_gen);  // rounds until one token is left at most
+                ++launches;
+                emitted = read_emitted();
+            }
+            if (emitted >= 0 && emitted < n_gen && ce == cudaSuccess) {
+                ce = E.run(E.progs[P_SINGLE], 0);
+                ++launches;
+            }
+        } else {
+            while (ce == cudaSuccess && emitted >= 0 && emitted < n_gen) {
+                const bool single = emitted >= n_gen - 1;
+                ce = E.run(E.progs[single ? P_SINGLE : P_ROUND], 0);
+                ++launches;
+                emitted = read_emitted();
+            }
         }
     }
     cudaEventRecord(ev[2], E.s);
@@ -1007,6 +1004,7 @@ int rk_engine_generate(rk_engine* e, const int* prompt, int n_prompt, int n_gen,
     }
     for (auto& v : ev) cudaEventDestroy(v);
     if (ce != cudaSuccess) return set_error(RK_ECUDA, "%s: %s", what, cudaGetErrorString(ce));
+    if (int rc2 = E.check_abort(what)) return rc2;
     if (back.bad) return set_error(RK_ERANGE, "%s: a token outside the vocabulary reached the device", what);
     if (back.n_emitted < n_gen) return set_error(RK_ECUDA, "%s: generation stopped early (%d of %d)", what, back.n_emitted, n_gen);
     if (stats) {
@@ -1017,8 +1015,8 @@ int rk_engine_generate(rk_engine* e, const int* prompt, int n_prompt, int n_gen,
         stats->mtp_accepted = back.accepted;
         stats->single_steps = back.singles;
         stats->graph_launches = launches;
-        stats->kernels_per_single_step = E.kernels_single;
-        stats->kernels_per_round = E.kernels_round;
+        stats->kernels_per_single_step = E.progs[P_SINGLE].kernels;
+        stats->kernels_per_round = E.progs[P_ROUND].kernels;
     }
     return RK_OK;
 }
@@ -1055,18 +1053,13 @@ int rk_engine_probe_gemv(rk_engine* e, int ncols, int iters, rk_probe_result* ou
     if (!e || !out) return set_error(RK_EINVAL, "%s: null argument", what);
     if (ncols < 1 || ncols > 2 || iters < 1) return set_error(RK_EINVAL, "%s: ncols 1..2, iters >= 1", what);
     EngineImpl& E = e->impl;
-    cudaGraphExec_t& g = E.g_probe[ncols - 1];
-    if (!g) {
-        int rc = ncols == 1 ? E.capture(&g, nullptr, [](EngineImpl* x) { x->probe_body<1>(); })
-                            : E.capture(&g, nullptr, [](EngineImpl* x) { x->probe_body<2>(); });
-        if (rc != RK_OK) return set_error(RK_ECUDA, "%s: capture failed: %s", what, cudaGetErrorString(E.err));
-    }
+    const Program& P = E.progs[ncols == 1 ? P_PROBE1 : P_PROBE2];
     cudaEvent_t a, b;
     cudaEventCreate(&a);
     cudaEventCreate(&b);
-    cudaError_t ce = cudaGraphLaunch(g, E.s);  // warm-up
+    cudaError_t ce = E.run(P, 0);  // warm-up
     if (ce == cudaSuccess) ce = cudaEventRecord(a, E.s);
-    for (int i = 0; i < iters && ce == cudaSuccess; ++i) ce = cudaGraphLaunch(g, E.s);
+    for (int i = 0; i < iters && ce == cudaSuccess; ++i) ce = E.run(P, 0);
     if (ce == cudaSuccess) ce = cudaEventRecord(b, E.s);
     if (ce == cudaSuccess) ce = cudaEventSynchronize(b);
     float ms = 0.0f;
@@ -1074,10 +1067,11 @@ int rk_engine_probe_gemv(rk_engine* e, int ncols, int iters, rk_probe_result* ou
     cudaEventDestroy(a);
     cudaEventDestroy(b);
     if (ce != cudaSuccess) return set_error(RK_ECUDA, "%s: %s", what, cudaGetErrorString(ce));
+    if (int rc = E.check_abort(what)) return rc;
     out->ms = ms;
-    out->launches = E.probe_launches;
-    out->weight_bytes = E.probe_weight_bytes;
-    out->algo_bytes = E.probe_algo_bytes;
+    out->launches = E.probe_gemvs;
+    out->weight_bytes = E.probe_weight_bytes[ncols - 1];
+    out->algo_bytes = E.probe_algo_bytes[ncols - 1];
     return RK_OK;
 }
 

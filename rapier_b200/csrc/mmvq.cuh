@@ -19,6 +19,9 @@
 // in fp32 as fma(float(isum), d8 * d, acc) per lane over the k-chunks, then reduced across the warp
 // by the xor butterfly. The per-row order does not depend on ncols, so every column of a
 // multi-column call is bitwise equal to a single-column call on that column.
+//
+// Activations, partials and residuals are read with ld.global.cg: the same prologues and epilogues run
+// inside the persistent decode kernel, where the producing op ran on other SMs of the same launch.
 #pragma once
 
 #include "common.cuh"
@@ -74,11 +77,13 @@ inline size_t mmvq_smem_bytes(int type, int n_in, int ncols, int stages) {
 // The fixed-order reduction of rms_quant_apply_kernel (src/qwythos.cpp:634-641) over `nslots`
 // partials, for a 256-thread block: thread t sums slots t, t+256, ... in order; shfl_down tree in each
 // warp; red[0] + ... + red[7] in order. Every thread returns the same value. Uses `red` (8 floats).
+// SMEM: the partials are in this block's shared memory (generic loads); else global, read through L2.
 // ---------------------------------------------------------------------------------------------------
+template <bool SMEM = false>
 __device__ __forceinline__ float block256_partials_sum(const float* partials, int nslots, float* red) {
     const int t = threadIdx.x;
     float part = 0.0f;
-    for (int p = t; p < nslots; p += 256) part = __fadd_rn(part, partials[p]);
+    for (int p = t; p < nslots; p += 256) part = __fadd_rn(part, SMEM ? partials[p] : __ldcg(partials + p));
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) part = __fadd_rn(part, __shfl_down_sync(0xffffffffu, part, off));
     __syncthreads();  // `red` may still be read by a previous call
@@ -142,9 +147,9 @@ __device__ __forceinline__ void mmvq_build_x(const MmvqParams& p, uint8_t* xsm, 
         for (int idx = threadIdx.x; idx < NC * ng; idx += blockDim.x) {
             const int c = idx / ng, g = idx - c * ng;
             const int* blk = reinterpret_cast<const int*>(p.xq + (size_t) c * col_bytes + (size_t) g * 36);
-            const uint32_t ds = (uint32_t) blk[0];
-            const int4 a = make_int4(blk[1], blk[2], blk[3], blk[4]);
-            const int4 b = make_int4(blk[5], blk[6], blk[7], blk[8]);
+            const uint32_t ds = (uint32_t) __ldcg(blk);
+            const int4 a = make_int4(__ldcg(blk + 1), __ldcg(blk + 2), __ldcg(blk + 3), __ldcg(blk + 4));
+            const int4 b = make_int4(__ldcg(blk + 5), __ldcg(blk + 6), __ldcg(blk + 7), __ldcg(blk + 8));
             const XStage s = xstage_col(xsm, ng, c);
             s.lo[g] = a;
             s.hi[g] = b;
@@ -172,7 +177,7 @@ __device__ __forceinline__ void mmvq_build_x(const MmvqParams& p, uint8_t* xsm, 
                 float4 xv[4], wv[4];
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
-                    xv[k] = xp4[k];
+                    xv[k] = __ldcg(xp4 + k);
                     wv[k] = wp4[k];
                 }
                 float invc = inv[0];
@@ -376,7 +381,7 @@ __device__ __forceinline__ void mmvq_epilogue(const MmvqParams& p, int unit, int
 #pragma unroll
                     for (int r = 0; r < 4; ++r) {
                         const float v =
-                            EPI == EPI_RES ? __fadd_rn(acc[c][r], p.res[(size_t) c * p.res_stride + row0 + r]) : acc[c][r];
+                            EPI == EPI_RES ? __fadd_rn(acc[c][r], __ldcg(p.res + (size_t) c * p.res_stride + row0 + r)) : acc[c][r];
                         y[r] = v;
                         part = __fmaf_rn(v, v, part);
                     }

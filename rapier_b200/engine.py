@@ -39,10 +39,25 @@ def config_tiny(max_ctx: int = 256, seed: int = 7, n_layer: int = 4, vocab: int 
 
 
 class Engine:
-    def __init__(self, cfg: ModelConfig, device: int = 0):
+    """mode: None (the library default, persistent), "persistent" or "graph"; the executor is chosen when
+    the engine is created (the library reads RK_ENGINE_MODE then)."""
+
+    def __init__(self, cfg: ModelConfig, device: int = 0, mode: str | None = None):
+        import os
+
         self.cfg = cfg
         h = C.c_void_p()
-        _lib.call("rk_engine_create", C.byref(cfg), device, C.byref(h))
+        old = os.environ.get("RK_ENGINE_MODE")
+        try:
+            if mode is not None:
+                os.environ["RK_ENGINE_MODE"] = mode
+            _lib.call("rk_engine_create", C.byref(cfg), device, C.byref(h))
+        finally:
+            if mode is not None:
+                if old is None:
+                    os.environ.pop("RK_ENGINE_MODE", None)
+                else:
+                    os.environ["RK_ENGINE_MODE"] = old
         self._h = h
 
     def close(self):
@@ -95,3 +110,8 @@ class Engine:
 
     def device_bytes(self) -> int:
         return _lib.lib().rk_engine_device_bytes(self._h)
+
+    @property
+    def mode(self) -> str:
+        """"persistent" (one cooperative kernel per step program) or "graph" (one kernel per op)."""
+        return "persistent" if _lib.lib().rk_engine_mode(self._h) == 1 else "graph"
