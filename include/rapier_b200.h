@@ -269,6 +269,16 @@ size_t rk_engine_device_bytes(const rk_engine* e);
 #define RK_ENGINE_GRAPH 0
 #define RK_ENGINE_PERSISTENT 1
 int rk_engine_mode(const rk_engine* e);
+/* Profiling hook (persistent executor only; no reference counterpart): runs one pass of a step program
+ * (0 single token, 1 MTP round, 2 / 3 GEMV probe with 1 / 2 columns, 4 the 2-column trunk) with CTA 0
+ * recording four stamps per op: op start, prologue done, its own work done, grid barrier passed, in
+ * microseconds from the first op's start (stamps_us[4*j .. 4*j+3]). kinds[j]: the op kind (a GEMV is
+ * reported as 100 + its epilogue). cta_us (may be NULL): per op and CTA b < max_ctas the CTA's op start
+ * and work-done stamps (cta_us[(j*max_ctas + b)*2 + 0/1]; -1 past the grid). Programs 0, 1 and 4 advance
+ * the decode state like a step. Returns the program's op count (at most max_ops are written) or a
+ * negative RK_E* code. */
+int rk_engine_trace(rk_engine* e, int program, double* stamps_us, int* kinds, int max_ops, double* cta_us,
+                    int max_ctas);
 
 #ifdef __cplusplus
 }

@@ -130,6 +130,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
         : "memory");
     return done != 0;
 }
+// Barrier over threads 0..255 (named barrier 1). The 256-thread op bodies and GEMV prologues use it so they
+// also run on the first 8 warps of the persistent decode kernel's 512-thread CTA; in a 256-thread block
+// it is __syncthreads.
+__device__ __forceinline__ void block_sync256() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 // Programmatic dependent launch: wait for the upstream grid's memory, and let the downstream grid launch.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }

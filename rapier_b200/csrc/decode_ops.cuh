@@ -92,10 +92,12 @@ struct CtrlArgs {
     int* out;
     int max_out;
 };
-struct POp {
+struct alignas(16) POp {  // 16-byte multiple: fetched into shared memory by 16-byte cp.async chunks
     int kind;
     int pro, epi;  // POP_GEMV: prologue / epilogue
     int draft;     // reads the draft position / tokens (ctrl->dpos, ctrl->dtok)
+    int next_gemv; // persistent executor: GEMV-table index of the first GEMV after this op (-1: none)
+    int pad_[3];
     union {
         MmvqParams g;
         EmbedArgs em;
@@ -105,6 +107,7 @@ struct POp {
         CtrlArgs ct;
     };
 };
+static_assert(sizeof(POp) % 16 == 0 && sizeof(POp) / 16 <= 256, "op records are copied in 16-byte chunks");
 
 // Work items of a non-GEMV op at position pos (column 0). Blocks or persistent CTAs take items
 // i = first, first + stride, ...
@@ -191,11 +194,11 @@ __device__ __forceinline__ void dequant_row(const uint8_t* row, int H, float* x,
 }
 
 // ------------------------------------------------------------------------------------------------
-// Bodies (one work item each, called by all 256 threads of a block)
+// Bodies (one work item each, called by threads 0..255 of a block; block_sync256 is their barrier)
 // ------------------------------------------------------------------------------------------------
 // Token embedding of column c (the reference copies a host-dequantized row, src/qwythos.cpp:1782-1789).
 // The trunk embedding also clears the argmax slots the lm_head fills.
-__device__ __forceinline__ void embed_body(const EmbedArgs& a, Ctrl* ctrl, int draft, int c) {
+__device__ __noinline__ void embed_body(const EmbedArgs& a, Ctrl* ctrl, int draft, int c) {
     const int tok = read_token(ctrl, draft, c, a.V);
     if (!draft && c == 0 && threadIdx.x == 0) {
         ctrl->amax[0] = 0ull;
@@ -219,7 +222,7 @@ __device__ __forceinline__ void embed_body(const EmbedArgs& a, Ctrl* ctrl, int d
 // channel xor trees added in order. History: 8 slots per channel; this launch writes slots pos, pos+1
 // and reads pos-3 .. pos-1 (mod 8), so no write of any block can meet a read of another.
 template <int NC>
-__device__ __forceinline__ void gdn_quarter_body(const GdnArgs& a, int head, int quarter, int pos, bool from_snap,
+__device__ __noinline__ void gdn_quarter_body(const GdnArgs& a, int head, int quarter, int pos, bool from_snap,
                                                  float* sm) {
     constexpr int S = kSsm;
     float* kq = sm;                     // [NC][256]: normalized k (0..127) | q (128..255)
@@ -232,7 +235,28 @@ __device__ __forceinline__ void gdn_quarter_body(const GdnArgs& a, int head, int
     const int hk = a.hk, hv = a.hv, kh = head % hk;
     const int C = 2 * hk * S + hv * S;
     const int off_z = C, off_beta = C + hv * S, off_alpha = off_beta + hv;
-    __syncthreads();  // scratch reuse across items
+    block_sync256();  // scratch reuse across items
+    // Loads that do not depend on the conv go out first: the state slice (threads 0..127: column = lane,
+    // row group = warp), the gate inputs and z.
+    const bool stepper = tid < 128;
+    const int col = lane, rg = wid & 3;
+    const size_t rs = (size_t) hv * S;
+    float* sbase = a.state + ((size_t) (rg * 32) * hv + head) * S + quarter * 32 + col;
+    float* pbase = a.snap + ((size_t) (rg * 32) * hv + head) * S + quarter * 32 + col;
+    float s[32];
+    float beta_in[NC], alpha_in[NC], z_in[NC];
+    if (stepper) {
+        const float* src = from_snap ? pbase : sbase;
+#pragma unroll
+        for (int r = 0; r < 32; ++r) s[r] = ld_cg(src + r * rs);
+#pragma unroll
+        for (int c = 0; c < NC; ++c) {
+            const float* pc = a.proj + (size_t) c * a.proj_stride;
+            beta_in[c] = ld_cg(pc + off_beta + head);
+            alpha_in[c] = ld_cg(pc + off_alpha + head);
+            z_in[c] = ld_cg(pc + off_z + head * S + wid * 32 + lane);  // column this thread normalizes if last
+        }
+    }
     auto conv = [&](int ch, float (&x)[NC], float (&yv)[NC]) {
         const float4* rp = reinterpret_cast<const float4*>(a.ring + (size_t) ch * kRingSlots);
         const float4 lo = __ldcg(rp), hi = __ldcg(rp + 1);
@@ -276,7 +300,7 @@ __device__ __forceinline__ void gdn_quarter_body(const GdnArgs& a, int head, int
             vloc[c * 32 + lane] = yv[c];
         }
     }
-    __syncthreads();
+    block_sync256();
 #pragma unroll
     for (int c = 0; c < NC; ++c) {  // L2 norms: q from warps 0-3' partials, k from warps 4-7'
         const float* p = qk_part + c * 8;
@@ -286,36 +310,24 @@ __device__ __forceinline__ void gdn_quarter_body(const GdnArgs& a, int head, int
         kq[c * 256 + idx] = __fmul_rn(kq[c * 256 + idx], rsqrtf(__fadd_rn(tid < S ? ssq : ssk, a.eps)));
     }
     // ---- the state step ----
-    const bool stepper = tid < 128;
-    const int col = lane, rg = wid & 3;
-    const size_t rs = (size_t) hv * S;
-    float* sbase = a.state + ((size_t) (rg * 32) * hv + head) * S + quarter * 32 + col;
-    float* pbase = a.snap + ((size_t) (rg * 32) * hv + head) * S + quarter * 32 + col;
-    float s[32];
-    if (stepper) {
-        const float* src = from_snap ? pbase : sbase;
-#pragma unroll
-        for (int r = 0; r < 32; ++r) s[r] = ld_cg(src + r * rs);
-    }
-    __syncthreads();
+    block_sync256();
     float oc[NC];
 #pragma unroll
     for (int c = 0; c < NC; ++c) {
-        const float* pc = a.proj + (size_t) c * a.proj_stride;
         const float* kk = kq + c * 256;
         const float* qq = kk + S;
         float* rk = red_kv + c * 128;
         float* ro = red_o + c * 128;
         float beta = 0.0f, g = 0.0f;
         if (stepper) {
-            beta = sigmoid_dev(ld_cg(pc + off_beta + head));
-            g = expf(softplus_gate_dev(ld_cg(pc + off_alpha + head), a.dt[head], a.ssm_a[head]));
+            beta = sigmoid_dev(beta_in[c]);
+            g = expf(softplus_gate_dev(alpha_in[c], a.dt[head], a.ssm_a[head]));
             float kv = 0.0f;
 #pragma unroll
             for (int r = 0; r < 32; ++r) kv = __fmaf_rn(s[r], kk[rg * 32 + r], kv);
             rk[rg * 32 + col] = kv;
         }
-        __syncthreads();
+        block_sync256();
         if (stepper) {
             const float kv_col = __fadd_rn(__fadd_rn(__fadd_rn(rk[col], rk[32 + col]), rk[64 + col]), rk[96 + col]);
             const float delta = __fmul_rn(__fsub_rn(vloc[c * 32 + col], __fmul_rn(g, kv_col)), beta);
@@ -327,7 +339,7 @@ __device__ __forceinline__ void gdn_quarter_body(const GdnArgs& a, int head, int
             }
             ro[rg * 32 + col] = o;
         }
-        __syncthreads();
+        block_sync256();
         oc[c] = 0.0f;
         if (stepper) {
             oc[c] = __fmul_rn(__fadd_rn(__fadd_rn(__fadd_rn(ro[col], ro[32 + col]), ro[64 + col]), ro[96 + col]),
@@ -352,9 +364,9 @@ __device__ __forceinline__ void gdn_quarter_body(const GdnArgs& a, int head, int
         }
         __threadfence();
     }
-    __syncthreads();
+    block_sync256();
     if (tid == 0) *last = atomicAdd(a.cnt + head, 1u) == 3u;
-    __syncthreads();
+    block_sync256();
     if (*last) {
         __threadfence();
         if (tid < S) {  // warp w: quarter w of the head
@@ -364,7 +376,7 @@ __device__ __forceinline__ void gdn_quarter_body(const GdnArgs& a, int head, int
                 const float* q4 = a.ss_scr + ((size_t) c * hv + head) * 4;
                 const float ss = __fadd_rn(__fadd_rn(__fadd_rn(ld_cg(q4), ld_cg(q4 + 1)), ld_cg(q4 + 2)), ld_cg(q4 + 3));
                 const float ocj = ld_cg(a.o_scr + ((size_t) c * hv + head) * S + j);
-                const float z = ld_cg(a.proj + (size_t) c * a.proj_stride + off_z + head * S + j);
+                const float z = z_in[c];
                 const float scale = rsqrtf(__fadd_rn(__fdiv_rn(ss, (float) S), a.eps));
                 const float yv = __fmul_rn(__fmul_rn(__fmul_rn(ocj, scale), a.gamma[j]), silu_dev(z));
                 if (a.y) a.y[(size_t) c * hv * S + head * S + j] = yv;
@@ -382,7 +394,7 @@ __device__ __forceinline__ void gdn_quarter_body(const GdnArgs& a, int head, int
 // position has exactly one owning chunk). Column c attends tokens <= pos + c. Partials: o
 // [n_head][NC][max_chunks][256], (m, l) [n_head][NC][max_chunks].
 template <int NC>
-__device__ __forceinline__ void attn_chunk_body(const AttnArgs& a, int pos, int chunk, int kvh, float* sm) {
+__device__ __noinline__ void attn_chunk_body(const AttnArgs& a, int pos, int chunk, int kvh, float* sm) {
     constexpr int G = kGqa;
     const int t0 = chunk * kChunkA;
     if (pos < 0 || pos + NC > a.max_ctx) {  // uniform over the block
@@ -394,7 +406,7 @@ __device__ __forceinline__ void attn_chunk_body(const AttnArgs& a, int pos, int 
     float (*sc)[NC][kChunkA] = reinterpret_cast<float (*)[NC][kChunkA]>(sm + G * NC * kHdA);  // [G][NC][256]
     float* rot = sm + 2 * G * NC * kHdA;                                // [8 warps][256]
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    __syncthreads();  // scratch reuse across items
+    block_sync256();  // scratch reuse across items
     // ---- prologue: one warp per head vector (lane holds dims j*32 + lane), the block256 order ----
     for (int job = warp; job < G * NC + NC; job += 8) {
         const bool is_q = job < G * NC;
@@ -454,7 +466,7 @@ __device__ __forceinline__ void attn_chunk_body(const AttnArgs& a, int pos, int 
             }
         }
     }
-    __syncthreads();  // q in smem; this block's K/V stores visible to its threads
+    block_sync256();  // q in smem; this block's K/V stores visible to its threads
     const __half* kbase = a.kc + ((size_t) kvh * a.max_ctx + t0) * kHdA;
     const __half* vbase = a.vc + ((size_t) kvh * a.max_ctx + t0) * kHdA;
     const int ntok = min(kChunkA, pos + NC - t0);  // tokens any column may read in this chunk
@@ -490,7 +502,7 @@ __device__ __forceinline__ void attn_chunk_body(const AttnArgs& a, int pos, int 
                 if (lane == 0) sc[g][c][t] = (t0 + t <= pos + c) ? __fmul_rn(d, a.scale) : -INFINITY;
             }
     }
-    __syncthreads();
+    block_sync256();
     // phase 2: per (head, column) the chunk max and the exponentials, one warp per pair
     for (int pair = warp; pair < G * NC; pair += 8) {
         const int g = pair / NC, c = pair % NC;
@@ -510,7 +522,7 @@ __device__ __forceinline__ void attn_chunk_body(const AttnArgs& a, int pos, int 
             ml[1] = l;
         }
     }
-    __syncthreads();
+    block_sync256();
     // phase 3: weighted V, thread = output dim
     float acc[G][NC];
 #pragma unroll
@@ -534,7 +546,7 @@ __device__ __forceinline__ void attn_chunk_body(const AttnArgs& a, int pos, int 
 // Combine of head h, column c: the chunks merged in order, then the Q8_1 blocks of o * sigmoid(gate)
 // (sig_mul_quant_kernel, src/qwythos.cpp:692-704; one warp = one 32-dim block).
 template <int NC>
-__device__ __forceinline__ void combine_body(const AttnArgs& a, int pos, int h, int c) {
+__device__ __noinline__ void combine_body(const AttnArgs& a, int pos, int h, int c) {
     const int d = threadIdx.x;
     if (pos < 0 || pos + NC > a.max_ctx) return;  // recorded by the chunk body
     const int nchunks = (pos + c) / kChunkA + 1;
@@ -558,18 +570,18 @@ __device__ __forceinline__ void combine_body(const AttnArgs& a, int pos, int h, 
 
 // MTP draft input of column c: Q8_1 of [enorm(emb(dtok)) | hnorm(h)] (src/qwythos.cpp:1316-1334); the
 // draft's argmax slots are cleared here. sm: H + H/4 floats.
-__device__ __forceinline__ void draft_prep_body(const DraftPrepArgs& a, Ctrl* ctrl, int c, float* sm, float* red) {
+__device__ __noinline__ void draft_prep_body(const DraftPrepArgs& a, Ctrl* ctrl, int c, float* sm, float* red) {
     const int H = a.H;
     float* e = sm;
     float* ep = sm + H;
-    __syncthreads();  // scratch reuse across items
+    block_sync256();  // scratch reuse across items
     if (c == 0 && threadIdx.x == 0) {
         ctrl->damax[0] = 0ull;
         ctrl->damax[1] = 0ull;
     }
     const int tok = read_token(ctrl, 1, c, a.V);
     dequant_row(a.emb + (size_t) tok * ((size_t) (H / 256) * 210), H, e, ep);
-    __syncthreads();
+    block_sync256();
     const float inv_e = rms_inv(block256_partials_sum<true>(ep, H / 4, red), H, a.eps);
     const float inv_h = rms_inv(block256_partials_sum(a.hsave_p + (size_t) c * (H / 4), H / 4, red), H, a.eps);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -583,7 +595,7 @@ __device__ __forceinline__ void draft_prep_body(const DraftPrepArgs& a, Ctrl* ct
 }
 
 // Control ops (thread 0 of one block).
-__device__ __forceinline__ void ctrl_body(const CtrlArgs& a, Ctrl* ctrl) {
+__device__ __noinline__ void ctrl_body(const CtrlArgs& a, Ctrl* ctrl) {
     volatile Ctrl* v = ctrl;
     if (a.kind == CTRL_SINGLE) {
         // emit the trunk argmax and advance (src/qwythos.cpp:1803-1811, :3184-3192)

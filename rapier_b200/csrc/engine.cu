@@ -142,6 +142,8 @@ struct TensorRec {
 struct Program {
     std::vector<POp> ops;
     POp* dev = nullptr;
+    std::vector<GemvEnt> gemvs;  // its GEMVs in order (the persistent kernel's weight cursors)
+    GemvEnt* gdev = nullptr;
     int nc = 1;
     cudaGraphExec_t graph = nullptr;
     int kernels = 0;  // kernels one run launches
@@ -189,8 +191,9 @@ struct EngineImpl {
     Program progs[P_COUNT];
     bool persistent = false;
     PSync* psync = nullptr;
-    int p_grid = 0, p_stages = 0, p_region = 0;
-    size_t p_smem = 0;
+    int p_grid = 0, p_stages[2] = {0, 0}, p_region[2] = {0, 0};  // per column count (1, 2)
+    int p_l2pf = 0;  // bytes of the next GEMV each CTA asks L2 for when an op starts
+    size_t p_smem[2] = {0, 0};
     double probe_weight_bytes[2] = {0, 0}, probe_algo_bytes[2] = {0, 0};
     int probe_gemvs = 0;
     std::vector<void*> allocs;
@@ -227,7 +230,7 @@ struct EngineImpl {
     int finalize(Program& P, int nc);
     template <int NC>
     cudaError_t launch_op(const POp& op);
-    cudaError_t run(const Program& P, int until = 0, int max_iters = 1);
+    cudaError_t run(const Program& P, int until = 0, int max_iters = 1, unsigned long long* trace = nullptr);
     void set_ctrl(const Ctrl& host_fields);
     int check_abort(const char* what);
 };
@@ -606,50 +609,58 @@ void EngineImpl::add_probe(std::vector<POp>& v, int nc) {
     probe_gemvs = n;
 }
 
-// The executor: persistent unless RK_ENGINE_MODE=graph, or unless the device cannot hold one CTA per SM
-// with at least two ring slots per warp. RK_PERSIST_STAGES forces the ring depth (a tuning knob, like the
-// reference's QWYTHOS_Q6ROWS sweep knob, src/native_mmvq.cu:3648-3651).
+// The executor: persistent unless RK_ENGINE_MODE=graph, or unless the device cannot hold one 512-thread
+// CTA per SM with at least two ring slots per warp. The shared-memory region (staged activations or op
+// scratch) and the ring depth are set per column count. Tuning knobs (like the reference's
+// QWYTHOS_Q6ROWS sweep knob, src/native_mmvq.cu:3648-3651): RK_PERSIST_STAGES caps the ring depth,
+// RK_PERSIST_L2PF_KB sets the per-CTA L2 prefetch of the next GEMV (KB, 0 = off).
 int EngineImpl::setup_executor() {
     const char* mode = std::getenv("RK_ENGINE_MODE");
     persistent = !(mode && std::strcmp(mode, "graph") == 0);
     if (!persistent) return RK_OK;
-    int optin = 0, sms = 0;
-    if ((err = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) != cudaSuccess) return RK_ECUDA;
+    int sms = 0, optin = 0;
     if ((err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return RK_ECUDA;
-    const int max_in = FF > 2 * H ? FF : 2 * H;
-    size_t region = (size_t) 2 * (max_in / 32) * 48;
-    if (op_scratch_bytes(2, H) > region) region = op_scratch_bytes(2, H);
-    region = (region + 127) & ~(size_t) 127;
-    cudaFuncAttributes fa1 = {}, fa2 = {};
-    if ((err = cudaFuncGetAttributes(&fa1, persistent_kernel<1>)) != cudaSuccess) return RK_ECUDA;
-    if ((err = cudaFuncGetAttributes(&fa2, persistent_kernel<2>)) != cudaSuccess) return RK_ECUDA;
-    const long long stat = (long long) (fa1.sharedSizeBytes > fa2.sharedSizeBytes ? fa1.sharedSizeBytes : fa2.sharedSizeBytes);
-    const long long avail = (long long) optin - stat - (long long) persistent_smem_bytes((int) region, 0);
-    int stages = (int) (avail / ((long long) kMmvqWarps * kQ6Tile));
-    if (stages > kMmvqMaxStages) stages = kMmvqMaxStages;
+    if ((err = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) != cudaSuccess)
+        return RK_ECUDA;
+    int cap = kMmvqMaxStages;
     if (const char* st = std::getenv("RK_PERSIST_STAGES")) {
         const int v = std::atoi(st);
-        if (v >= 2 && v <= stages) stages = v;
+        if (v >= 2 && v <= kMmvqMaxStages) cap = v;
     }
-    if (stages < 2) {
-        persistent = false;
-        return RK_OK;
+    p_l2pf = 256 * 1024;
+    if (const char* pf = std::getenv("RK_PERSIST_L2PF_KB")) {
+        const int v = std::atoi(pf);
+        if (v >= 0 && v <= 4096) p_l2pf = v * 1024;
     }
-    p_smem = persistent_smem_bytes((int) region, stages);
-    if ((err = cudaFuncSetAttribute(persistent_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) p_smem)) != cudaSuccess)
-        return RK_ECUDA;
-    if ((err = cudaFuncSetAttribute(persistent_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) p_smem)) != cudaSuccess)
-        return RK_ECUDA;
-    int occ1 = 0, occ2 = 0;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ1, persistent_kernel<1>, 256, p_smem);
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ2, persistent_kernel<2>, 256, p_smem);
-    if (occ1 < 1 || occ2 < 1) {
-        persistent = false;
-        return RK_OK;
+    const int max_in = FF > 2 * H ? FF : 2 * H;
+    for (int nc = 1; nc <= 2; ++nc) {
+        const void* fn = nc == 1 ? (const void*) persistent_kernel<1> : (const void*) persistent_kernel<2>;
+        cudaFuncAttributes fa = {};
+        if ((err = cudaFuncGetAttributes(&fa, fn)) != cudaSuccess) return RK_ECUDA;
+        size_t region = (size_t) nc * (max_in / 32) * 48;
+        if (op_scratch_bytes(nc, H) > region) region = op_scratch_bytes(nc, H);
+        region = (region + 127) & ~(size_t) 127;
+        const long long budget = (long long) optin - (long long) fa.sharedSizeBytes;
+        int stages = (int) ((budget - (long long) persistent_smem_bytes((int) region, 0)) / ((long long) kPWarps * kQ6Tile));
+        if (stages > cap) stages = cap;
+        if (stages < 2) {
+            persistent = false;
+            return RK_OK;
+        }
+        const size_t smem = persistent_smem_bytes((int) region, stages);
+        if ((err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem)) != cudaSuccess)
+            return RK_ECUDA;
+        int occ = 0;
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, kPWarps * 32, smem);
+        if (occ < 1) {
+            persistent = false;
+            return RK_OK;
+        }
+        p_stages[nc - 1] = stages;
+        p_region[nc - 1] = (int) region;
+        p_smem[nc - 1] = smem;
     }
     p_grid = sms;
-    p_stages = stages;
-    p_region = (int) region;
     return RK_OK;
 }
 
@@ -680,11 +691,26 @@ cudaError_t EngineImpl::launch_op(const POp& op) {
 // Upload a program; in graph mode also capture its launches.
 int EngineImpl::finalize(Program& P, int nc) {
     P.nc = nc;
-    for (const POp& op : P.ops)
-        if (op.kind == POP_GEMV && !gemv_combo_supported(op.pro, op.epi)) return RK_EINVAL;
+    for (const POp& op : P.ops) {
+        if (op.kind != POP_GEMV) continue;
+        if (!gemv_combo_supported(op.pro, op.epi)) return RK_EINVAL;
+        P.gemvs.push_back({op.g.w, op.g.n_out / 4, op.g.n_in / 1024});
+    }
+    if (P.gemvs.size() > (size_t) kMaxGemvOps) return RK_EINVAL;
+    // the first GEMV after each op (wrapping to the program's first for the last ones)
+    {
+        int gi = (int) P.gemvs.size();
+        for (int j = (int) P.ops.size() - 1; j >= 0; --j) {
+            P.ops[j].next_gemv = gi < (int) P.gemvs.size() ? gi : (P.gemvs.empty() ? -1 : 0);
+            if (P.ops[j].kind == POP_GEMV) --gi;
+        }
+    }
     P.dev = alloc<POp>(P.ops.size());
+    P.gdev = alloc<GemvEnt>(P.gemvs.size() ? P.gemvs.size() : 1);
     if (err == cudaSuccess)
         err = cudaMemcpyAsync(P.dev, P.ops.data(), sizeof(POp) * P.ops.size(), cudaMemcpyHostToDevice, s);
+    if (err == cudaSuccess && !P.gemvs.empty())
+        err = cudaMemcpyAsync(P.gdev, P.gemvs.data(), sizeof(GemvEnt) * P.gemvs.size(), cudaMemcpyHostToDevice, s);
     if (err == cudaSuccess) err = cudaStreamSynchronize(s);
     if (err != cudaSuccess) return RK_ECUDA;
     if (persistent) {
@@ -709,12 +735,12 @@ int EngineImpl::finalize(Program& P, int nc) {
 
 // Enqueue one run of a program. Persistent: until > 0 repeats it while ctrl->n_emitted < until, at most
 // max_iters times. Graph mode runs it once (the caller loops).
-cudaError_t EngineImpl::run(const Program& P, int until, int max_iters) {
+cudaError_t EngineImpl::run(const Program& P, int until, int max_iters, unsigned long long* trace) {
     if (!persistent) return cudaGraphLaunch(P.graph, s);
     cudaLaunchConfig_t c = {};
     c.gridDim = dim3((unsigned) p_grid);
-    c.blockDim = dim3(256);
-    c.dynamicSmemBytes = p_smem;
+    c.blockDim = dim3(kPWarps * 32);
+    c.dynamicSmemBytes = p_smem[P.nc - 1];
     c.stream = s;
     cudaLaunchAttribute at[1];
     at[0].id = cudaLaunchAttributeCooperative;
@@ -722,10 +748,13 @@ cudaError_t EngineImpl::run(const Program& P, int until, int max_iters) {
     c.attrs = at;
     c.numAttrs = 1;
     const POp* prog = P.dev;
-    const int nops = (int) P.ops.size();
+    const GemvEnt* gt = P.gdev;
+    const int nops = (int) P.ops.size(), ng = (int) P.gemvs.size();
     if (P.nc == 1)
-        return cudaLaunchKernelEx(&c, persistent_kernel<1>, prog, nops, ctrl, psync, p_stages, p_region, until, max_iters);
-    return cudaLaunchKernelEx(&c, persistent_kernel<2>, prog, nops, ctrl, psync, p_stages, p_region, until, max_iters);
+        return cudaLaunchKernelEx(&c, persistent_kernel<1>, prog, nops, gt, ng, ctrl, psync, p_stages[0], p_region[0],
+                                  p_l2pf, until, max_iters, trace);
+    return cudaLaunchKernelEx(&c, persistent_kernel<2>, prog, nops, gt, ng, ctrl, psync, p_stages[1], p_region[1],
+                              p_l2pf, until, max_iters, trace);
 }
 
 // Host writes of the control fields go through a ring of pinned slots so that queued copies never
@@ -1073,6 +1102,49 @@ int rk_engine_probe_gemv(rk_engine* e, int ncols, int iters, rk_probe_result* ou
     out->weight_bytes = E.probe_weight_bytes[ncols - 1];
     out->algo_bytes = E.probe_algo_bytes[ncols - 1];
     return RK_OK;
+}
+
+int rk_engine_trace(rk_engine* e, int program, double* stamps_us, int* kinds, int max_ops, double* cta_us,
+                    int max_ctas) {
+    const char* what = "rk_engine_trace";
+    if (!e || !stamps_us || !kinds) return set_error(RK_EINVAL, "%s: null argument", what);
+    EngineImpl& E = e->impl;
+    if (!E.persistent) return set_error(RK_EUNSUPPORTED, "%s: needs the persistent executor", what);
+    static const int ids[] = {P_SINGLE, P_ROUND, P_PROBE1, P_PROBE2, P_TRUNK2};
+    if (program < 0 || program > 4) return set_error(RK_EINVAL, "%s: program must be 0..4", what);
+    const Program& P = E.progs[ids[program]];
+    const int nops = (int) P.ops.size();
+    if (nops == 0) return set_error(RK_EINVAL, "%s: the engine has no such program (built without MTP)", what);
+    if (program == 0 || program == 1 || program == 4) {
+        Ctrl h = {};
+        cudaMemcpy(&h, E.ctrl, sizeof h, cudaMemcpyDeviceToHost);
+        if (h.pos < 0 || h.pos + 2 >= E.cfg.max_ctx) return set_error(RK_ERANGE, "%s: no room left in the cache", what);
+    }
+    const size_t entries = (size_t) 4 * nops + (size_t) 2 * nops * E.p_grid;
+    unsigned long long* dt = nullptr;
+    if (cudaMalloc(&dt, sizeof(unsigned long long) * entries) != cudaSuccess)
+        return set_error(RK_ENOMEM, "%s: out of device memory", what);
+    cudaError_t ce = cudaMemsetAsync(dt, 0, sizeof(unsigned long long) * entries, E.s);
+    if (ce == cudaSuccess) ce = E.run(P, 0, 1, dt);
+    std::vector<unsigned long long> h(entries);
+    if (ce == cudaSuccess) ce = cudaMemcpyAsync(h.data(), dt, h.size() * 8, cudaMemcpyDeviceToHost, E.s);
+    if (ce == cudaSuccess) ce = cudaStreamSynchronize(E.s);
+    cudaFree(dt);
+    if (ce != cudaSuccess) return set_error(RK_ECUDA, "%s: %s", what, cudaGetErrorString(ce));
+    if (int rc = E.check_abort(what)) return rc;
+    const int n = nops < max_ops ? nops : max_ops;
+    for (int j = 0; j < n; ++j) {
+        for (int k = 0; k < 4; ++k) stamps_us[4 * j + k] = (double) (h[4 * (size_t) j + k] - h[0]) * 1e-3;
+        kinds[j] = P.ops[j].kind == POP_GEMV ? 100 + P.ops[j].epi : P.ops[j].kind;
+        if (cta_us)
+            for (int b = 0; b < max_ctas; ++b)
+                for (int k = 0; k < 2; ++k) {
+                    const size_t src = (size_t) 4 * nops + ((size_t) j * E.p_grid + b) * 2 + k;
+                    cta_us[((size_t) j * max_ctas + b) * 2 + k] =
+                        b < E.p_grid ? (double) (h[src] - h[0]) * 1e-3 : -1.0;
+                }
+    }
+    return nops;
 }
 
 size_t rk_engine_device_bytes(const rk_engine* e) { return e ? e->impl.bytes : 0; }

@@ -86,9 +86,9 @@ __device__ __forceinline__ float block256_partials_sum(const float* partials, in
     for (int p = t; p < nslots; p += 256) part = __fadd_rn(part, SMEM ? partials[p] : __ldcg(partials + p));
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) part = __fadd_rn(part, __shfl_down_sync(0xffffffffu, part, off));
-    __syncthreads();  // `red` may still be read by a previous call
+    block_sync256();  // `red` may still be read by a previous call
     if ((t & 31) == 0) red[t >> 5] = part;
-    __syncthreads();
+    block_sync256();
     float ss = red[0];
 #pragma unroll
     for (int w = 1; w < 8; ++w) ss = __fadd_rn(ss, red[w]);
@@ -133,18 +133,18 @@ __device__ __forceinline__ void xstage_put_warp(const XStage& s, int g, int code
     if (lane == 0) s.meta[g] = make_float4(half_bits_to_float(ds), __int_as_float(32 * s0), __int_as_float(32 * s1), 0.0f);
 }
 
-// Build every column's staged activations. All 256 threads participate (contains __syncthreads).
+// Build every column's staged activations. Threads 0..255 participate (contains block_sync256).
 // PRO_Q8: one thread per Q8_1 block (9 ints) -> planes + meta.
 // PRO_RMS: the reference's rms_quant_apply (inv from the partials, v = x * w * inv, Q8_1 per 32 values)
 // with one thread per 16-value half block: every load is issued before any arithmetic, the two halves of
 // a block meet through one shuffle (amax), and each half's codes go to its plane. The codes and scale are
 // those of the standalone kernel (same q8_* rules on the same fp32 values).
 template <int NC, int PRO>
-__device__ __forceinline__ void mmvq_build_x(const MmvqParams& p, uint8_t* xsm, float* red) {
+__device__ __noinline__ void mmvq_build_x(const MmvqParams& p, uint8_t* xsm, float* red) {
     const int ng = p.n_in >> 5;
     if constexpr (PRO == PRO_Q8) {
         const size_t col_bytes = (size_t) ng * 36;
-        for (int idx = threadIdx.x; idx < NC * ng; idx += blockDim.x) {
+        for (int idx = threadIdx.x; idx < NC * ng; idx += 256) {
             const int c = idx / ng, g = idx - c * ng;
             const int* blk = reinterpret_cast<const int*>(p.xq + (size_t) c * col_bytes + (size_t) g * 36);
             const uint32_t ds = (uint32_t) __ldcg(blk);
@@ -158,11 +158,27 @@ __device__ __forceinline__ void mmvq_build_x(const MmvqParams& p, uint8_t* xsm, 
             s.meta[g] = make_float4(half_bits_to_float(ds), __int_as_float(32 * s0), __int_as_float(32 * s1), 0.0f);
         }
     } else {
+        const int items = NC * ng * 2;  // half blocks; the two halves of a block sit on adjacent lanes
+        // The first pass's x / weight loads go out before the partial sums are reduced (they do not
+        // depend on them), so the two global round trips overlap.
+        float4 xv[4], wv[4];
+        auto load = [&](int it) {
+            const int c = it / (2 * ng);
+            const int rem = it - c * 2 * ng;
+            const int i0 = ((rem >> 1) << 5) + ((rem & 1) << 4);
+            const float4* xp4 = reinterpret_cast<const float4*>(p.xa + (size_t) c * p.n_in + i0);
+            const float4* wp4 = reinterpret_cast<const float4*>(p.xb + i0);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                xv[k] = __ldcg(xp4 + k);
+                wv[k] = wp4[k];
+            }
+        };
+        if ((int) threadIdx.x < items) load((int) threadIdx.x);
         float inv[NC];
 #pragma unroll
         for (int c = 0; c < NC; ++c)
             inv[c] = rms_inv(block256_partials_sum(p.pin + (size_t) c * (p.n_in / 4), p.n_in / 4, red), p.n_in, p.eps);
-        const int items = NC * ng * 2;  // half blocks; the two halves of a block sit on adjacent lanes
         for (int base = 0; base < items; base += 256) {
             const int it = base + (int) threadIdx.x;
             const bool live = it < items;
@@ -172,14 +188,7 @@ __device__ __forceinline__ void mmvq_build_x(const MmvqParams& p, uint8_t* xsm, 
             const int i0 = (g << 5) + (h << 4);
             float v[16];
             if (live) {
-                const float4* xp4 = reinterpret_cast<const float4*>(p.xa + (size_t) c * p.n_in + i0);
-                const float4* wp4 = reinterpret_cast<const float4*>(p.xb + i0);
-                float4 xv[4], wv[4];
-#pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    xv[k] = __ldcg(xp4 + k);
-                    wv[k] = wp4[k];
-                }
+                if (base > 0) load(it);
                 float invc = inv[0];
 #pragma unroll
                 for (int cc = 1; cc < NC; ++cc)
@@ -320,10 +329,11 @@ __host__ __device__ __forceinline__ int argmax_key_row(unsigned long long k) { r
 
 // best[c] (EPI_ARGMAX): the warp's running packed (value, ~row) maximum of column c; the caller issues one
 // atomicMax per warp and column after its last unit (the reference's atomicMax on (monotonic bits, n-1-idx),
-// src/qwythos.cpp:70-84, with the lowest-index tie rule).
+// src/qwythos.cpp:70-84, with the lowest-index tie rule). resv (EPI_RES): lane c < NC holds the residual
+// rows of column c for this unit, loaded by mmvq_res_prefetch when the unit started.
 template <int NC, int EPI>
 __device__ __forceinline__ void mmvq_epilogue(const MmvqParams& p, int unit, int lane, float (&acc)[NC][4],
-                                              unsigned long long (&best)[NC]) {
+                                              unsigned long long (&best)[NC], const float (&resv)[4]) {
 #pragma unroll
     for (int c = 0; c < NC; ++c)
 #pragma unroll
@@ -349,28 +359,6 @@ __device__ __forceinline__ void mmvq_epilogue(const MmvqParams& p, int unit, int
                         best[c] = k > best[c] ? k : best[c];
                     }
         }
-        if constexpr (EPI == EPI_SWIGLU) {
-            // units [0, half/4) are up rows, [half/4, half/2) gate rows; block group = 8 units of each
-            const int half = p.n_out >> 1;
-            const int u_half = unit < (half >> 2) ? unit : unit - (half >> 2);
-            const int grp = u_half >> 3;
-            __threadfence();  // every lane's y stores, before the count that publishes them
-            __syncwarp();
-            unsigned last = 0;
-            if (lane == 0) last = atomicAdd(p.cnt + grp, 1u) == 15u;
-            last = __shfl_sync(0xffffffffu, last, 0);
-            if (last) {
-                __threadfence();
-                const int i = (grp << 5) + lane;
-#pragma unroll
-                for (int c = 0; c < NC; ++c) {
-                    const float up = __ldcg(p.y + (size_t) c * p.y_stride + i);
-                    const float g = __ldcg(p.y + (size_t) c * p.y_stride + half + i);
-                    q8_1_warp_store(swiglu_value(up, g), p.q8out + ((size_t) c * (half >> 5) + grp) * 36, lane);
-                }
-                if (lane == 0) p.cnt[grp] = 0u;
-            }
-        }
     } else {  // EPI_RES (y = acc + res) / EPI_STORE_P (y = acc), both with the 4-row partials
         if (lane < NC) {
 #pragma unroll
@@ -380,13 +368,60 @@ __device__ __forceinline__ void mmvq_epilogue(const MmvqParams& p, int unit, int
                     float part = 0.0f;
 #pragma unroll
                     for (int r = 0; r < 4; ++r) {
-                        const float v =
-                            EPI == EPI_RES ? __fadd_rn(acc[c][r], __ldcg(p.res + (size_t) c * p.res_stride + row0 + r)) : acc[c][r];
+                        const float v = EPI == EPI_RES ? __fadd_rn(acc[c][r], resv[r]) : acc[c][r];
                         y[r] = v;
                         part = __fmaf_rn(v, v, part);
                     }
                     p.pout[(size_t) c * p.pout_stride + unit] = part;
                 }
+        }
+    }
+}
+
+// EPI_RES: the residual rows of a unit, issued when the unit starts so the load overlaps its tiles.
+template <int NC, int EPI>
+__device__ __forceinline__ void mmvq_res_prefetch(const MmvqParams& p, int unit, int lane, float (&resv)[4]) {
+    if constexpr (EPI == EPI_RES) {
+        if (lane < NC) {
+            const float* r = p.res + (size_t) lane * p.res_stride + (size_t) unit * 4;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) resv[k] = __ldcg(r + k);
+        }
+    }
+}
+
+// EPI_SWIGLU, after a warp's units [first, end) (stride `stride`) are written: one fence, then one arrival
+// per unit (issued by different lanes at once); for every 32-position block whose 16 units (8 up + 8 gate)
+// are done, the warp whose arrival completed it writes the Q8_1 block of silu(gate) * up (the down GEMV's
+// input; swiglu_quant_kernel, src/qwythos.cpp:676-689) and re-zeroes the counter.
+template <int NC>
+__device__ __forceinline__ void mmvq_swiglu_finish(const MmvqParams& p, int first, int stride, int end, int lane) {
+    if (first >= end) return;
+    __threadfence();
+    __syncwarp();
+    const int half = p.n_out >> 1;
+    for (int base = first; base < end; base += 32 * stride) {
+        const int u = base + lane * stride;
+        int grp = 0;
+        bool last = false;
+        if (u < end) {
+            grp = (u < (half >> 2) ? u : u - (half >> 2)) >> 3;
+            last = atomicAdd(p.cnt + grp, 1u) == 15u;
+        }
+        unsigned m = __ballot_sync(0xffffffffu, last);
+        if (m) __threadfence();
+        while (m) {
+            const int src = __ffs(m) - 1;
+            m &= m - 1;
+            const int g = __shfl_sync(0xffffffffu, grp, src);
+            const int i = (g << 5) + lane;
+#pragma unroll
+            for (int c = 0; c < NC; ++c) {
+                const float up = __ldcg(p.y + (size_t) c * p.y_stride + i);
+                const float gt = __ldcg(p.y + (size_t) c * p.y_stride + half + i);
+                q8_1_warp_store(swiglu_value(up, gt), p.q8out + ((size_t) c * (half >> 5) + g) * 36, lane);
+            }
+            if (lane == 0) p.cnt[g] = 0u;
         }
     }
 }
@@ -445,6 +480,8 @@ __global__ void __launch_bounds__(kMmvqWarps * 32, 2) mmvq_packed_kernel(const M
 
     int s = 0, kc = 0, unit = ubeg + warp;
     uint32_t parity = 0;
+    float resv[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    if (ntiles > 0) mmvq_res_prefetch<NC, EPI>(p, unit, lane, resv);
     for (int i = 0; i < ntiles; ++i) {
         const bool landed = mbar_wait_bounded(smem_u32(bars + s), parity);
         if (!__all_sync(0xffffffffu, landed)) break;
@@ -471,15 +508,17 @@ __global__ void __launch_bounds__(kMmvqWarps * 32, 2) mmvq_packed_kernel(const M
             parity ^= 1u;
         }
         if (++kc == KC) {
-            mmvq_epilogue<NC, EPI>(p, unit, lane, acc, best);
+            mmvq_epilogue<NC, EPI>(p, unit, lane, acc, best, resv);
 #pragma unroll
             for (int c = 0; c < NC; ++c)
 #pragma unroll
                 for (int r = 0; r < 4; ++r) acc[c][r] = 0.0f;
             kc = 0;
             unit += kMmvqWarps;
+            if (unit < uend) mmvq_res_prefetch<NC, EPI>(p, unit, lane, resv);
         }
     }
+    if constexpr (EPI == EPI_SWIGLU) mmvq_swiglu_finish<NC>(p, ubeg + warp, kMmvqWarps, unit, lane);
     if constexpr (EPI == EPI_ARGMAX) {
 #pragma unroll
         for (int c = 0; c < NC; ++c)

@@ -3,18 +3,28 @@
 // * op_kernel<NC>: one launch per non-GEMV op (grid = the op's largest item count, one item per block,
 //   blocks past the op's live item count return); GEMV ops launch mmvq_packed_kernel. The engine
 //   captures the launches of a program in a CUDA graph.
-// * persistent_kernel<NC>: the whole program in one cooperative launch, one 256-thread CTA per SM. Ops
-//   run in program order separated by grid barriers; the items of a non-GEMV op are dealt to CTAs
-//   round-robin. The weight tiles of every GEMV stream through per-warp rings of `stages` 3360-B slots
-//   (one 1-D bulk copy and one mbarrier per slot, lane 0 issuing) whose producer cursor walks the
-//   program's GEMV sequence ahead of the consumer: the slots a warp frees at the end of one GEMV are
-//   refilled with the next GEMV's tiles, so HBM keeps streaming through the op's tail, the grid barrier,
-//   the next prologue and the non-GEMV ops in between. With `until` > 0 the program repeats while
-//   ctrl->n_emitted < until, at most `max_iters` times (a whole generation in one launch), and the
-//   producer wraps around to the program's first GEMV.
+// * persistent_kernel<NC>: the whole program in one cooperative launch, one 512-thread CTA per SM. Ops
+//   run in program order separated by grid barriers. All 16 warps consume GEMV tiles (16 warps per SM
+//   hide the latency of the tile decode) against one staged copy of the activations; the 256-thread
+//   GEMV prologue and the non-GEMV op bodies run on warps 0..7 (named barrier 1), whose items are dealt
+//   to CTAs round-robin.
+//   Weight streaming runs ahead of the op boundaries: each warp walks the program's sequence of GEMV
+//   tiles (its units of every GEMV, in order, from a GEMV table in shared memory) with a cursor that
+//   fills a private ring of `stages` 3360-B shared-memory slots by 1-D bulk copies (one mbarrier per
+//   slot). A slot freed by the consumer is refilled at once, so at the end of one GEMV the ring already
+//   holds the next GEMV's first tiles, and HBM keeps streaming through the op's tail, the grid barrier,
+//   the next prologue and the non-GEMV ops in between. Further ahead, when an op starts each CTA asks L2
+//   for the first `l2pf` bytes of its (contiguous) share of the next GEMV's weights with one bulk L2
+//   prefetch, so that GEMV's ring refills find their tiles in L2. With `until` > 0 the program repeats while
+//   ctrl->n_emitted < until, at most `max_iters` times (a whole generation in one launch), and the cursor
+//   wraps around to the program's first GEMV.
 //
 // A GEMV's work split (contiguous unit ranges per CTA, units dealt to warps round-robin) and its per-row
 // arithmetic are those of mmvq_packed_kernel, so both executors write the same bits.
+//
+// Tracing: with a non-null `trace`, CTA 0 records four globaltimer stamps per op of the first pass (op
+// start, prologue done, its own work done, barrier passed) and every CTA its op start and work-done
+// stamps; ncu sees a persistent launch only as a whole.
 //
 // Failure handling: every mbarrier wait and grid-barrier spin is bounded. A CTA that gives up sets the
 // sticky `abort` word and a status bit; every CTA then skips the rest of the program, waits (bounded)
@@ -32,6 +42,16 @@ struct PSync {
     unsigned abort;             // sticky give-up flag, cleared by the host
 };
 
+// One GEMV of a program, as the weight cursors see it (built by the host in program order).
+struct GemvEnt {
+    const uint8_t* w;  // packed tiles
+    int units;         // n_out / 4
+    int KC;            // n_in / 1024: tiles per unit
+};
+static_assert(sizeof(GemvEnt) == 16, "GemvEnt is copied in 16-byte chunks");
+constexpr int kMaxGemvOps = 256;
+constexpr int kPWarps = 16;  // warps of a persistent CTA; all consume GEMV tiles
+
 constexpr unsigned long long kGridSpinNs = 1000000000ull;  // a grid barrier gives up after 1 s
 
 __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p) {
@@ -41,6 +61,9 @@ __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long
 }
 __device__ __forceinline__ unsigned ld_volatile_u32(const unsigned* p) {
     return *reinterpret_cast<const volatile unsigned*>(p);
+}
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 __device__ __forceinline__ unsigned long long globaltimer_ns() {
     unsigned long long t;
@@ -54,8 +77,8 @@ __device__ __forceinline__ bool grid_sync(PSync* sync, unsigned long long& targe
     __syncthreads();
     target += gridDim.x;
     if (threadIdx.x == 0) {
-        __threadfence();
-        atomicAdd(&sync->arrive, 1ull);
+        // release: this CTA's writes (ordered before by the bar.sync above) become visible with the arrival
+        asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(&sync->arrive), "l"(1ull) : "memory");
         int good = 1;
         unsigned long long t0 = 0;
         for (uint32_t it = 0; ld_acquire_u64(&sync->arrive) < target; ++it) {
@@ -74,7 +97,7 @@ __device__ __forceinline__ bool grid_sync(PSync* sync, unsigned long long& targe
                     break;
                 }
             }
-            __nanosleep(32);
+            if (it >= 256u) __nanosleep(32);
         }
         if (good && ld_volatile_u32(&sync->abort)) good = 0;
         __threadfence();
@@ -85,8 +108,45 @@ __device__ __forceinline__ bool grid_sync(PSync* sync, unsigned long long& targe
 }
 
 // ---------------------------------------------------------------------------------------------------
-// Per-warp weight ring. All lanes keep the same cursor state; lane 0 issues the copies.
+// Weight cursors: position in a warp's tile sequence (GEMV table index gi, -1 when none is left; unit u
+// of the CTA's range [.., uend); k-chunk kc).
 // ---------------------------------------------------------------------------------------------------
+struct Cursor {
+    int gi, u, uend, kc;
+};
+
+__device__ __forceinline__ void cur_seek(Cursor& c, const GemvEnt* gt, int ng, int from, int warp, bool wrap) {
+    for (int n = 0; n < ng; ++n) {
+        int i = from + n;
+        if (i >= ng) {
+            if (!wrap) break;
+            i -= ng;
+        }
+        const int units = gt[i].units;
+        const int ubeg = (int) (((long long) blockIdx.x * units) / gridDim.x);
+        const int uend = (int) (((long long) (blockIdx.x + 1) * units) / gridDim.x);
+        if (ubeg + warp < uend) {
+            c.gi = i;
+            c.u = ubeg + warp;
+            c.uend = uend;
+            c.kc = 0;
+            return;
+        }
+    }
+    c.gi = -1;
+}
+__device__ __forceinline__ void cur_next(Cursor& c, const GemvEnt* gt, int ng, int warp, bool wrap) {
+    if (++c.kc == gt[c.gi].KC) {
+        c.kc = 0;
+        c.u += kPWarps;
+        if (c.u >= c.uend) cur_seek(c, gt, ng, c.gi + 1, warp, wrap);
+    }
+}
+__device__ __forceinline__ const uint8_t* cur_src(const Cursor& c, const GemvEnt* gt) {
+    return gt[c.gi].w + ((size_t) c.u * gt[c.gi].KC + c.kc) * kQ6Tile;
+}
+
+// Per-warp ring state, the same in every lane (lane 0 issues the copies).
 struct WarpPipe {
     uint32_t bar0, ring0;  // shared-memory addresses of the warp's first mbarrier and first slot
     const uint8_t* ring;
@@ -95,63 +155,51 @@ struct WarpPipe {
     uint32_t cpar;  // consumer phase parity
     int ps;         // producer slot
     int inflight;   // tiles issued and not yet consumed
-    int pj, pu, puend, pkc, pKC;  // producer cursor: op (-1: none left), unit, unit end, k-chunk, k-chunks
-    const uint8_t* pw;
     uint64_t pol;
-    int wrap;
+    bool wrap;
+    Cursor pc;  // ring cursor
+    const GemvEnt* gt;
+    int ng;
 };
 
-// Point the producer at the first GEMV op at or after `from` (wrapping once when w.wrap) that has units
-// for this warp.
-__device__ __forceinline__ void pipe_seek(WarpPipe& w, const POp* prog, int nops, int from, int warp) {
-    for (int n = 0; n < nops; ++n) {
-        int j = from + n;
-        if (j >= nops) {
-            if (!w.wrap) break;
-            j -= nops;
-        }
-        const POp& op = prog[j];
-        if (op.kind != POP_GEMV) continue;
-        const int units = op.g.n_out >> 2;
-        const int ubeg = (int) (((long long) blockIdx.x * units) / gridDim.x);
-        const int uend = (int) (((long long) (blockIdx.x + 1) * units) / gridDim.x);
-        if (ubeg + warp < uend) {
-            w.pj = j;
-            w.pu = ubeg + warp;
-            w.puend = uend;
-            w.pkc = 0;
-            w.pKC = op.g.n_in >> 10;
-            w.pw = op.g.w;
-            return;
-        }
-    }
-    w.pj = -1;
-}
-
-__device__ __forceinline__ void pipe_issue(WarpPipe& w, const POp* prog, int nops, int warp, int lane) {
-    if (w.pj < 0) return;
+// The cursor's next tile into the free slot.
+__device__ __forceinline__ void pipe_issue(WarpPipe& w, int warp, int lane) {
+    if (w.pc.gi < 0) return;
     if (lane == 0) {
         const uint32_t bar = w.bar0 + 8u * (uint32_t) w.ps;
         mbar_arrive_expect_tx(bar, kQ6Tile);
-        bulk_g2s(w.ring0 + (uint32_t) (w.ps * kQ6Tile), w.pw + ((size_t) w.pu * w.pKC + w.pkc) * kQ6Tile, kQ6Tile, bar,
-                 w.pol);
+        bulk_g2s(w.ring0 + (uint32_t) (w.ps * kQ6Tile), cur_src(w.pc, w.gt), kQ6Tile, bar, w.pol);
     }
     if (++w.ps == w.stages) w.ps = 0;
     ++w.inflight;
-    if (++w.pkc == w.pKC) {
-        w.pkc = 0;
-        w.pu += kMmvqWarps;
-        if (w.pu >= w.puend) pipe_seek(w, prog, nops, w.pj + 1, warp);
-    }
+    cur_next(w.pc, w.gt, w.ng, warp, w.wrap);
 }
 
-__device__ __forceinline__ bool pipe_wait(const WarpPipe& w) {
-    const bool landed = mbar_wait_bounded(w.bar0 + 8u * (uint32_t) w.cs, w.cpar);
+// Place the cursor at the start and fill the ring.
+__device__ __forceinline__ void pipe_start(WarpPipe& w, int warp, int lane) {
+    cur_seek(w.pc, w.gt, w.ng, 0, warp, w.wrap);
+    for (int k = 0; k < w.stages; ++k) pipe_issue(w, warp, lane);
+}
+
+// Wait (bounded) for the tile `ahead` slots past the consumer's.
+__device__ __forceinline__ bool pipe_wait(const WarpPipe& w, int ahead) {
+    int s = w.cs + ahead;
+    uint32_t par = w.cpar;
+    if (s >= w.stages) {
+        s -= w.stages;
+        par ^= 1u;
+    }
+    const bool landed = mbar_wait_bounded(w.bar0 + 8u * (uint32_t) s, par);
     return __all_sync(0xffffffffu, landed);
+}
+__device__ __forceinline__ const uint8_t* pipe_tile(const WarpPipe& w, int ahead) {
+    int s = w.cs + ahead;
+    if (s >= w.stages) s -= w.stages;
+    return w.ring + (size_t) s * kQ6Tile;
 }
 
 // The warp is done reading the current slot: hand it back to the async proxy and refill it.
-__device__ __forceinline__ void pipe_release(WarpPipe& w, const POp* prog, int nops, int warp, int lane) {
+__device__ __forceinline__ void pipe_release(WarpPipe& w, int warp, int lane) {
     __syncwarp();
     if (lane == 0) fence_proxy_async_smem();
     --w.inflight;
@@ -159,7 +207,7 @@ __device__ __forceinline__ void pipe_release(WarpPipe& w, const POp* prog, int n
         w.cs = 0;
         w.cpar ^= 1u;
     }
-    pipe_issue(w, prog, nops, warp, lane);
+    pipe_issue(w, warp, lane);
 }
 
 // Wait (bounded) for every copy still in flight, so no copy lands after the CTA has exited.
@@ -179,11 +227,12 @@ __device__ __forceinline__ void pipe_drain(WarpPipe& w) {
 // One GEMV op: the prologue builds the staged activations, then every unit of this CTA's range that
 // belongs to this warp is accumulated tile by tile from the ring (mmvq_packed_kernel's loop).
 template <int NC, int PRO, int EPI>
-__device__ __forceinline__ bool p_gemv(const MmvqParams& p, uint8_t* xsm, float* red, WarpPipe& w, const POp* prog,
-                                       int nops) {
+__device__ __forceinline__ bool p_gemv(const MmvqParams& p, uint8_t* xsm, float* red, WarpPipe& w,
+                                       unsigned long long* tp) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    mmvq_build_x<NC, PRO>(p, xsm, red);
+    if (warp < 8) mmvq_build_x<NC, PRO>(p, xsm, red);
     __syncthreads();
+    if (tp != nullptr && threadIdx.x == 0) *tp = globaltimer_ns();
     const int KC = p.n_in >> 10, ng = p.n_in >> 5;
     const int units = p.n_out >> 2;
     const int ubeg = (int) (((long long) blockIdx.x * units) / gridDim.x);
@@ -192,18 +241,20 @@ __device__ __forceinline__ bool p_gemv(const MmvqParams& p, uint8_t* xsm, float*
 #pragma unroll
     for (int c = 0; c < NC; ++c) best[c] = 0ull;
     bool ok = true;
-    for (int unit = ubeg + warp; unit < uend && ok; unit += kMmvqWarps) {
+    int unit = ubeg + warp;
+    for (; unit < uend; unit += kPWarps) {
         float acc[NC][4];
 #pragma unroll
         for (int c = 0; c < NC; ++c)
 #pragma unroll
             for (int r = 0; r < 4; ++r) acc[c][r] = 0.0f;
+        float resv[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        mmvq_res_prefetch<NC, EPI>(p, unit, lane, resv);
         for (int kc = 0; kc < KC; ++kc) {
-            if (!pipe_wait(w)) {
+            if (!pipe_wait(w, 0)) {
                 ok = false;
                 break;
             }
-            const uint8_t* t = w.ring + (size_t) w.cs * kQ6Tile;
             int4 xa[NC], xb[NC];
             float4 xm[NC];
             const int g = (kc << 5) + lane;
@@ -214,11 +265,13 @@ __device__ __forceinline__ bool p_gemv(const MmvqParams& p, uint8_t* xsm, float*
                 xb[c] = xs.hi[g];
                 xm[c] = xs.meta[g];
             }
-            q6_tile<NC>(t, lane, xa, xb, xm, acc);
-            pipe_release(w, prog, nops, warp, lane);
+            q6_tile<NC>(pipe_tile(w, 0), lane, xa, xb, xm, acc);
+            pipe_release(w, warp, lane);
         }
-        if (ok) mmvq_epilogue<NC, EPI>(p, unit, lane, acc, best);
+        if (!ok) break;
+        mmvq_epilogue<NC, EPI>(p, unit, lane, acc, best, resv);
     }
+    if constexpr (EPI == EPI_SWIGLU) mmvq_swiglu_finish<NC>(p, ubeg + warp, kPWarps, unit, lane);
     if constexpr (EPI == EPI_ARGMAX) {
 #pragma unroll
         for (int c = 0; c < NC; ++c)
@@ -234,33 +287,55 @@ __host__ __device__ __forceinline__ bool gemv_combo_supported(int pro, int epi) 
 }
 
 template <int NC>
-__device__ __forceinline__ bool p_gemv_dispatch(const POp& op, uint8_t* xsm, float* red, WarpPipe& w, const POp* prog,
-                                                int nops) {
+__device__ __forceinline__ bool p_gemv_dispatch(const POp& op, uint8_t* xsm, float* red, WarpPipe& w,
+                                                unsigned long long* tp) {
     const MmvqParams& p = op.g;
     if (op.pro == PRO_RMS) {
-        if (op.epi == EPI_STORE) return p_gemv<NC, PRO_RMS, EPI_STORE>(p, xsm, red, w, prog, nops);
-        if (op.epi == EPI_SWIGLU) return p_gemv<NC, PRO_RMS, EPI_SWIGLU>(p, xsm, red, w, prog, nops);
-        return p_gemv<NC, PRO_RMS, EPI_ARGMAX>(p, xsm, red, w, prog, nops);
+        if (op.epi == EPI_STORE) return p_gemv<NC, PRO_RMS, EPI_STORE>(p, xsm, red, w, tp);
+        if (op.epi == EPI_SWIGLU) return p_gemv<NC, PRO_RMS, EPI_SWIGLU>(p, xsm, red, w, tp);
+        return p_gemv<NC, PRO_RMS, EPI_ARGMAX>(p, xsm, red, w, tp);
     }
-    if (op.epi == EPI_RES) return p_gemv<NC, PRO_Q8, EPI_RES>(p, xsm, red, w, prog, nops);
-    return p_gemv<NC, PRO_Q8, EPI_STORE_P>(p, xsm, red, w, prog, nops);
+    if (op.epi == EPI_RES) return p_gemv<NC, PRO_Q8, EPI_RES>(p, xsm, red, w, tp);
+    return p_gemv<NC, PRO_Q8, EPI_STORE_P>(p, xsm, red, w, tp);
 }
+
+// Asynchronous copy of op record j into shared memory (16-byte cp.async chunks, one per thread), so the
+// next op's record arrives while the current op runs.
+__device__ __forceinline__ void op_fetch(const POp* prog, int j, POp* dst) {
+    constexpr int kChunks = (int) (sizeof(POp) / 16);
+    if ((int) threadIdx.x < kChunks) {
+        const uint32_t d = smem_u32(dst) + 16u * threadIdx.x;
+        const char* src = reinterpret_cast<const char*>(prog + j) + 16 * threadIdx.x;
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    }
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 // Shared memory of the persistent kernel: mbarriers | region (staged activations or op scratch) | rings.
 inline size_t persistent_smem_bytes(int region_bytes, int stages) {
-    return (size_t) kMmvqWarps * kMmvqMaxStages * 8 + (size_t) region_bytes + (size_t) kMmvqWarps * stages * kQ6Tile;
+    return (size_t) kPWarps * kMmvqMaxStages * 8 + (size_t) region_bytes + (size_t) kPWarps * stages * kQ6Tile;
 }
 
 template <int NC>
-__global__ void __launch_bounds__(256, 1)
-    persistent_kernel(const POp* __restrict__ prog, int nops, Ctrl* ctrl, PSync* sync, int stages, int region_bytes,
-                      int until, int max_iters) {
+__global__ void __launch_bounds__(kPWarps * 32, 1)
+    persistent_kernel(const POp* __restrict__ prog, int nops, const GemvEnt* __restrict__ gtab, int ngemv, Ctrl* ctrl,
+                      PSync* sync, int stages, int region_bytes, int l2pf, int until, int max_iters,
+                      unsigned long long* trace) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ float red[8];
     __shared__ int flag;
-    __shared__ __align__(16) POp op_sm;
+    __shared__ POp op_sm[2];  // the running op's record and the next one's (fetched while the op runs)
+    __shared__ GemvEnt gt_sm[kMaxGemvOps];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    uint8_t* region = smem + kMmvqWarps * kMmvqMaxStages * 8;
+    uint8_t* region = smem + kPWarps * kMmvqMaxStages * 8;
+    // the GEMV table and the first op record
+    for (int i = (int) threadIdx.x; i < ngemv; i += (int) blockDim.x) {
+        const uint32_t d = smem_u32(&gt_sm[i]);
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(gtab + i) : "memory");
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    }
+    op_fetch(prog, 0, &op_sm[0]);
     WarpPipe w;
     w.bar0 = smem_u32(smem) + (uint32_t) (warp * kMmvqMaxStages * 8);
     w.ring = region + region_bytes + (size_t) warp * stages * kQ6Tile;
@@ -270,42 +345,67 @@ __global__ void __launch_bounds__(256, 1)
     w.cpar = 0u;
     w.ps = 0;
     w.inflight = 0;
-    w.pj = -1;
-    w.pu = w.puend = w.pkc = w.pKC = 0;
-    w.pw = nullptr;
     w.pol = policy_evict_first();
     w.wrap = until > 0;
+    w.pc.gi = -1;
+    w.gt = gt_sm;
+    w.ng = ngemv;
     if (lane == 0) {
         for (int s = 0; s < stages; ++s) mbar_init(w.bar0 + 8u * (uint32_t) s, 1);
         fence_mbar_init();
     }
-    __syncwarp();
+    cp_async_wait_all();
+    __syncthreads();
     unsigned long long target = 0ull;
     bool alive = ld_volatile_u32(&sync->abort) == 0u;
-    if (alive) {
-        pipe_seek(w, prog, nops, 0, warp);
-        for (int k = 0; k < stages; ++k) pipe_issue(w, prog, nops, warp, lane);
-    }
+    if (alive) pipe_start(w, warp, lane);
+    int k = 0;  // ops started; op_sm[k & 1] holds the running op
     for (int iter = 1; alive; ++iter) {
-        for (int j = 0; j < nops && alive; ++j) {
-            {
-                const int* src = reinterpret_cast<const int*>(prog + j);
-                int* dst = reinterpret_cast<int*>(&op_sm);
-                for (int i = threadIdx.x; i < (int) (sizeof(POp) / 4); i += blockDim.x) dst[i] = src[i];
+        for (int j = 0; j < nops && alive; ++j, ++k) {
+            const POp& op = op_sm[k & 1];
+            const int next = j + 1 < nops ? j + 1 : (until > 0 ? 0 : -1);
+            if (next >= 0) op_fetch(prog, next, &op_sm[(k + 1) & 1]);
+            // this CTA's share of the next GEMV into L2 (warp 8: off the prologue's warps)
+            if (threadIdx.x == 256 && l2pf > 0 && op.next_gemv >= 0) {
+                const GemvEnt& e = gt_sm[op.next_gemv];
+                const int ubeg = (int) (((long long) blockIdx.x * e.units) / gridDim.x);
+                const int uend = (int) (((long long) (blockIdx.x + 1) * e.units) / gridDim.x);
+                const size_t bytes = (size_t) (uend - ubeg) * e.KC * kQ6Tile;
+                if (bytes > 0)
+                    prefetch_l2(e.w + (size_t) ubeg * e.KC * kQ6Tile, (uint32_t) (bytes < (size_t) l2pf ? bytes : (size_t) l2pf));
             }
-            __syncthreads();
+            // op trace (CTA 0, first pass): start, prologue done, this CTA's work done, barrier passed;
+            // per CTA (first pass): start, work done
+            unsigned long long* tr = trace != nullptr && blockIdx.x == 0 && iter == 1 ? trace + 4 * j : nullptr;
+            unsigned long long* tc =
+                trace != nullptr && iter == 1 ? trace + 4 * (size_t) nops + ((size_t) j * gridDim.x + blockIdx.x) * 2 : nullptr;
+            if (threadIdx.x == 0) {
+                if (tr != nullptr) tr[0] = tr[1] = globaltimer_ns();
+                if (tc != nullptr) tc[0] = globaltimer_ns();
+            }
             bool ok = true;
-            if (op_sm.kind == POP_GEMV) {
-                ok = p_gemv_dispatch<NC>(op_sm, region, red, w, prog, nops);
+            if (op.kind == POP_GEMV) {
+                ok = p_gemv_dispatch<NC>(op, region, red, w, tr != nullptr ? tr + 1 : nullptr);
             } else {
-                const int pos = ld_cg(op_sm.draft ? &ctrl->dpos : &ctrl->pos);
+                const int pos = ld_cg(op.draft ? &ctrl->dpos : &ctrl->pos);
                 const int rb = ld_cg(&ctrl->rollback);
-                const int items = pop_items<NC>(op_sm, pos);
-                for (int it = (int) blockIdx.x; it < items; it += (int) gridDim.x)
-                    run_item<NC>(op_sm, ctrl, it, pos, rb, reinterpret_cast<float*>(region), red);
+                const int items = pop_items<NC>(op, pos);
+                if (warp < 8)
+                    for (int it = (int) blockIdx.x; it < items; it += (int) gridDim.x)
+                        run_item<NC>(op, ctrl, it, pos, rb, reinterpret_cast<float*>(region), red);
             }
             if (!ok && lane == 0) atomicExch(&sync->abort, 1u);
+            if (tc != nullptr) {
+                __syncthreads();
+                if (threadIdx.x == 0) {
+                    const unsigned long long t = globaltimer_ns();
+                    tc[1] = t;
+                    if (tr != nullptr) tr[2] = t;
+                }
+            }
+            cp_async_wait_all();  // the next record has landed (made visible by the barrier's bar.sync)
             if (j + 1 < nops || until > 0) alive = grid_sync(sync, target, &flag);
+            if (tr != nullptr && threadIdx.x == 0) tr[3] = globaltimer_ns();
         }
         if (!alive || until <= 0 || iter >= max_iters) break;
         if (ld_cg(&ctrl->n_emitted) >= until) break;

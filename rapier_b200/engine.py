@@ -111,6 +111,18 @@ class Engine:
     def device_bytes(self) -> int:
         return _lib.lib().rk_engine_device_bytes(self._h)
 
+    def trace(self, program: int, max_ops: int = 512, max_ctas: int = 296):
+        """Per-op stamps of one pass of a step program (rk_engine_trace): (stamps [n, 4] us, kinds [n],
+        per-CTA [n, max_ctas, 2] us with -1 past the grid)."""
+        st = (C.c_double * (4 * max_ops))()
+        kd = (C.c_int * max_ops)()
+        ct = (C.c_double * (2 * max_ops * max_ctas))()
+        n = _lib.call("rk_engine_trace", self._h, program, st, kd, max_ops, ct, max_ctas)
+        n = min(n, max_ops)
+        return (np.frombuffer(st, dtype=np.float64)[:4 * n].reshape(n, 4).copy(),
+                np.frombuffer(kd, dtype=np.int32)[:n].copy(),
+                np.frombuffer(ct, dtype=np.float64)[:2 * n * max_ctas].reshape(n, max_ctas, 2).copy())
+
     @property
     def mode(self) -> str:
         """"persistent" (one cooperative kernel per step program) or "graph" (one kernel per op)."""
