@@ -231,6 +231,21 @@ typedef struct rk_gen_stats {
 /* Allocates the engine on `device`, generates the synthetic model and builds the step programs.
  * Returns RK_ENOMEM when the device cannot hold it. */
 int rk_engine_create(const rk_model_config* cfg, int device, rk_engine** out);
+/* Tensor parallelism (the reference's optional row split, src/qwythos.cpp:908-935, generalized to 2/4/8
+ * ranks; one process and one GPU per rank). Rank tp_rank of tp_size holds: its k-heads and the v-heads
+ * paired with them (GDN), its q and kv heads (attention), its FF rows of up||gate, its vocabulary shard of
+ * the lm_head; the row-parallel GEMVs (ssm_out, wo, down, eh_proj) take its share of their inputs and
+ * sum the ranks' partials over NVLink peer memory inside the decode kernel, so every rank keeps the same
+ * residual stream; the argmax is global. Every rank's share of a row-parallel input must be a multiple of
+ * 1024 (the 9B geometry: 2 and 4 ranks) else RK_EUNSUPPORTED. Needs the persistent executor. After all
+ * ranks have created their engines: rk_engine_tp_export on each, an exchange of the handles between the
+ * processes, rk_engine_tp_connect on each with all handles (rank-major, rk_tp_handle_bytes each). All
+ * ranks then call generate / step / probe in lockstep; logits hold the rank's vocabulary shard. No
+ * reference counterpart for the API shape. */
+int rk_engine_create_tp(const rk_model_config* cfg, int device, int tp_rank, int tp_size, rk_engine** out);
+size_t rk_tp_handle_bytes(void);
+int rk_engine_tp_export(rk_engine* e, void* handle, size_t bytes);
+int rk_engine_tp_connect(rk_engine* e, const void* handles, size_t bytes_per_rank);
 int rk_engine_destroy(rk_engine* e);
 /* Clears KV caches, GDN states, conv rings and the draft cache (the reference's op:reset,
  * src/qwythos.cpp:2533-2549). */

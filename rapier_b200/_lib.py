@@ -96,6 +96,10 @@ SIGNATURES = {
     "rk_engine_read_tensor": (sz, [vp, i32, vp, sz]),
     "rk_engine_device_bytes": (sz, [vp]),
     "rk_engine_mode": (i32, [vp]),
+    "rk_engine_create_tp": (i32, [C.POINTER(ModelConfig), i32, i32, i32, C.POINTER(vp)]),
+    "rk_tp_handle_bytes": (sz, []),
+    "rk_engine_tp_export": (i32, [vp, vp, sz]),
+    "rk_engine_tp_connect": (i32, [vp, vp, sz]),
     "rk_engine_trace": (i32, [vp, i32, C.POINTER(C.c_double), C.POINTER(C.c_int), i32, C.POINTER(C.c_double), i32]),
     "rk_engine_probe_gemv": (i32, [vp, i32, i32, C.POINTER(ProbeResult)]),
 }

@@ -15,7 +15,8 @@
 namespace rk {
 
 constexpr int kHdA = 256;     // attention head dim
-constexpr int kChunkA = 256;  // flash-decode chunk (tokens)
+constexpr int kSubA = 256;    // tokens scored per pass inside a flash-decode chunk (shared-memory scores)
+constexpr int kMaxChunksA = 64;  // flash-decode chunks per kv head at most (bounds the partials)
 constexpr int kGqa = 4;       // query heads per kv head
 constexpr int kSsm = 128;     // GDN head size
 constexpr float kInvSqrtSsm = 0.08838834764831845f;  // 1/sqrt(128)
@@ -46,7 +47,7 @@ __device__ __forceinline__ float ld_cg(const float* p) { return __ldcg(p); }
 // ------------------------------------------------------------------------------------------------
 // Op records
 // ------------------------------------------------------------------------------------------------
-enum : int { POP_GEMV = 1, POP_EMBED, POP_GDN, POP_ATTN, POP_COMBINE, POP_DRAFT_PREP, POP_CTRL };
+enum : int { POP_GEMV = 1, POP_EMBED, POP_GDN, POP_ATTN, POP_COMBINE, POP_DRAFT_PREP, POP_CTRL, POP_XARGMAX };
 enum : int { CTRL_SINGLE = 1, CTRL_ACCEPT, CTRL_ROUND, CTRL_DRAFT1 };
 
 struct EmbedArgs {
@@ -92,6 +93,9 @@ struct CtrlArgs {
     int* out;
     int max_out;
 };
+struct XArgmaxArgs {  // tensor parallelism: the global argmax over the ranks' vocabulary shards
+    const XchDesc* xch;
+};
 struct alignas(16) POp {  // 16-byte multiple: fetched into shared memory by 16-byte cp.async chunks
     int kind;
     int pro, epi;  // POP_GEMV: prologue / epilogue
@@ -105,9 +109,19 @@ struct alignas(16) POp {  // 16-byte multiple: fetched into shared memory by 16-
         AttnArgs at;
         DraftPrepArgs dp;
         CtrlArgs ct;
+        XArgmaxArgs xa;
     };
 };
 static_assert(sizeof(POp) % 16 == 0 && sizeof(POp) / 16 <= 256, "op records are copied in 16-byte chunks");
+
+// Tokens per flash-decode chunk for a step at positions pos .. pos+nc-1: the smallest of 32, 64, 128, ...
+// that keeps a kv head's chunks at most kMaxChunksA (many small chunks spread a short context over
+// many CTAs; long contexts get longer chunks and a bounded partial buffer).
+__host__ __device__ __forceinline__ int attn_chunk_len(int pos, int nc) {
+    int len = 32;
+    while ((pos + nc + len - 1) / len > kMaxChunksA) len <<= 1;
+    return len;
+}
 
 // Work items of a non-GEMV op at position pos (column 0). Blocks or persistent CTAs take items
 // i = first, first + stride, ...
@@ -118,7 +132,7 @@ __host__ __device__ __forceinline__ int pop_items(const POp& op, int pos) {
         case POP_GDN: return op.gd.hv * 4;
         case POP_ATTN: {  // positions outside the cache are refused by the body; bound the count
             const int p = pos < 0 ? 0 : (pos > op.at.max_ctx - NC ? op.at.max_ctx - NC : pos);
-            return ((p + NC - 1) / kChunkA + 1) * op.at.n_kv;
+            return ((p + NC - 1) / attn_chunk_len(p, NC) + 1) * op.at.n_kv;
         }
         case POP_COMBINE: return op.at.n_head * NC;
         case POP_DRAFT_PREP: return NC;
@@ -129,7 +143,9 @@ __host__ __device__ __forceinline__ int pop_items(const POp& op, int pos) {
 
 // Shared-memory scratch (bytes) of the non-GEMV bodies.
 __host__ __device__ constexpr int gdn_scratch_floats(int nc) { return nc * (256 + 32 + 128 + 128 + 8) + 4; }
-__host__ __device__ constexpr int attn_scratch_floats(int nc) { return 2 * kGqa * nc * kHdA + 8 * kHdA; }
+__host__ __device__ constexpr int attn_scratch_floats(int nc) {
+    return kGqa * nc * kHdA + kGqa * nc * kSubA + 8 * kHdA + 4 * kGqa * nc;
+}
 inline size_t op_scratch_bytes(int nc, int H) {
     size_t b = (size_t) gdn_scratch_floats(nc) * 4;
     const size_t a = (size_t) attn_scratch_floats(nc) * 4, d = (size_t) (H + H / 4) * 4;
@@ -388,23 +404,28 @@ __device__ __noinline__ void gdn_quarter_body(const GdnArgs& a, int head, int qu
 }
 
 // Flash-decode chunk `chunk` of kv head kvh for NC query columns (gqa_head_kernel, src/qwythos.cpp:380-442,
-// split over 256-token chunks), with the attention prologue of the tokens it needs folded in: split of
-// q / gate (split_qg_kernel, :320-327), per-head RMSNorm, NEOX RoPE over n_rot dims from the cos / sin
-// table, and the fp16 K/V store (store_kv2_kernel, :340-345) of the new positions inside this chunk (each
-// position has exactly one owning chunk). Column c attends tokens <= pos + c. Partials: o
-// [n_head][NC][max_chunks][256], (m, l) [n_head][NC][max_chunks].
+// split over chunks of attn_chunk_len tokens), with the attention prologue of the tokens it needs folded
+// in: split of q / gate (split_qg_kernel, :320-327), per-head RMSNorm, NEOX RoPE over n_rot dims from the
+// cos / sin table, and the fp16 K/V store (store_kv2_kernel, :340-345) of the new positions inside this
+// chunk (each position has exactly one owning chunk). Column c attends tokens <= pos + c. The chunk is
+// scored in passes of up to kSubA tokens with a running (max, sum) per head and column (the flash-decode
+// rescaling); K and V rows are loaded several at a time. Partials: o [n_head][NC][max_chunks][256],
+// (m, l) [n_head][NC][max_chunks].
 template <int NC>
 __device__ __noinline__ void attn_chunk_body(const AttnArgs& a, int pos, int chunk, int kvh, float* sm) {
     constexpr int G = kGqa;
-    const int t0 = chunk * kChunkA;
     if (pos < 0 || pos + NC > a.max_ctx) {  // uniform over the block
         if (threadIdx.x == 0) atomicOr(&g_rk_status, kStatusBadIndex);
         return;
     }
-    if (t0 > pos + NC - 1) return;  // beyond every column (uniform over the block)
-    float* qs = sm;                                                     // [G][NC][256]
-    float (*sc)[NC][kChunkA] = reinterpret_cast<float (*)[NC][kChunkA]>(sm + G * NC * kHdA);  // [G][NC][256]
-    float* rot = sm + 2 * G * NC * kHdA;                                // [8 warps][256]
+    const int len = attn_chunk_len(pos, NC);
+    const int t0 = chunk * len;
+    if (t0 > pos + NC - 1 || chunk >= a.max_chunks) return;  // beyond every column (uniform over the block)
+    const int tend = min(t0 + len, pos + NC);                  // tokens [t0, tend) some column may read
+    float* qs = sm;                                            // [G][NC][256]
+    float (*sc)[NC][kSubA] = reinterpret_cast<float (*)[NC][kSubA]>(sm + G * NC * kHdA);  // [G][NC][kSubA]
+    float* rot = sm + G * NC * kHdA + G * NC * kSubA;          // [8 warps][256]
+    float* run = rot + 8 * kHdA;                               // [G*NC][4]: running max, sum, rescale
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     block_sync256();  // scratch reuse across items
     // ---- prologue: one warp per head vector (lane holds dims j*32 + lane), the block256 order ----
@@ -413,7 +434,7 @@ __device__ __noinline__ void attn_chunk_body(const AttnArgs& a, int pos, int chu
         const int g = is_q ? job / NC : 0;
         const int c = is_q ? job % NC : job - G * NC;
         const int pc = pos + c;
-        if (!is_q && (pc < t0 || pc >= t0 + kChunkA)) continue;  // a key this chunk does not own
+        if (!is_q && (pc < t0 || pc >= t0 + len)) continue;  // a key this chunk does not own
         const float* col = a.proj + (size_t) c * a.proj_stride;
         const float* src = is_q ? col + (kvh * G + g) * 2 * kHdA : col + a.n_head * 2 * kHdA + kvh * kHdA;
         float x[8];
@@ -434,29 +455,23 @@ __device__ __noinline__ void attn_chunk_body(const AttnArgs& a, int pos, int chu
             r[j * 32 + lane] = x[j];
         }
         __syncwarp();
-        const bool pos_ok = pc >= 0 && pc < a.max_ctx;
-        if (pos_ok) {
-            const int half = a.n_rot / 2;
+        const int half = a.n_rot / 2;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int d = j * 32 + lane;
-                if (d < a.n_rot) {
-                    const int i = d < half ? d : d - half;
-                    const float cs = a.rope[((size_t) pc * half + i) * 2 + 0];
-                    const float sn = a.rope[((size_t) pc * half + i) * 2 + 1];
-                    const float x0 = r[i], x1 = r[i + half];
-                    x[j] = d < half ? __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn))
-                                    : __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
-                }
+        for (int j = 0; j < 8; ++j) {
+            const int d = j * 32 + lane;
+            if (d < a.n_rot) {
+                const int i = d < half ? d : d - half;
+                const float cs = a.rope[((size_t) pc * half + i) * 2 + 0];
+                const float sn = a.rope[((size_t) pc * half + i) * 2 + 1];
+                const float x0 = r[i], x1 = r[i + half];
+                x[j] = d < half ? __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn)) : __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
             }
-        } else if (lane == 0) {
-            atomicOr(&g_rk_status, kStatusBadIndex);
         }
         __syncwarp();  // `r` is rewritten by this warp's next job
         if (is_q) {
 #pragma unroll
             for (int j = 0; j < 8; ++j) qs[(g * NC + c) * kHdA + j * 32 + lane] = x[j];
-        } else if (pos_ok) {
+        } else {
             const size_t dst = ((size_t) kvh * a.max_ctx + pc) * kHdA;
             const float* vsrc = col + a.n_head * 2 * kHdA + a.n_kv * kHdA + kvh * kHdA;
 #pragma unroll
@@ -466,81 +481,111 @@ __device__ __noinline__ void attn_chunk_body(const AttnArgs& a, int pos, int chu
             }
         }
     }
+    if (tid < G * NC) {
+        run[tid * 4 + 0] = -INFINITY;
+        run[tid * 4 + 1] = 0.0f;
+    }
     block_sync256();  // q in smem; this block's K/V stores visible to its threads
-    const __half* kbase = a.kc + ((size_t) kvh * a.max_ctx + t0) * kHdA;
-    const __half* vbase = a.vc + ((size_t) kvh * a.max_ctx + t0) * kHdA;
-    const int ntok = min(kChunkA, pos + NC - t0);  // tokens any column may read in this chunk
-    float qr[G][NC][8];
-#pragma unroll
-    for (int g = 0; g < G; ++g)
-#pragma unroll
-        for (int c = 0; c < NC; ++c) {
-            const float4* qp = reinterpret_cast<const float4*>(qs + (g * NC + c) * kHdA + lane * 8);
-            const float4 u = qp[0], v = qp[1];
-            qr[g][c][0] = u.x; qr[g][c][1] = u.y; qr[g][c][2] = u.z; qr[g][c][3] = u.w;
-            qr[g][c][4] = v.x; qr[g][c][5] = v.y; qr[g][c][6] = v.z; qr[g][c][7] = v.w;
-        }
-    // phase 1: scores, one warp per token, lanes over 8-dim slices, xor tree per (head, column)
-    for (int t = warp; t < ntok; t += 8) {
-        const uint4 kraw = __ldcg(reinterpret_cast<const uint4*>(kbase + (size_t) t * kHdA + lane * 8));
-        const __half2* kh2 = reinterpret_cast<const __half2*>(&kraw);
-        float kf[8];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const float2 f = __half22float2(kh2[i]);
-            kf[2 * i] = f.x;
-            kf[2 * i + 1] = f.y;
-        }
-#pragma unroll
-        for (int g = 0; g < G; ++g)
-#pragma unroll
-            for (int c = 0; c < NC; ++c) {
-                float d = 0.0f;
-#pragma unroll
-                for (int i = 0; i < 8; ++i) d = __fmaf_rn(qr[g][c][i], kf[i], d);
-                d = warp_sum(d);
-                if (lane == 0) sc[g][c][t] = (t0 + t <= pos + c) ? __fmul_rn(d, a.scale) : -INFINITY;
-            }
-    }
-    block_sync256();
-    // phase 2: per (head, column) the chunk max and the exponentials, one warp per pair
-    for (int pair = warp; pair < G * NC; pair += 8) {
-        const int g = pair / NC, c = pair % NC;
-        float m = -INFINITY;
-        for (int t = lane; t < ntok; t += 32) m = fmaxf(m, sc[g][c][t]);
-        m = warp_max(m);
-        float l = 0.0f;
-        for (int t = lane; t < ntok; t += 32) {
-            const float e = m == -INFINITY ? 0.0f : expf(__fsub_rn(sc[g][c][t], m));  // masked: exp(-inf) = 0
-            sc[g][c][t] = e;
-            l = __fadd_rn(l, e);
-        }
-        l = warp_sum(l);
-        if (lane == 0) {
-            float* ml = a.part_ml + (((size_t) (kvh * G + g) * NC + c) * a.max_chunks + chunk) * 2;
-            ml[0] = m;
-            ml[1] = l;
-        }
-    }
-    block_sync256();
-    // phase 3: weighted V, thread = output dim
+    const __half* kbase = a.kc + (size_t) kvh * a.max_ctx * kHdA;
+    const __half* vbase = a.vc + (size_t) kvh * a.max_ctx * kHdA;
     float acc[G][NC];
 #pragma unroll
     for (int g = 0; g < G; ++g)
 #pragma unroll
         for (int c = 0; c < NC; ++c) acc[g][c] = 0.0f;
-    for (int t = 0; t < ntok; ++t) {
-        const float vv = __half2float(__ldcg(vbase + (size_t) t * kHdA + tid));
+    for (int s0 = t0; s0 < tend; s0 += kSubA) {
+        const int ntok = min(kSubA, tend - s0);
+        // phase 1: scores, a warp per 4 consecutive tokens (their K rows loaded together), lanes over 8-dim
+        // slices, xor tree per (head, column)
+        for (int tb = warp * 4; tb < ntok; tb += 32) {
+            float kf[4][8];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                uint4 kraw = make_uint4(0u, 0u, 0u, 0u);
+                if (tb + u < ntok) kraw = __ldcg(reinterpret_cast<const uint4*>(kbase + (size_t) (s0 + tb + u) * kHdA + lane * 8));
+                const __half2* kh2 = reinterpret_cast<const __half2*>(&kraw);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float2 f = __half22float2(kh2[i]);
+                    kf[u][2 * i] = f.x;
+                    kf[u][2 * i + 1] = f.y;
+                }
+            }
+#pragma unroll
+            for (int g = 0; g < G; ++g)
+#pragma unroll
+                for (int c = 0; c < NC; ++c) {
+                    const float4* qp = reinterpret_cast<const float4*>(qs + (g * NC + c) * kHdA + lane * 8);
+                    const float4 q0 = qp[0], q1 = qp[1];
+                    const float qv[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        float d = 0.0f;
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) d = __fmaf_rn(qv[i], kf[u][i], d);
+                        d = warp_sum(d);
+                        const int t = tb + u;
+                        if (lane == 0 && t < ntok) sc[g][c][t] = (s0 + t <= pos + c) ? __fmul_rn(d, a.scale) : -INFINITY;
+                    }
+                }
+        }
+        block_sync256();
+        // phase 2: per (head, column) the pass's max, the exponentials against the new running max, the
+        // running sum and the rescale factor of what was accumulated before; one warp per pair
+        for (int pair = warp; pair < G * NC; pair += 8) {
+            const int g = pair / NC, c = pair % NC;
+            float m = -INFINITY;
+            for (int t = lane; t < ntok; t += 32) m = fmaxf(m, sc[g][c][t]);
+            m = warp_max(m);
+            const float m_old = run[pair * 4 + 0];
+            const float m_new = fmaxf(m_old, m);
+            float l = 0.0f;
+            for (int t = lane; t < ntok; t += 32) {
+                const float e = m_new == -INFINITY ? 0.0f : expf(__fsub_rn(sc[g][c][t], m_new));  // masked: 0
+                sc[g][c][t] = e;
+                l = __fadd_rn(l, e);
+            }
+            l = warp_sum(l);
+            if (lane == 0) {
+                const float alpha = m_old == -INFINITY ? 0.0f : expf(__fsub_rn(m_old, m_new));
+                run[pair * 4 + 0] = m_new;
+                run[pair * 4 + 1] = __fmaf_rn(run[pair * 4 + 1], alpha, l);
+                run[pair * 4 + 2] = alpha;
+            }
+        }
+        block_sync256();
+        // phase 3: weighted V, thread = output dim, V rows loaded 8 at a time, added in token order
 #pragma unroll
         for (int g = 0; g < G; ++g)
 #pragma unroll
-            for (int c = 0; c < NC; ++c) acc[g][c] = __fmaf_rn(sc[g][c][t], vv, acc[g][c]);
+            for (int c = 0; c < NC; ++c) acc[g][c] = __fmul_rn(acc[g][c], run[(g * NC + c) * 4 + 2]);
+        for (int tb = 0; tb < ntok; tb += 8) {
+            float vv[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                vv[u] = tb + u < ntok ? __half2float(__ldcg(vbase + (size_t) (s0 + tb + u) * kHdA + tid)) : 0.0f;
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                if (tb + u < ntok) {
+#pragma unroll
+                    for (int g = 0; g < G; ++g)
+#pragma unroll
+                        for (int c = 0; c < NC; ++c) acc[g][c] = __fmaf_rn(sc[g][c][tb + u], vv[u], acc[g][c]);
+                }
+        }
+        block_sync256();  // sc and run are rewritten by the next pass
     }
 #pragma unroll
     for (int g = 0; g < G; ++g)
 #pragma unroll
-        for (int c = 0; c < NC; ++c)
-            a.part_o[(((size_t) (kvh * G + g) * NC + c) * a.max_chunks + chunk) * kHdA + tid] = acc[g][c];
+        for (int c = 0; c < NC; ++c) {
+            const size_t slot = ((size_t) (kvh * G + g) * NC + c) * a.max_chunks + chunk;
+            a.part_o[slot * kHdA + tid] = acc[g][c];
+            if (tid == 0) {
+                a.part_ml[slot * 2 + 0] = run[(g * NC + c) * 4 + 0];
+                a.part_ml[slot * 2 + 1] = run[(g * NC + c) * 4 + 1];
+            }
+        }
 }
 
 // Combine of head h, column c: the chunks merged in order, then the Q8_1 blocks of o * sigmoid(gate)
@@ -549,7 +594,7 @@ template <int NC>
 __device__ __noinline__ void combine_body(const AttnArgs& a, int pos, int h, int c) {
     const int d = threadIdx.x;
     if (pos < 0 || pos + NC > a.max_ctx) return;  // recorded by the chunk body
-    const int nchunks = (pos + c) / kChunkA + 1;
+    const int nchunks = (pos + c) / attn_chunk_len(pos, NC) + 1;
     const float* ml = a.part_ml + ((size_t) h * NC + c) * a.max_chunks * 2;
     const float* po = a.part_o + ((size_t) h * NC + c) * a.max_chunks * kHdA;
     float M = -INFINITY;

@@ -17,6 +17,7 @@
 //          folded in) -> combine (sigmoid gate + Q8_1) -> GEMV wo (+residual) -> FFN as above
 // then the lm_head GEMV with the final RMSNorm prologue and a fused argmax epilogue.
 #include <cmath>
+#include <cstddef>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -49,10 +50,18 @@ float synth_scale(double std) { return (float) (std * std::sqrt(3.0) / 65536.0);
 
 // Q6_K encoder (this library's definition, restated by the CPU oracle): per 16-value sub-block amax_j,
 // d = half((max_j amax_j / 31) / 127), scale_j = clamp(roundf((amax_j / 31) / d), 0, 127),
-// code = clamp(roundf(x / (d * scale_j)), -32, 31) + 32.
-__global__ void gen_q6k_kernel(uint64_t seed, float scale, long long n_blocks, uint8_t* __restrict__ out) {
+// code = clamp(roundf(x / (d * scale_j)), -32, 31) + 32. One thread per 256-value block of a slice of the
+// tensor: local rows are global rows grow0 + r, local column blocks are global column blocks
+// [cb_a, cb_a + ncb_a) then [cb_b, cb_b + ncb_b) (nb_full blocks per global row); block bg of the global
+// tensor holds values bg*256 .. bg*256+255, so a slice holds exactly the global tensor's values.
+__global__ void gen_q6k_kernel(uint64_t seed, float scale, long long rows, long long grow0, int nb_full, int ncb_a,
+                               int cb_a, int ncb_b, int cb_b, uint8_t* __restrict__ out) {
     const long long b = (long long) blockIdx.x * blockDim.x + threadIdx.x;
-    if (b >= n_blocks) return;
+    const int ncb = ncb_a + ncb_b;
+    if (b >= rows * ncb) return;
+    const long long lr = b / ncb;
+    const int lcb = (int) (b - lr * ncb);
+    const long long bg = (grow0 + lr) * nb_full + (lcb < ncb_a ? cb_a + lcb : cb_b + (lcb - ncb_a));
     float x[256];
     float amax[16];
     float smax = 0.0f;
@@ -60,7 +69,7 @@ __global__ void gen_q6k_kernel(uint64_t seed, float scale, long long n_blocks, u
     for (int j = 0; j < 16; ++j) {
         float a = 0.0f;
         for (int i = 0; i < 16; ++i) {
-            const float v = __fmul_rn((float) synth_sum(seed, (uint64_t) b * 256 + 16 * j + i), scale);
+            const float v = __fmul_rn((float) synth_sum(seed, (uint64_t) bg * 256 + 16 * j + i), scale);
             x[16 * j + i] = v;
             a = fmaxf(a, fabsf(v));
         }
@@ -163,7 +172,10 @@ struct EngineImpl {
     rk_model_config cfg;
     int dev = 0;
     cudaStream_t s = nullptr;
-    int H = 0, FF = 0, V = 0, hk = 0, hv = 0, nh = 0, nkv = 0;
+    // Tensor parallelism: this rank's shard of the model (tp_size 1: the whole model). H is replicated;
+    // FF, hk, hv, nh, nkv and V (lm_head rows) are this rank's shares; Vg is the vocabulary.
+    int tp_rank = 0, tp_size = 1;
+    int H = 0, FF = 0, V = 0, Vg = 0, hk = 0, hv = 0, nh = 0, nkv = 0;
     int qkvzab_rows = 0, qkv3_rows = 0, max_in_rows = 0, max_chunks = 0;
     std::vector<Layer> layers;
     Layer draft;
@@ -196,6 +208,13 @@ struct EngineImpl {
     size_t p_smem[2] = {0, 0};
     double probe_weight_bytes[2] = {0, 0}, probe_algo_bytes[2] = {0, 0};
     int probe_gemvs = 0;
+    // tensor parallelism: this rank's exchange memory (exported by CUDA IPC), the peers' mappings, and the
+    // descriptor the kernels read
+    uint8_t* xmem = nullptr;
+    size_t xmem_bytes = 0, xoff_flags = 0, xoff_keys = 0;
+    XchDesc* xdesc = nullptr;
+    std::vector<void*> peer_maps;
+    bool tp_connected = false;
     std::vector<void*> allocs;
     std::vector<TensorRec> tensors;
     size_t bytes = 0;
@@ -214,17 +233,27 @@ struct EngineImpl {
         return static_cast<T*>(p);
     }
     int build();
-    void gen_f32(int tid, float* dst, size_t n, double std, double mean, int kind);
-    void gen_q6k_into(int tid, Mat& group, int row_off, int n_in, int n_out, uint8_t* scratch);
+    void gen_f32(int tid, float* dst, size_t n, double std, double mean, int kind,
+                 const std::vector<long long>* pick = nullptr);
+    void gen_q6k(int tid, Mat& group, int row_off, int n_in_full, int grow0, int rows, int cb_a, int ncb_a, int cb_b,
+                 int ncb_b, uint8_t* scratch);
+    void gen_q6k_into(int tid, Mat& group, int row_off, int n_in, int n_out, uint8_t* scratch) {
+        gen_q6k(tid, group, row_off, n_in, 0, n_out, 0, n_in / 256, 0, 0, scratch);
+    }
+    int gdn_vhead(int j) const {  // global v-head of local v-head j (the v-heads paired with this rank's k-heads)
+        return j < hk ? tp_rank * hk + j : cfg.ssm_h_k + tp_rank * hk + (j - hk);
+    }
     // programs
     MmvqParams rms_params(const Mat& m, const float* x_, const float* w, const float* part, float* y, int y_stride);
     MmvqParams q8_params(const Mat& m, const uint8_t* xq, float* y, const float* res, float* part);
     void add_gemv(std::vector<POp>& v, int pro, int epi, const MmvqParams& p);
+    void add_rowpar(std::vector<POp>& v, MmvqParams p);
     void add_ffn(std::vector<POp>& v, const Layer& L, float* xres, float* part);
     POp attn_op(int kind, const Layer& L, int draft_flag);
     void add_trunk(std::vector<POp>& v);
     void add_draft(std::vector<POp>& v, bool head);
     void add_ctrl(std::vector<POp>& v, int kind);
+    void add_xargmax(std::vector<POp>& v, int draft_flag);
     void add_probe(std::vector<POp>& v, int nc);
     int setup_executor();
     int finalize(Program& P, int nc);
@@ -239,19 +268,24 @@ EngineImpl::~EngineImpl() {
     if (s) cudaStreamSynchronize(s);
     for (Program& P : progs)
         if (P.graph) cudaGraphExecDestroy(P.graph);
+    for (void* p : peer_maps)
+        if (p) cudaIpcCloseMemHandle(p);
     for (void* p : allocs) cudaFree(p);
     if (ctrl_stage) cudaFreeHost(ctrl_stage);
     if (s) cudaStreamDestroy(s);
 }
 
 // f32 tensors are generated on the host (they are small) with the same counter-based values the device
-// uses; kind 1: ssm_a = -exp(value) computed in double.
-void EngineImpl::gen_f32(int tid, float* dst, size_t n, double std, double mean, int kind) {
+// uses; kind 1: ssm_a = -exp(value) computed in double. pick: the global indices this rank keeps (a
+// tensor-parallel slice), n of them; else the whole tensor.
+void EngineImpl::gen_f32(int tid, float* dst, size_t n, double std, double mean, int kind,
+                         const std::vector<long long>* pick) {
     std::vector<float> h(n);
     const uint64_t st = hash64(cfg.seed, (uint64_t) tid);
     const float scale = synth_scale(std), m = (float) mean;
     for (size_t i = 0; i < n; ++i) {
-        volatile float v = (float) synth_sum(st, i) * scale;
+        const uint64_t gi = pick ? (uint64_t) (*pick)[i] : (uint64_t) i;
+        volatile float v = (float) synth_sum(st, gi) * scale;
         float r = v + m;
         if (kind == 1) r = (float) -std::exp((double) r);
         h[i] = r;
@@ -261,32 +295,40 @@ void EngineImpl::gen_f32(int tid, float* dst, size_t n, double std, double mean,
     tensors.push_back({tid, false, (int) n, 1, dst, 0, false});
 }
 
-// Q6_K matrix rows [row_off, row_off + n_out) of a packed group: generate GGUF rows, repack in place.
-void EngineImpl::gen_q6k_into(int tid, Mat& group, int row_off, int n_in, int n_out, uint8_t* scratch) {
-    const long long nb = (long long) n_out * (n_in / 256);
+// Q6_K rows [grow0, grow0 + rows) of tensor tid (n_in_full columns), keeping the 256-column blocks
+// [cb_a, cb_a + ncb_a) then [cb_b, cb_b + ncb_b) of each row: generated as GGUF rows, then repacked into
+// rows [row_off, row_off + rows) of a packed group whose rows are (ncb_a + ncb_b) * 256 wide.
+void EngineImpl::gen_q6k(int tid, Mat& group, int row_off, int n_in_full, int grow0, int rows, int cb_a, int ncb_a,
+                         int cb_b, int ncb_b, uint8_t* scratch) {
+    const int n_in = (ncb_a + ncb_b) * 256;
+    const long long nb = (long long) rows * (ncb_a + ncb_b);
     const uint64_t st = hash64(cfg.seed, (uint64_t) tid);
-    gen_q6k_kernel<<<(unsigned) ((nb + 127) / 128), 128, 0, s>>>(st, synth_scale(0.02), nb, scratch);
+    gen_q6k_kernel<<<(unsigned) ((nb + 127) / 128), 128, 0, s>>>(st, synth_scale(0.02), rows, grow0, n_in_full / 256,
+                                                                 ncb_a, cb_a, ncb_b, cb_b, scratch);
     if (err == cudaSuccess) err = cudaGetLastError();
     if (err != cudaSuccess) return;
     uint8_t* dst = group.w + (size_t) (row_off / 4) * (n_in / 1024) * kQ6Tile;
-    const int rc = rk_pack_weights(RK_TYPE_Q6_K, scratch, dst, n_in, n_out, s);
+    const int rc = rk_pack_weights(RK_TYPE_Q6_K, scratch, dst, n_in, rows, s);
     if (rc != RK_OK && err == cudaSuccess) err = cudaErrorInvalidValue;
-    tensors.push_back({tid, true, n_in, n_out, group.w, (size_t) row_off, false});
+    tensors.push_back({tid, true, n_in, rows, group.w, (size_t) row_off, false});
 }
 
 int EngineImpl::build() {
     const rk_model_config& c = cfg;
-    H = c.n_embd, FF = c.n_ff, V = c.n_vocab, hk = c.ssm_h_k, hv = c.ssm_h_v, nh = c.n_head, nkv = c.n_head_kv;
-    qkvzab_rows = 2 * hk * kSsm + 2 * hv * kSsm + 2 * hv;
+    const int N = tp_size, g = tp_rank;
+    H = c.n_embd, Vg = c.n_vocab;
+    FF = c.n_ff / N, V = c.n_vocab / N, hk = c.ssm_h_k / N, hv = c.ssm_h_v / N, nh = c.n_head / N, nkv = c.n_head_kv / N;
+    const int hkg = c.ssm_h_k, hvg = c.ssm_h_v, S = kSsm;
+    qkvzab_rows = 2 * hk * S + 2 * hv * S + 2 * hv;
     qkv3_rows = 2 * nh * kHdA + 2 * nkv * kHdA;
     max_in_rows = qkvzab_rows > qkv3_rows ? qkvzab_rows : qkv3_rows;
-    max_chunks = (c.max_ctx + kChunkA - 1) / kChunkA;
+    max_chunks = kMaxChunksA;
     max_out = c.max_ctx;
     if ((err = cudaSetDevice(dev)) != cudaSuccess) return RK_ECUDA;
     if ((err = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking)) != cudaSuccess) return RK_ECUDA;
-    const size_t scratch_bytes = rk_weight_bytes(RK_TYPE_Q6_K, H, V) > rk_weight_bytes(RK_TYPE_Q6_K, FF, H)
-                                     ? rk_weight_bytes(RK_TYPE_Q6_K, H, V)
-                                     : rk_weight_bytes(RK_TYPE_Q6_K, H, 2 * FF);
+    const size_t scratch_bytes = rk_weight_bytes(RK_TYPE_Q6_K, H, Vg) > rk_weight_bytes(RK_TYPE_Q6_K, c.n_ff, H)
+                                     ? rk_weight_bytes(RK_TYPE_Q6_K, H, Vg)
+                                     : rk_weight_bytes(RK_TYPE_Q6_K, H, 2 * c.n_ff);
     uint8_t* scratch = nullptr;
     if ((err = cudaMalloc(&scratch, scratch_bytes)) != cudaSuccess) return RK_ENOMEM;
     auto mat = [&](int n_in, int n_out) {
@@ -301,17 +343,25 @@ int EngineImpl::build() {
         if (p) gen_f32(tid, p, (size_t) n, 0.02, 1.0, 0);
         return p;
     };
-    // globals
-    tok_embd = alloc<uint8_t>(rk_weight_bytes(RK_TYPE_Q6_K, H, V));
+    // rows [grow0, grow0 + rows) of a tensor, all columns
+    auto rows_of = [&](int tid, Mat& m, int row_off, int n_in, int grow0, int rows) {
+        gen_q6k(tid, m, row_off, n_in, grow0, rows, 0, n_in / 256, 0, 0, scratch);
+    };
+    // this rank's column share [col0, col0 + cols) of every row (a row-parallel weight)
+    auto cols_of = [&](int tid, Mat& m, int n_in_full, int n_out, int col0, int cols) {
+        gen_q6k(tid, m, 0, n_in_full, 0, n_out, col0 / 256, cols / 256, 0, 0, scratch);
+    };
+    // globals: the embedding table is replicated; the lm_head is vocabulary-sharded
+    tok_embd = alloc<uint8_t>(rk_weight_bytes(RK_TYPE_Q6_K, H, Vg));
     if (tok_embd) {
-        const long long nb = (long long) V * (H / 256);
-        gen_q6k_kernel<<<(unsigned) ((nb + 127) / 128), 128, 0, s>>>(hash64(c.seed, T_TOK_EMBD), synth_scale(0.02), nb,
-                                                                     tok_embd);
-        tensors.push_back({T_TOK_EMBD, true, H, V, tok_embd, 0, true});
+        const long long nb = (long long) Vg * (H / 256);
+        gen_q6k_kernel<<<(unsigned) ((nb + 127) / 128), 128, 0, s>>>(hash64(c.seed, T_TOK_EMBD), synth_scale(0.02), Vg,
+                                                                     0, H / 256, H / 256, 0, 0, 0, tok_embd);
+        tensors.push_back({T_TOK_EMBD, true, H, Vg, tok_embd, 0, true});
     }
     out_norm = norm(T_OUT_NORM, H);
     lm_head = mat(H, V);
-    if (lm_head.w) gen_q6k_into(T_OUTPUT, lm_head, 0, H, V, scratch);
+    if (lm_head.w) rows_of(T_OUTPUT, lm_head, 0, H, g * V, V);
     const int n_blocks = c.n_layer + (c.has_mtp ? 1 : 0);
     layers.resize(c.n_layer);
     for (int il = 0; il < n_blocks && err == cudaSuccess; ++il) {
@@ -320,43 +370,75 @@ int EngineImpl::build() {
         L.gdn = !is_draft && ((il + 1) % c.attn_interval) != 0;
         L.attn_norm = norm(layer_tid(il, L_ATTN_NORM), H);
         L.post_norm = norm(layer_tid(il, L_POST_NORM), H);
+        // FFN: up||gate column-parallel (this rank's FF rows of each), down row-parallel (its FF inputs)
         L.upgate = mat(H, 2 * FF);
         if (L.upgate.w) {
-            gen_q6k_into(layer_tid(il, L_FFN_UP), L.upgate, 0, H, FF, scratch);
-            gen_q6k_into(layer_tid(il, L_FFN_GATE), L.upgate, FF, H, FF, scratch);
+            rows_of(layer_tid(il, L_FFN_UP), L.upgate, 0, H, g * FF, FF);
+            rows_of(layer_tid(il, L_FFN_GATE), L.upgate, FF, H, g * FF, FF);
         }
         L.down = mat(FF, H);
-        if (L.down.w) gen_q6k_into(layer_tid(il, L_FFN_DOWN), L.down, 0, FF, H, scratch);
+        if (L.down.w) cols_of(layer_tid(il, L_FFN_DOWN), L.down, c.n_ff, H, g * FF, FF);
         if (L.gdn) {
+            // this rank's k-heads [g*hk, (g+1)*hk) and the v-heads paired with them (h and h + hkg):
+            // local layout [q | k | v (pairs a, b) | z | beta | alpha], a model with hk, hv heads
+            const int qa = g * hk * S, n = hk * S;  // first row / rows of this rank's q (and k) block
+            const int va = g * hk * S, vb = (hkg + g * hk) * S;
             L.in_proj = mat(H, qkvzab_rows);
-            if (L.in_proj.w) {
-                gen_q6k_into(layer_tid(il, L_GDN_QKV), L.in_proj, 0, H, 2 * hk * kSsm + hv * kSsm, scratch);
-                gen_q6k_into(layer_tid(il, L_GDN_Z), L.in_proj, 2 * hk * kSsm + hv * kSsm, H, hv * kSsm, scratch);
-                gen_q6k_into(layer_tid(il, L_GDN_BETA), L.in_proj, 2 * hk * kSsm + 2 * hv * kSsm, H, hv, scratch);
-                gen_q6k_into(layer_tid(il, L_GDN_ALPHA), L.in_proj, 2 * hk * kSsm + 2 * hv * kSsm + hv, H, hv, scratch);
+            if (L.in_proj.w && N == 1) {  // whole tensors (one record each for rk_engine_read_tensor)
+                rows_of(layer_tid(il, L_GDN_QKV), L.in_proj, 0, H, 0, 2 * hkg * S + hvg * S);
+                rows_of(layer_tid(il, L_GDN_Z), L.in_proj, 2 * hkg * S + hvg * S, H, 0, hvg * S);
+                rows_of(layer_tid(il, L_GDN_BETA), L.in_proj, 2 * hkg * S + 2 * hvg * S, H, 0, hvg);
+                rows_of(layer_tid(il, L_GDN_ALPHA), L.in_proj, 2 * hkg * S + 2 * hvg * S + hvg, H, 0, hvg);
+            } else if (L.in_proj.w) {
+                const int tq = layer_tid(il, L_GDN_QKV);
+                rows_of(tq, L.in_proj, 0, H, qa, n);                        // q
+                rows_of(tq, L.in_proj, n, H, hkg * S + qa, n);              // k
+                rows_of(tq, L.in_proj, 2 * n, H, 2 * hkg * S + va, n);      // v, first v-heads
+                rows_of(tq, L.in_proj, 3 * n, H, 2 * hkg * S + vb, n);      // v, paired v-heads
+                const int z0 = 2 * hk * S + hv * S;
+                rows_of(layer_tid(il, L_GDN_Z), L.in_proj, z0, H, va, n);
+                rows_of(layer_tid(il, L_GDN_Z), L.in_proj, z0 + n, H, vb, n);
+                const int b0 = z0 + hv * S;
+                rows_of(layer_tid(il, L_GDN_BETA), L.in_proj, b0, H, g * hk, hk);
+                rows_of(layer_tid(il, L_GDN_BETA), L.in_proj, b0 + hk, H, hkg + g * hk, hk);
+                rows_of(layer_tid(il, L_GDN_ALPHA), L.in_proj, b0 + hv, H, g * hk, hk);
+                rows_of(layer_tid(il, L_GDN_ALPHA), L.in_proj, b0 + hv + hk, H, hkg + g * hk, hk);
             }
-            L.out_proj = mat(hv * kSsm, H);
-            if (L.out_proj.w) gen_q6k_into(layer_tid(il, L_GDN_OUT), L.out_proj, 0, hv * kSsm, H, scratch);
-            const int C = 2 * hk * kSsm + hv * kSsm;
+            // ssm_out row-parallel over this rank's v-head outputs (two column ranges)
+            L.out_proj = mat(hv * S, H);
+            if (L.out_proj.w)
+                gen_q6k(layer_tid(il, L_GDN_OUT), L.out_proj, 0, hvg * S, 0, H, va / 256, n / 256, vb / 256, n / 256,
+                        scratch);
+            const int C = 2 * hk * S + hv * S;
+            std::vector<long long> chans;  // global conv channel of each local channel
+            for (int i = 0; i < n; ++i) chans.push_back(qa + i);
+            for (int i = 0; i < n; ++i) chans.push_back(hkg * S + qa + i);
+            for (int j = 0; j < hv; ++j)
+                for (int i = 0; i < S; ++i) chans.push_back(2 * hkg * S + (long long) gdn_vhead(j) * S + i);
+            std::vector<long long> taps, heads;
+            for (long long ch : chans)
+                for (int t = 0; t < 4; ++t) taps.push_back(ch * 4 + t);
+            for (int j = 0; j < hv; ++j) heads.push_back(gdn_vhead(j));
             L.conv_w = alloc<float>((size_t) C * 4);
-            if (L.conv_w) gen_f32(layer_tid(il, L_GDN_CONV), L.conv_w, (size_t) C * 4, 0.3, 0.0, 0);
+            if (L.conv_w) gen_f32(layer_tid(il, L_GDN_CONV), L.conv_w, (size_t) C * 4, 0.3, 0.0, 0, N > 1 ? &taps : nullptr);
             L.ssm_a = alloc<float>(hv);
-            if (L.ssm_a) gen_f32(layer_tid(il, L_GDN_A), L.ssm_a, hv, 0.5, 0.0, 1);
+            if (L.ssm_a) gen_f32(layer_tid(il, L_GDN_A), L.ssm_a, hv, 0.5, 0.0, 1, N > 1 ? &heads : nullptr);
             L.dt = alloc<float>(hv);
-            if (L.dt) gen_f32(layer_tid(il, L_GDN_DT), L.dt, hv, 0.5, 0.0, 0);
-            L.ssm_norm = norm(layer_tid(il, L_GDN_NORM), kSsm);
-            L.state = alloc<float>((size_t) kSsm * hv * kSsm);
-            L.snap = alloc<float>((size_t) kSsm * hv * kSsm);
+            if (L.dt) gen_f32(layer_tid(il, L_GDN_DT), L.dt, hv, 0.5, 0.0, 0, N > 1 ? &heads : nullptr);
+            L.ssm_norm = norm(layer_tid(il, L_GDN_NORM), S);
+            L.state = alloc<float>((size_t) S * hv * S);
+            L.snap = alloc<float>((size_t) S * hv * S);
             L.ring = alloc<float>((size_t) C * kRingSlots);
         } else {
+            // this rank's q heads [g*nh, (g+1)*nh) and kv heads [g*nkv, (g+1)*nkv)
             L.in_proj = mat(H, qkv3_rows);
             if (L.in_proj.w) {
-                gen_q6k_into(layer_tid(il, L_ATT_Q), L.in_proj, 0, H, 2 * nh * kHdA, scratch);
-                gen_q6k_into(layer_tid(il, L_ATT_K), L.in_proj, 2 * nh * kHdA, H, nkv * kHdA, scratch);
-                gen_q6k_into(layer_tid(il, L_ATT_V), L.in_proj, 2 * nh * kHdA + nkv * kHdA, H, nkv * kHdA, scratch);
+                rows_of(layer_tid(il, L_ATT_Q), L.in_proj, 0, H, g * nh * 2 * kHdA, nh * 2 * kHdA);
+                rows_of(layer_tid(il, L_ATT_K), L.in_proj, 2 * nh * kHdA, H, g * nkv * kHdA, nkv * kHdA);
+                rows_of(layer_tid(il, L_ATT_V), L.in_proj, 2 * nh * kHdA + nkv * kHdA, H, g * nkv * kHdA, nkv * kHdA);
             }
-            L.out_proj = mat(nh * kHdA, H);
-            if (L.out_proj.w) gen_q6k_into(layer_tid(il, L_ATT_O), L.out_proj, 0, nh * kHdA, H, scratch);
+            L.out_proj = mat(nh * kHdA, H);  // wo row-parallel over this rank's heads
+            if (L.out_proj.w) cols_of(layer_tid(il, L_ATT_O), L.out_proj, c.n_head * kHdA, H, g * nh * kHdA, nh * kHdA);
             L.q_norm = norm(layer_tid(il, L_ATT_QN), kHdA);
             L.k_norm = norm(layer_tid(il, L_ATT_KN), kHdA);
             L.kc = alloc<__half>((size_t) nkv * c.max_ctx * kHdA);
@@ -367,8 +449,8 @@ int EngineImpl::build() {
         enorm = norm(T_ENORM, H);
         hnorm = norm(T_HNORM, H);
         shnorm = norm(T_SHNORM, H);
-        eh_proj = mat(2 * H, H);
-        if (eh_proj.w) gen_q6k_into(T_EH_PROJ, eh_proj, 0, 2 * H, H, scratch);
+        eh_proj = mat(2 * H / N, H);  // row-parallel over this rank's share of [emb | h]
+        if (eh_proj.w) cols_of(T_EH_PROJ, eh_proj, 2 * H, H, g * 2 * H / N, 2 * H / N);
     }
     cudaStreamSynchronize(s);
     cudaFree(scratch);
@@ -392,8 +474,8 @@ int EngineImpl::build() {
     xp = alloc<float>(2 * (size_t) H / 4);
     proj = alloc<float>(2 * (size_t) max_in_rows);
     ug = alloc<float>(2 * 2 * (size_t) FF);
-    q8 = alloc<uint8_t>(2 * rk_q8_1_bytes(hv * kSsm, 1));
-    gdn_o = alloc<float>(2 * (size_t) hv * kSsm);
+    q8 = alloc<uint8_t>(2 * rk_q8_1_bytes(hv * S, 1));
+    gdn_o = alloc<float>(2 * (size_t) hv * S);
     gdn_ss = alloc<float>(2 * (size_t) hv * 4);
     gdn_cnt = alloc<unsigned>((size_t) hv);
     attn_scratch = alloc<float>((size_t) nh * 2 * max_chunks * (kHdA + 2));
@@ -409,6 +491,7 @@ int EngineImpl::build() {
     ctrl = alloc<Ctrl>(1);
     out = alloc<int>((size_t) max_out);
     psync = alloc<PSync>(1);
+    xdesc = alloc<XchDesc>(1);
     stage_slots = 4096;  // plus one slot after them for the emitted-count readback
     if (err == cudaSuccess) err = cudaMallocHost(&ctrl_stage, sizeof(Ctrl) * (stage_slots + 1));
     if (err == cudaSuccess) err = cudaStreamSynchronize(s);
@@ -462,11 +545,31 @@ void EngineImpl::add_gemv(std::vector<POp>& v, int pro, int epi, const MmvqParam
     v.push_back(op);
 }
 
+// A row-parallel GEMV (ssm_out, wo, down, eh_proj): y = W . xq (+ res) with the 4-row partials; under
+// tensor parallelism the ranks' partial sums are added over peer memory inside the op (EPI_XRES).
+void EngineImpl::add_rowpar(std::vector<POp>& v, MmvqParams p) {
+    if (tp_size == 1) {
+        add_gemv(v, PRO_Q8, p.res != nullptr ? EPI_RES : EPI_STORE_P, p);
+        return;
+    }
+    p.xch = xdesc;
+    add_gemv(v, PRO_Q8, EPI_XRES, p);
+}
+
+// Tensor parallelism: after an lm_head over this rank's vocabulary shard, the global argmax.
+void EngineImpl::add_xargmax(std::vector<POp>& v, int draft_flag) {
+    if (tp_size == 1) return;
+    POp op = make_op(POP_XARGMAX);
+    op.draft = draft_flag;
+    op.xa.xch = xdesc;
+    v.push_back(op);
+}
+
 // FFN (src/qwythos.cpp:1011-1042): RMSNorm(post_norm)+Q8_1 -> up||gate with the SwiGLU+Q8_1 epilogue ->
 // down + residual.
 void EngineImpl::add_ffn(std::vector<POp>& v, const Layer& L, float* xres, float* part) {
     add_gemv(v, PRO_RMS, EPI_SWIGLU, rms_params(L.upgate, xres, L.post_norm, part, ug, 2 * FF));
-    add_gemv(v, PRO_Q8, EPI_RES, q8_params(L.down, q8_ff, xres, xres, part));
+    add_rowpar(v, q8_params(L.down, q8_ff, xres, xres, part));
 }
 
 POp EngineImpl::attn_op(int kind, const Layer& L, int draft_flag) {
@@ -498,7 +601,7 @@ void EngineImpl::add_trunk(std::vector<POp>& v) {
     POp e = make_op(POP_EMBED);
     e.em.emb = tok_embd;
     e.em.H = H;
-    e.em.V = V;
+    e.em.V = Vg;
     e.em.x = x;
     e.em.xp = xp;
     v.push_back(e);
@@ -525,11 +628,11 @@ void EngineImpl::add_trunk(std::vector<POp>& v) {
             a.hv = hv;
             a.eps = cfg.eps;
             v.push_back(g);
-            add_gemv(v, PRO_Q8, EPI_RES, q8_params(L.out_proj, q8, x, x, xp));
+            add_rowpar(v, q8_params(L.out_proj, q8, x, x, xp));
         } else {
             v.push_back(attn_op(POP_ATTN, L, 0));
             v.push_back(attn_op(POP_COMBINE, L, 0));
-            add_gemv(v, PRO_Q8, EPI_RES, q8_params(L.out_proj, q8_attn, x, x, xp));
+            add_rowpar(v, q8_params(L.out_proj, q8_attn, x, x, xp));
         }
         add_ffn(v, L, x, xp);
     }
@@ -538,7 +641,9 @@ void EngineImpl::add_trunk(std::vector<POp>& v) {
     p.xn_out = hsave;
     p.xn_part = hsave_p;
     p.amax = &ctrl->amax[0];
+    p.row_off = tp_rank * V;
     add_gemv(v, PRO_RMS, EPI_ARGMAX, p);
+    add_xargmax(v, 0);
 }
 
 // The MTP draft (draft_predict, src/qwythos.cpp:1316-1406): [enorm(emb) | hnorm(h)] -> eh_proj -> the
@@ -548,7 +653,7 @@ void EngineImpl::add_draft(std::vector<POp>& v, bool head) {
     d.draft = 1;
     d.dp.emb = tok_embd;
     d.dp.H = H;
-    d.dp.V = V;
+    d.dp.V = Vg;
     d.dp.enorm = enorm;
     d.dp.hnorm = hnorm;
     d.dp.hsave = hsave;
@@ -556,17 +661,23 @@ void EngineImpl::add_draft(std::vector<POp>& v, bool head) {
     d.dp.eps = cfg.eps;
     d.dp.eh_q8 = eh_q8;
     v.push_back(d);
-    add_gemv(v, PRO_Q8, EPI_STORE_P, q8_params(eh_proj, eh_q8, dx, nullptr, dxp));  // no residual
+    {  // no residual; under tensor parallelism this rank's share of the [emb | h] input columns
+        MmvqParams p = q8_params(eh_proj, eh_q8 + (size_t) tp_rank * (eh_proj.n_in / 32) * 36, dx, nullptr, dxp);
+        p.xq_stride = (int) rk_q8_1_bytes(2 * H, 1);
+        add_rowpar(v, p);
+    }
     const Layer& D = draft;
     add_gemv(v, PRO_RMS, EPI_STORE, rms_params(D.in_proj, dx, D.attn_norm, dxp, proj, D.in_proj.n_out));
     v.push_back(attn_op(POP_ATTN, D, 1));
     v.push_back(attn_op(POP_COMBINE, D, 1));
-    add_gemv(v, PRO_Q8, EPI_RES, q8_params(D.out_proj, q8_attn, dx, dx, dxp));
+    add_rowpar(v, q8_params(D.out_proj, q8_attn, dx, dx, dxp));
     add_ffn(v, D, dx, dxp);
     if (head) {
         MmvqParams p = rms_params(lm_head, dx, shnorm, dxp, nullptr, V);
         p.amax = &ctrl->damax[0];
+        p.row_off = tp_rank * V;
         add_gemv(v, PRO_RMS, EPI_ARGMAX, p);
+        add_xargmax(v, 1);
     }
 }
 
@@ -592,7 +703,7 @@ void EngineImpl::add_probe(std::vector<POp>& v, int nc) {
     for (const Layer& L : layers) {
         add_gemv(v, PRO_RMS, EPI_STORE, rms_params(L.in_proj, x, L.attn_norm, xp, proj, L.in_proj.n_out));
         count(L.in_proj, true, false);
-        add_gemv(v, PRO_Q8, EPI_RES, q8_params(L.out_proj, L.gdn ? q8 : q8_attn, x, x, xp));
+        add_rowpar(v, q8_params(L.out_proj, L.gdn ? q8 : q8_attn, x, x, xp));
         count(L.out_proj, false, true);
         add_ffn(v, L, x, xp);
         count(L.upgate, true, false);
@@ -676,8 +787,8 @@ cudaError_t EngineImpl::launch_op(const POp& op) {
         if (op.epi == EPI_RES) return mmvq_launch<RK_TYPE_Q6_K, NC, PRO_Q8, EPI_RES>(p, s, true);
         return mmvq_launch<RK_TYPE_Q6_K, NC, PRO_Q8, EPI_STORE_P>(p, s, true);
     }
-    // grid: the op's largest item count (positions up to the end of the cache)
-    const int grid = pop_items<NC>(op, cfg.max_ctx - NC);
+    // grid: the op's largest item count over all positions (attention: kMaxChunksA chunks per kv head)
+    const int grid = op.kind == POP_ATTN ? kMaxChunksA * op.at.n_kv : pop_items<NC>(op, 0);
     const size_t smem = op_scratch_bytes(NC, H);
     static bool attr_set[2] = {false, false};
     if (smem > 48 * 1024 && !attr_set[NC - 1]) {
@@ -809,9 +920,29 @@ void rk_model_config_9b(rk_model_config* c, int max_ctx, uint64_t seed) {
 }
 
 int rk_engine_create(const rk_model_config* cfg, int device, rk_engine** out) {
+    return rk_engine_create_tp(cfg, device, 0, 1, out);
+}
+
+int rk_engine_create_tp(const rk_model_config* cfg, int device, int tp_rank, int tp_size, rk_engine** out) {
     const char* what = "rk_engine_create";
     if (!cfg || !out) return set_error(RK_EINVAL, "%s: null argument", what);
     const rk_model_config& c = *cfg;
+    if (tp_size < 1 || tp_size > kMaxRanks || tp_rank < 0 || tp_rank >= tp_size)
+        return set_error(RK_EINVAL, "%s: bad tensor-parallel rank / size", what);
+    if (tp_size > 1) {
+        // every rank's share of a row-parallel input must be a whole number of 1024-value tiles; kv heads
+        // and k-heads split evenly
+        const int N = tp_size;
+        if (c.ssm_h_k % N || c.n_head_kv % N || c.n_ff % (1024 * N) || (c.ssm_h_v * kSsm) % (1024 * N) ||
+            (c.n_head * kHdA) % (1024 * N) || (2 * c.n_embd) % (1024 * N) || c.n_vocab % (4 * N))
+            return set_error(RK_EUNSUPPORTED,
+                             "%s: tensor parallelism over %d ranks needs k-heads and kv-heads divisible by it and "
+                             "every rank's row-parallel input a multiple of 1024",
+                             what, N);
+        const char* mode = std::getenv("RK_ENGINE_MODE");
+        if (mode && std::strcmp(mode, "graph") == 0)
+            return set_error(RK_EUNSUPPORTED, "%s: tensor parallelism needs the persistent executor", what);
+    }
     if (c.n_layer < 1 || c.n_embd <= 0 || c.n_embd % 1024 || c.n_ff <= 0 || c.n_ff % 1024 || c.n_vocab <= 0 ||
         c.n_vocab % 4)
         return set_error(RK_EINVAL, "%s: n_embd and n_ff must be multiples of 1024, n_vocab of 4", what);
@@ -825,9 +956,26 @@ int rk_engine_create(const rk_model_config* cfg, int device, rk_engine** out) {
     if (!e) return set_error(RK_ENOMEM, "%s: host allocation failed", what);
     e->impl.cfg = c;
     e->impl.dev = device;
+    e->impl.tp_rank = tp_rank;
+    e->impl.tp_size = tp_size;
     EngineImpl& E = e->impl;
     int rc = E.build();
     if (rc == RK_OK) rc = E.setup_executor();
+    if (rc == RK_OK && tp_size > 1 && !E.persistent) rc = RK_EUNSUPPORTED;
+    if (rc == RK_OK && tp_size > 1) {
+        // this rank's exchange memory: partials [2][2][H] floats | flags [grid + 1][8] | keys [2][8][2]
+        E.xoff_flags = (size_t) 4 * E.H * sizeof(float);
+        E.xoff_keys = E.xoff_flags + (size_t) (E.p_grid + 1) * kMaxRanks * 8;
+        E.xmem_bytes = E.xoff_keys + (size_t) 2 * kMaxRanks * 2 * 8;
+        void* p = nullptr;
+        if ((E.err = cudaMalloc(&p, E.xmem_bytes)) != cudaSuccess) rc = RK_ENOMEM;
+        if (rc == RK_OK) {
+            E.xmem = static_cast<uint8_t*>(p);
+            E.allocs.push_back(p);
+            E.err = cudaMemset(p, 0, E.xmem_bytes);
+            if (E.err != cudaSuccess) rc = RK_ECUDA;
+        }
+    }
     if (rc == RK_OK) {
         E.add_trunk(E.progs[P_SINGLE].ops);
         E.add_ctrl(E.progs[P_SINGLE].ops, CTRL_SINGLE);
@@ -868,9 +1016,62 @@ int rk_engine_create(const rk_model_config* cfg, int device, rk_engine** out) {
         if (rc == RK_ENOMEM || ce == cudaErrorMemoryAllocation)
             return set_error(RK_ENOMEM, "%s: out of device memory", what);
         if (rc == RK_EINVAL) return set_error(RK_EINVAL, "%s: unsupported GEMV prologue/epilogue pair", what);
+        if (rc == RK_EUNSUPPORTED)
+            return set_error(RK_EUNSUPPORTED, "%s: tensor parallelism needs the persistent executor", what);
         return set_error(RK_ECUDA, "%s: %s", what, cudaGetErrorString(ce));
     }
     *out = e;
+    return RK_OK;
+}
+
+size_t rk_tp_handle_bytes(void) { return sizeof(cudaIpcMemHandle_t); }
+
+int rk_engine_tp_export(rk_engine* e, void* handle, size_t bytes) {
+    const char* what = "rk_engine_tp_export";
+    if (!e || !handle || bytes < sizeof(cudaIpcMemHandle_t)) return set_error(RK_EINVAL, "%s: bad argument", what);
+    EngineImpl& E = e->impl;
+    if (E.tp_size < 2) return set_error(RK_EINVAL, "%s: the engine is not tensor-parallel", what);
+    cudaIpcMemHandle_t h;
+    const cudaError_t ce = cudaIpcGetMemHandle(&h, E.xmem);
+    if (ce != cudaSuccess) return set_error(RK_ECUDA, "%s: %s", what, cudaGetErrorString(ce));
+    std::memcpy(handle, &h, sizeof h);
+    return RK_OK;
+}
+
+int rk_engine_tp_connect(rk_engine* e, const void* handles, size_t bytes_per_rank) {
+    const char* what = "rk_engine_tp_connect";
+    if (!e || !handles || bytes_per_rank < sizeof(cudaIpcMemHandle_t)) return set_error(RK_EINVAL, "%s: bad argument", what);
+    EngineImpl& E = e->impl;
+    if (E.tp_size < 2) return set_error(RK_EINVAL, "%s: the engine is not tensor-parallel", what);
+    if (E.tp_connected) return set_error(RK_EINVAL, "%s: already connected", what);
+    if (cudaSetDevice(E.dev) != cudaSuccess) return set_error(RK_ECUDA, "%s: cudaSetDevice failed", what);
+    XchDesc d = {};
+    d.rank = E.tp_rank;
+    d.n = E.tp_size;
+    d.rows = E.H;
+    d.slots = E.p_grid + 1;
+    E.peer_maps.assign(E.tp_size, nullptr);
+    for (int q = 0; q < E.tp_size; ++q) {
+        uint8_t* base = nullptr;
+        if (q == E.tp_rank) {
+            base = E.xmem;
+        } else {
+            cudaIpcMemHandle_t h;
+            std::memcpy(&h, static_cast<const uint8_t*>(handles) + (size_t) q * bytes_per_rank, sizeof h);
+            void* p = nullptr;
+            const cudaError_t ce = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+            if (ce != cudaSuccess)
+                return set_error(RK_ECUDA, "%s: opening rank %d's exchange memory: %s", what, q, cudaGetErrorString(ce));
+            E.peer_maps[q] = p;
+            base = static_cast<uint8_t*>(p);
+        }
+        d.buf[q] = reinterpret_cast<float*>(base);
+        d.flags[q] = reinterpret_cast<unsigned long long*>(base + E.xoff_flags);
+        d.keys[q] = reinterpret_cast<unsigned long long*>(base + E.xoff_keys);
+    }
+    const cudaError_t ce = cudaMemcpy(E.xdesc, &d, sizeof d, cudaMemcpyHostToDevice);
+    if (ce != cudaSuccess) return set_error(RK_ECUDA, "%s: %s", what, cudaGetErrorString(ce));
+    E.tp_connected = true;
     return RK_OK;
 }
 
@@ -902,7 +1103,7 @@ int rk_engine_reset(rk_engine* e) {
     cudaMemsetAsync(E.ctrl, 0, sizeof(Ctrl), E.s);
     cudaMemsetAsync(E.swiglu_cnt, 0, sizeof(unsigned) * (size_t) E.FF / 32, E.s);
     cudaMemsetAsync(E.gdn_cnt, 0, sizeof(unsigned) * (size_t) E.hv, E.s);
-    cudaMemsetAsync(E.psync, 0, sizeof(PSync), E.s);
+    cudaMemsetAsync(E.psync, 0, offsetof(PSync, xepoch), E.s);  // the exchange epoch keeps counting
     const cudaError_t ce = cudaStreamSynchronize(E.s);
     if (ce != cudaSuccess) return set_error(RK_ECUDA, "rk_engine_reset: %s", cudaGetErrorString(ce));
     return RK_OK;
@@ -912,10 +1113,11 @@ int rk_engine_step(rk_engine* e, const int* tokens, int ncols, int pos, float* l
     const char* what = "rk_engine_step";
     if (!e || !tokens) return set_error(RK_EINVAL, "%s: null argument", what);
     EngineImpl& E = e->impl;
+    if (E.tp_size > 1 && !E.tp_connected) return set_error(RK_EINVAL, "%s: call rk_engine_tp_connect first", what);
     if (ncols < 1 || ncols > 2) return set_error(RK_EINVAL, "%s: ncols must be 1 or 2", what);
     if (pos < 0 || pos + ncols > E.cfg.max_ctx) return set_error(RK_ERANGE, "%s: position out of range", what);
     for (int c = 0; c < ncols; ++c)
-        if (tokens[c] < 0 || tokens[c] >= E.V) return set_error(RK_ERANGE, "%s: token out of range", what);
+        if (tokens[c] < 0 || tokens[c] >= E.Vg) return set_error(RK_ERANGE, "%s: token out of range", what);
     Ctrl h = {};
     h.pos = pos;
     h.tok[0] = tokens[0];
@@ -939,11 +1141,12 @@ int rk_engine_generate(rk_engine* e, const int* prompt, int n_prompt, int n_gen,
     const char* what = "rk_engine_generate";
     if (!e || !prompt || !out_ids) return set_error(RK_EINVAL, "%s: null argument", what);
     EngineImpl& E = e->impl;
+    if (E.tp_size > 1 && !E.tp_connected) return set_error(RK_EINVAL, "%s: call rk_engine_tp_connect first", what);
     if (n_prompt < 1 || n_gen < 1) return set_error(RK_EINVAL, "%s: needs n_prompt >= 1 and n_gen >= 1", what);
     if (n_prompt + n_gen + 2 > E.cfg.max_ctx) return set_error(RK_ERANGE, "%s: prompt + generation exceed max_ctx", what);
     if (use_mtp && !E.cfg.has_mtp) return set_error(RK_EINVAL, "%s: model built without the MTP block", what);
     for (int i = 0; i < n_prompt; ++i)
-        if (prompt[i] < 0 || prompt[i] >= E.V) return set_error(RK_ERANGE, "%s: prompt token out of range", what);
+        if (prompt[i] < 0 || prompt[i] >= E.Vg) return set_error(RK_ERANGE, "%s: prompt token out of range", what);
     int rc = rk_engine_reset(e);
     if (rc) return rc;
     cudaEvent_t ev[3];
@@ -1082,6 +1285,7 @@ int rk_engine_probe_gemv(rk_engine* e, int ncols, int iters, rk_probe_result* ou
     if (!e || !out) return set_error(RK_EINVAL, "%s: null argument", what);
     if (ncols < 1 || ncols > 2 || iters < 1) return set_error(RK_EINVAL, "%s: ncols 1..2, iters >= 1", what);
     EngineImpl& E = e->impl;
+    if (E.tp_size > 1 && !E.tp_connected) return set_error(RK_EINVAL, "%s: call rk_engine_tp_connect first", what);
     const Program& P = E.progs[ncols == 1 ? P_PROBE1 : P_PROBE2];
     cudaEvent_t a, b;
     cudaEventCreate(&a);
@@ -1110,6 +1314,7 @@ int rk_engine_trace(rk_engine* e, int program, double* stamps_us, int* kinds, in
     if (!e || !stamps_us || !kinds) return set_error(RK_EINVAL, "%s: null argument", what);
     EngineImpl& E = e->impl;
     if (!E.persistent) return set_error(RK_EUNSUPPORTED, "%s: needs the persistent executor", what);
+    if (E.tp_size > 1 && !E.tp_connected) return set_error(RK_EINVAL, "%s: call rk_engine_tp_connect first", what);
     static const int ids[] = {P_SINGLE, P_ROUND, P_PROBE1, P_PROBE2, P_TRUNK2};
     if (program < 0 || program > 4) return set_error(RK_EINVAL, "%s: program must be 0..4", what);
     const Program& P = E.progs[ids[program]];

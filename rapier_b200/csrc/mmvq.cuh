@@ -36,7 +36,11 @@ enum MmvqPro { PRO_Q8 = 0, PRO_RMS = 1 };
 // EPI_SWIGLU: y as EPI_STORE for a [up (n_out/2) | gate (n_out/2)] matrix, and for every 32-position block
 // whose 16 units (8 up + 8 gate) are done, the last warp to finish one of them writes the Q8_1 block of
 // silu(gate) * up (the down GEMV's input; swiglu_quant_kernel, src/qwythos.cpp:676-689).
-enum MmvqEpi { EPI_STORE = 0, EPI_RES = 1, EPI_ARGMAX = 2, EPI_STORE_P = 3, EPI_SWIGLU = 4 };
+// EPI_XRES (persistent decode kernel under tensor parallelism): a row-parallel GEMV's partial sums are
+// summed over the ranks (peer memory), then as EPI_RES (res != null) or EPI_STORE_P (res == null).
+enum MmvqEpi { EPI_STORE = 0, EPI_RES = 1, EPI_ARGMAX = 2, EPI_STORE_P = 3, EPI_SWIGLU = 4, EPI_XRES = 5 };
+
+struct XchDesc;  // persistent.cuh
 
 struct MmvqParams {
     const uint8_t* w;  // packed tiles
@@ -44,7 +48,8 @@ struct MmvqParams {
     int stages;
     int prefetch_before_wait;  // 1: weights are static, stream them before waiting on the upstream grid
     // prologue inputs
-    const uint8_t* xq;  // PRO_Q8: Q8_1 blocks, column stride rk_q8_1_bytes(n_in, 1)
+    const uint8_t* xq;  // PRO_Q8: Q8_1 blocks, column stride xq_stride bytes (0: rk_q8_1_bytes(n_in, 1))
+    int xq_stride;
     const float* xa;    // PRO_RMS: x (column stride n_in)
     const float* xb;    // PRO_RMS: norm weight
     const float* pin;   // PRO_RMS: partials, column stride n_in/4
@@ -57,6 +62,7 @@ struct MmvqParams {
     float* pout;        // EPI_RES partials, column stride pout_stride
     int pout_stride;
     unsigned long long* amax;  // EPI_ARGMAX: one packed (value, ~row) slot per column
+    int row_off;               // EPI_ARGMAX: global index of row 0 (a vocabulary shard's first row)
     uint8_t* q8out;            // EPI_SWIGLU: Q8_1 of silu(gate) * up, column stride rk_q8_1_bytes(n_out/2, 1)
     unsigned* cnt;             // EPI_SWIGLU: n_out/64 zeroed counters (left zeroed on exit)
     // PRO_RMS write-through (optional): CTA 0 stores the normalized fp32 row (x * w * inv) of every
@@ -64,6 +70,7 @@ struct MmvqParams {
     // rms_norm_out + row_sum_partials of the final hidden (src/qwythos.cpp:1236-1237).
     float* xn_out;
     float* xn_part;
+    const XchDesc* xch;  // EPI_XRES: the ranks' exchange buffers
 };
 
 // Smem bytes a launch needs for the activation staging and the rings.
@@ -143,7 +150,7 @@ template <int NC, int PRO>
 __device__ __noinline__ void mmvq_build_x(const MmvqParams& p, uint8_t* xsm, float* red) {
     const int ng = p.n_in >> 5;
     if constexpr (PRO == PRO_Q8) {
-        const size_t col_bytes = (size_t) ng * 36;
+        const size_t col_bytes = p.xq_stride > 0 ? (size_t) p.xq_stride : (size_t) ng * 36;
         for (int idx = threadIdx.x; idx < NC * ng; idx += 256) {
             const int c = idx / ng, g = idx - c * ng;
             const int* blk = reinterpret_cast<const int*>(p.xq + (size_t) c * col_bytes + (size_t) g * 36);
@@ -355,7 +362,7 @@ __device__ __forceinline__ void mmvq_epilogue(const MmvqParams& p, int unit, int
 #pragma unroll
                 for (int r = 0; r < 4; ++r)
                     if (acc[c][r] == acc[c][r]) {  // NaN never wins
-                        const unsigned long long k = argmax_key(acc[c][r], row0 + r);
+                        const unsigned long long k = argmax_key(acc[c][r], p.row_off + row0 + r);
                         best[c] = k > best[c] ? k : best[c];
                     }
         }

@@ -40,6 +40,23 @@ struct PSync {
     unsigned long long arrive;  // grid-barrier arrivals of the running launch
     unsigned exits;             // CTAs of the running launch that have finished
     unsigned abort;             // sticky give-up flag, cleared by the host
+    unsigned long long xepoch;  // tensor parallelism: exchanges done so far (monotonic, never cleared)
+};
+
+// Tensor parallelism: every rank's exchange memory, mapped into this rank's address space (CUDA IPC over
+// NVLink). A rank writes its row-parallel partial sums into its own buffer and signals each peer by a
+// system-scope release store of the exchange's epoch into the peer's flag slot; a peer that has acquired
+// all the signals of a slot reads the partials with uncached loads. Epochs only grow, the flag words of
+// a slot only grow, so no flag is ever cleared; buffers alternate by epoch parity, and a rank starts an
+// exchange only after every peer has signalled the previous one, so no buffer is rewritten while read.
+constexpr int kMaxRanks = 8;
+struct XchDesc {
+    int rank, n;  // this rank, number of ranks
+    int rows;     // rows of a partial column (the hidden size)
+    int slots;    // flag slots: one per persistent CTA + one for the argmax exchange
+    float* buf[kMaxRanks];                 // per rank: partials [2 parity][2 columns][rows]
+    unsigned long long* flags[kMaxRanks];  // per rank: [slots][kMaxRanks] epochs, written by the peers
+    unsigned long long* keys[kMaxRanks];   // per rank: argmax keys [2 parity][kMaxRanks][2 columns]
 };
 
 // One GEMV of a program, as the weight cursors see it (built by the host in program order).
@@ -53,6 +70,7 @@ constexpr int kMaxGemvOps = 256;
 constexpr int kPWarps = 16;  // warps of a persistent CTA; all consume GEMV tiles
 
 constexpr unsigned long long kGridSpinNs = 1000000000ull;  // a grid barrier gives up after 1 s
+constexpr unsigned long long kPeerSpinNs = 5000000000ull;  // a cross-rank wait after 5 s (a peer's host may lag)
 
 __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p) {
     unsigned long long v;
@@ -105,6 +123,66 @@ __device__ __forceinline__ bool grid_sync(PSync* sync, unsigned long long& targe
     }
     __syncthreads();
     return *flag != 0;
+}
+
+__device__ __forceinline__ void st_release_sys_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// One thread: signal flag slot `slot` of every peer with `epoch` (after a system-scope fence that makes
+// this CTA's preceding writes visible), then wait until every peer has signalled this rank's slot. The
+// wait gives up after 5 s (status bit, abort). Returns false when the program must stop.
+__device__ __noinline__ bool xch_signal_wait(const XchDesc* x, int slot, unsigned long long epoch, PSync* sync) {
+    const int me = x->rank, n = x->n;
+    __threadfence_system();
+    for (int q = 0; q < n; ++q)
+        if (q != me) st_release_sys_u64(x->flags[q] + (size_t) slot * kMaxRanks + me, epoch);
+    const unsigned long long* mine = x->flags[me] + (size_t) slot * kMaxRanks;
+    const unsigned long long t0 = globaltimer_ns();
+    for (int q = 0; q < n; ++q) {
+        if (q == me) continue;
+        for (uint32_t it = 0; ld_acquire_sys_u64(mine + q) < epoch; ++it) {
+            if (ld_volatile_u32(&sync->abort)) return false;
+            if ((it & 63u) == 63u && globaltimer_ns() - t0 > kPeerSpinNs) {
+                atomicOr(&g_rk_status, kStatusGridTimeout);
+                atomicExch(&sync->abort, 1u);
+                return false;
+            }
+            if (it >= 256u) __nanosleep(32);
+        }
+    }
+    return true;
+}
+
+// The global argmax of the ranks' vocabulary shards (thread 0 of CTA 0): every rank's per-column keys
+// (value, ~global row) go to every rank, and the maximum replaces this rank's slot, so all ranks continue
+// with the same token.
+template <int NC>
+__device__ __noinline__ bool xch_argmax(const XchDesc* x, unsigned long long* slots, unsigned long long epoch,
+                                        PSync* sync) {
+    const int me = x->rank, n = x->n, par = (int) (epoch & 1ull);
+    volatile unsigned long long* vs = slots;
+    unsigned long long mine[NC];
+#pragma unroll
+    for (int c = 0; c < NC; ++c) mine[c] = vs[c];
+    for (int q = 0; q < n; ++q)
+#pragma unroll
+        for (int c = 0; c < NC; ++c) x->keys[q][((size_t) par * kMaxRanks + me) * 2 + c] = mine[c];
+    if (!xch_signal_wait(x, x->slots - 1, epoch, sync)) return false;
+    const volatile unsigned long long* k = x->keys[me] + (size_t) par * kMaxRanks * 2;
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+        unsigned long long best = 0ull;
+        for (int q = 0; q < n; ++q) best = k[q * 2 + c] > best ? k[q * 2 + c] : best;
+        vs[c] = best;
+    }
+    __threadfence();
+    return true;
 }
 
 // ---------------------------------------------------------------------------------------------------
@@ -228,8 +306,15 @@ __device__ __forceinline__ void pipe_drain(WarpPipe& w) {
 // belongs to this warp is accumulated tile by tile from the ring (mmvq_packed_kernel's loop).
 template <int NC, int PRO, int EPI>
 __device__ __forceinline__ bool p_gemv(const MmvqParams& p, uint8_t* xsm, float* red, WarpPipe& w,
-                                       unsigned long long* tp) {
+                                       unsigned long long* tp, unsigned long long& xep, PSync* sync, int* sflag) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // EPI_XRES: this exchange's epoch and this rank's partial buffer (by epoch parity)
+    unsigned long long ep = 0ull;
+    float* ybuf = nullptr;
+    if constexpr (EPI == EPI_XRES) {
+        ep = ++xep;
+        ybuf = p.xch->buf[p.xch->rank] + (size_t) (ep & 1ull) * 2 * p.xch->rows;
+    }
     if (warp < 8) mmvq_build_x<NC, PRO>(p, xsm, red);
     __syncthreads();
     if (tp != nullptr && threadIdx.x == 0) *tp = globaltimer_ns();
@@ -269,7 +354,50 @@ __device__ __forceinline__ bool p_gemv(const MmvqParams& p, uint8_t* xsm, float*
             pipe_release(w, warp, lane);
         }
         if (!ok) break;
-        mmvq_epilogue<NC, EPI>(p, unit, lane, acc, best, resv);
+        if constexpr (EPI == EPI_XRES) {  // this rank's partial rows
+#pragma unroll
+            for (int c = 0; c < NC; ++c)
+#pragma unroll
+                for (int r = 0; r < 4; ++r) acc[c][r] = warp_sum(acc[c][r]);
+            float out = 0.0f;
+#pragma unroll
+            for (int c = 0; c < NC; ++c)
+#pragma unroll
+                for (int r = 0; r < 4; ++r)
+                    if (lane == c * 4 + r) out = acc[c][r];
+            if (lane < NC * 4) ybuf[(size_t) (lane >> 2) * p.xch->rows + unit * 4 + (lane & 3)] = out;
+        } else {
+            mmvq_epilogue<NC, EPI>(p, unit, lane, acc, best, resv);
+        }
+    }
+    if constexpr (EPI == EPI_XRES) {
+        // sum this CTA's rows over the ranks (the same rows on every rank: same grid, same split), in rank
+        // order, then the residual add and the 4-row partials as EPI_RES (or EPI_STORE_P without res)
+        __syncthreads();
+        if (threadIdx.x == 0) *sflag = ok && xch_signal_wait(p.xch, (int) blockIdx.x, ep, sync);
+        __syncthreads();
+        if (!*sflag) return false;
+        const XchDesc* x = p.xch;
+        const int n = x->n, me = x->rank;
+        const size_t base = (size_t) (ep & 1ull) * 2 * x->rows;
+        for (int idx = (int) threadIdx.x; idx < (uend - ubeg) * NC; idx += (int) blockDim.x) {
+            const int u = ubeg + idx / NC, c = idx % NC;
+            float part = 0.0f;
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                const size_t off = base + (size_t) c * x->rows + (size_t) u * 4 + r;
+                float v = 0.0f;
+                for (int q = 0; q < n; ++q) {
+                    const float pq = q == me ? __ldcg(x->buf[me] + off) : __ldcv(x->buf[q] + off);
+                    v = q == 0 ? pq : __fadd_rn(v, pq);
+                }
+                if (p.res != nullptr) v = __fadd_rn(v, __ldcg(p.res + (size_t) c * p.res_stride + (size_t) u * 4 + r));
+                p.y[(size_t) c * p.y_stride + (size_t) u * 4 + r] = v;
+                part = __fmaf_rn(v, v, part);
+            }
+            p.pout[(size_t) c * p.pout_stride + u] = part;
+        }
+        return ok;
     }
     if constexpr (EPI == EPI_SWIGLU) mmvq_swiglu_finish<NC>(p, ubeg + warp, kPWarps, unit, lane);
     if constexpr (EPI == EPI_ARGMAX) {
@@ -283,20 +411,22 @@ __device__ __forceinline__ bool p_gemv(const MmvqParams& p, uint8_t* xsm, float*
 // The prologue / epilogue pairs the engine's programs use (checked when a program is built).
 __host__ __device__ __forceinline__ bool gemv_combo_supported(int pro, int epi) {
     return (pro == PRO_RMS && (epi == EPI_STORE || epi == EPI_SWIGLU || epi == EPI_ARGMAX)) ||
-           (pro == PRO_Q8 && (epi == EPI_RES || epi == EPI_STORE_P));
+           (pro == PRO_Q8 && (epi == EPI_RES || epi == EPI_STORE_P || epi == EPI_XRES));
 }
 
 template <int NC>
 __device__ __forceinline__ bool p_gemv_dispatch(const POp& op, uint8_t* xsm, float* red, WarpPipe& w,
-                                                unsigned long long* tp) {
+                                                unsigned long long* tp, unsigned long long& xep, PSync* sync,
+                                                int* sflag) {
     const MmvqParams& p = op.g;
     if (op.pro == PRO_RMS) {
-        if (op.epi == EPI_STORE) return p_gemv<NC, PRO_RMS, EPI_STORE>(p, xsm, red, w, tp);
-        if (op.epi == EPI_SWIGLU) return p_gemv<NC, PRO_RMS, EPI_SWIGLU>(p, xsm, red, w, tp);
-        return p_gemv<NC, PRO_RMS, EPI_ARGMAX>(p, xsm, red, w, tp);
+        if (op.epi == EPI_STORE) return p_gemv<NC, PRO_RMS, EPI_STORE>(p, xsm, red, w, tp, xep, sync, sflag);
+        if (op.epi == EPI_SWIGLU) return p_gemv<NC, PRO_RMS, EPI_SWIGLU>(p, xsm, red, w, tp, xep, sync, sflag);
+        return p_gemv<NC, PRO_RMS, EPI_ARGMAX>(p, xsm, red, w, tp, xep, sync, sflag);
     }
-    if (op.epi == EPI_RES) return p_gemv<NC, PRO_Q8, EPI_RES>(p, xsm, red, w, tp);
-    return p_gemv<NC, PRO_Q8, EPI_STORE_P>(p, xsm, red, w, tp);
+    if (op.epi == EPI_RES) return p_gemv<NC, PRO_Q8, EPI_RES>(p, xsm, red, w, tp, xep, sync, sflag);
+    if (op.epi == EPI_XRES) return p_gemv<NC, PRO_Q8, EPI_XRES>(p, xsm, red, w, tp, xep, sync, sflag);
+    return p_gemv<NC, PRO_Q8, EPI_STORE_P>(p, xsm, red, w, tp, xep, sync, sflag);
 }
 
 // Asynchronous copy of op record j into shared memory (16-byte cp.async chunks, one per thread), so the
@@ -357,6 +487,8 @@ __global__ void __launch_bounds__(kPWarps * 32, 1)
     cp_async_wait_all();
     __syncthreads();
     unsigned long long target = 0ull;
+    unsigned long long xep = *reinterpret_cast<volatile unsigned long long*>(&sync->xepoch);
+    __shared__ int xflag;
     bool alive = ld_volatile_u32(&sync->abort) == 0u;
     if (alive) pipe_start(w, warp, lane);
     int k = 0;  // ops started; op_sm[k & 1] holds the running op
@@ -385,7 +517,11 @@ __global__ void __launch_bounds__(kPWarps * 32, 1)
             }
             bool ok = true;
             if (op.kind == POP_GEMV) {
-                ok = p_gemv_dispatch<NC>(op, region, red, w, tr != nullptr ? tr + 1 : nullptr);
+                ok = p_gemv_dispatch<NC>(op, region, red, w, tr != nullptr ? tr + 1 : nullptr, xep, sync, &xflag);
+            } else if (op.kind == POP_XARGMAX) {
+                const unsigned long long ep = ++xep;
+                if (blockIdx.x == 0 && threadIdx.x == 0)
+                    ok = xch_argmax<NC>(op.xa.xch, op.draft ? ctrl->damax : ctrl->amax, ep, sync);
             } else {
                 const int pos = ld_cg(op.draft ? &ctrl->dpos : &ctrl->pos);
                 const int rb = ld_cg(&ctrl->rollback);
@@ -412,6 +548,7 @@ __global__ void __launch_bounds__(kPWarps * 32, 1)
     }
     pipe_drain(w);
     __syncthreads();
+    if (blockIdx.x == 0 && threadIdx.x == 0) *reinterpret_cast<volatile unsigned long long*>(&sync->xepoch) = xep;
     if (threadIdx.x == 0) {
         __threadfence();
         if (atomicAdd(&sync->exits, 1u) == gridDim.x - 1) {

@@ -40,18 +40,21 @@ def config_tiny(max_ctx: int = 256, seed: int = 7, n_layer: int = 4, vocab: int 
 
 class Engine:
     """mode: None (the library default, persistent), "persistent" or "graph"; the executor is chosen when
-    the engine is created (the library reads RK_ENGINE_MODE then)."""
+    the engine is created (the library reads RK_ENGINE_MODE then). tp_rank / tp_size: this process's shard
+    under tensor parallelism (rk_engine_create_tp); connect the ranks with connect_tp() before use."""
 
-    def __init__(self, cfg: ModelConfig, device: int = 0, mode: str | None = None):
+    def __init__(self, cfg: ModelConfig, device: int = 0, mode: str | None = None, tp_rank: int = 0,
+                 tp_size: int = 1):
         import os
 
         self.cfg = cfg
+        self.tp_rank, self.tp_size = tp_rank, tp_size
         h = C.c_void_p()
         old = os.environ.get("RK_ENGINE_MODE")
         try:
             if mode is not None:
                 os.environ["RK_ENGINE_MODE"] = mode
-            _lib.call("rk_engine_create", C.byref(cfg), device, C.byref(h))
+            _lib.call("rk_engine_create_tp", C.byref(cfg), device, tp_rank, tp_size, C.byref(h))
         finally:
             if mode is not None:
                 if old is None:
@@ -82,11 +85,40 @@ class Engine:
         stats = {f: getattr(st, f) for f, _ in GenStats._fields_}
         return np.frombuffer(out, dtype=np.int32).copy(), stats
 
+    def tp_export(self) -> bytes:
+        """This rank's exchange-memory handle (rk_engine_tp_export)."""
+        n = _lib.lib().rk_tp_handle_bytes()
+        buf = (C.c_uint8 * n)()
+        _lib.call("rk_engine_tp_export", self._h, buf, n)
+        return bytes(buf)
+
+    def tp_connect(self, handles: list) -> None:
+        """Map every rank's exchange memory (handles in rank order, rk_engine_tp_connect)."""
+        n = _lib.lib().rk_tp_handle_bytes()
+        blob = b"".join(bytes(hh) for hh in handles)
+        if len(blob) != n * self.tp_size:
+            raise ValueError("one handle per rank expected")
+        buf = (C.c_uint8 * len(blob)).from_buffer_copy(blob)
+        _lib.call("rk_engine_tp_connect", self._h, buf, n)
+
+    def connect_tp(self, group=None) -> None:
+        """Exchange the handles over torch.distributed (any backend; `group` spans this engine's ranks, in
+        tensor-parallel rank order) and connect."""
+        import torch
+        import torch.distributed as dist
+
+        mine = self.tp_export()
+        dev = "cuda" if dist.get_backend(group) == "nccl" else "cpu"
+        t = torch.tensor(list(mine), dtype=torch.uint8, device=dev)
+        got = [torch.empty_like(t) for _ in range(self.tp_size)]
+        dist.all_gather(got, t, group=group)
+        self.tp_connect([bytes(g.cpu().tolist()) for g in got])
+
     def step(self, tokens, pos: int, want_logits: bool = True):
         n = len(tokens)
         t = (C.c_int * n)(*[int(x) for x in tokens])
         am = (C.c_int * n)()
-        logits = np.empty(n * self.cfg.n_vocab, np.float32) if want_logits else None
+        logits = np.empty(n * (self.cfg.n_vocab // self.tp_size), np.float32) if want_logits else None
         _lib.call("rk_engine_step", self._h, t, n, pos,
                   logits.ctypes.data_as(C.c_void_p) if want_logits else None, am)
         return (logits.reshape(n, -1) if want_logits else None), list(am)
