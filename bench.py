@@ -252,6 +252,18 @@ def cpu_baseline_gemv(sample_rows=4096):
 N_PROMPT, N_GEN = 32, 400
 
 
+def tp_layout(world: int) -> tuple:
+    """(tensor-parallel size, groups) for `world` GPUs: one tensor-parallel group of up to 4 ranks (the 9B
+    geometry's row-parallel inputs split into whole 1024-value tiles over 2 and 4 ranks), groups of 4
+    (independent streams) beyond that."""
+    if world in (1, 2, 4):
+        return world, 1
+    for tp in (4, 2):
+        if world % tp == 0:
+            return tp, world // tp
+    return 1, world
+
+
 def run_decode(args, rank, world, local, pg):
     import torch
 
@@ -259,9 +271,18 @@ def run_decode(args, rank, world, local, pg):
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    cfg = config_9b(max_ctx=args.ctx, seed=1 + rank)
-    eng = Engine(cfg, device=local)
-    prompt = [int(t) for t in np.random.default_rng(1234 + rank).integers(0, cfg.n_vocab, N_PROMPT)]
+    tp, groups = tp_layout(world)
+    grp, tp_rank = rank // tp, rank % tp
+    group = None
+    if tp > 1:
+        subgroups = [pg.new_group(list(range(g * tp, (g + 1) * tp))) for g in range(groups)]
+        group = subgroups[grp]
+    cfg = config_9b(max_ctx=args.ctx, seed=1 + grp)
+    eng = Engine(cfg, device=local, tp_rank=tp_rank, tp_size=tp)
+    if tp > 1:
+        eng.connect_tp(group)
+        barrier(pg, dev)
+    prompt = [int(t) for t in np.random.default_rng(1234 + grp).integers(0, cfg.n_vocab, N_PROMPT)]
     mtp = not args.no_mtp
     n_gen = args.gen
     for _ in range(args.warmup):
@@ -278,33 +299,43 @@ def run_decode(args, rank, world, local, pg):
     wall_s = time.perf_counter() - t0
     gen_ms = max_over_ranks(gen_ms, pg, dev)
     wall_s = max_over_ranks(wall_s, pg, dev)
-    tokens = n_gen * args.steps * world
+    tokens = n_gen * args.steps * groups
     probe = eng.probe_gemv(ncols=2 if mtp else 1, iters=20)
+    persistent = eng.mode == "persistent"
     eng.close()
     peak, peak_kind = measured_peaks()
     per_launch_s = probe["ms"] / 1e3 / (probe["iters"] * probe["launches"])
     algo_per_launch = probe["algo_bytes"] / probe["launches"]
     achieved = algo_per_launch / per_launch_s / 1e9
     rounds = stats["mtp_steps"]
-    launches_per_gen = (stats["single_steps"] * stats["kernels_per_single_step"] +
-                        rounds * stats["kernels_per_round"])
+    if persistent:  # one kernel per program run (a whole greedy generation is one run)
+        launches_per_gen = stats["graph_launches"]
+    else:
+        launches_per_gen = ((stats["graph_launches"] - rounds) * stats["kernels_per_single_step"] +
+                            rounds * stats["kernels_per_round"])
+    par = "single GPU" if world == 1 else (f"tensor parallel x{tp}" + (f", {groups} independent groups" if groups > 1 else ""))
     line = {
         "metric": "greedy decode tok/s (1 B200, exact MTP)" if mtp else "greedy decode tok/s (1 B200, no MTP)",
         "value": round(tokens / (gen_ms / 1e3), 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(gen_ms / args.steps, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "q6_k x q8_1 int8 dp4a, fp32 accumulate, fp16 KV",
+        "scaling": "strong" if (world > 1 and groups == 1) else "weak", "vs_baseline": None,
+        "dtype": "q6_k x q8_1 int8 dp4a, fp32 accumulate, fp16 KV",
         "data": "synthetic (random-init weights, seeded prompt)",
         "config": {"workload": "config5-decode-mtp" if mtp else "config4-decode", "model": "qwen35-9b-shaped",
                    "layers": "24 GDN + 8 GQA (+1 MTP block)", "n_prompt": N_PROMPT, "n_gen": n_gen,
-                   "ctx": args.ctx, "parallelism": f"replicas x{world}",
+                   "ctx": args.ctx, "parallelism": par, "tensor_parallel": tp, "groups": groups,
+                   "executor": "persistent" if persistent else "graph",
                    "l2": "6.5 GB of weights per token > 126 MB L2"},
         "mtp": {"rounds": rounds, "accepted": stats["mtp_accepted"],
                 "acceptance": round(stats["mtp_accepted"] / rounds, 4) if rounds else None,
                 "single_steps": stats["single_steps"]} if mtp else None,
-        "roofline": {"bound": "hbm", "kernel": "mmvq_packed_kernel (all GEMVs of one trunk step, graph replay)",
+        "roofline": {"bound": "hbm",
+                     "kernel": ("persistent_kernel (the GEMV ops of one trunk step, one launch)" if persistent else
+                                "mmvq_packed_kernel (all GEMVs of one trunk step, graph replay)"),
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
                      "traffic": None, "peak_source": peak_kind, "algorithmic_bytes_per_launch": round(algo_per_launch),
-                     "launches": probe["launches"], "avg_launch_us": round(per_launch_s * 1e6, 3)},
+                     "gemv_ops": probe["launches"], "avg_gemv_us": round(per_launch_s * 1e6, 3),
+                     "per_gpu": tp > 1},
         "e2e": {"value": round(tokens / wall_s, 2), "unit": "tok/s",
                 "h2d_bytes_per_step": N_PROMPT * 4 + 32 * (N_PROMPT + 2),
                 "d2h_bytes_per_step": n_gen * 4 + 4 * rounds + 96},
