@@ -209,12 +209,28 @@ typedef struct rk_model_config {
     float eps;         /* RMSNorm epsilon (1e-6) */
     double rope_base;  /* 1e7 */
     uint64_t seed;
+    double rope_yarn_factor; /* YaRN context scaling (src/qwythos.cpp:1990-1999); <= 1: plain RoPE */
+    double rope_orig_ctx;    /* YaRN original context length */
 } rk_model_config;
 
 /* Fills `cfg` with the 9B (Qwythos / Qwen3.5-9B) geometry and the given context and seed. */
 void rk_model_config_9b(rk_model_config* cfg, int max_ctx, uint64_t seed);
 
+
 typedef struct rk_engine rk_engine;
+
+/* The model geometry of a qwen35 GGUF file (the reference's load_model, src/qwythos.cpp:1978-2016):
+ * layer count from qwen35.block_count minus qwen35.nextn_predict_layers, widths and head counts from the
+ * tensor shapes, eps / rope base / YaRN factor and original context from the metadata. Reads the file
+ * only (no GPU). RK_EUNSUPPORTED for another architecture. */
+int rk_gguf_model_config(const char* path, int max_ctx, rk_model_config* cfg);
+/* An engine whose weights come from a qwen35 GGUF file (Q6_K matrices, F32/F16 vectors) instead of the
+ * synthetic generator; otherwise as rk_engine_create_tp (tp_size 1: a single GPU). Matrices of other
+ * quantization types are refused with RK_EUNSUPPORTED (this engine's GEMVs are Q6_K). */
+int rk_engine_create_gguf(const char* path, int device, int max_ctx, int tp_rank, int tp_size, rk_engine** out);
+/* The engine's RoPE table [n_pos][n_rot/2][cos, sin] (YaRN when factor > 1). No reference counterpart
+ * (a test hook for the table the engine builds). */
+int rk_rope_table(int n_rot, double base, double factor, double orig_ctx, int n_pos, float* out);
 
 typedef struct rk_gen_stats {
     double prefill_ms; /* prompt positions 0..P-2 */

@@ -37,7 +37,8 @@ class ModelConfig(C.Structure):
     _fields_ = [("n_layer", C.c_int), ("n_embd", C.c_int), ("n_ff", C.c_int), ("n_vocab", C.c_int),
                 ("ssm_h_k", C.c_int), ("ssm_h_v", C.c_int), ("n_head", C.c_int), ("n_head_kv", C.c_int),
                 ("n_rot", C.c_int), ("attn_interval", C.c_int), ("has_mtp", C.c_int), ("max_ctx", C.c_int),
-                ("eps", C.c_float), ("rope_base", C.c_double), ("seed", C.c_uint64)]
+                ("eps", C.c_float), ("rope_base", C.c_double), ("seed", C.c_uint64),
+                ("rope_yarn_factor", C.c_double), ("rope_orig_ctx", C.c_double)]
 
 
 class GenStats(C.Structure):
@@ -96,6 +97,9 @@ SIGNATURES = {
     "rk_engine_read_tensor": (sz, [vp, i32, vp, sz]),
     "rk_engine_device_bytes": (sz, [vp]),
     "rk_engine_mode": (i32, [vp]),
+    "rk_gguf_model_config": (i32, [C.c_char_p, i32, C.POINTER(ModelConfig)]),
+    "rk_engine_create_gguf": (i32, [C.c_char_p, i32, i32, i32, i32, C.POINTER(vp)]),
+    "rk_rope_table": (i32, [i32, C.c_double, C.c_double, C.c_double, i32, vp]),
     "rk_engine_create_tp": (i32, [C.POINTER(ModelConfig), i32, i32, i32, C.POINTER(vp)]),
     "rk_tp_handle_bytes": (sz, []),
     "rk_engine_tp_export": (i32, [vp, vp, sz]),

@@ -22,8 +22,10 @@
 #include <cstdlib>
 #include <cstring>
 #include <new>
+#include <string>
 #include <vector>
 
+#include "gguf.cuh"
 #include "persistent.cuh"
 
 namespace rk {
@@ -215,6 +217,11 @@ struct EngineImpl {
     XchDesc* xdesc = nullptr;
     std::vector<void*> peer_maps;
     bool tp_connected = false;
+    // weights from a GGUF file instead of the synthetic generator (during build only)
+    const GgufFile* gg = nullptr;
+    int src_rc = RK_OK;
+    std::string src_msg;
+    std::vector<uint8_t> stage;
     std::vector<void*> allocs;
     std::vector<TensorRec> tensors;
     size_t bytes = 0;
@@ -239,6 +246,15 @@ struct EngineImpl {
                  int ncb_b, uint8_t* scratch);
     void gen_q6k_into(int tid, Mat& group, int row_off, int n_in, int n_out, uint8_t* scratch) {
         gen_q6k(tid, group, row_off, n_in, 0, n_out, 0, n_in / 256, 0, 0, scratch);
+    }
+    std::string gguf_name(int tid) const;
+    bool src_fail(int rc, const std::string& msg) {
+        if (src_rc == RK_OK) {
+            src_rc = rc;
+            src_msg = msg;
+        }
+        if (err == cudaSuccess) err = cudaErrorInvalidValue;
+        return false;
     }
     int gdn_vhead(int j) const {  // global v-head of local v-head j (the v-heads paired with this rank's k-heads)
         return j < hk ? tp_rank * hk + j : cfg.ssm_h_k + tp_rank * hk + (j - hk);
@@ -278,8 +294,65 @@ EngineImpl::~EngineImpl() {
 // f32 tensors are generated on the host (they are small) with the same counter-based values the device
 // uses; kind 1: ssm_a = -exp(value) computed in double. pick: the global indices this rank keeps (a
 // tensor-parallel slice), n of them; else the whole tensor.
+// The GGUF tensor name of this library's tensor id (the reference's names, src/qwythos.cpp:2003-2124).
+std::string EngineImpl::gguf_name(int tid) const {
+    const std::string nx = "blk." + std::to_string(cfg.n_layer) + ".nextn.";
+    switch (tid) {
+        case T_TOK_EMBD: return "token_embd.weight";
+        case T_OUT_NORM: return "output_norm.weight";
+        case T_OUTPUT: return "output.weight";
+        case T_ENORM: return nx + "enorm.weight";
+        case T_HNORM: return nx + "hnorm.weight";
+        case T_EH_PROJ: return nx + "eh_proj.weight";
+        case T_SHNORM: return nx + "shared_head_norm.weight";
+        default: break;
+    }
+    const int il = (tid - 100) / 32, slot = (tid - 100) % 32;
+    const bool gdn = il < cfg.n_layer && (il + 1) % cfg.attn_interval != 0;
+    static const char* common[] = {"attn_norm.weight", "post_attention_norm.weight", "ffn_up.weight", "ffn_gate.weight",
+                                   "ffn_down.weight"};
+    static const char* gdn_names[] = {"attn_qkv.weight", "attn_gate.weight", "ssm_beta.weight", "ssm_alpha.weight",
+                                      "ssm_out.weight", "ssm_conv1d.weight", "ssm_a", "ssm_dt.bias", "ssm_norm.weight"};
+    static const char* att_names[] = {"attn_q.weight", "attn_k.weight", "attn_v.weight", "attn_output.weight",
+                                      "attn_q_norm.weight", "attn_k_norm.weight"};
+    const std::string b = "blk." + std::to_string(il) + ".";
+    if (slot < 5) return b + common[slot];
+    if (gdn && slot - 5 < 9) return b + gdn_names[slot - 5];
+    if (!gdn && slot - 5 < 6) return b + att_names[slot - 5];
+    return b + "?";
+}
+
 void EngineImpl::gen_f32(int tid, float* dst, size_t n, double std, double mean, int kind,
                          const std::vector<long long>* pick) {
+    if (gg) {  // from the file: F32 / F16 / BF16, the picked global indices or the whole tensor
+        const std::string name = gguf_name(tid);
+        const GgufTensor* t = gg->find(name);
+        if (!t) return (void) src_fail(RK_EINVAL, "tensor " + name + " missing");
+        const size_t total = (size_t) (t->ne[0] * t->ne[1] * t->ne[2] * t->ne[3]);
+        if ((t->type != kGgmlF32 && t->type != kGgmlF16 && t->type != kGgmlBF16) || (!pick && total != n))
+            return (void) src_fail(RK_EUNSUPPORTED, "tensor " + name + ": expected " + std::to_string(n) + " F32/F16 values");
+        std::vector<float> h(n);
+        for (size_t i = 0; i < n; ++i) {
+            const size_t gi = pick ? (size_t) (*pick)[i] : i;
+            if (gi >= total) return (void) src_fail(RK_EINVAL, "tensor " + name + " too small");
+            if (t->type == kGgmlF32) {
+                std::memcpy(&h[i], t->data + gi * 4, 4);
+            } else {
+                uint16_t b16;
+                std::memcpy(&b16, t->data + gi * 2, 2);
+                if (t->type == kGgmlF16) {
+                    h[i] = __half2float(__ushort_as_half(b16));
+                } else {
+                    const uint32_t u = (uint32_t) b16 << 16;
+                    std::memcpy(&h[i], &u, 4);
+                }
+            }
+        }
+        if (err == cudaSuccess) err = cudaMemcpyAsync(dst, h.data(), n * sizeof(float), cudaMemcpyHostToDevice, s);
+        if (err == cudaSuccess) err = cudaStreamSynchronize(s);
+        tensors.push_back({tid, false, (int) n, 1, dst, 0, false});
+        return;
+    }
     std::vector<float> h(n);
     const uint64_t st = hash64(cfg.seed, (uint64_t) tid);
     const float scale = synth_scale(std), m = (float) mean;
@@ -302,10 +375,30 @@ void EngineImpl::gen_q6k(int tid, Mat& group, int row_off, int n_in_full, int gr
                          int cb_b, int ncb_b, uint8_t* scratch) {
     const int n_in = (ncb_a + ncb_b) * 256;
     const long long nb = (long long) rows * (ncb_a + ncb_b);
-    const uint64_t st = hash64(cfg.seed, (uint64_t) tid);
-    gen_q6k_kernel<<<(unsigned) ((nb + 127) / 128), 128, 0, s>>>(st, synth_scale(0.02), rows, grow0, n_in_full / 256,
-                                                                 ncb_a, cb_a, ncb_b, cb_b, scratch);
-    if (err == cudaSuccess) err = cudaGetLastError();
+    if (gg) {  // the GGUF rows' bytes (this slice's column blocks), then the same repack
+        const std::string name = gguf_name(tid);
+        const GgufTensor* t = gg->find(name);
+        if (!t) return (void) src_fail(RK_EINVAL, "tensor " + name + " missing");
+        if (t->type != kGgmlQ6_K)
+            return (void) src_fail(RK_EUNSUPPORTED, "tensor " + name + " is ggml type " + std::to_string(t->type) +
+                                                        "; the engine's GEMVs take Q6_K (14)");
+        if (t->ne[0] != n_in_full || t->ne[1] < (int64_t) grow0 + rows)
+            return (void) src_fail(RK_EINVAL, "tensor " + name + " has an unexpected shape");
+        const size_t rb = ggml_row_bytes(kGgmlQ6_K, n_in_full), lrb = (size_t) (ncb_a + ncb_b) * 210;
+        stage.resize((size_t) rows * lrb);
+        for (int r = 0; r < rows; ++r) {
+            const uint8_t* src = t->data + (size_t) (grow0 + r) * rb;
+            std::memcpy(stage.data() + (size_t) r * lrb, src + (size_t) cb_a * 210, (size_t) ncb_a * 210);
+            if (ncb_b) std::memcpy(stage.data() + (size_t) r * lrb + (size_t) ncb_a * 210, src + (size_t) cb_b * 210, (size_t) ncb_b * 210);
+        }
+        if (err == cudaSuccess) err = cudaMemcpyAsync(scratch, stage.data(), stage.size(), cudaMemcpyHostToDevice, s);
+        if (err == cudaSuccess) err = cudaStreamSynchronize(s);
+    } else {
+        const uint64_t st = hash64(cfg.seed, (uint64_t) tid);
+        gen_q6k_kernel<<<(unsigned) ((nb + 127) / 128), 128, 0, s>>>(st, synth_scale(0.02), rows, grow0, n_in_full / 256,
+                                                                     ncb_a, cb_a, ncb_b, cb_b, scratch);
+        if (err == cudaSuccess) err = cudaGetLastError();
+    }
     if (err != cudaSuccess) return;
     uint8_t* dst = group.w + (size_t) (row_off / 4) * (n_in / 1024) * kQ6Tile;
     const int rc = rk_pack_weights(RK_TYPE_Q6_K, scratch, dst, n_in, rows, s);
@@ -353,7 +446,14 @@ int EngineImpl::build() {
     };
     // globals: the embedding table is replicated; the lm_head is vocabulary-sharded
     tok_embd = alloc<uint8_t>(rk_weight_bytes(RK_TYPE_Q6_K, H, Vg));
-    if (tok_embd) {
+    if (tok_embd && gg) {
+        const GgufTensor* t = gg->find("token_embd.weight");
+        if (!t || t->type != kGgmlQ6_K || t->ne[0] != H || t->ne[1] != Vg)
+            src_fail(RK_EUNSUPPORTED, "token_embd.weight must be Q6_K [n_embd x n_vocab]");
+        else if (err == cudaSuccess)
+            err = cudaMemcpy(tok_embd, t->data, t->bytes, cudaMemcpyHostToDevice);
+        tensors.push_back({T_TOK_EMBD, true, H, Vg, tok_embd, 0, true});
+    } else if (tok_embd) {
         const long long nb = (long long) Vg * (H / 256);
         gen_q6k_kernel<<<(unsigned) ((nb + 127) / 128), 128, 0, s>>>(hash64(c.seed, T_TOK_EMBD), synth_scale(0.02), Vg,
                                                                      0, H / 256, H / 256, 0, 0, 0, tok_embd);
@@ -454,16 +554,10 @@ int EngineImpl::build() {
     }
     cudaStreamSynchronize(s);
     cudaFree(scratch);
-    // rope table (double precision on the host, stored as float)
+    // rope table (double precision on the host, stored as float; YaRN when the factor is > 1)
     {
-        const int half = c.n_rot / 2;
-        std::vector<float> t((size_t) c.max_ctx * half * 2);
-        for (int p = 0; p < c.max_ctx; ++p)
-            for (int i = 0; i < half; ++i) {
-                const double a = (double) p * std::pow(c.rope_base, -2.0 * i / (double) c.n_rot);
-                t[((size_t) p * half + i) * 2 + 0] = (float) std::cos(a);
-                t[((size_t) p * half + i) * 2 + 1] = (float) std::sin(a);
-            }
+        std::vector<float> t;
+        build_rope_table(c.n_rot, c.rope_base, c.rope_yarn_factor, c.rope_orig_ctx, c.max_ctx, t);
         rope = alloc<float>(t.size());
         if (rope && err == cudaSuccess)
             err = cudaMemcpyAsync(rope, t.data(), t.size() * sizeof(float), cudaMemcpyHostToDevice, s);
@@ -495,6 +589,7 @@ int EngineImpl::build() {
     stage_slots = 4096;  // plus one slot after them for the emitted-count readback
     if (err == cudaSuccess) err = cudaMallocHost(&ctrl_stage, sizeof(Ctrl) * (stage_slots + 1));
     if (err == cudaSuccess) err = cudaStreamSynchronize(s);
+    if (src_rc != RK_OK) return src_rc;
     if (err == cudaErrorMemoryAllocation) return RK_ENOMEM;
     return err == cudaSuccess ? RK_OK : RK_ECUDA;
 }
@@ -917,13 +1012,16 @@ void rk_model_config_9b(rk_model_config* c, int max_ctx, uint64_t seed) {
     c->eps = 1e-6f;
     c->rope_base = 1e7;
     c->seed = seed;
+    c->rope_yarn_factor = 1.0;
+    c->rope_orig_ctx = 262144.0;
 }
 
 int rk_engine_create(const rk_model_config* cfg, int device, rk_engine** out) {
     return rk_engine_create_tp(cfg, device, 0, 1, out);
 }
 
-int rk_engine_create_tp(const rk_model_config* cfg, int device, int tp_rank, int tp_size, rk_engine** out) {
+static int create_engine(const rk_model_config* cfg, int device, int tp_rank, int tp_size, const GgufFile* gg,
+                         rk_engine** out) {
     const char* what = "rk_engine_create";
     if (!cfg || !out) return set_error(RK_EINVAL, "%s: null argument", what);
     const rk_model_config& c = *cfg;
@@ -959,12 +1057,19 @@ int rk_engine_create_tp(const rk_model_config* cfg, int device, int tp_rank, int
     e->impl.tp_rank = tp_rank;
     e->impl.tp_size = tp_size;
     EngineImpl& E = e->impl;
+    E.gg = gg;
     int rc = E.build();
+    E.gg = nullptr;
+    if (rc != RK_OK && E.src_rc != RK_OK) {
+        const std::string msg = E.src_msg;
+        delete e;
+        return set_error(rc, "%s: %s", what, msg.c_str());
+    }
     if (rc == RK_OK) rc = E.setup_executor();
     if (rc == RK_OK && tp_size > 1 && !E.persistent) rc = RK_EUNSUPPORTED;
     if (rc == RK_OK && tp_size > 1) {
-        // this rank's exchange memory: partials [2][2][H] floats | flags [grid + 1][8] | keys [2][8][2]
-        E.xoff_flags = (size_t) 4 * E.H * sizeof(float);
+        // this rank's exchange memory: partials [2][8][2][H] floats | flags [grid + 1][8] | keys [2][8][2]
+        E.xoff_flags = (size_t) 2 * kMaxRanks * 2 * E.H * sizeof(float);
         E.xoff_keys = E.xoff_flags + (size_t) (E.p_grid + 1) * kMaxRanks * 8;
         E.xmem_bytes = E.xoff_keys + (size_t) 2 * kMaxRanks * 2 * 8;
         void* p = nullptr;
@@ -1022,6 +1127,19 @@ int rk_engine_create_tp(const rk_model_config* cfg, int device, int tp_rank, int
     }
     *out = e;
     return RK_OK;
+}
+
+int rk_engine_create_tp(const rk_model_config* cfg, int device, int tp_rank, int tp_size, rk_engine** out) {
+    return create_engine(cfg, device, tp_rank, tp_size, nullptr, out);
+}
+
+int rk_engine_create_gguf(const char* path, int device, int max_ctx, int tp_rank, int tp_size, rk_engine** out) {
+    rk_model_config c;
+    if (int rc = rk_gguf_model_config(path, max_ctx, &c)) return rc;
+    GgufFile f;
+    std::string err;
+    if (!f.open(path, err)) return set_error(RK_EINVAL, "rk_engine_create_gguf: %s", err.c_str());
+    return create_engine(&c, device, tp_rank, tp_size, &f, out);
 }
 
 size_t rk_tp_handle_bytes(void) { return sizeof(cudaIpcMemHandle_t); }

@@ -44,17 +44,18 @@ struct PSync {
 };
 
 // Tensor parallelism: every rank's exchange memory, mapped into this rank's address space (CUDA IPC over
-// NVLink). A rank writes its row-parallel partial sums into its own buffer and signals each peer by a
-// system-scope release store of the exchange's epoch into the peer's flag slot; a peer that has acquired
-// all the signals of a slot reads the partials with uncached loads. Epochs only grow, the flag words of
-// a slot only grow, so no flag is ever cleared; buffers alternate by epoch parity, and a rank starts an
-// exchange only after every peer has signalled the previous one, so no buffer is rewritten while read.
+// NVLink). A rank pushes its row-parallel partial sums into its own slot of every rank's buffer (posted
+// peer stores), then signals each peer by a system-scope release store of the exchange's epoch into the
+// peer's flag slot; a rank that has acquired all the signals of a slot sums the partials from its own
+// memory. Epochs only grow, the flag words of a slot only grow, so no flag is ever cleared; buffers
+// alternate by epoch parity, and a rank starts an exchange only after every peer has signalled the
+// previous one (which a peer does after reading), so no buffer is rewritten while read.
 constexpr int kMaxRanks = 8;
 struct XchDesc {
     int rank, n;  // this rank, number of ranks
     int rows;     // rows of a partial column (the hidden size)
     int slots;    // flag slots: one per persistent CTA + one for the argmax exchange
-    float* buf[kMaxRanks];                 // per rank: partials [2 parity][2 columns][rows]
+    float* buf[kMaxRanks];                 // per rank: partials [2 parity][kMaxRanks source][2 columns][rows]
     unsigned long long* flags[kMaxRanks];  // per rank: [slots][kMaxRanks] epochs, written by the peers
     unsigned long long* keys[kMaxRanks];   // per rank: argmax keys [2 parity][kMaxRanks][2 columns]
 };
@@ -310,10 +311,10 @@ __device__ __forceinline__ bool p_gemv(const MmvqParams& p, uint8_t* xsm, float*
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // EPI_XRES: this exchange's epoch and this rank's partial buffer (by epoch parity)
     unsigned long long ep = 0ull;
-    float* ybuf = nullptr;
+    size_t yoff = 0;  // this rank's slot in every rank's partial buffer for this exchange
     if constexpr (EPI == EPI_XRES) {
         ep = ++xep;
-        ybuf = p.xch->buf[p.xch->rank] + (size_t) (ep & 1ull) * 2 * p.xch->rows;
+        yoff = (((size_t) (ep & 1ull) * kMaxRanks + p.xch->rank) * 2) * p.xch->rows;
     }
     if (warp < 8) mmvq_build_x<NC, PRO>(p, xsm, red);
     __syncthreads();
@@ -365,7 +366,10 @@ __device__ __forceinline__ bool p_gemv(const MmvqParams& p, uint8_t* xsm, float*
 #pragma unroll
                 for (int r = 0; r < 4; ++r)
                     if (lane == c * 4 + r) out = acc[c][r];
-            if (lane < NC * 4) ybuf[(size_t) (lane >> 2) * p.xch->rows + unit * 4 + (lane & 3)] = out;
+            if (lane < NC * 4) {  // pushed to every rank (peer stores are posted)
+                const size_t o = yoff + (size_t) (lane >> 2) * p.xch->rows + unit * 4 + (lane & 3);
+                for (int q = 0; q < p.xch->n; ++q) p.xch->buf[q][o] = out;
+            }
         } else {
             mmvq_epilogue<NC, EPI>(p, unit, lane, acc, best, resv);
         }
@@ -373,24 +377,28 @@ __device__ __forceinline__ bool p_gemv(const MmvqParams& p, uint8_t* xsm, float*
     if constexpr (EPI == EPI_XRES) {
         // sum this CTA's rows over the ranks (the same rows on every rank: same grid, same split), in rank
         // order, then the residual add and the 4-row partials as EPI_RES (or EPI_STORE_P without res)
+        __threadfence_system();  // this thread's pushed partials, before the CTA's signal
         __syncthreads();
         if (threadIdx.x == 0) *sflag = ok && xch_signal_wait(p.xch, (int) blockIdx.x, ep, sync);
         __syncthreads();
         if (!*sflag) return false;
         const XchDesc* x = p.xch;
-        const int n = x->n, me = x->rank;
-        const size_t base = (size_t) (ep & 1ull) * 2 * x->rows;
+        const int n = x->n;
+        const float* mine = x->buf[x->rank] + (size_t) (ep & 1ull) * kMaxRanks * 2 * x->rows;
+        const size_t src_stride = (size_t) 2 * x->rows;
         for (int idx = (int) threadIdx.x; idx < (uend - ubeg) * NC; idx += (int) blockDim.x) {
             const int u = ubeg + idx / NC, c = idx % NC;
             float part = 0.0f;
 #pragma unroll
             for (int r = 0; r < 4; ++r) {
-                const size_t off = base + (size_t) c * x->rows + (size_t) u * 4 + r;
-                float v = 0.0f;
-                for (int q = 0; q < n; ++q) {
-                    const float pq = q == me ? __ldcg(x->buf[me] + off) : __ldcv(x->buf[q] + off);
-                    v = q == 0 ? pq : __fadd_rn(v, pq);
-                }
+                const size_t off = (size_t) c * x->rows + (size_t) u * 4 + r;
+                float pq[kMaxRanks];
+#pragma unroll
+                for (int q = 0; q < kMaxRanks; ++q) pq[q] = q < n ? __ldcg(mine + q * src_stride + off) : 0.0f;
+                float v = pq[0];
+#pragma unroll
+                for (int q = 1; q < kMaxRanks; ++q)
+                    if (q < n) v = __fadd_rn(v, pq[q]);
                 if (p.res != nullptr) v = __fadd_rn(v, __ldcg(p.res + (size_t) c * p.res_stride + (size_t) u * 4 + r));
                 p.y[(size_t) c * p.y_stride + (size_t) u * 4 + r] = v;
                 part = __fmaf_rn(v, v, part);

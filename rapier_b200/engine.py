@@ -38,30 +38,59 @@ def config_tiny(max_ctx: int = 256, seed: int = 7, n_layer: int = 4, vocab: int 
     return c
 
 
+def gguf_config(path: str, max_ctx: int = 4096) -> ModelConfig:
+    """The model geometry of a qwen35 GGUF file (rk_gguf_model_config; reads the file only)."""
+    c = ModelConfig()
+    _lib.call("rk_gguf_model_config", str(path).encode(), max_ctx, C.byref(c))
+    return c
+
+
+class _engine_mode:
+    """Sets RK_ENGINE_MODE around an engine's creation (the library reads it there)."""
+
+    def __init__(self, mode):
+        self.mode = mode
+
+    def __enter__(self):
+        import os
+
+        self.old = os.environ.get("RK_ENGINE_MODE")
+        if self.mode is not None:
+            os.environ["RK_ENGINE_MODE"] = self.mode
+
+    def __exit__(self, *exc):
+        import os
+
+        if self.mode is not None:
+            if self.old is None:
+                os.environ.pop("RK_ENGINE_MODE", None)
+            else:
+                os.environ["RK_ENGINE_MODE"] = self.old
+
+
 class Engine:
     """mode: None (the library default, persistent), "persistent" or "graph"; the executor is chosen when
     the engine is created (the library reads RK_ENGINE_MODE then). tp_rank / tp_size: this process's shard
     under tensor parallelism (rk_engine_create_tp); connect the ranks with connect_tp() before use."""
 
     def __init__(self, cfg: ModelConfig, device: int = 0, mode: str | None = None, tp_rank: int = 0,
-                 tp_size: int = 1):
-        import os
-
+                 tp_size: int = 1, _gguf: str | None = None):
         self.cfg = cfg
         self.tp_rank, self.tp_size = tp_rank, tp_size
         h = C.c_void_p()
-        old = os.environ.get("RK_ENGINE_MODE")
-        try:
-            if mode is not None:
-                os.environ["RK_ENGINE_MODE"] = mode
-            _lib.call("rk_engine_create_tp", C.byref(cfg), device, tp_rank, tp_size, C.byref(h))
-        finally:
-            if mode is not None:
-                if old is None:
-                    os.environ.pop("RK_ENGINE_MODE", None)
-                else:
-                    os.environ["RK_ENGINE_MODE"] = old
+        with _engine_mode(mode):
+            if _gguf is None:
+                _lib.call("rk_engine_create_tp", C.byref(cfg), device, tp_rank, tp_size, C.byref(h))
+            else:
+                _lib.call("rk_engine_create_gguf", _gguf.encode(), device, cfg.max_ctx, tp_rank, tp_size,
+                          C.byref(h))
         self._h = h
+
+    @classmethod
+    def from_gguf(cls, path: str, device: int = 0, max_ctx: int = 4096, mode: str | None = None,
+                  tp_rank: int = 0, tp_size: int = 1) -> "Engine":
+        """An engine over the weights of a qwen35 GGUF file (Q6_K matrices; rk_engine_create_gguf)."""
+        return cls(gguf_config(path, max_ctx), device, mode, tp_rank, tp_size, _gguf=str(path))
 
     def close(self):
         if self._h:
