@@ -828,7 +828,9 @@ int EngineImpl::setup_executor() {
     if ((err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return RK_ECUDA;
     if ((err = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) != cudaSuccess)
         return RK_ECUDA;
-    int cap = kMmvqMaxStages;
+    // Two slots per warp (32 tiles, 107 KB in flight per SM) keep HBM busy; deeper rings only queue more
+    // bulk copies ahead of the activation loads at op boundaries, which then wait longer.
+    int cap = 2;
     if (const char* st = std::getenv("RK_PERSIST_STAGES")) {
         const int v = std::atoi(st);
         if (v >= 2 && v <= kMmvqMaxStages) cap = v;

@@ -90,27 +90,30 @@ __device__ __forceinline__ unsigned long long globaltimer_ns() {
     return t;
 }
 
-// Grid barrier: the counter starts at 0 in every launch and every barrier adds gridDim.x arrivals.
-// Returns false when the program must stop (abort seen, or this spin gave up).
-__device__ __forceinline__ bool grid_sync(PSync* sync, unsigned long long& target, int* flag) {
-    __syncthreads();
+// Grid barrier: the counter starts at 0 in every launch and every barrier adds gridDim.x arrivals. A CTA
+// that failed (any thread's `failed`) arrives with kAbortArrive more, so every waiter of this barrier and
+// of all later ones sees the failure in the same load that ends its wait; the sticky abort word (set by the
+// failing CTA for the host) is polled only every 64 spins, for a CTA that gave up without arriving.
+// Returns false when the program must stop (a failed arrival, abort seen, or this spin gave up).
+constexpr unsigned long long kAbortArrive = 1ull << 40;
+__device__ __forceinline__ bool grid_sync(PSync* sync, unsigned long long& target, int* flag, bool failed) {
+    const int any_failed = __syncthreads_or(failed ? 1 : 0);
     target += gridDim.x;
     if (threadIdx.x == 0) {
-        // release: this CTA's writes (ordered before by the bar.sync above) become visible with the arrival
-        asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(&sync->arrive), "l"(1ull) : "memory");
+        // release: this CTA's writes (ordered before by the bar.red above) become visible with the arrival
+        const unsigned long long add = any_failed ? kAbortArrive + 1ull : 1ull;
+        asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(&sync->arrive), "l"(add) : "memory");
         int good = 1;
-        unsigned long long t0 = 0;
-        for (uint32_t it = 0; ld_acquire_u64(&sync->arrive) < target; ++it) {
-            if (ld_volatile_u32(&sync->abort)) {
-                good = 0;
-                break;
-            }
+        unsigned long long t0 = 0, v = 0;
+        for (uint32_t it = 0;; ++it) {
+            v = ld_acquire_u64(&sync->arrive);
+            if (v >= target) break;
             if ((it & 63u) == 0u) {
                 const unsigned long long now = globaltimer_ns();
                 if (it == 0u) {
                     t0 = now;
-                } else if (now - t0 > kGridSpinNs) {
-                    atomicOr(&g_rk_status, kStatusGridTimeout);
+                } else if (ld_volatile_u32(&sync->abort) || now - t0 > kGridSpinNs) {
+                    if (!ld_volatile_u32(&sync->abort)) atomicOr(&g_rk_status, kStatusGridTimeout);
                     atomicExch(&sync->abort, 1u);
                     good = 0;
                     break;
@@ -118,10 +121,10 @@ __device__ __forceinline__ bool grid_sync(PSync* sync, unsigned long long& targe
             }
             if (it >= 256u) __nanosleep(32);
         }
-        if (good && ld_volatile_u32(&sync->abort)) good = 0;
-        __threadfence();
+        if (v >= kAbortArrive) good = 0;
         *flag = good;
     }
+    // the acquire above and this bar.sync order the whole CTA's later reads after every arrival
     __syncthreads();
     return *flag != 0;
 }
@@ -538,7 +541,7 @@ __global__ void __launch_bounds__(kPWarps * 32, 1)
                     for (int it = (int) blockIdx.x; it < items; it += (int) gridDim.x)
                         run_item<NC>(op, ctrl, it, pos, rb, reinterpret_cast<float*>(region), red);
             }
-            if (!ok && lane == 0) atomicExch(&sync->abort, 1u);
+            if (!ok && lane == 0) atomicExch(&sync->abort, 1u);  // for the host; the barrier carries it too
             if (tc != nullptr) {
                 __syncthreads();
                 if (threadIdx.x == 0) {
@@ -548,7 +551,8 @@ __global__ void __launch_bounds__(kPWarps * 32, 1)
                 }
             }
             cp_async_wait_all();  // the next record has landed (made visible by the barrier's bar.sync)
-            if (j + 1 < nops || until > 0) alive = grid_sync(sync, target, &flag);
+            if (j + 1 < nops || until > 0) alive = grid_sync(sync, target, &flag, !ok);
+            else if (!ok) alive = false;
             if (tr != nullptr && threadIdx.x == 0) tr[3] = globaltimer_ns();
         }
         if (!alive || until <= 0 || iter >= max_iters) break;

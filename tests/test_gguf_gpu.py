@@ -39,8 +39,8 @@ def test_tensors_and_logits_bitwise(pair):
     syn.reset()
     fil.reset()
     for pos, tok in enumerate([5, 900, 17, 4000, 3]):
-        a, b = syn.step([tok], pos), fil.step([tok], pos)
-        assert np.array_equal(a, b), pos
+        (la, ta), (lb, tb) = syn.step([tok], pos), fil.step([tok], pos)
+        assert np.array_equal(la, lb) and ta == tb, pos
 
 
 @pytest.mark.parametrize("mtp", [False, True])
