@@ -140,18 +140,21 @@ __device__ __forceinline__ void xstage_put_warp(const XStage& s, int g, int code
     if (lane == 0) s.meta[g] = make_float4(half_bits_to_float(ds), __int_as_float(32 * s0), __int_as_float(32 * s1), 0.0f);
 }
 
-// Build every column's staged activations. Threads 0..255 participate (contains block_sync256).
+// Build every column's staged activations, with every thread of the block (256 in the per-op kernel,
+// 512 in the persistent one); the result does not depend on the block size.
 // PRO_Q8: one thread per Q8_1 block (9 ints) -> planes + meta.
 // PRO_RMS: the reference's rms_quant_apply (inv from the partials, v = x * w * inv, Q8_1 per 32 values)
 // with one thread per 16-value half block: every load is issued before any arithmetic, the two halves of
 // a block meet through one shuffle (amax), and each half's codes go to its plane. The codes and scale are
-// those of the standalone kernel (same q8_* rules on the same fp32 values).
+// those of the standalone kernel (same q8_* rules on the same fp32 values). The partial sums are reduced
+// as block256_partials_sum does (threads 0..255, then the 8 warp totals in order), every column at once,
+// with one block-wide barrier; `red` holds NC * 8 floats.
 template <int NC, int PRO>
 __device__ __noinline__ void mmvq_build_x(const MmvqParams& p, uint8_t* xsm, float* red) {
     const int ng = p.n_in >> 5;
     if constexpr (PRO == PRO_Q8) {
         const size_t col_bytes = p.xq_stride > 0 ? (size_t) p.xq_stride : (size_t) ng * 36;
-        for (int idx = threadIdx.x; idx < NC * ng; idx += 256) {
+        for (int idx = threadIdx.x; idx < NC * ng; idx += (int) blockDim.x) {
             const int c = idx / ng, g = idx - c * ng;
             const int* blk = reinterpret_cast<const int*>(p.xq + (size_t) c * col_bytes + (size_t) g * 36);
             const uint32_t ds = (uint32_t) __ldcg(blk);
@@ -182,11 +185,28 @@ __device__ __noinline__ void mmvq_build_x(const MmvqParams& p, uint8_t* xsm, flo
             }
         };
         if ((int) threadIdx.x < items) load((int) threadIdx.x);
+        if (threadIdx.x < 256) {
+            const int t = (int) threadIdx.x, nslots = p.n_in / 4;
+#pragma unroll
+            for (int c = 0; c < NC; ++c) {
+                const float* pc = p.pin + (size_t) c * nslots;
+                float part = 0.0f;
+                for (int q = t; q < nslots; q += 256) part = __fadd_rn(part, __ldcg(pc + q));
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) part = __fadd_rn(part, __shfl_down_sync(0xffffffffu, part, off));
+                if ((t & 31) == 0) red[c * 8 + (t >> 5)] = part;
+            }
+        }
+        __syncthreads();
         float inv[NC];
 #pragma unroll
-        for (int c = 0; c < NC; ++c)
-            inv[c] = rms_inv(block256_partials_sum(p.pin + (size_t) c * (p.n_in / 4), p.n_in / 4, red), p.n_in, p.eps);
-        for (int base = 0; base < items; base += 256) {
+        for (int c = 0; c < NC; ++c) {
+            float ss = red[c * 8];
+#pragma unroll
+            for (int w = 1; w < 8; ++w) ss = __fadd_rn(ss, red[c * 8 + w]);
+            inv[c] = rms_inv(ss, p.n_in, p.eps);
+        }
+        for (int base = 0; base < items; base += (int) blockDim.x) {
             const int it = base + (int) threadIdx.x;
             const bool live = it < items;
             const int c = live ? it / (2 * ng) : 0;
@@ -437,7 +457,7 @@ template <int TYPE, int NC, int PRO, int EPI>
 __global__ void __launch_bounds__(kMmvqWarps * 32, 2) mmvq_packed_kernel(const MmvqParams p) {
     constexpr int TILE = TYPE == RK_TYPE_Q6_K ? kQ6Tile : kQ80Tile;
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ float red[8];
+    __shared__ float red[16];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int KC = p.n_in >> 10;
     const int ng = p.n_in >> 5;

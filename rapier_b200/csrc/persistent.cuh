@@ -308,9 +308,16 @@ __device__ __forceinline__ void pipe_drain(WarpPipe& w) {
 
 // One GEMV op: the prologue builds the staged activations, then every unit of this CTA's range that
 // belongs to this warp is accumulated tile by tile from the ring (mmvq_packed_kernel's loop).
+// An L2 prefetch request (the next GEMV's share of this CTA; bytes 0: none).
+struct L2Pf {
+    const void* ptr;
+    uint32_t bytes;
+};
+
 template <int NC, int PRO, int EPI>
 __device__ __forceinline__ bool p_gemv(const MmvqParams& p, uint8_t* xsm, float* red, WarpPipe& w,
-                                       unsigned long long* tp, unsigned long long& xep, PSync* sync, int* sflag) {
+                                       unsigned long long* tp, unsigned long long& xep, PSync* sync, int* sflag,
+                                       const L2Pf& pf) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // EPI_XRES: this exchange's epoch and this rank's partial buffer (by epoch parity)
     unsigned long long ep = 0ull;
@@ -319,9 +326,11 @@ __device__ __forceinline__ bool p_gemv(const MmvqParams& p, uint8_t* xsm, float*
         ep = ++xep;
         yoff = (((size_t) (ep & 1ull) * kMaxRanks + p.xch->rank) * 2) * p.xch->rows;
     }
-    if (warp < 8) mmvq_build_x<NC, PRO>(p, xsm, red);
+    mmvq_build_x<NC, PRO>(p, xsm, red);
     __syncthreads();
     if (tp != nullptr && threadIdx.x == 0) *tp = globaltimer_ns();
+    // the next GEMV's L2 prefetch goes out only now, behind this prologue's loads
+    if (threadIdx.x == 256 && pf.bytes > 0) prefetch_l2(pf.ptr, pf.bytes);
     const int KC = p.n_in >> 10, ng = p.n_in >> 5;
     const int units = p.n_out >> 2;
     const int ubeg = (int) (((long long) blockIdx.x * units) / gridDim.x);
@@ -428,16 +437,16 @@ __host__ __device__ __forceinline__ bool gemv_combo_supported(int pro, int epi) 
 template <int NC>
 __device__ __forceinline__ bool p_gemv_dispatch(const POp& op, uint8_t* xsm, float* red, WarpPipe& w,
                                                 unsigned long long* tp, unsigned long long& xep, PSync* sync,
-                                                int* sflag) {
+                                                int* sflag, const L2Pf& pf) {
     const MmvqParams& p = op.g;
     if (op.pro == PRO_RMS) {
-        if (op.epi == EPI_STORE) return p_gemv<NC, PRO_RMS, EPI_STORE>(p, xsm, red, w, tp, xep, sync, sflag);
-        if (op.epi == EPI_SWIGLU) return p_gemv<NC, PRO_RMS, EPI_SWIGLU>(p, xsm, red, w, tp, xep, sync, sflag);
-        return p_gemv<NC, PRO_RMS, EPI_ARGMAX>(p, xsm, red, w, tp, xep, sync, sflag);
+        if (op.epi == EPI_STORE) return p_gemv<NC, PRO_RMS, EPI_STORE>(p, xsm, red, w, tp, xep, sync, sflag, pf);
+        if (op.epi == EPI_SWIGLU) return p_gemv<NC, PRO_RMS, EPI_SWIGLU>(p, xsm, red, w, tp, xep, sync, sflag, pf);
+        return p_gemv<NC, PRO_RMS, EPI_ARGMAX>(p, xsm, red, w, tp, xep, sync, sflag, pf);
     }
-    if (op.epi == EPI_RES) return p_gemv<NC, PRO_Q8, EPI_RES>(p, xsm, red, w, tp, xep, sync, sflag);
-    if (op.epi == EPI_XRES) return p_gemv<NC, PRO_Q8, EPI_XRES>(p, xsm, red, w, tp, xep, sync, sflag);
-    return p_gemv<NC, PRO_Q8, EPI_STORE_P>(p, xsm, red, w, tp, xep, sync, sflag);
+    if (op.epi == EPI_RES) return p_gemv<NC, PRO_Q8, EPI_RES>(p, xsm, red, w, tp, xep, sync, sflag, pf);
+    if (op.epi == EPI_XRES) return p_gemv<NC, PRO_Q8, EPI_XRES>(p, xsm, red, w, tp, xep, sync, sflag, pf);
+    return p_gemv<NC, PRO_Q8, EPI_STORE_P>(p, xsm, red, w, tp, xep, sync, sflag, pf);
 }
 
 // Asynchronous copy of op record j into shared memory (16-byte cp.async chunks, one per thread), so the
@@ -464,7 +473,7 @@ __global__ void __launch_bounds__(kPWarps * 32, 1)
                       PSync* sync, int stages, int region_bytes, int l2pf, int until, int max_iters,
                       unsigned long long* trace) {
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ float red[8];
+    __shared__ float red[16];
     __shared__ int flag;
     __shared__ POp op_sm[2];  // the running op's record and the next one's (fetched while the op runs)
     __shared__ GemvEnt gt_sm[kMaxGemvOps];
@@ -508,14 +517,16 @@ __global__ void __launch_bounds__(kPWarps * 32, 1)
             const POp& op = op_sm[k & 1];
             const int next = j + 1 < nops ? j + 1 : (until > 0 ? 0 : -1);
             if (next >= 0) op_fetch(prog, next, &op_sm[(k + 1) & 1]);
-            // this CTA's share of the next GEMV into L2 (warp 8: off the prologue's warps)
+            // this CTA's share of the next GEMV into L2 (thread 256; a GEMV issues it after its prologue)
+            L2Pf pf = {nullptr, 0u};
             if (threadIdx.x == 256 && l2pf > 0 && op.next_gemv >= 0) {
                 const GemvEnt& e = gt_sm[op.next_gemv];
                 const int ubeg = (int) (((long long) blockIdx.x * e.units) / gridDim.x);
                 const int uend = (int) (((long long) (blockIdx.x + 1) * e.units) / gridDim.x);
                 const size_t bytes = (size_t) (uend - ubeg) * e.KC * kQ6Tile;
-                if (bytes > 0)
-                    prefetch_l2(e.w + (size_t) ubeg * e.KC * kQ6Tile, (uint32_t) (bytes < (size_t) l2pf ? bytes : (size_t) l2pf));
+                pf.ptr = e.w + (size_t) ubeg * e.KC * kQ6Tile;
+                pf.bytes = (uint32_t) (bytes < (size_t) l2pf ? bytes : (size_t) l2pf);
+                if (op.kind != POP_GEMV && pf.bytes > 0) prefetch_l2(pf.ptr, pf.bytes);
             }
             // op trace (CTA 0, first pass): start, prologue done, this CTA's work done, barrier passed;
             // per CTA (first pass): start, work done
@@ -528,7 +539,7 @@ __global__ void __launch_bounds__(kPWarps * 32, 1)
             }
             bool ok = true;
             if (op.kind == POP_GEMV) {
-                ok = p_gemv_dispatch<NC>(op, region, red, w, tr != nullptr ? tr + 1 : nullptr, xep, sync, &xflag);
+                ok = p_gemv_dispatch<NC>(op, region, red, w, tr != nullptr ? tr + 1 : nullptr, xep, sync, &xflag, pf);
             } else if (op.kind == POP_XARGMAX) {
                 const unsigned long long ep = ++xep;
                 if (blockIdx.x == 0 && threadIdx.x == 0)
