@@ -345,6 +345,27 @@ def run_decode(args, rank, world, local, pg):
     return line
 
 
+def run_pass(args):
+    """Four single-token passes of a 9B-shaped model cut to --layers layers (the full lm_head): the small
+    case for an ncu capture of the persistent kernel (the kernel is the one the 32-layer engine runs). Not a
+    bench line: prints the four pass times."""
+    import torch
+
+    from rapier_b200.engine import Engine, config_9b
+
+    torch.cuda.set_device(0)
+    cfg = config_9b(max_ctx=args.ctx, seed=1)
+    cfg.n_layer = args.layers
+    eng = Engine(cfg)
+    times = []
+    for pos, t in enumerate([5, 17, 99, 1000]):
+        t0 = time.perf_counter()
+        eng.step([t], pos, want_logits=False)
+        times.append(round((time.perf_counter() - t0) * 1e3, 3))
+    print(json.dumps({"workload": "pass", "layers": args.layers, "step_ms_wall": times}), flush=True)
+    eng.close()
+
+
 def cpu_baseline_decode(budget_s=20.0):
     """The oracle (C restatement, OpenMP over the host cores) on one GDN layer, one attention layer and the
     lm_head of the 9B shape; token time extrapolated as 24 x GDN + 8 x attention + head."""
@@ -419,7 +440,9 @@ def main():
     ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=None)
     ap.add_argument("--impl", default="rapier", choices=["rapier", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "gemv"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "gemv", "pass"],
+                    help="pass: four single-token steps of a --layers model (a small case for ncu captures)")
+    ap.add_argument("--layers", type=int, default=8, help="pass: decoder layers of the 9B-shaped model")
     ap.add_argument("--ctx", type=int, default=512, help="decode: KV capacity (512 or 65536)")
     ap.add_argument("--no-mtp", action="store_true", help="decode: plain greedy (config 4)")
     ap.add_argument("--gen", type=int, default=N_GEN, help="decode: tokens per generation (400; fewer for profiling)")
@@ -453,6 +476,9 @@ def main():
         print(json.dumps(line), flush=True)
         return
 
+    if args.workload == "pass":
+        run_pass(args)
+        return
     rank, world, local, pg = dist_init(args.gpus)
     line = (run_decode if args.workload == "decode" else run_gemv)(args, rank, world, local, pg)
     if rank == 0:
