@@ -276,6 +276,20 @@ int rk_engine_generate(rk_engine* e, const int* prompt, int n_prompt, int n_gen,
  * positions pos, pos+1: updates the caches and states like a decode step and copies the logits
  * (ncols x n_vocab floats) and argmax ids to the host (either may be NULL). */
 int rk_engine_step(rk_engine* e, const int* tokens, int ncols, int pos, float* logits, int* argmax);
+/* Serving session (the reference's --serve loop, src/qwythos.cpp:2593-2812): the engine keeps a context
+ * across runs. rk_engine_session_reset clears it (op "reset"; same as rk_engine_reset). A run (op "run")
+ * ingests the previous run's last emitted token (still pending) and then tokens[0..n_tokens), all but the
+ * last teacher-forced, and generates up to n_gen tokens greedily into out_ids (*n_out of them), stopping
+ * after eos_id (-1: never). use_mtp != 0: exact MTP rounds (the stream is the same as use_mtp == 0); the
+ * first run after a reset seeds the draft's slot 0. Every emitted token except a final eos_id belongs to the
+ * context afterwards. first_logits (n_vocab floats, may be NULL) receives the logits of the first generated
+ * token. RK_ERANGE when the context cannot hold the run ("context full; send op reset"). rk_engine_generate
+ * leaves a session positioned after its generation. */
+int rk_engine_session_reset(rk_engine* e);
+int rk_engine_session_run(rk_engine* e, const int* tokens, int n_tokens, int n_gen, int use_mtp, int eos_id,
+                          int* out_ids, int* n_out, float* first_logits, rk_gen_stats* stats);
+/* The session's next position (tokens in the context plus the pending one), -1 for a NULL engine. */
+int rk_engine_session_pos(const rk_engine* e);
 /* Copies tensor `tid` (this library's synthetic tensor id) to the host: GGUF Q6_K bytes for quantized
  * matrices, fp32 values otherwise. bytes == 0 returns the size. Test hook, no reference counterpart. */
 size_t rk_engine_read_tensor(rk_engine* e, int tid, void* host, size_t bytes);

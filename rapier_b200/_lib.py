@@ -94,6 +94,10 @@ SIGNATURES = {
     "rk_engine_reset": (i32, [vp]),
     "rk_engine_generate": (i32, [vp, C.POINTER(C.c_int), i32, i32, i32, C.POINTER(C.c_int), C.POINTER(GenStats)]),
     "rk_engine_step": (i32, [vp, C.POINTER(C.c_int), i32, i32, vp, C.POINTER(C.c_int)]),
+    "rk_engine_session_reset": (i32, [vp]),
+    "rk_engine_session_run": (i32, [vp, C.POINTER(C.c_int), i32, i32, i32, i32, C.POINTER(C.c_int),
+                                    C.POINTER(C.c_int), vp, C.POINTER(GenStats)]),
+    "rk_engine_session_pos": (i32, [vp]),
     "rk_engine_read_tensor": (sz, [vp, i32, vp, sz]),
     "rk_engine_device_bytes": (sz, [vp]),
     "rk_engine_mode": (i32, [vp]),

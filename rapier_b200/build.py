@@ -68,7 +68,26 @@ def build(verbose: bool = False) -> str:
         if verbose:
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)
+    build_serve(verbose)
     return LIB
+
+
+SERVE_SRC = os.path.join(PKG, "serve", "rapier_serve.cpp")
+SERVE_BIN = os.path.join(PKG, "rapier_serve")
+
+
+def build_serve(verbose: bool = False) -> str:
+    """The --serve host binary (C++, the C-ABI only), linked to the in-tree library by rpath."""
+    deps = [SERVE_SRC, LIB, os.path.join(ROOT, "include", "rapier_b200.h")]
+    if os.path.exists(SERVE_BIN) and os.path.getmtime(SERVE_BIN) >= max(os.path.getmtime(d) for d in deps):
+        return SERVE_BIN
+    cxx = os.environ.get("CXX", "g++")
+    cmd = [cxx, "-O2", "-std=c++17", "-Wall", "-I" + os.path.join(ROOT, "include"), SERVE_SRC, "-o", SERVE_BIN,
+           "-L" + PKG, "-l:librapier_b200.so", "-Wl,-rpath,$ORIGIN"]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    subprocess.run(cmd, check=True)
+    return SERVE_BIN
 
 
 if __name__ == "__main__":

@@ -35,7 +35,9 @@ struct Ctrl {
     int n_emitted;
     int steps, accepted, singles;
     int bad;       // a token id outside the vocabulary reached a kernel
-    int pad[3];
+    int eos1;      // end-of-sequence token id + 1 (0: none); emitting it stops the generation
+    int stop;      // the generation emitted eos1 - 1 (the persistent loop ends after the pass)
+    int pad;
     unsigned long long amax[2];   // trunk argmax keys per column
     unsigned long long damax[2];  // draft argmax keys per column
 };
@@ -648,6 +650,7 @@ __device__ __noinline__ void ctrl_body(const CtrlArgs& a, Ctrl* ctrl) {
         const int n = v->n_emitted;
         if (n < a.max_out) a.out[n] = id;
         v->n_emitted = n + 1;
+        if (id + 1 == v->eos1) v->stop = 1;  // emitted, never ingested
         v->tok[0] = id;
         v->dtok[0] = id;
         v->dpos = v->pos + 1;
@@ -658,10 +661,25 @@ __device__ __noinline__ void ctrl_body(const CtrlArgs& a, Ctrl* ctrl) {
         // greedy acceptance (src/qwythos.cpp:3196-3238): c0 = argmax of column 0; accepted iff c0 == the
         // candidate; emit c0 (and c1 when accepted); the draft then runs on (c0 at pos+1, c1 at pos+2)
         const int c0 = argmax_key_row(v->amax[0]), c1 = argmax_key_row(v->amax[1]);
-        const int acc = c0 == v->tok[1];
         int n = v->n_emitted;
         if (n < a.max_out) a.out[n] = c0;
         ++n;
+        if (c0 + 1 == v->eos1) {
+            // emitted and not ingested: the state keeps column 0 only (the snapshot), whatever the draft was
+            v->n_emitted = n;
+            v->stop = 1;
+            v->dtok[0] = c0;
+            v->dtok[1] = c1;
+            v->dpos = v->pos + 1;
+            v->pos = v->pos + 1;
+            v->rollback = 1;
+            v->accept = 0;
+            v->steps = v->steps + 1;
+            __threadfence();
+            return;
+        }
+        const int acc = c0 == v->tok[1];
+        if (acc && c1 + 1 == v->eos1) v->stop = 1;  // c1 is emitted below and stays pending
         if (acc) {
             if (n < a.max_out) a.out[n] = c1;
             ++n;

@@ -23,6 +23,7 @@
 #include <cstring>
 #include <new>
 #include <string>
+#include <algorithm>
 #include <vector>
 
 #include "gguf.cuh"
@@ -201,6 +202,10 @@ struct EngineImpl {
     int max_out = 0;
     Ctrl* ctrl_stage = nullptr;  // pinned host staging, one slot per queued host write
     int stage_slots = 0, stage_next = 0;
+    // session (rk_engine_session_*): the next position to write, the last emitted token not yet ingested
+    // (-1: none), the GDN rollback the next pass must honour, and whether the draft slot 0 was seeded
+    int s_pos = 0, s_pending = -1, s_rollback = 0;
+    bool s_primed = false;
     // programs and executors
     Program progs[P_COUNT];
     bool persistent = false;
@@ -278,6 +283,7 @@ struct EngineImpl {
     cudaError_t run(const Program& P, int until = 0, int max_iters = 1, unsigned long long* trace = nullptr);
     void set_ctrl(const Ctrl& host_fields);
     int check_abort(const char* what);
+    void set_ctrl_eos(int eos_id);
 };
 
 EngineImpl::~EngineImpl() {
@@ -976,6 +982,19 @@ void EngineImpl::set_ctrl(const Ctrl& h) {
     if (e != cudaSuccess && err == cudaSuccess) err = e;
 }
 
+// The generation counters and the end-of-sequence id (-1: none) for the next run.
+void EngineImpl::set_ctrl_eos(int eos_id) {
+    Ctrl* slot = ctrl_stage + stage_next;
+    stage_next = (stage_next + 1) % stage_slots;
+    if (stage_next == 0) cudaStreamSynchronize(s);
+    *slot = Ctrl{};
+    slot->eos1 = eos_id + 1;
+    const size_t off = offsetof(Ctrl, n_emitted), end = offsetof(Ctrl, pad);
+    const cudaError_t e = cudaMemcpyAsync(reinterpret_cast<char*>(ctrl) + off, reinterpret_cast<char*>(slot) + off,
+                                          end - off, cudaMemcpyHostToDevice, s);
+    if (e != cudaSuccess && err == cudaSuccess) err = e;
+}
+
 // After a synchronized run: a persistent launch that gave up on a wait leaves the sticky abort word.
 int EngineImpl::check_abort(const char* what) {
     if (!persistent) return RK_OK;
@@ -1226,6 +1245,10 @@ int rk_engine_reset(rk_engine* e) {
     cudaMemsetAsync(E.psync, 0, offsetof(PSync, xepoch), E.s);  // the exchange epoch keeps counting
     const cudaError_t ce = cudaStreamSynchronize(E.s);
     if (ce != cudaSuccess) return set_error(RK_ECUDA, "rk_engine_reset: %s", cudaGetErrorString(ce));
+    E.s_pos = 0;
+    E.s_pending = -1;
+    E.s_rollback = 0;
+    E.s_primed = false;
     return RK_OK;
 }
 
@@ -1300,7 +1323,7 @@ int rk_engine_generate(rk_engine* e, const int* prompt, int n_prompt, int n_gen,
         ce = E.run(E.progs[P_SEED], 0);
         ++launches;
     }
-    cudaMemsetAsync(&E.ctrl->n_emitted, 0, sizeof(int) * 4, E.s);  // n_emitted, steps, accepted, singles
+    E.set_ctrl_eos(-1);  // n_emitted, steps, accepted, singles, bad cleared; no end-of-sequence stop
     cudaEventRecord(ev[1], E.s);
     // the seed pass at position P-1 produces the first generated token
     Ctrl h = {};
@@ -1359,10 +1382,154 @@ int rk_engine_generate(rk_engine* e, const int* prompt, int n_prompt, int n_gen,
     if (int rc2 = E.check_abort(what)) return rc2;
     if (back.bad) return set_error(RK_ERANGE, "%s: a token outside the vocabulary reached the device", what);
     if (back.n_emitted < n_gen) return set_error(RK_ECUDA, "%s: generation stopped early (%d of %d)", what, back.n_emitted, n_gen);
+    E.s_pos = back.pos;  // a session may continue the generation (its last token is pending)
+    E.s_pending = back.tok[0];
+    E.s_rollback = back.rollback;
+    E.s_primed = true;
     if (stats) {
         stats->prefill_ms = pre;
         stats->gen_ms = gen;
         stats->n_gen = n_gen;
+        stats->mtp_steps = back.steps;
+        stats->mtp_accepted = back.accepted;
+        stats->single_steps = back.singles;
+        stats->graph_launches = launches;
+        stats->kernels_per_single_step = E.progs[P_SINGLE].kernels;
+        stats->kernels_per_round = E.progs[P_ROUND].kernels;
+    }
+    return RK_OK;
+}
+
+int rk_engine_session_reset(rk_engine* e) { return rk_engine_reset(e); }
+
+int rk_engine_session_pos(const rk_engine* e) { return e ? e->impl.s_pos + (e->impl.s_pending >= 0 ? 1 : 0) : -1; }
+
+// The serve loop's run (src/qwythos.cpp:2650-2812): the pending token of the previous run and then
+// tokens[0..n) are ingested at the session position (every one but the last teacher-forced, the last as
+// the seed pass), then up to n_gen tokens are generated greedily, stopping after eos_id. Afterwards every
+// emitted token except a final eos_id is part of the context: the last one stays pending and is ingested
+// first by the next run. The first run after a reset seeds the draft slot 0 when use_mtp.
+int rk_engine_session_run(rk_engine* e, const int* tokens, int n_tokens, int n_gen, int use_mtp, int eos_id,
+                          int* out_ids, int* n_out, float* first_logits, rk_gen_stats* stats) {
+    const char* what = "rk_engine_session_run";
+    if (!e || !out_ids || !n_out || (n_tokens > 0 && !tokens)) return set_error(RK_EINVAL, "%s: null argument", what);
+    EngineImpl& E = e->impl;
+    *n_out = 0;
+    if (E.tp_size > 1 && !E.tp_connected) return set_error(RK_EINVAL, "%s: call rk_engine_tp_connect first", what);
+    if (n_tokens < 0 || n_gen < 1) return set_error(RK_EINVAL, "%s: needs n_tokens >= 0 and n_gen >= 1", what);
+    if (use_mtp && !E.cfg.has_mtp) return set_error(RK_EINVAL, "%s: model built without the MTP block", what);
+    if (eos_id < -1 || eos_id >= E.Vg) return set_error(RK_ERANGE, "%s: eos_id out of range", what);
+    std::vector<int> list;
+    if (E.s_pending >= 0) list.push_back(E.s_pending);
+    for (int i = 0; i < n_tokens; ++i) {
+        if (tokens[i] < 0 || tokens[i] >= E.Vg) return set_error(RK_ERANGE, "%s: token out of range", what);
+        list.push_back(tokens[i]);
+    }
+    if (list.empty()) return set_error(RK_EINVAL, "%s: nothing to ingest (no tokens and no pending token)", what);
+    const int L = (int) list.size(), start = E.s_pos;
+    if ((long long) start + L + n_gen + 2 > E.cfg.max_ctx)
+        return set_error(RK_ERANGE, "%s: context full (position %d + %d tokens + %d generated); reset the session",
+                         what, start, L, n_gen);
+    cudaEvent_t ev[3];
+    for (auto& v : ev) cudaEventCreate(&v);
+    int launches = 0;
+    cudaError_t ce = cudaSuccess;
+    int* pinned = reinterpret_cast<int*>(E.ctrl_stage + E.stage_slots);
+    auto read_ctrl = [&](Ctrl& h) {
+        if (ce == cudaSuccess) ce = cudaMemcpyAsync(pinned, E.ctrl, sizeof(Ctrl), cudaMemcpyDeviceToHost, E.s);
+        if (ce == cudaSuccess) ce = cudaStreamSynchronize(E.s);
+        if (ce == cudaSuccess) std::memcpy(&h, pinned, sizeof(Ctrl));
+    };
+    cudaEventRecord(ev[0], E.s);
+    for (int i = 0; i + 1 < L && ce == cudaSuccess; ++i) {  // teacher-forced ingest
+        Ctrl h = {};
+        h.pos = start + i;
+        h.tok[0] = list[(size_t) i];
+        h.rollback = i == 0 ? E.s_rollback : 0;
+        E.set_ctrl(h);
+        ce = E.run(E.progs[P_SINGLE], 0);
+        ++launches;
+    }
+    if (use_mtp && !E.s_primed && ce == cudaSuccess) {  // draft slot 0: (emb(first token), h = 0)
+        cudaMemsetAsync(E.hsave, 0, sizeof(float) * E.H, E.s);
+        cudaMemsetAsync(E.hsave_p, 0, sizeof(float) * E.H / 4, E.s);
+        Ctrl h = {};
+        h.dpos = start;
+        h.dtok[0] = list[0];
+        E.set_ctrl(h);
+        ce = E.run(E.progs[P_SEED], 0);
+        ++launches;
+    }
+    E.s_primed = true;
+    E.set_ctrl_eos(eos_id);
+    cudaEventRecord(ev[1], E.s);
+    {  // the seed pass: the last ingested token, the first generated one
+        Ctrl h = {};
+        h.pos = start + L - 1;
+        h.tok[0] = list[(size_t) L - 1];
+        h.rollback = L == 1 ? E.s_rollback : 0;
+        E.set_ctrl(h);
+        if (ce == cudaSuccess) ce = E.run(E.progs[P_SINGLE], 0);
+        ++launches;
+    }
+    if (first_logits && ce == cudaSuccess)
+        ce = cudaMemcpyAsync(first_logits, E.logits, sizeof(float) * (size_t) E.V, cudaMemcpyDeviceToHost, E.s);
+    Ctrl back = {};
+    read_ctrl(back);
+    if (!use_mtp) {
+        if (E.persistent && !back.stop && back.n_emitted < n_gen && ce == cudaSuccess) {
+            ce = E.run(E.progs[P_SINGLE], n_gen, n_gen);
+            ++launches;
+            read_ctrl(back);
+        }
+        while (!E.persistent && !back.stop && back.n_emitted < n_gen && ce == cudaSuccess) {
+            ce = E.run(E.progs[P_SINGLE], 0);
+            ++launches;
+            read_ctrl(back);
+        }
+    } else if (!back.stop && back.n_emitted < n_gen && ce == cudaSuccess) {
+        ce = E.run(E.progs[P_DRAFT1], 0);  // first candidate
+        ++launches;
+        if (E.persistent) {
+            if (n_gen - 1 > 1 && ce == cudaSuccess) {
+                ce = E.run(E.progs[P_ROUND], n_gen - 1, n_gen);
+                ++launches;
+            }
+            read_ctrl(back);
+        } else {
+            while (!back.stop && back.n_emitted < n_gen - 1 && ce == cudaSuccess) {
+                ce = E.run(E.progs[P_ROUND], 0);
+                ++launches;
+                read_ctrl(back);
+            }
+        }
+        if (!back.stop && back.n_emitted < n_gen && ce == cudaSuccess) {
+            ce = E.run(E.progs[P_SINGLE], 0);
+            ++launches;
+            read_ctrl(back);
+        }
+    }
+    cudaEventRecord(ev[2], E.s);
+    if (ce == cudaSuccess && back.n_emitted > 0)
+        ce = cudaMemcpyAsync(out_ids, E.out, sizeof(int) * (size_t) std::min(back.n_emitted, n_gen), cudaMemcpyDeviceToHost, E.s);
+    if (ce == cudaSuccess) ce = cudaStreamSynchronize(E.s);
+    float pre = 0.0f, gen = 0.0f;
+    if (ce == cudaSuccess) {
+        cudaEventElapsedTime(&pre, ev[0], ev[1]);
+        cudaEventElapsedTime(&gen, ev[1], ev[2]);
+    }
+    for (auto& v : ev) cudaEventDestroy(v);
+    if (ce != cudaSuccess) return set_error(RK_ECUDA, "%s: %s", what, cudaGetErrorString(ce));
+    if (int rc = E.check_abort(what)) return rc;
+    if (back.bad) return set_error(RK_ERANGE, "%s: a token outside the vocabulary reached the device", what);
+    *n_out = std::min(back.n_emitted, n_gen);
+    E.s_pos = back.pos;
+    E.s_pending = back.stop ? -1 : back.tok[0];
+    E.s_rollback = back.rollback;
+    if (stats) {
+        stats->prefill_ms = pre;
+        stats->gen_ms = gen;
+        stats->n_gen = *n_out;
         stats->mtp_steps = back.steps;
         stats->mtp_accepted = back.accepted;
         stats->single_steps = back.singles;

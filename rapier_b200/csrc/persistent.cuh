@@ -567,7 +567,7 @@ __global__ void __launch_bounds__(kPWarps * 32, 1)
             if (tr != nullptr && threadIdx.x == 0) tr[3] = globaltimer_ns();
         }
         if (!alive || until <= 0 || iter >= max_iters) break;
-        if (ld_cg(&ctrl->n_emitted) >= until) break;
+        if (ld_cg(&ctrl->n_emitted) >= until || ld_cg(&ctrl->stop)) break;
     }
     pipe_drain(w);
     __syncthreads();

@@ -114,6 +114,28 @@ class Engine:
         stats = {f: getattr(st, f) for f, _ in GenStats._fields_}
         return np.frombuffer(out, dtype=np.int32).copy(), stats
 
+    # ---- serving session (rk_engine_session_*; the reference's --serve loop) ----
+    def session_reset(self):
+        _lib.call("rk_engine_session_reset", self._h)
+
+    def session_run(self, tokens, n_gen: int, mtp: bool = False, eos: int = -1, first_logits: bool = False):
+        """Ingest the pending token and `tokens`, generate up to n_gen tokens (stop after `eos`). Returns
+        (ids, stats, logits of the first generated token or None)."""
+        n = len(tokens)
+        t = (C.c_int * max(1, n))(*[int(x) for x in tokens])
+        out = (C.c_int * n_gen)()
+        n_out = C.c_int(0)
+        st = GenStats()
+        lg = np.empty(self.cfg.n_vocab // self.tp_size, np.float32) if first_logits else None
+        _lib.call("rk_engine_session_run", self._h, t, n, n_gen, 1 if mtp else 0, eos, out, C.byref(n_out),
+                  lg.ctypes.data_as(C.c_void_p) if first_logits else None, C.byref(st))
+        stats = {f: getattr(st, f) for f, _ in GenStats._fields_}
+        return np.frombuffer(out, dtype=np.int32)[:n_out.value].copy(), stats, lg
+
+    @property
+    def session_pos(self) -> int:
+        return _lib.lib().rk_engine_session_pos(self._h)
+
     def tp_export(self) -> bytes:
         """This rank's exchange-memory handle (rk_engine_tp_export)."""
         n = _lib.lib().rk_tp_handle_bytes()
