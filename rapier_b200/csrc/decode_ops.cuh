@@ -27,7 +27,7 @@ constexpr int kRingSlots = 8;  // conv history per channel: the input at positio
 // ------------------------------------------------------------------------------------------------
 struct Ctrl {
     int pos;       // trunk position of column 0
-    int tok[2];    // trunk input tokens (tok[1] = the draft candidate in a verify round)
+    int tok[4];    // trunk input tokens (tok[1] = the draft candidate in a verify round; 4 in a prefill pass)
     int dpos;      // draft position of column 0
     int dtok[2];   // draft input tokens
     int rollback;  // GDN state from the snapshot (the previous verify's draft was rejected)
@@ -41,7 +41,8 @@ struct Ctrl {
     unsigned long long amax[2];   // trunk argmax keys per column
     unsigned long long damax[2];  // draft argmax keys per column
 };
-constexpr int kCtrlHostFields = 8;  // pos, tok[2], dpos, dtok[2], rollback, accept: written by the host
+constexpr int kCtrlHostFields = 10;  // pos, tok[4], dpos, dtok[2], rollback, accept: written by the host
+constexpr int kMaxCols = 4;          // columns of a step program: 1 (decode), 2 (verify), 4 (prefill)
 
 __device__ __forceinline__ int ld_cg(const int* p) { return __ldcg(p); }
 __device__ __forceinline__ float ld_cg(const float* p) { return __ldcg(p); }
@@ -362,7 +363,7 @@ __device__ __noinline__ void gdn_quarter_body(const GdnArgs& a, int head, int qu
         if (stepper) {
             oc[c] = __fmul_rn(__fadd_rn(__fadd_rn(__fadd_rn(ro[col], ro[32 + col]), ro[64 + col]), ro[96 + col]),
                               kInvSqrtSsm);
-            if (NC > 1 && c == 0) {
+            if (NC == 2 && c == 0) {  // the verify's rollback point
 #pragma unroll
                 for (int r = 0; r < 32; ++r) pbase[r * rs] = s[r];
             }

@@ -160,7 +160,9 @@ struct Program {
     cudaGraphExec_t graph = nullptr;
     int kernels = 0;  // kernels one run launches
 };
-enum : int { P_SINGLE = 0, P_TRUNK2, P_ROUND, P_DRAFT1, P_SEED, P_PROBE1, P_PROBE2, P_COUNT };
+enum : int { P_SINGLE = 0, P_TRUNK2, P_ROUND, P_DRAFT1, P_SEED, P_PROBE1, P_PROBE2, P_PREFILL, P_COUNT };
+// executor slot of a column count (1, 2, 4)
+inline int col_slot(int nc) { return nc >= 4 ? 2 : nc - 1; }
 
 POp make_op(int kind) {
     POp op;
@@ -210,9 +212,10 @@ struct EngineImpl {
     Program progs[P_COUNT];
     bool persistent = false;
     PSync* psync = nullptr;
-    int p_grid = 0, p_stages[2] = {0, 0}, p_region[2] = {0, 0};  // per column count (1, 2)
+    int p_grid = 0, p_stages[3] = {0, 0, 0}, p_region[3] = {0, 0, 0};  // per column count (1, 2, 4)
     int p_l2pf = 0;  // bytes of the next GEMV each CTA asks L2 for when an op starts
-    size_t p_smem[2] = {0, 0};
+    size_t p_smem[3] = {0, 0, 0};
+    bool prefill4 = false;  // the 4-column prefill program exists (single GPU, and the executor fits it)
     double probe_weight_bytes[2] = {0, 0}, probe_algo_bytes[2] = {0, 0};
     int probe_gemvs = 0;
     // tensor parallelism: this rank's exchange memory (exported by CUDA IPC), the peers' mappings, and the
@@ -271,7 +274,7 @@ struct EngineImpl {
     void add_rowpar(std::vector<POp>& v, MmvqParams p);
     void add_ffn(std::vector<POp>& v, const Layer& L, float* xres, float* part);
     POp attn_op(int kind, const Layer& L, int draft_flag);
-    void add_trunk(std::vector<POp>& v);
+    void add_trunk(std::vector<POp>& v, bool head = true);
     void add_draft(std::vector<POp>& v, bool head);
     void add_ctrl(std::vector<POp>& v, int kind);
     void add_xargmax(std::vector<POp>& v, int draft_flag);
@@ -284,6 +287,7 @@ struct EngineImpl {
     void set_ctrl(const Ctrl& host_fields);
     int check_abort(const char* what);
     void set_ctrl_eos(int eos_id);
+    cudaError_t ingest(const int* toks, int n, int start, int rollback0, int& launches);
 };
 
 EngineImpl::~EngineImpl() {
@@ -570,17 +574,18 @@ int EngineImpl::build() {
         if (err == cudaSuccess) err = cudaStreamSynchronize(s);
     }
     // activations (2 columns)
-    x = alloc<float>(2 * (size_t) H);
-    xp = alloc<float>(2 * (size_t) H / 4);
-    proj = alloc<float>(2 * (size_t) max_in_rows);
-    ug = alloc<float>(2 * 2 * (size_t) FF);
-    q8 = alloc<uint8_t>(2 * rk_q8_1_bytes(hv * S, 1));
-    gdn_o = alloc<float>(2 * (size_t) hv * S);
-    gdn_ss = alloc<float>(2 * (size_t) hv * 4);
+    const size_t K = kMaxCols;  // activations of up to kMaxCols columns (a prefill pass)
+    x = alloc<float>(K * (size_t) H);
+    xp = alloc<float>(K * (size_t) H / 4);
+    proj = alloc<float>(K * (size_t) max_in_rows);
+    ug = alloc<float>(K * 2 * (size_t) FF);
+    q8 = alloc<uint8_t>(K * rk_q8_1_bytes(hv * S, 1));
+    gdn_o = alloc<float>(K * (size_t) hv * S);
+    gdn_ss = alloc<float>(K * (size_t) hv * 4);
     gdn_cnt = alloc<unsigned>((size_t) hv);
-    attn_scratch = alloc<float>((size_t) nh * 2 * max_chunks * (kHdA + 2));
-    q8_ff = alloc<uint8_t>(2 * rk_q8_1_bytes(FF, 1));
-    q8_attn = alloc<uint8_t>(2 * rk_q8_1_bytes(nh * kHdA, 1));
+    attn_scratch = alloc<float>((size_t) nh * K * max_chunks * (kHdA + 2));
+    q8_ff = alloc<uint8_t>(K * rk_q8_1_bytes(FF, 1));
+    q8_attn = alloc<uint8_t>(K * rk_q8_1_bytes(nh * kHdA, 1));
     swiglu_cnt = alloc<unsigned>((size_t) FF / 32);
     hsave = alloc<float>(2 * (size_t) H);
     hsave_p = alloc<float>(2 * (size_t) H / 4);
@@ -692,13 +697,13 @@ POp EngineImpl::attn_op(int kind, const Layer& L, int draft_flag) {
     a.kc = L.kc;
     a.vc = L.vc;
     a.part_o = attn_scratch;
-    a.part_ml = attn_scratch + (size_t) nh * 2 * max_chunks * kHdA;
+    a.part_ml = attn_scratch + (size_t) nh * kMaxCols * max_chunks * kHdA;
     a.o = nullptr;
     a.q8 = q8_attn;
     return op;
 }
 
-void EngineImpl::add_trunk(std::vector<POp>& v) {
+void EngineImpl::add_trunk(std::vector<POp>& v, bool head) {
     POp e = make_op(POP_EMBED);
     e.em.emb = tok_embd;
     e.em.H = H;
@@ -737,6 +742,7 @@ void EngineImpl::add_trunk(std::vector<POp>& v) {
         }
         add_ffn(v, L, x, xp);
     }
+    if (!head) return;  // a prefill pass: no logits
     // final norm + lm_head + argmax; the normed hidden and its partials feed the draft (src/qwythos.cpp:1234-1237)
     MmvqParams p = rms_params(lm_head, x, out_norm, xp, logits, V);
     p.xn_out = hsave;
@@ -847,8 +853,9 @@ int EngineImpl::setup_executor() {
         if (v >= 0 && v <= 4096) p_l2pf = v * 1024;
     }
     const int max_in = FF > 2 * H ? FF : 2 * H;
-    for (int nc = 1; nc <= 2; ++nc) {
-        const void* fn = nc == 1 ? (const void*) persistent_kernel<1> : (const void*) persistent_kernel<2>;
+    for (int nc = 1; nc <= 4; nc *= 2) {
+        const void* fn = nc == 1 ? (const void*) persistent_kernel<1>
+                                 : nc == 2 ? (const void*) persistent_kernel<2> : (const void*) persistent_kernel<4>;
         cudaFuncAttributes fa = {};
         if ((err = cudaFuncGetAttributes(&fa, fn)) != cudaSuccess) return RK_ECUDA;
         size_t region = (size_t) nc * (max_in / 32) * 48;
@@ -858,6 +865,7 @@ int EngineImpl::setup_executor() {
         int stages = (int) ((budget - (long long) persistent_smem_bytes((int) region, 0)) / ((long long) kPWarps * kQ6Tile));
         if (stages > cap) stages = cap;
         if (stages < 2) {
+            if (nc == 4) break;  // no 4-column prefill: prompts go one token per pass
             persistent = false;
             return RK_OK;
         }
@@ -867,12 +875,14 @@ int EngineImpl::setup_executor() {
         int occ = 0;
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, kPWarps * 32, smem);
         if (occ < 1) {
+            if (nc == 4) break;
             persistent = false;
             return RK_OK;
         }
-        p_stages[nc - 1] = stages;
-        p_region[nc - 1] = (int) region;
-        p_smem[nc - 1] = smem;
+        p_stages[col_slot(nc)] = stages;
+        p_region[col_slot(nc)] = (int) region;
+        p_smem[col_slot(nc)] = smem;
+        if (nc == 4) prefill4 = true;
     }
     p_grid = sms;
     return RK_OK;
@@ -893,11 +903,11 @@ cudaError_t EngineImpl::launch_op(const POp& op) {
     // grid: the op's largest item count over all positions (attention: kMaxChunksA chunks per kv head)
     const int grid = op.kind == POP_ATTN ? kMaxChunksA * op.at.n_kv : pop_items<NC>(op, 0);
     const size_t smem = op_scratch_bytes(NC, H);
-    static bool attr_set[2] = {false, false};
-    if (smem > 48 * 1024 && !attr_set[NC - 1]) {
+    static bool attr_set[3] = {false, false, false};
+    if (smem > 48 * 1024 && !attr_set[col_slot(NC)]) {
         const cudaError_t e = cudaFuncSetAttribute(op_kernel<NC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
         if (e != cudaSuccess) return e;
-        attr_set[NC - 1] = true;
+        attr_set[col_slot(NC)] = true;
     }
     return launch_pdl(op_kernel<NC>, dim3((unsigned) grid), dim3(256), smem, s, true, op, ctrl);
 }
@@ -935,7 +945,7 @@ int EngineImpl::finalize(Program& P, int nc) {
     if ((err = cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal)) != cudaSuccess) return RK_ECUDA;
     int launches = 0;
     for (const POp& op : P.ops) {
-        const cudaError_t e = nc == 1 ? launch_op<1>(op) : launch_op<2>(op);
+        const cudaError_t e = nc == 1 ? launch_op<1>(op) : nc == 2 ? launch_op<2>(op) : launch_op<4>(op);
         if (e != cudaSuccess && err == cudaSuccess) err = e;
         ++launches;
     }
@@ -954,7 +964,7 @@ cudaError_t EngineImpl::run(const Program& P, int until, int max_iters, unsigned
     cudaLaunchConfig_t c = {};
     c.gridDim = dim3((unsigned) p_grid);
     c.blockDim = dim3(kPWarps * 32);
-    c.dynamicSmemBytes = p_smem[P.nc - 1];
+    c.dynamicSmemBytes = p_smem[col_slot(P.nc)];
     c.stream = s;
     cudaLaunchAttribute at[1];
     at[0].id = cudaLaunchAttributeCooperative;
@@ -967,7 +977,10 @@ cudaError_t EngineImpl::run(const Program& P, int until, int max_iters, unsigned
     if (P.nc == 1)
         return cudaLaunchKernelEx(&c, persistent_kernel<1>, prog, nops, gt, ng, ctrl, psync, p_stages[0], p_region[0],
                                   p_l2pf, until, max_iters, trace);
-    return cudaLaunchKernelEx(&c, persistent_kernel<2>, prog, nops, gt, ng, ctrl, psync, p_stages[1], p_region[1],
+    if (P.nc == 2)
+        return cudaLaunchKernelEx(&c, persistent_kernel<2>, prog, nops, gt, ng, ctrl, psync, p_stages[1], p_region[1],
+                                  p_l2pf, until, max_iters, trace);
+    return cudaLaunchKernelEx(&c, persistent_kernel<4>, prog, nops, gt, ng, ctrl, psync, p_stages[2], p_region[2],
                               p_l2pf, until, max_iters, trace);
 }
 
@@ -980,6 +993,34 @@ void EngineImpl::set_ctrl(const Ctrl& h) {
     std::memcpy(slot, &h, sizeof(int) * kCtrlHostFields);
     const cudaError_t e = cudaMemcpyAsync(ctrl, slot, sizeof(int) * kCtrlHostFields, cudaMemcpyHostToDevice, s);
     if (e != cudaSuccess && err == cudaSuccess) err = e;
+}
+
+// Teacher-forced ingest of toks[0..n) at positions start.. (the reference's batched ingest,
+// src/qwythos.cpp:2151-2502): 4-column passes of the trunk without the lm_head while four tokens remain
+// (each column bitwise the single-token pass), then single-token passes. rollback0: the GDN rollback the
+// first pass honours.
+cudaError_t EngineImpl::ingest(const int* toks, int n, int start, int rollback0, int& launches) {
+    cudaError_t ce = cudaSuccess;
+    int i = 0;
+    for (; prefill4 && n - i >= 4 && ce == cudaSuccess; i += 4) {
+        Ctrl h = {};
+        h.pos = start + i;
+        for (int c = 0; c < 4; ++c) h.tok[c] = toks[i + c];
+        h.rollback = i == 0 ? rollback0 : 0;
+        set_ctrl(h);
+        ce = run(progs[P_PREFILL], 0);
+        ++launches;
+    }
+    for (; i < n && ce == cudaSuccess; ++i) {
+        Ctrl h = {};
+        h.pos = start + i;
+        h.tok[0] = toks[i];
+        h.rollback = i == 0 ? rollback0 : 0;
+        set_ctrl(h);
+        ce = run(progs[P_SINGLE], 0);
+        ++launches;
+    }
+    return ce;
 }
 
 // The generation counters and the end-of-sequence id (-1: none) for the next run.
@@ -1110,6 +1151,12 @@ static int create_engine(const rk_model_config* cfg, int device, int tp_rank, in
     if (rc == RK_OK) {
         E.add_trunk(E.progs[P_TRUNK2].ops);
         rc = E.finalize(E.progs[P_TRUNK2], 2);
+    }
+    if (!E.persistent) E.prefill4 = true;  // one kernel per op takes any column count
+    if (tp_size > 1) E.prefill4 = false;   // the exchange buffers hold two columns
+    if (rc == RK_OK && E.prefill4) {
+        E.add_trunk(E.progs[P_PREFILL].ops, false);
+        rc = E.finalize(E.progs[P_PREFILL], 4);
     }
     if (rc == RK_OK && c.has_mtp) {
         std::vector<POp>& r = E.progs[P_ROUND].ops;
@@ -1302,16 +1349,9 @@ int rk_engine_generate(rk_engine* e, const int* prompt, int n_prompt, int n_gen,
         if (ce == cudaSuccess) ce = cudaStreamSynchronize(E.s);
         return ce == cudaSuccess ? *pinned : -1;
     };
-    // prefill: positions 0..P-2, teacher forced, one trunk pass each (the reference's per-token path)
+    // prefill: positions 0..P-2, teacher forced (4-column passes, then single tokens)
     cudaEventRecord(ev[0], E.s);
-    for (int i = 0; i + 1 < n_prompt && ce == cudaSuccess; ++i) {
-        Ctrl h = {};
-        h.pos = i;
-        h.tok[0] = prompt[i];
-        E.set_ctrl(h);
-        ce = E.run(E.progs[P_SINGLE], 0);
-        ++launches;
-    }
+    ce = E.ingest(prompt, n_prompt - 1, 0, 0, launches);
     if (use_mtp && ce == cudaSuccess) {
         // seed the draft cache slot 0 with (emb(prompt[0]), h = 0) (src/qwythos.cpp:2955-2958)
         cudaMemsetAsync(E.hsave, 0, sizeof(float) * E.H, E.s);
@@ -1441,15 +1481,7 @@ int rk_engine_session_run(rk_engine* e, const int* tokens, int n_tokens, int n_g
         if (ce == cudaSuccess) std::memcpy(&h, pinned, sizeof(Ctrl));
     };
     cudaEventRecord(ev[0], E.s);
-    for (int i = 0; i + 1 < L && ce == cudaSuccess; ++i) {  // teacher-forced ingest
-        Ctrl h = {};
-        h.pos = start + i;
-        h.tok[0] = list[(size_t) i];
-        h.rollback = i == 0 ? E.s_rollback : 0;
-        E.set_ctrl(h);
-        ce = E.run(E.progs[P_SINGLE], 0);
-        ++launches;
-    }
+    ce = E.ingest(list.data(), L - 1, start, E.s_rollback, launches);  // teacher-forced ingest
     if (use_mtp && !E.s_primed && ce == cudaSuccess) {  // draft slot 0: (emb(first token), h = 0)
         cudaMemsetAsync(E.hsave, 0, sizeof(float) * E.H, E.s);
         cudaMemsetAsync(E.hsave_p, 0, sizeof(float) * E.H / 4, E.s);

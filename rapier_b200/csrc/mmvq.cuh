@@ -30,6 +30,7 @@ namespace rk {
 
 constexpr int kMmvqWarps = 8;      // consumer warps per CTA (256 threads)
 constexpr int kMmvqMaxStages = 8;  // ring slots per warp (runtime `stages` <= this)
+constexpr int kRedCols = 4;        // columns whose RMS partial sums one prologue reduces (red: 8 floats each)
 constexpr int kMmvqMaxCols = 4;    // columns per launch (more are split into launches over column chunks)
 
 enum MmvqPro { PRO_Q8 = 0, PRO_RMS = 1 };
@@ -151,6 +152,7 @@ __device__ __forceinline__ void xstage_put_warp(const XStage& s, int g, int code
 // with one block-wide barrier; `red` holds NC * 8 floats.
 template <int NC, int PRO>
 __device__ __noinline__ void mmvq_build_x(const MmvqParams& p, uint8_t* xsm, float* red) {
+    static_assert(PRO != PRO_RMS || NC <= kRedCols, "red holds kRedCols columns of warp totals");
     const int ng = p.n_in >> 5;
     if constexpr (PRO == PRO_Q8) {
         const size_t col_bytes = p.xq_stride > 0 ? (size_t) p.xq_stride : (size_t) ng * 36;
@@ -457,7 +459,7 @@ template <int TYPE, int NC, int PRO, int EPI>
 __global__ void __launch_bounds__(kMmvqWarps * 32, 2) mmvq_packed_kernel(const MmvqParams p) {
     constexpr int TILE = TYPE == RK_TYPE_Q6_K ? kQ6Tile : kQ80Tile;
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ float red[16];
+    __shared__ float red[kRedCols * 8];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int KC = p.n_in >> 10;
     const int ng = p.n_in >> 5;

@@ -445,7 +445,8 @@ __device__ __forceinline__ bool p_gemv_dispatch(const POp& op, uint8_t* xsm, flo
         return p_gemv<NC, PRO_RMS, EPI_ARGMAX>(p, xsm, red, w, tp, xep, sync, sflag, pf);
     }
     if (op.epi == EPI_RES) return p_gemv<NC, PRO_Q8, EPI_RES>(p, xsm, red, w, tp, xep, sync, sflag, pf);
-    if (op.epi == EPI_XRES) return p_gemv<NC, PRO_Q8, EPI_XRES>(p, xsm, red, w, tp, xep, sync, sflag, pf);
+    if constexpr (NC <= 2)  // the exchange buffers hold two columns (tensor parallelism has no prefill program)
+        if (op.epi == EPI_XRES) return p_gemv<NC, PRO_Q8, EPI_XRES>(p, xsm, red, w, tp, xep, sync, sflag, pf);
     return p_gemv<NC, PRO_Q8, EPI_STORE_P>(p, xsm, red, w, tp, xep, sync, sflag, pf);
 }
 
@@ -473,7 +474,7 @@ __global__ void __launch_bounds__(kPWarps * 32, 1)
                       PSync* sync, int stages, int region_bytes, int l2pf, int until, int max_iters,
                       unsigned long long* trace) {
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ float red[16];
+    __shared__ float red[kRedCols * 8];
     __shared__ int flag;
     __shared__ POp op_sm[2];  // the running op's record and the next one's (fetched while the op runs)
     __shared__ GemvEnt gt_sm[kMaxGemvOps];
@@ -542,8 +543,9 @@ __global__ void __launch_bounds__(kPWarps * 32, 1)
                 ok = p_gemv_dispatch<NC>(op, region, red, w, tr != nullptr ? tr + 1 : nullptr, xep, sync, &xflag, pf);
             } else if (op.kind == POP_XARGMAX) {
                 const unsigned long long ep = ++xep;
-                if (blockIdx.x == 0 && threadIdx.x == 0)
-                    ok = xch_argmax<NC>(op.xa.xch, op.draft ? ctrl->damax : ctrl->amax, ep, sync);
+                if constexpr (NC <= 2)
+                    if (blockIdx.x == 0 && threadIdx.x == 0)
+                        ok = xch_argmax<NC>(op.xa.xch, op.draft ? ctrl->damax : ctrl->amax, ep, sync);
             } else {
                 const int pos = ld_cg(op.draft ? &ctrl->dpos : &ctrl->pos);
                 const int rb = ld_cg(&ctrl->rollback);
