@@ -11,7 +11,8 @@
  *     the last failure on the calling thread is rk_last_error(). Where the reference throws
  *     std::invalid_argument (src/native_mmvq.cu:2312-2331) or calls exit(1) (src/fused_gdn.cu:169-176),
  *     this returns RK_EINVAL;
- *   - weight type ids are ggml's: RK_TYPE_Q6_K = 14, RK_TYPE_Q8_0 = 8.
+ *   - weight type ids are ggml's: RK_TYPE_Q6_K = 14, RK_TYPE_Q5_K = 13, RK_TYPE_Q4_K = 12, RK_TYPE_Q8_0 = 8
+ *     (the K-quants on GGUF rows only: rk_mmvq, rk_mmvq_res, rk_weight_bytes, rk_mmvq_isums).
  */
 #ifndef RAPIER_B200_H
 #define RAPIER_B200_H
@@ -31,6 +32,8 @@ extern "C" {
 #define RK_EUNSUPPORTED (-5) /* weight type or layout not handled by this entry */
 
 #define RK_TYPE_Q8_0 8
+#define RK_TYPE_Q4_K 12
+#define RK_TYPE_Q5_K 13
 #define RK_TYPE_Q6_K 14
 
 /* ---------------------------------------------------------------------------------------------- */
@@ -57,14 +60,16 @@ int rk_quantize_q8_1(const float* x, void* x_q8_1, int n_in, int ncols, void* st
 /* ---------------------------------------------------------------------------------------------- */
 /* Quantized GEMV, GGUF block layout (drop-in)                                                      */
 /* ---------------------------------------------------------------------------------------------- */
-/* Replaces native_mmvq_weight_bytes (src/native_mmvq.cu:3765-3785) for types 14 and 8. */
+/* Replaces native_mmvq_weight_bytes (src/native_mmvq.cu:3765-3785) for types 14, 13, 12 and 8. */
 size_t rk_weight_bytes(int type, int n_in, int n_out);
 /* Replaces native_mmvq (src/native_mmvq.cu:3787-3818) / native_q6_k_mmvq (:3627-3660) /
- * native_q8_0_mmvq (:3732-3736): y[j*n_out + r] = W[r,:] . x[:, j] on GGUF Q6_K / Q8_0 rows,
+ * native_q5_k_mmvq (:3341) / native_q4_k_mmvq (:3587) / native_q8_0_mmvq (:3732-3736):
+ * y[j*n_out + r] = W[r,:] . x[:, j] on GGUF Q6_K / Q5_K / Q4_K / Q8_0 rows (K-quant rows 4-byte aligned),
  * 1 <= ncols <= 16. */
 int rk_mmvq(int type, const void* weights, const void* x_q8_1, float* y, int n_in, int n_out, int ncols,
             void* stream);
-/* Replaces native_q6_k_mmvq_res (src/native_mmvq.cu:3187-3200) / native_q8_0_mmvq_res (:3326-3339):
+/* Replaces native_q6_k_mmvq_res (src/native_mmvq.cu:3187-3200) / native_q5_k_mmvq_res and
+ * native_q4_k_mmvq_res (:3202-3324) / native_q8_0_mmvq_res (:3326-3339):
  * y[r] = W[r,:] . x + res[r]; partials[r/4] = sum of y^2 over rows 4(r/4)..4(r/4)+3 (y == res allowed). */
 int rk_mmvq_res(int type, const void* weights, const void* x_q8_1, float* y, const float* res, float* partials,
                 int n_in, int n_out, void* stream);
@@ -94,7 +99,10 @@ int rk_mmvq_packed_res(int type, const void* packed, const void* x_q8_1, float* 
                        float* partials, int n_in, int n_out, int ncols, void* stream);
 /* Parity probe (no reference counterpart): the exact integer sums the packed GEMV accumulates.
  * out[((j*n_out) + r)*nsub + s]; Q6_K: nsub = n_in/16, s = 16-value sub-block, value
- * sum((code-32) * x_code) * scale; Q8_0: nsub = n_in/32, value sum(w_code * x_code). */
+ * sum((code-32) * x_code) * scale; Q8_0: nsub = n_in/32, value sum(w_code * x_code).
+ * Q5_K / Q4_K (GGUF rows in `packed`, which they have no packed layout for): nsub = 2 * n_in/32, entries
+ * 2s, 2s+1 of 32-value sub-block s = the sums of dot1 * scale and dot2 * min of the reference's block
+ * threads that cover it (vec_dot_q5_K_q8_1 / _q4_K_q8_1, src/native_mmvq.cu:191-252, :543-595). */
 int rk_mmvq_isums(int type, const void* packed, const void* x_q8_1, int32_t* out, int n_in, int n_out, int ncols,
                   void* stream);
 

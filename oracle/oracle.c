@@ -207,6 +207,8 @@ void or_dequantize_q8_1(const void* y, float* x, int n) {
 /* ------------------------------------------------------------------------------------------------ */
 size_t or_weight_bytes(int type, int n_in, int n_out) {
     if (type == 14) return (size_t) (n_in / 256) * 210u * (size_t) n_out;
+    if (type == 13) return (size_t) (n_in / 256) * 176u * (size_t) n_out;
+    if (type == 12) return (size_t) (n_in / 256) * 144u * (size_t) n_out;
     if (type == 8) return (size_t) (n_in / 32) * 34u * (size_t) n_out;
     return 0;
 }
@@ -519,6 +521,87 @@ static float q80_q8_dot(const uint8_t* blk, const uint8_t* xb, int iqs, int* isu
     return d0 * d1 * (float) sumi;
 }
 
+/* ---- Q5_K / Q4_K (ggml's K-quants with a per-32-value 6-bit scale and min) ----
+ * Block: half2 dm {d, dmin}, scales[12], (Q5_K: qh[32]), qs[128]; 256 values in 8 sub-blocks of 32.
+ * Sub-block j's (scale, min) are ggml's get_scale_min_k4: j < 4: (s[j] & 63, s[j+4] & 63); else
+ * ((s[j+4] & 15) | ((s[j-4] >> 6) << 4), (s[j+4] >> 4) | ((s[j] >> 6) << 4)). Value k of sub-block j:
+ * low 4 bits = nibble (j & 1) of qs[32 * (j / 2) + k]; Q5_K's fifth bit = bit j of qh[k];
+ * value = d * scale * code - dmin * min. */
+static void kq_scale_min(const uint8_t* s, int j, int* sc, int* m) {
+    if (j < 4) {
+        *sc = s[j] & 63;
+        *m = s[j + 4] & 63;
+    } else {
+        *sc = (s[j + 4] & 15) | ((s[j - 4] >> 6) << 4);
+        *m = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
+    }
+}
+static int kq_code(int type, const uint8_t* blk, int v) {
+    const int j = v / 32, k = v % 32;
+    const uint8_t* qs = blk + (type == 13 ? 48 : 16);
+    int code = (qs[32 * (j / 2) + k] >> (4 * (j & 1))) & 15;
+    if (type == 13) code |= ((blk[16 + k] >> j) & 1) << 4;
+    return code;
+}
+void or_dequant_kq(int type, const void* w, float* y, int n_values) {
+    const size_t bb = type == 13 ? 176u : 144u;
+    for (int b = 0; b < n_values / 256; ++b) {
+        const uint8_t* blk = (const uint8_t*) w + bb * (size_t) b;
+        uint16_t h[2];
+        memcpy(h, blk, 4);
+        const float d = or_f16_to_f32(h[0]), dmin = or_f16_to_f32(h[1]);
+        for (int v = 0; v < 256; ++v) {
+            int sc, m;
+            kq_scale_min(blk + 4, v / 32, &sc, &m);
+            y[b * 256 + v] = d * (float) sc * (float) kq_code(type, blk, v) - dmin * (float) m;
+        }
+    }
+}
+
+/* vec_dot_q5_K_q8_1 / vec_dot_q4_K_q8_1 as the reference pins them (native_mmvq.cu:191-252, :543-595):
+ * thread iqs (even, 0..30) covers sub-blocks bq8 = 2 * ((iqs / 2) / 4) and bq8 + 1, and within each the
+ * ints (iqs / 2) % 4 and + 4 of the Q8_1 block (8 values). Per sub-block i: dot1 = sum(code * q8),
+ * dot2 = sum(q8) (dp4a chains in the reference's order), sumf_d += d8 * (dot1 * sc), sumf_m += d8 *
+ * (dot2 * m); the result d * sumf_d - dmin * sumf_m. isum_out (optional): dot1 * sc, dot2 * m per i. */
+static float kq_q8_dot(int type, const uint8_t* blk, const uint8_t* x, int iqs, int* isum_out) {
+    const int bq8 = 2 * ((iqs / 2) / 4), k4 = (iqs / 2) % 4;
+    const uint8_t* qs = blk + (type == 13 ? 48 : 16);
+    const int32_t vl0 = load_i32(qs + 16 * bq8 + 4 * k4), vl1 = load_i32(qs + 16 * bq8 + 4 * k4 + 16);
+    int32_t vh0 = 0, vh1 = 0;
+    if (type == 13) {
+        vh0 = (int32_t) ((uint32_t) load_i32(blk + 16 + 4 * k4) >> bq8);
+        vh1 = (int32_t) ((uint32_t) load_i32(blk + 16 + 4 * k4 + 16) >> bq8);
+    }
+    uint16_t h[2];
+    memcpy(h, blk, 4);
+    const float d = or_f16_to_f32(h[0]), dmin = or_f16_to_f32(h[1]);
+    float sumf_d = 0.0f, sumf_m = 0.0f;
+    for (int i = 0; i < 2; ++i) {
+        int sc, m;
+        kq_scale_min(blk + 4, bq8 + i, &sc, &m);
+        const uint8_t* xb = x + (size_t) (bq8 + i) * 36;
+        const int32_t u0 = load_i32(xb + 4 + 4 * k4), u1 = load_i32(xb + 4 + 4 * k4 + 16);
+        int32_t v0 = (int32_t) (((uint32_t) vl0 >> (4 * i)) & 0x0f0f0f0fu);
+        int32_t v1 = (int32_t) (((uint32_t) vl1 >> (4 * i)) & 0x0f0f0f0fu);
+        if (type == 13) {
+            v0 |= (int32_t) ((((uint32_t) vh0 >> i) << 4) & 0x10101010u);
+            v1 |= (int32_t) ((((uint32_t) vh1 >> i) << 4) & 0x10101010u);
+        }
+        /* Q5_K chains v0 into v1 (the reference's dp4a(v0, u0, dp4a(v1, u1, 0))); Q4_K v1 into v0 */
+        const int dot1 = type == 13 ? dp4a_ss(v0, u0, dp4a_ss(v1, u1, 0)) : dp4a_ss(v1, u1, dp4a_ss(v0, u0, 0));
+        const int dot2 = type == 13 ? dp4a_ss(0x01010101, u0, dp4a_ss(0x01010101, u1, 0))
+                                    : dp4a_ss(0x01010101, u1, dp4a_ss(0x01010101, u0, 0));
+        const float d8 = q81_d(xb);
+        if (isum_out) {
+            isum_out[2 * i] = dot1 * sc;
+            isum_out[2 * i + 1] = dot2 * m;
+        }
+        sumf_d += d8 * (float) (dot1 * sc);
+        sumf_m += d8 * (float) (dot2 * m);
+    }
+    return d * sumf_d - dmin * sumf_m;
+}
+
 /* Per row and column, the reference's reduction order: 4 warps x 32 lanes; warp w walks blocks
  * w, w+4, ... (Q6_K) and accumulates per lane; warps 1..3 add into warp 0 in order; then the xor tree.
  * (Q8_0 with n_in/32 >= 32: one row per block, kbx = tid/4 step 32, kqs = 2*(tid%4).) */
@@ -532,6 +615,13 @@ static float or_row_dot(int type, const uint8_t* wrow, const uint8_t* xcol, int 
                 const int nb = n_in / 256;
                 for (int kbx = tid / 32; kbx < nb; kbx += 4) {
                     const float f = q6_q8_dot(wrow + (size_t) kbx * 210, xcol + (size_t) kbx * 8 * 36, tid % 32, NULL);
+                    acc = acc + f;
+                }
+            } else if (type == 13 || type == 12) { /* QI 32, VDR 2: kbx = tid/16 step 8, kqs = 2*(tid%16) */
+                const int nb = n_in / 256;
+                for (int kbx = tid / 16; kbx < nb; kbx += 8) {
+                    const float f = kq_q8_dot(type, wrow + (size_t) kbx * (type == 13 ? 176 : 144),
+                                              xcol + (size_t) kbx * 8 * 36, 2 * (tid % 16), NULL);
                     acc = acc + f;
                 }
             } else { /* kbx = tid/4 step 32 for both SmallK variants (they differ only in rows per block) */
@@ -586,11 +676,13 @@ void or_mmvq_res(int type, const void* w, const void* xq, float* y, const float*
 /* Exact integer sums, the bit-exact parity target. Layout out[((j * n_out) + r) * nsub + s]:
  *   Q6_K: nsub = n_in/16, s = 16-value sub-block: sum over its 16 values of (code-32) * x_code * scale
  *         (the sum of the reference's per-lane dp4a(vi, u) * sc over the four lanes that cover it);
- *   Q8_0: nsub = n_in/32, s = 32-value block: sum of w_code * x_code. */
+ *   Q8_0: nsub = n_in/32, s = 32-value block: sum of w_code * x_code;
+ *   Q5_K / Q4_K: nsub = 2 * n_in/32, entries 2s and 2s+1 of 32-value sub-block s: the sums of dot1 * scale
+ *         and dot2 * min over the four threads that cover it. */
 void or_mmvq_isums(int type, const void* w, const void* xq, int32_t* out, int n_in, int n_out, int ncols) {
     const size_t rb = or_weight_bytes(type, n_in, 1);
     const size_t xbytes = or_q8_1_bytes(n_in, 1);
-    const int nsub = type == 14 ? n_in / 16 : n_in / 32;
+    const int nsub = type == 14 ? n_in / 16 : (type == 13 || type == 12) ? 2 * (n_in / 32) : n_in / 32;
 #pragma omp parallel for schedule(static)
     for (int r = 0; r < n_out; ++r)
         for (int j = 0; j < ncols; ++j) {
@@ -607,6 +699,18 @@ void or_mmvq_isums(int type, const void* w, const void* xq, int32_t* out, int n_
                          * 16-value sub-block index is scale_offset + 4i within the super-block */
                         const int scale_offset = 8 * (iqs / 16) + (iqs % 16) / 4;
                         for (int i = 0; i < 2; ++i) o[kbx * 16 + scale_offset + 4 * i] += p[i];
+                    }
+            } else if (type == 13 || type == 12) {
+                /* per 32-value sub-block s: (sum of dot1 * sc, sum of dot2 * m) over the four threads */
+                for (int kbx = 0; kbx < n_in / 256; ++kbx)
+                    for (int iqs = 0; iqs < 32; iqs += 2) {
+                        int p[4];
+                        kq_q8_dot(type, wrow + (size_t) kbx * (type == 13 ? 176 : 144), xcol + (size_t) kbx * 8 * 36, iqs, p);
+                        const int bq8 = 2 * ((iqs / 2) / 4);
+                        for (int i = 0; i < 2; ++i) {
+                            o[2 * (kbx * 8 + bq8 + i)] += p[2 * i];
+                            o[2 * (kbx * 8 + bq8 + i) + 1] += p[2 * i + 1];
+                        }
                     }
             } else {
                 for (int kbx = 0; kbx < n_in / 32; ++kbx)

@@ -43,6 +43,8 @@ void or_dequantize_q8_1(const void* y, float* x, int n);
 
 /* ---- weights: GGUF layouts (type 14 = Q6_K, type 8 = Q8_0) ---- */
 size_t or_weight_bytes(int type, int n_in, int n_out);
+/* Q5_K (13) / Q4_K (12) blocks to fp32 (ggml's dequantize_row_q5_K / _q4_K). */
+void or_dequant_kq(int type, const void* w, float* y, int n_values);
 size_t or_packed_bytes(int type, int n_in, int n_out);
 void or_quantize_weights(int type, const float* w, void* dst, int n_in, int n_out);
 void or_dequantize_weights(int type, const void* w, float* dst, int n_in, int n_out);

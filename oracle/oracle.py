@@ -14,6 +14,8 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 _LIB_PATH = os.path.join(_HERE, "liboracle.so")
 
 TYPE_Q8_0 = 8
+TYPE_Q4_K = 12
+TYPE_Q5_K = 13
 TYPE_Q6_K = 14
 
 _lib = None
@@ -53,6 +55,7 @@ def _declare(L):
         "or_quantize_q8_1": (None, [_f32p, _u8p, _i, _i]),
         "or_dequantize_q8_1": (None, [_u8p, _f32p, _i]),
         "or_weight_bytes": (_sz, [_i, _i, _i]),
+        "or_dequant_kq": (None, [_i, _u8p, _f32p, _i]),
         "or_packed_bytes": (_sz, [_i, _i, _i]),
         "or_quantize_weights": (None, [_i, _f32p, _u8p, _i, _i]),
         "or_dequantize_weights": (None, [_i, _u8p, _f32p, _i, _i]),
@@ -141,6 +144,24 @@ def weight_bytes(t, n_in, n_out):
     return lib().or_weight_bytes(t, n_in, n_out)
 
 
+def random_kquant_weights(t, n_in, n_out, seed):
+    """Q5_K (13) / Q4_K (12) rows of random blocks: uniform code, scale and high-bit bytes, and the block
+    scales d, dmin drawn as small positive fp16 (every byte pattern of the rest is a valid block)."""
+    bb = 176 if t == TYPE_Q5_K else 144
+    nb = n_out * (n_in // 256)
+    rng = np.random.default_rng(seed)
+    raw = rng.integers(0, 256, size=(nb, bb), dtype=np.uint8)
+    dm = np.stack([rng.uniform(0.5e-3, 2e-3, nb), rng.uniform(0.5e-3, 2e-3, nb)], 1).astype(np.float16)
+    raw[:, 0:4] = dm.view(np.uint8).reshape(nb, 4)
+    return raw.reshape(-1)
+
+
+def dequant_kq(t, w, n_values):
+    y = np.empty(n_values, np.float32)
+    lib().or_dequant_kq(t, _c(w, np.uint8), y, n_values)
+    return y
+
+
 def quantize_weights(t, w, n_in, n_out):
     w = _c(w, np.float32).ravel()
     dst = np.empty(weight_bytes(t, n_in, n_out), np.uint8)
@@ -186,7 +207,7 @@ def mmvq_res(t, w, xq, res, n_in, n_out, ncols=1):
 
 
 def mmvq_isums(t, w, xq, n_in, n_out, ncols=1):
-    nsub = n_in // 16 if t == TYPE_Q6_K else n_in // 32
+    nsub = n_in // 16 if t == TYPE_Q6_K else (2 * (n_in // 32) if t in (TYPE_Q5_K, TYPE_Q4_K) else n_in // 32)
     out = np.empty(ncols * n_out * nsub, np.int32)
     lib().or_mmvq_isums(t, _c(w, np.uint8), _c(xq, np.uint8), out, n_in, n_out, ncols)
     return out

@@ -16,7 +16,7 @@ HEADER = os.path.join(ROOT, "include", "rapier_b200.h")
 
 RK_FLAG_STATIC_WEIGHTS = 1
 RK_OK, RK_EINVAL, RK_ECUDA, RK_ENOMEM, RK_ERANGE, RK_EUNSUPPORTED = 0, -1, -2, -3, -4, -5
-TYPE_Q8_0, TYPE_Q6_K = 8, 14
+TYPE_Q8_0, TYPE_Q4_K, TYPE_Q5_K, TYPE_Q6_K = 8, 12, 13, 14
 _CODE_NAMES = {RK_EINVAL: "RK_EINVAL", RK_ECUDA: "RK_ECUDA", RK_ENOMEM: "RK_ENOMEM", RK_ERANGE: "RK_ERANGE",
                RK_EUNSUPPORTED: "RK_EUNSUPPORTED"}
 

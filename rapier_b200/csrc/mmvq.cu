@@ -31,6 +31,68 @@ __device__ __forceinline__ int ld_b2(const uint8_t* p) {  // two little-endian u
     return (int) ((uint32_t) q[0] | ((uint32_t) q[1] << 16));
 }
 
+__host__ __device__ constexpr size_t raw_row_bytes(int type, int n_in) {
+    return type == RK_TYPE_Q6_K   ? (size_t) (n_in / 256) * 210
+           : type == RK_TYPE_Q5_K ? (size_t) (n_in / 256) * 176
+           : type == RK_TYPE_Q4_K ? (size_t) (n_in / 256) * 144
+                                  : (size_t) (n_in / 32) * 34;
+}
+
+// Q5_K / Q4_K sub-block j's 6-bit (scale, min): ggml's get_scale_min_k4 over the block's 12 scale bytes.
+__device__ __forceinline__ void kq_scale_min(const uint8_t* s, int j, int& sc, int& m) {
+    if (j < 4) {
+        sc = s[j] & 63;
+        m = s[j + 4] & 63;
+    } else {
+        sc = (s[j + 4] & 15) | ((s[j - 4] >> 6) << 4);
+        m = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
+    }
+}
+
+// Thread iqs (even) of a Q5_K / Q4_K block against one Q8_1 column (vec_dot_q5_K_q8_1 / _q4_K_q8_1 as
+// src/native_mmvq.cu:191-252 and :543-595 pin them): sub-blocks bq8 and bq8 + 1, 8 values of each. ip
+// (optional) receives dot1 * scale and dot2 * min per sub-block; returns d * sumf_d - dmin * sumf_m.
+template <int TYPE>
+__device__ __forceinline__ float kq_q8_dot(const uint8_t* blk, const uint8_t* x, int iqs, int* ip) {
+    constexpr int QS = TYPE == RK_TYPE_Q5_K ? 48 : 16;
+    const int bq8 = 2 * ((iqs / 2) / 4), k4 = (iqs / 2) % 4;
+    const uint32_t vl0 = *reinterpret_cast<const uint32_t*>(blk + QS + 16 * bq8 + 4 * k4);
+    const uint32_t vl1 = *reinterpret_cast<const uint32_t*>(blk + QS + 16 * bq8 + 4 * k4 + 16);
+    uint32_t vh0 = 0, vh1 = 0;
+    if constexpr (TYPE == RK_TYPE_Q5_K) {
+        vh0 = *reinterpret_cast<const uint32_t*>(blk + 16 + 4 * k4) >> bq8;
+        vh1 = *reinterpret_cast<const uint32_t*>(blk + 16 + 4 * k4 + 16) >> bq8;
+    }
+    const uint32_t dm = *reinterpret_cast<const uint32_t*>(blk);
+    float sumf_d = 0.0f, sumf_m = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        int sc, m;
+        kq_scale_min(blk + 4, bq8 + i, sc, m);
+        const uint8_t* xb = x + (size_t) (bq8 + i) * 36;
+        const int u0 = *reinterpret_cast<const int*>(xb + 4 + 4 * k4), u1 = *reinterpret_cast<const int*>(xb + 20 + 4 * k4);
+        int v0 = (int) ((vl0 >> (4 * i)) & 0x0f0f0f0fu), v1 = (int) ((vl1 >> (4 * i)) & 0x0f0f0f0fu);
+        int dot1, dot2;
+        if constexpr (TYPE == RK_TYPE_Q5_K) {
+            v0 |= (int) (((vh0 >> i) << 4) & 0x10101010u);
+            v1 |= (int) (((vh1 >> i) << 4) & 0x10101010u);
+            dot1 = __dp4a(v0, u0, __dp4a(v1, u1, 0));
+            dot2 = __dp4a(0x01010101, u0, __dp4a(0x01010101, u1, 0));
+        } else {
+            dot1 = __dp4a(v1, u1, __dp4a(v0, u0, 0));
+            dot2 = __dp4a(0x01010101, u1, __dp4a(0x01010101, u0, 0));
+        }
+        if (ip) {
+            ip[2 * i] = dot1 * sc;
+            ip[2 * i + 1] = dot2 * m;
+        }
+        const float d8 = half_bits_to_float(*reinterpret_cast<const uint16_t*>(xb));
+        sumf_d = __fadd_rn(sumf_d, __fmul_rn(d8, (float) (dot1 * sc)));
+        sumf_m = __fadd_rn(sumf_m, __fmul_rn(d8, (float) (dot2 * m)));
+    }
+    return __fsub_rn(__fmul_rn(half_bits_to_float(dm), sumf_d), __fmul_rn(half_bits_to_float(dm >> 16), sumf_m));
+}
+
 template <int TYPE, int NC>
 __device__ __forceinline__ void raw_row_dot(const uint8_t* wrow, const uint8_t* xq, size_t xcol, int n_in, int lane,
                                             float (&acc)[NC]) {
@@ -60,6 +122,15 @@ __device__ __forceinline__ void raw_row_dot(const uint8_t* wrow, const uint8_t* 
                 acc[c] = __fmaf_rn(d, sumf, acc[c]);
             }
         }
+    } else if constexpr (TYPE == RK_TYPE_Q5_K || TYPE == RK_TYPE_Q4_K) {
+        // lanes 0..15: the even blocks, 16..31 the odd ones; thread iqs = 2 * (lane % 16) of each
+        const size_t bb = raw_row_bytes(TYPE, 256);
+        for (int kb = lane >> 4; kb < n_in / 256; kb += 2) {
+            const uint8_t* blk = wrow + (size_t) kb * bb;
+#pragma unroll
+            for (int c = 0; c < NC; ++c)
+                acc[c] = __fadd_rn(acc[c], kq_q8_dot<TYPE>(blk, xq + c * xcol + (size_t) kb * 8 * 36, 2 * (lane & 15), nullptr));
+        }
     } else {
         // lane l: ints 2*(l%4), 2*(l%4)+1 of blocks l/4, l/4 + 8, ...
         const int sub = lane >> 2, iqs = 2 * (lane & 3);
@@ -87,7 +158,7 @@ __global__ void __launch_bounds__(128) mmvq_raw_kernel(const uint8_t* __restrict
     pdl_wait();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int row = blockIdx.x * 4 + warp;
-    const size_t rb = TYPE == RK_TYPE_Q6_K ? (size_t) (n_in / 256) * 210 : (size_t) (n_in / 32) * 34;
+    const size_t rb = raw_row_bytes(TYPE, n_in);
     const size_t xcol = (size_t) (n_in / 32) * 36;
     float acc[NC];
 #pragma unroll
@@ -301,8 +372,12 @@ __global__ void isums_kernel(const uint8_t* __restrict__ w, const uint8_t* __res
 // host validation (the reference's validate_shape / validate_pointer / validate_stream,
 // src/native_mmvq.cu:2312-2331)
 // ---------------------------------------------------------------------------------------------------
-bool type_ok(int type) { return type == RK_TYPE_Q6_K || type == RK_TYPE_Q8_0; }
-int block_elems(int type) { return type == RK_TYPE_Q6_K ? 256 : 32; }
+bool type_ok(int type) {  // GGUF rows
+    return type == RK_TYPE_Q6_K || type == RK_TYPE_Q8_0 || type == RK_TYPE_Q5_K || type == RK_TYPE_Q4_K;
+}
+bool packed_ok(int type) { return type == RK_TYPE_Q6_K || type == RK_TYPE_Q8_0; }  // packed tiles
+int block_elems(int type) { return type == RK_TYPE_Q8_0 ? 32 : 256; }
+bool kquant(int type) { return type == RK_TYPE_Q5_K || type == RK_TYPE_Q4_K; }
 int check_ptr(const void* p, const char* what) {
     if (!p || (reinterpret_cast<uintptr_t>(p) & 3u) != 0)
         return set_error(RK_EINVAL, "%s: requires non-null 4-byte aligned device pointers", what);
@@ -318,7 +393,8 @@ int check_stream(void* s, const char* what) {
     return RK_OK;
 }
 int check_gemv_shape(int type, int n_in, int n_out, int ncols, const char* what) {
-    if (!type_ok(type)) return set_error(RK_EUNSUPPORTED, "%s: unsupported weight type %d (14 = Q6_K, 8 = Q8_0)", what, type);
+    if (!type_ok(type))
+        return set_error(RK_EUNSUPPORTED, "%s: unsupported weight type %d (14 = Q6_K, 13 = Q5_K, 12 = Q4_K, 8 = Q8_0)", what, type);
     if (n_in <= 0 || n_in % block_elems(type) != 0)
         return set_error(RK_EINVAL, "%s: requires n_in > 0 and divisible by its block element count", what);
     if (n_out <= 0) return set_error(RK_EINVAL, "%s: requires n_out > 0", what);
@@ -328,6 +404,7 @@ int check_gemv_shape(int type, int n_in, int n_out, int ncols, const char* what)
 int check_packed_shape(int type, int n_in, int n_out, int ncols, const char* what) {
     int rc = check_gemv_shape(type, n_in, n_out, ncols, what);
     if (rc) return rc;
+    if (!packed_ok(type)) return set_error(RK_EUNSUPPORTED, "%s: type %d has no packed layout (Q6_K and Q8_0 do)", what, type);
     if (n_in % 1024 != 0 || n_out % 4 != 0)
         return set_error(RK_EINVAL, "%s: packed layout requires n_in %% 1024 == 0 and n_out %% 4 == 0", what);
     if (n_in > 32768) return set_error(RK_EINVAL, "%s: packed GEMV supports n_in <= 32768", what);
@@ -345,6 +422,42 @@ cudaError_t raw_launch_cols(const uint8_t* w, const uint8_t* xq, float* y, const
         case 3: return launch_pdl(mmvq_raw_kernel<TYPE, 3, false>, grid, dim3(128), 0, s, true, w, xq, y, res, partials, n_in, n_out);
         default: return launch_pdl(mmvq_raw_kernel<TYPE, 4, false>, grid, dim3(128), 0, s, true, w, xq, y, res, partials, n_in, n_out);
     }
+}
+
+template <bool RES>
+cudaError_t raw_dispatch(int type, const uint8_t* w, const uint8_t* xq, float* y, const float* res, float* partials,
+                         int n_in, int n_out, int nc, cudaStream_t s) {
+    switch (type) {
+        case RK_TYPE_Q6_K: return raw_launch_cols<RK_TYPE_Q6_K, RES>(w, xq, y, res, partials, n_in, n_out, nc, s);
+        case RK_TYPE_Q5_K: return raw_launch_cols<RK_TYPE_Q5_K, RES>(w, xq, y, res, partials, n_in, n_out, nc, s);
+        case RK_TYPE_Q4_K: return raw_launch_cols<RK_TYPE_Q4_K, RES>(w, xq, y, res, partials, n_in, n_out, nc, s);
+        default: return raw_launch_cols<RK_TYPE_Q8_0, RES>(w, xq, y, res, partials, n_in, n_out, nc, s);
+    }
+}
+
+// Parity probe for the K-quants on GGUF rows: one thread per (column, row, 32-value sub-block), the sums
+// of dot1 * scale and dot2 * min over the four block threads that cover the sub-block (kq_q8_dot).
+template <int TYPE>
+__global__ void isums_kq_kernel(const uint8_t* __restrict__ w, const uint8_t* __restrict__ xq, int32_t* __restrict__ out,
+                                int n_in, int n_out, int ncols) {
+    const long long nsub = n_in / 32;
+    const long long idx = (long long) blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= (long long) ncols * n_out * nsub) return;
+    const int s = (int) (idx % nsub);
+    const long long cr = idx / nsub;
+    const int r = (int) (cr % n_out), c = (int) (cr / n_out);
+    const int kb = s / 8, j = s % 8, p = j / 2, i = j % 2;
+    const uint8_t* blk = w + (size_t) r * raw_row_bytes(TYPE, n_in) + (size_t) kb * raw_row_bytes(TYPE, 256);
+    const uint8_t* x = xq + (size_t) c * (n_in / 32) * 36 + (size_t) kb * 8 * 36;
+    int a = 0, b = 0;
+    for (int t = 4 * p; t < 4 * p + 4; ++t) {  // threads iqs = 2t cover sub-blocks 2p, 2p + 1
+        int ip[4];
+        kq_q8_dot<TYPE>(blk, x, 2 * t, ip);
+        a += ip[2 * i];
+        b += ip[2 * i + 1];
+    }
+    out[2 * idx] = a;
+    out[2 * idx + 1] = b;
 }
 
 template <int TYPE, int EPI>
@@ -385,12 +498,11 @@ int rk_quantize_q8_1(const float* x, void* x_q8_1, int n_in, int ncols, void* st
 
 size_t rk_weight_bytes(int type, int n_in, int n_out) {
     if (!type_ok(type) || n_in <= 0 || n_out <= 0 || n_in % block_elems(type) != 0) return 0;
-    const size_t rb = type == RK_TYPE_Q6_K ? (size_t) (n_in / 256) * 210 : (size_t) (n_in / 32) * 34;
-    return rb * (size_t) n_out;
+    return raw_row_bytes(type, n_in) * (size_t) n_out;
 }
 
 size_t rk_packed_bytes(int type, int n_in, int n_out) {
-    if (!type_ok(type) || n_in <= 0 || n_out <= 0 || n_in % 1024 != 0 || n_out % 4 != 0) return 0;
+    if (!packed_ok(type) || n_in <= 0 || n_out <= 0 || n_in % 1024 != 0 || n_out % 4 != 0) return 0;
     return rk_weight_bytes(type, n_in, n_out);
 }
 
@@ -398,8 +510,8 @@ int rk_mmvq(int type, const void* weights, const void* x_q8_1, float* y, int n_i
             void* stream) {
     const char* what = "rk_mmvq";
     if (int rc = check_gemv_shape(type, n_in, n_out, ncols, what)) return rc;
-    if (!weights || (reinterpret_cast<uintptr_t>(weights) & 1u))
-        return set_error(RK_EINVAL, "%s: requires non-null 2-byte aligned weights", what);
+    if (!weights || (reinterpret_cast<uintptr_t>(weights) & (kquant(type) ? 3u : 1u)))
+        return set_error(RK_EINVAL, "%s: requires non-null weights, 2-byte aligned (4-byte for Q5_K / Q4_K)", what);
     if (int rc = check_ptr(x_q8_1, what)) return rc;
     if (int rc = check_ptr(y, what)) return rc;
     if (int rc = check_stream(stream, what)) return rc;
@@ -408,9 +520,8 @@ int rk_mmvq(int type, const void* weights, const void* x_q8_1, float* y, int n_i
         const int nc = ncols - j < 4 ? ncols - j : 4;
         const uint8_t* xq = (const uint8_t*) x_q8_1 + (size_t) j * xcol;
         float* yj = y + (size_t) j * n_out;
-        cudaError_t e = type == RK_TYPE_Q6_K
-                            ? raw_launch_cols<RK_TYPE_Q6_K, false>((const uint8_t*) weights, xq, yj, nullptr, nullptr, n_in, n_out, nc, (cudaStream_t) stream)
-                            : raw_launch_cols<RK_TYPE_Q8_0, false>((const uint8_t*) weights, xq, yj, nullptr, nullptr, n_in, n_out, nc, (cudaStream_t) stream);
+        cudaError_t e = raw_dispatch<false>(type, (const uint8_t*) weights, xq, yj, nullptr, nullptr, n_in, n_out, nc,
+                                            (cudaStream_t) stream);
         if (e != cudaSuccess) return set_error(RK_ECUDA, "%s: %s", what, cudaGetErrorString(e));
     }
     return check_launch(what);
@@ -420,16 +531,15 @@ int rk_mmvq_res(int type, const void* weights, const void* x_q8_1, float* y, con
                 int n_in, int n_out, void* stream) {
     const char* what = "rk_mmvq_res";
     if (int rc = check_gemv_shape(type, n_in, n_out, 1, what)) return rc;
-    if (!weights || (reinterpret_cast<uintptr_t>(weights) & 1u))
-        return set_error(RK_EINVAL, "%s: requires non-null 2-byte aligned weights", what);
+    if (!weights || (reinterpret_cast<uintptr_t>(weights) & (kquant(type) ? 3u : 1u)))
+        return set_error(RK_EINVAL, "%s: requires non-null weights, 2-byte aligned (4-byte for Q5_K / Q4_K)", what);
     if (int rc = check_ptr(x_q8_1, what)) return rc;
     if (int rc = check_ptr(y, what)) return rc;
     if (int rc = check_ptr(res, what)) return rc;
     if (int rc = check_ptr(partials, what)) return rc;
     if (int rc = check_stream(stream, what)) return rc;
-    cudaError_t e = type == RK_TYPE_Q6_K
-                        ? raw_launch_cols<RK_TYPE_Q6_K, true>((const uint8_t*) weights, (const uint8_t*) x_q8_1, y, res, partials, n_in, n_out, 1, (cudaStream_t) stream)
-                        : raw_launch_cols<RK_TYPE_Q8_0, true>((const uint8_t*) weights, (const uint8_t*) x_q8_1, y, res, partials, n_in, n_out, 1, (cudaStream_t) stream);
+    cudaError_t e = raw_dispatch<true>(type, (const uint8_t*) weights, (const uint8_t*) x_q8_1, y, res, partials, n_in,
+                                       n_out, 1, (cudaStream_t) stream);
     if (e != cudaSuccess) return set_error(RK_ECUDA, "%s: %s", what, cudaGetErrorString(e));
     return check_launch(what);
 }
@@ -531,6 +641,20 @@ int rk_mmvq_packed_res(int type, const void* packed, const void* x_q8_1, float* 
 int rk_mmvq_isums(int type, const void* packed, const void* x_q8_1, int32_t* out, int n_in, int n_out, int ncols,
                   void* stream) {
     const char* what = "rk_mmvq_isums";
+    if (kquant(type)) {  // GGUF rows (the K-quants have no packed layout)
+        if (int rc = check_gemv_shape(type, n_in, n_out, ncols, what)) return rc;
+        if (int rc = check_ptr(packed, what)) return rc;
+        if (int rc = check_ptr(x_q8_1, what)) return rc;
+        if (int rc = check_ptr(out, what)) return rc;
+        if (int rc = check_stream(stream, what)) return rc;
+        const long long items = (long long) ncols * n_out * (n_in / 32);
+        const unsigned blocks = (unsigned) ((items + 255) / 256);
+        if (type == RK_TYPE_Q5_K)
+            isums_kq_kernel<RK_TYPE_Q5_K><<<blocks, 256, 0, (cudaStream_t) stream>>>((const uint8_t*) packed, (const uint8_t*) x_q8_1, out, n_in, n_out, ncols);
+        else
+            isums_kq_kernel<RK_TYPE_Q4_K><<<blocks, 256, 0, (cudaStream_t) stream>>>((const uint8_t*) packed, (const uint8_t*) x_q8_1, out, n_in, n_out, ncols);
+        return check_launch(what);
+    }
     if (int rc = check_packed_shape(type, n_in, n_out, ncols, what)) return rc;
     if (int rc = check_ptr16(packed, what)) return rc;
     if (int rc = check_ptr(x_q8_1, what)) return rc;

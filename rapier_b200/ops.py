@@ -13,12 +13,13 @@ throws std::invalid_argument, src/native_mmvq.cu:2312-2331); a failed launch rai
 from __future__ import annotations
 
 from . import _lib
-from ._lib import RK_EINVAL, RK_EUNSUPPORTED, RkError, TYPE_Q6_K, TYPE_Q8_0
+from ._lib import RK_EINVAL, RK_EUNSUPPORTED, RkError, TYPE_Q4_K, TYPE_Q5_K, TYPE_Q6_K, TYPE_Q8_0
 
 __all__ = [
-    "TYPE_Q6_K", "TYPE_Q8_0", "RkError",
+    "TYPE_Q6_K", "TYPE_Q5_K", "TYPE_Q4_K", "TYPE_Q8_0", "RkError",
     "native_q8_1_bytes", "native_quantize_q8_1", "native_mmvq_weight_bytes", "native_mmvq",
     "native_q6_k_mmvq", "native_q8_0_mmvq", "native_q6_k_mmvq_res", "native_q8_0_mmvq_res",
+    "native_q5_k_mmvq", "native_q4_k_mmvq", "native_q5_k_mmvq_res", "native_q4_k_mmvq_res",
     "packed_bytes", "pack_weights", "unpack_weights", "mmvq_packed", "mmvq_packed_ex", "mmvq_packed_res", "mmvq_isums",
     "row_sum_partials", "add_partials", "rms_quant_apply", "rms_norm_out", "swiglu_quant", "sig_mul_quant",
     "beta_gate", "rms_norm_weighted", "argmax", "fused_gdn_conv_l2", "fused_gdn_step_norm_silu_q8",
@@ -103,6 +104,24 @@ def native_q6_k_mmvq_res(weights, x_q8_1, y, res, partials, n_in, n_out, stream=
 
 def native_q8_0_mmvq_res(weights, x_q8_1, y, res, partials, n_in, n_out, stream=None):
     _call("rk_mmvq_res", TYPE_Q8_0, _ptr(weights), _ptr(x_q8_1), _ptr(y), _ptr(res), _ptr(partials), n_in, n_out,
+          _stream(stream))
+
+
+def native_q5_k_mmvq(weights, x_q8_1, y, n_in, n_out, ncols, stream=None):
+    native_mmvq(TYPE_Q5_K, weights, x_q8_1, y, n_in, n_out, ncols, stream)
+
+
+def native_q4_k_mmvq(weights, x_q8_1, y, n_in, n_out, ncols, stream=None):
+    native_mmvq(TYPE_Q4_K, weights, x_q8_1, y, n_in, n_out, ncols, stream)
+
+
+def native_q5_k_mmvq_res(weights, x_q8_1, y, res, partials, n_in, n_out, stream=None):
+    _call("rk_mmvq_res", TYPE_Q5_K, _ptr(weights), _ptr(x_q8_1), _ptr(y), _ptr(res), _ptr(partials), n_in, n_out,
+          _stream(stream))
+
+
+def native_q4_k_mmvq_res(weights, x_q8_1, y, res, partials, n_in, n_out, stream=None):
+    _call("rk_mmvq_res", TYPE_Q4_K, _ptr(weights), _ptr(x_q8_1), _ptr(y), _ptr(res), _ptr(partials), n_in, n_out,
           _stream(stream))
 
 
