@@ -315,10 +315,11 @@ typedef struct rk_probe_result {
 int rk_engine_probe_gemv(rk_engine* e, int ncols, int iters, rk_probe_result* out);
 /* Device bytes the engine holds. */
 size_t rk_engine_device_bytes(const rk_engine* e);
-/* The executor the engine runs its step programs with: RK_ENGINE_PERSISTENT (one cooperative kernel per
- * program, a whole generation in one launch; the default) or RK_ENGINE_GRAPH (one kernel per op, replayed
- * from CUDA graphs; chosen by the environment variable RK_ENGINE_MODE=graph at rk_engine_create). Both
- * produce the same bits. No reference counterpart (the reference replays a CUDA graph). */
+/* The executor the engine runs its step programs with: RK_ENGINE_GRAPH (one kernel per op, replayed from
+ * CUDA graphs; the single-GPU default) or RK_ENGINE_PERSISTENT (one cooperative kernel per program, a
+ * whole generation in one launch; the tensor-parallel default, required there). The environment variable
+ * RK_ENGINE_MODE=graph|persistent, read at rk_engine_create, overrides. Both produce the same bits. No
+ * reference counterpart (the reference replays a CUDA graph). */
 #define RK_ENGINE_GRAPH 0
 #define RK_ENGINE_PERSISTENT 1
 int rk_engine_mode(const rk_engine* e);

@@ -574,16 +574,14 @@ cudaError_t mmvq_launch(MmvqParams p, cudaStream_t s, bool pdl) {
     }
     const size_t tile = TYPE == RK_TYPE_Q6_K ? kQ6Tile : kQ80Tile;
     const size_t fixed = mmvq_smem_bytes(TYPE, p.n_in, NC, 0);
-    // Two CTAs per SM (16 warps; measured best for 1-2 columns) with the deepest ring that fits both in
-    // ~113 KB; when the staged activations leave room for fewer than 2 slots, one CTA with a deeper ring.
-    int ctas = 2;
-    int stages = (int) ((113 * 1024 - (long long) fixed) / (long long) (kMmvqWarps * tile));
-    if (stages > 3) stages = 3;
-    if (stages < 2) {
-        ctas = 1;
-        stages = (int) (((long long) max_optin - 2048 - (long long) fixed) / (long long) (kMmvqWarps * tile));
-        if (stages > 4) stages = 4;
-    }
+    // One CTA per SM (8 warps) with a ring of up to 5 slots: measured best on B200 for config 1 (12288 x
+    // 4096, 2 columns: 2.8 vs 2.4-2.6 TB/s) and for a decode step of one GEMV launch per op (2.45 vs
+    // 2.59 ms). Two 3-slot CTAs per SM leave the busiest warp 8 tiles where the average is 5 (units are
+    // dealt to warps whole), with 16 warps sharing the SM's issue slots, and let the next op's CTAs become
+    // resident and start their weight prefetch while this one still runs.
+    int ctas = 1;
+    int stages = (int) (((long long) max_optin - 2048 - (long long) fixed) / (long long) (kMmvqWarps * tile));
+    if (stages > 5) stages = 5;
     if (mmvq_env_stages() > 0) stages = mmvq_env_stages();
     if (mmvq_env_ctas() > 0) ctas = mmvq_env_ctas();
     if (stages < 2 || stages > kMmvqMaxStages) return cudaErrorInvalidValue;
