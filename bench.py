@@ -277,7 +277,8 @@ def run_decode(args, rank, world, local, pg):
     if tp > 1:
         subgroups = [pg.new_group(list(range(g * tp, (g + 1) * tp))) for g in range(groups)]
         group = subgroups[grp]
-    cfg = config_9b(max_ctx=args.ctx, seed=1 + grp)
+    fill = args.ctx_fill
+    cfg = config_9b(max_ctx=max(args.ctx, fill + N_PROMPT + args.gen + 64) if fill else args.ctx, seed=1 + grp)
     eng = Engine(cfg, device=local, tp_rank=tp_rank, tp_size=tp)
     if tp > 1:
         eng.connect_tp(group)
@@ -285,14 +286,22 @@ def run_decode(args, rank, world, local, pg):
     prompt = [int(t) for t in np.random.default_rng(1234 + grp).integers(0, cfg.n_vocab, N_PROMPT)]
     mtp = not args.no_mtp
     n_gen = args.gen
+
+    def one_generation():
+        if fill:  # decode after a synthetic context of `fill` tokens (seeded caches, rk_engine_session_fill)
+            eng.session_fill(fill, 7 + grp)
+            ids, st, _ = eng.session_run(prompt, n_gen, mtp=mtp)
+            return ids, st
+        return eng.generate(prompt, n_gen, mtp=mtp)
+
     for _ in range(args.warmup):
-        eng.generate(prompt, n_gen, mtp=mtp)
+        one_generation()
     barrier(pg, dev)
     gen_ms, stats = 0.0, None
     t0 = time.perf_counter()
     with ClockSampler(local) as clk:
         for _ in range(args.steps):
-            ids, st = eng.generate(prompt, n_gen, mtp=mtp)
+            ids, st = one_generation()
             gen_ms += st["gen_ms"]
             stats = st
         barrier(pg, dev)
@@ -323,7 +332,8 @@ def run_decode(args, rank, world, local, pg):
         "data": "synthetic (random-init weights, seeded prompt)",
         "config": {"workload": "config5-decode-mtp" if mtp else "config4-decode", "model": "qwen35-9b-shaped",
                    "layers": "24 GDN + 8 GQA (+1 MTP block)", "n_prompt": N_PROMPT, "n_gen": n_gen,
-                   "ctx": args.ctx, "parallelism": par, "tensor_parallel": tp, "groups": groups,
+                   "ctx": (fill + N_PROMPT + n_gen) if fill else args.ctx, "kv_context": fill + N_PROMPT if fill else N_PROMPT,
+                   "parallelism": par, "tensor_parallel": tp, "groups": groups,
                    "executor": "persistent" if persistent else "graph",
                    "l2": "6.5 GB of weights per token > 126 MB L2"},
         "mtp": {"rounds": rounds, "accepted": stats["mtp_accepted"],
@@ -444,6 +454,9 @@ def main():
                     help="pass: four single-token steps of a --layers model (a small case for ncu captures)")
     ap.add_argument("--layers", type=int, default=8, help="pass: decoder layers of the 9B-shaped model")
     ap.add_argument("--ctx", type=int, default=512, help="decode: KV capacity (512 or 65536)")
+    ap.add_argument("--ctx-fill", type=int, default=0,
+                    help="decode: start each generation after a synthetic context of this many tokens (65536: "
+                         "config 5 at long context; seeded fp16 K/V and GDN states, rk_engine_session_fill)")
     ap.add_argument("--no-mtp", action="store_true", help="decode: plain greedy (config 4)")
     ap.add_argument("--gen", type=int, default=N_GEN, help="decode: tokens per generation (400; fewer for profiling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")

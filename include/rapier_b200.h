@@ -296,6 +296,12 @@ int rk_engine_step(rk_engine* e, const int* tokens, int ncols, int pos, float* l
 int rk_engine_session_reset(rk_engine* e);
 int rk_engine_session_run(rk_engine* e, const int* tokens, int n_tokens, int n_gen, int use_mtp, int eos_id,
                           int* out_ids, int* n_out, float* first_logits, rk_gen_stats* stats);
+/* Benchmark helper (no reference counterpart): resets the engine, fills the caches of a context of n_pos
+ * tokens with seeded synthetic values (fp16 K and V ~ N(0, 1) in every attention layer and the draft
+ * layer; GDN states ~ N(0, 0.01)) and places the session after them, so the next rk_engine_session_run
+ * decodes at positions n_pos, n_pos + 1, ... (config 5 at a 65536-token context without a 65536-token
+ * prompt). */
+int rk_engine_session_fill(rk_engine* e, int n_pos, unsigned long long seed);
 /* The session's next position (tokens in the context plus the pending one), -1 for a NULL engine. */
 int rk_engine_session_pos(const rk_engine* e);
 /* Copies tensor `tid` (this library's synthetic tensor id) to the host: GGUF Q6_K bytes for quantized

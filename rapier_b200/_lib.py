@@ -98,6 +98,7 @@ SIGNATURES = {
     "rk_engine_session_run": (i32, [vp, C.POINTER(C.c_int), i32, i32, i32, i32, C.POINTER(C.c_int),
                                     C.POINTER(C.c_int), vp, C.POINTER(GenStats)]),
     "rk_engine_session_pos": (i32, [vp]),
+    "rk_engine_session_fill": (i32, [vp, i32, C.c_uint64]),
     "rk_engine_read_tensor": (sz, [vp, i32, vp, sz]),
     "rk_engine_device_bytes": (sz, [vp]),
     "rk_engine_mode": (i32, [vp]),

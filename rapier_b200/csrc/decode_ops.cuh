@@ -16,7 +16,7 @@ namespace rk {
 
 constexpr int kHdA = 256;     // attention head dim
 constexpr int kSubA = 256;    // tokens scored per pass inside a flash-decode chunk (shared-memory scores)
-constexpr int kMaxChunksA = 64;  // flash-decode chunks per kv head at most (bounds the partials)
+constexpr int kMaxChunksA = 512;  // flash-decode chunks per kv head at most (bounds the partials)
 constexpr int kGqa = 4;       // query heads per kv head
 constexpr int kSsm = 128;     // GDN head size
 constexpr float kInvSqrtSsm = 0.08838834764831845f;  // 1/sqrt(128)
@@ -118,8 +118,8 @@ struct alignas(16) POp {  // 16-byte multiple: fetched into shared memory by 16-
 static_assert(sizeof(POp) % 16 == 0 && sizeof(POp) / 16 <= 256, "op records are copied in 16-byte chunks");
 
 // Tokens per flash-decode chunk for a step at positions pos .. pos+nc-1: the smallest of 32, 64, 128, ...
-// that keeps a kv head's chunks at most kMaxChunksA (many small chunks spread a short context over
-// many CTAs; long contexts get longer chunks and a bounded partial buffer).
+// that keeps a kv head's chunks at most kMaxChunksA (many small chunks spread any context over many CTAs:
+// 17 chunks of 32 at 512 tokens, 257 of 256 at 65536; the partial buffer stays bounded).
 __host__ __device__ __forceinline__ int attn_chunk_len(int pos, int nc) {
     int len = 32;
     while ((pos + nc + len - 1) / len > kMaxChunksA) len <<= 1;
@@ -425,6 +425,12 @@ __device__ __noinline__ void attn_chunk_body(const AttnArgs& a, int pos, int chu
     const int t0 = chunk * len;
     if (t0 > pos + NC - 1 || chunk >= a.max_chunks) return;  // beyond every column (uniform over the block)
     const int tend = min(t0 + len, pos + NC);                  // tokens [t0, tend) some column may read
+    if (threadIdx.x == 0) {  // the chunk's K and V rows (contiguous per kv head) head for L2 now
+        const uint32_t bytes = (uint32_t) (tend - t0) * kHdA * 2;
+        const size_t row0 = ((size_t) kvh * a.max_ctx + t0) * kHdA;
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a.kc + row0), "r"(bytes) : "memory");
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a.vc + row0), "r"(bytes) : "memory");
+    }
     float* qs = sm;                                            // [G][NC][256]
     float (*sc)[NC][kSubA] = reinterpret_cast<float (*)[NC][kSubA]>(sm + G * NC * kHdA);  // [G][NC][kSubA]
     float* rot = sm + G * NC * kHdA + G * NC * kSubA;          // [8 warps][256]
@@ -533,6 +539,12 @@ __device__ __noinline__ void attn_chunk_body(const AttnArgs& a, int pos, int chu
                 }
         }
         block_sync256();
+        // V rows of the pass (thread = output dim), 32 tokens per batch; the first batch goes out now so its
+        // round trip overlaps phase 2
+        __half vh[32];
+#pragma unroll
+        for (int u = 0; u < 32; ++u)
+            vh[u] = u < ntok ? __ldcg(vbase + (size_t) (s0 + u) * kHdA + tid) : __float2half_rn(0.0f);
         // phase 2: per (head, column) the pass's max, the exponentials against the new running max, the
         // running sum and the rescale factor of what was accumulated before; one warp per pair
         for (int pair = warp; pair < G * NC; pair += 8) {
@@ -557,23 +569,24 @@ __device__ __noinline__ void attn_chunk_body(const AttnArgs& a, int pos, int chu
             }
         }
         block_sync256();
-        // phase 3: weighted V, thread = output dim, V rows loaded 8 at a time, added in token order
+        // phase 3: weighted V, added in token order
 #pragma unroll
         for (int g = 0; g < G; ++g)
 #pragma unroll
             for (int c = 0; c < NC; ++c) acc[g][c] = __fmul_rn(acc[g][c], run[(g * NC + c) * 4 + 2]);
-        for (int tb = 0; tb < ntok; tb += 8) {
-            float vv[8];
+        for (int tb = 0; tb < ntok; tb += 32) {
+            if (tb > 0)
 #pragma unroll
-            for (int u = 0; u < 8; ++u)
-                vv[u] = tb + u < ntok ? __half2float(__ldcg(vbase + (size_t) (s0 + tb + u) * kHdA + tid)) : 0.0f;
+                for (int u = 0; u < 32; ++u)
+                    vh[u] = tb + u < ntok ? __ldcg(vbase + (size_t) (s0 + tb + u) * kHdA + tid) : __float2half_rn(0.0f);
 #pragma unroll
-            for (int u = 0; u < 8; ++u)
+            for (int u = 0; u < 32; ++u)
                 if (tb + u < ntok) {
+                    const float vf = __half2float(vh[u]);
 #pragma unroll
                     for (int g = 0; g < G; ++g)
 #pragma unroll
-                        for (int c = 0; c < NC; ++c) acc[g][c] = __fmaf_rn(sc[g][c][tb + u], vv[u], acc[g][c]);
+                        for (int c = 0; c < NC; ++c) acc[g][c] = __fmaf_rn(sc[g][c][tb + u], vf, acc[g][c]);
                 }
         }
         block_sync256();  // sc and run are rewritten by the next pass
@@ -591,29 +604,72 @@ __device__ __noinline__ void attn_chunk_body(const AttnArgs& a, int pos, int chu
         }
 }
 
-// Combine of head h, column c: the chunks merged in order, then the Q8_1 blocks of o * sigmoid(gate)
-// (sig_mul_quant_kernel, src/qwythos.cpp:692-704; one warp = one 32-dim block).
+// Combine of head h, column c, then the Q8_1 blocks of o * sigmoid(gate) (sig_mul_quant_kernel,
+// src/qwythos.cpp:692-704; one warp = one 32-dim block). Warp w merges chunks [w n / 8, (w + 1) n / 8)
+// over all 256 dims (lane: dims 8 lane .. 8 lane + 7, four chunks' rows in flight), then thread d merges the
+// eight warp partials in warp order: the same merge for any column count. sm: 8 x 256 + 16 floats.
 template <int NC>
-__device__ __noinline__ void combine_body(const AttnArgs& a, int pos, int h, int c) {
-    const int d = threadIdx.x;
+__device__ __noinline__ void combine_body(const AttnArgs& a, int pos, int h, int c, float* sm) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (pos < 0 || pos + NC > a.max_ctx) return;  // recorded by the chunk body
-    const int nchunks = (pos + c) / attn_chunk_len(pos, NC) + 1;
+    float* wnum = sm;           // [8][256]
+    float* wm = sm + 8 * kHdA;  // [8] warp maxima (-inf: the warp had no chunk)
+    float* wden = wm + 8;       // [8]
+    block_sync256();            // scratch reuse across items
+    const int n = (pos + c) / attn_chunk_len(pos, NC) + 1;
     const float* ml = a.part_ml + ((size_t) h * NC + c) * a.max_chunks * 2;
     const float* po = a.part_o + ((size_t) h * NC + c) * a.max_chunks * kHdA;
-    float M = -INFINITY;
-    for (int k = 0; k < nchunks; ++k) M = fmaxf(M, ld_cg(ml + 2 * k));
-    float num = 0.0f, den = 0.0f;
-    for (int k = 0; k < nchunks; ++k) {
-        const float w = expf(__fsub_rn(ld_cg(ml + 2 * k), M));
-        num = __fmaf_rn(w, ld_cg(po + (size_t) k * kHdA + d), num);
-        den = __fmaf_rn(w, ld_cg(ml + 2 * k + 1), den);
+    const int k0 = warp * n / 8, k1 = (warp + 1) * n / 8;
+    float m = -INFINITY;
+    for (int k = k0 + lane; k < k1; k += 32) m = fmaxf(m, ld_cg(ml + 2 * k));
+    m = warp_max(m);
+    float num[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f}, den = 0.0f;
+    for (int k = k0; k < k1; k += 4) {
+        float mk[4], lk[4];
+        float4 oa[4], ob[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+            if (k + u < k1) {
+                mk[u] = ld_cg(ml + 2 * (k + u));
+                lk[u] = ld_cg(ml + 2 * (k + u) + 1);
+                const float4* row = reinterpret_cast<const float4*>(po + (size_t) (k + u) * kHdA + 8 * lane);
+                oa[u] = __ldcg(row);
+                ob[u] = __ldcg(row + 1);
+            }
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+            if (k + u < k1) {
+                const float w = expf(__fsub_rn(mk[u], m));
+                const float o8[8] = {oa[u].x, oa[u].y, oa[u].z, oa[u].w, ob[u].x, ob[u].y, ob[u].z, ob[u].w};
+#pragma unroll
+                for (int i = 0; i < 8; ++i) num[i] = __fmaf_rn(w, o8[i], num[i]);
+                den = __fmaf_rn(w, lk[u], den);
+            }
     }
-    const float ov = __fdiv_rn(num, den);
-    const size_t oi = ((size_t) c * a.n_head + h) * kHdA + d;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) wnum[warp * kHdA + 8 * lane + i] = num[i];
+    if (lane == 0) {
+        wm[warp] = k1 > k0 ? m : -INFINITY;
+        wden[warp] = den;
+    }
+    block_sync256();
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) M = fmaxf(M, wm[w]);
+    float nu = 0.0f, de = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w)
+        if (wm[w] != -INFINITY) {
+            const float sw = expf(__fsub_rn(wm[w], M));
+            nu = __fmaf_rn(sw, wnum[w * kHdA + tid], nu);
+            de = __fmaf_rn(sw, wden[w], de);
+        }
+    const float ov = __fdiv_rn(nu, de);
+    const size_t oi = ((size_t) c * a.n_head + h) * kHdA + tid;
     if (a.o) a.o[oi] = ov;
-    const float gate = ld_cg(a.proj + (size_t) c * a.proj_stride + h * 2 * kHdA + kHdA + d);
-    q8_1_warp_store(sigmul_value(ov, gate), a.q8 + (((size_t) c * a.n_head + h) * (kHdA / 32) + (d >> 5)) * 36,
-                    d & 31);
+    const float gate = ld_cg(a.proj + (size_t) c * a.proj_stride + h * 2 * kHdA + kHdA + tid);
+    q8_1_warp_store(sigmul_value(ov, gate), a.q8 + (((size_t) c * a.n_head + h) * (kHdA / 32) + (tid >> 5)) * 36,
+                    lane);
 }
 
 // MTP draft input of column c: Q8_1 of [enorm(emb(dtok)) | hnorm(h)] (src/qwythos.cpp:1316-1334); the
@@ -713,7 +769,7 @@ __device__ __forceinline__ void run_item(const POp& op, Ctrl* ctrl, int item, in
         case POP_EMBED: embed_body(op.em, ctrl, op.draft, item); break;
         case POP_GDN: gdn_quarter_body<NC>(op.gd, item >> 2, item & 3, pos, rollback != 0, sm); break;
         case POP_ATTN: attn_chunk_body<NC>(op.at, pos, item / op.at.n_kv, item % op.at.n_kv, sm); break;
-        case POP_COMBINE: combine_body<NC>(op.at, pos, item / NC, item % NC); break;
+        case POP_COMBINE: combine_body<NC>(op.at, pos, item / NC, item % NC, sm); break;
         case POP_DRAFT_PREP: draft_prep_body(op.dp, ctrl, item, sm, red); break;
         case POP_CTRL:
             if (threadIdx.x == 0) ctrl_body(op.ct, ctrl);

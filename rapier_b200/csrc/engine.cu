@@ -51,6 +51,21 @@ __host__ __device__ __forceinline__ int synth_sum(uint64_t seed, uint64_t idx) {
 }
 float synth_scale(double std) { return (float) (std * std::sqrt(3.0) / 65536.0); }
 
+// A seeded synthetic context (rk_engine_session_fill): rows [0, n_pos) of every kv head of a cache
+// [n_kv][max_ctx][256] as fp16 of synthetic N(0, 1) values; a float buffer of synthetic N(0, std) values.
+__global__ void fill_kv_kernel(__half* cache, int n_kv, int max_ctx, int n_pos, uint64_t seed, float scale) {
+    const long long per_head = (long long) n_pos * 256;
+    const long long n = per_head * n_kv;
+    for (long long i = (long long) blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long) gridDim.x * blockDim.x) {
+        const long long h = i / per_head, r = i - h * per_head;
+        cache[(size_t) h * max_ctx * 256 + (size_t) r] = __float2half_rn((float) synth_sum(seed, (uint64_t) i) * scale);
+    }
+}
+__global__ void fill_float_kernel(float* dst, long long n, uint64_t seed, float scale) {
+    for (long long i = (long long) blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long) gridDim.x * blockDim.x)
+        dst[i] = (float) synth_sum(seed, (uint64_t) i) * scale;
+}
+
 // Q6_K encoder (this library's definition, restated by the CPU oracle): per 16-value sub-block amax_j,
 // d = half((max_j amax_j / 31) / 127), scale_j = clamp(roundf((amax_j / 31) / d), 0, 127),
 // code = clamp(roundf(x / (d * scale_j)), -32, 31) + 32. One thread per 256-value block of a slice of the
@@ -903,8 +918,11 @@ cudaError_t EngineImpl::launch_op(const POp& op) {
         if (op.epi == EPI_RES) return mmvq_launch<RK_TYPE_Q6_K, NC, PRO_Q8, EPI_RES>(p, s, true);
         return mmvq_launch<RK_TYPE_Q6_K, NC, PRO_Q8, EPI_STORE_P>(p, s, true);
     }
-    // grid: the op's largest item count over all positions (attention: kMaxChunksA chunks per kv head)
-    const int grid = op.kind == POP_ATTN ? kMaxChunksA * op.at.n_kv : pop_items<NC>(op, 0);
+    // grid: the op's item count, which does not depend on the position, or for the attention chunks (their
+    // count grows with the position) four CTAs per SM taking items in turn
+    static int sms = 0;
+    if (sms == 0 && cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) sms = 148;
+    const int grid = op.kind == POP_ATTN ? std::min(kMaxChunksA * op.at.n_kv, 4 * sms) : pop_items<NC>(op, 0);
     const size_t smem = op_scratch_bytes(NC, H);
     static bool attr_set[3] = {false, false, false};
     if (smem > 48 * 1024 && !attr_set[col_slot(NC)]) {
@@ -1444,6 +1462,38 @@ int rk_engine_generate(rk_engine* e, const int* prompt, int n_prompt, int n_gen,
 }
 
 int rk_engine_session_reset(rk_engine* e) { return rk_engine_reset(e); }
+
+// Config 5 at a long context without a long prompt: the caches of a context of n_pos tokens filled with
+// seeded synthetic values (fp16 K and V ~ N(0, 1) in every attention layer and the draft layer, the
+// configuration's KV distribution; GDN states ~ N(0, 0.01), conv rings 0), and the session placed after
+// them, so the next run decodes at positions n_pos, n_pos + 1, ...
+int rk_engine_session_fill(rk_engine* e, int n_pos, unsigned long long seed) {
+    const char* what = "rk_engine_session_fill";
+    if (!e) return set_error(RK_EINVAL, "%s: null engine", what);
+    EngineImpl& E = e->impl;
+    if (n_pos < 1 || n_pos + 8 > E.cfg.max_ctx) return set_error(RK_ERANGE, "%s: n_pos must leave room in max_ctx", what);
+    if (int rc = rk_engine_reset(e)) return rc;
+    const float sk = synth_scale(1.0), ss = synth_scale(0.01);
+    int li = 0;
+    auto fill = [&](Layer& L) {
+        const uint64_t sd = hash64(seed, (uint64_t) (1000 + li++));
+        if (L.kc) {
+            fill_kv_kernel<<<4 * 148, 256, 0, E.s>>>(L.kc, E.nkv, E.cfg.max_ctx, n_pos, hash64(sd, 1), sk);
+            fill_kv_kernel<<<4 * 148, 256, 0, E.s>>>(L.vc, E.nkv, E.cfg.max_ctx, n_pos, hash64(sd, 2), sk);
+        }
+        if (L.gdn && L.state)
+            fill_float_kernel<<<4 * 148, 256, 0, E.s>>>(L.state, (long long) kSsm * E.hv * kSsm, hash64(sd, 3), ss);
+    };
+    for (Layer& L : E.layers) fill(L);
+    if (E.cfg.has_mtp) fill(E.draft);
+    const cudaError_t ce = cudaStreamSynchronize(E.s);
+    if (ce != cudaSuccess) return set_error(RK_ECUDA, "%s: %s", what, cudaGetErrorString(ce));
+    E.s_pos = n_pos;
+    E.s_pending = -1;
+    E.s_rollback = 0;
+    E.s_primed = true;
+    return RK_OK;
+}
 
 int rk_engine_session_pos(const rk_engine* e) { return e ? e->impl.s_pos + (e->impl.s_pending >= 0 ? 1 : 0) : -1; }
 

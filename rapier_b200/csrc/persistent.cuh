@@ -594,8 +594,9 @@ __global__ void __launch_bounds__(256) op_kernel(const POp op, Ctrl* ctrl) {
     pdl_wait();
     const int pos = ld_cg(op.draft ? &ctrl->dpos : &ctrl->pos);
     const int rb = ld_cg(&ctrl->rollback);
-    if ((int) blockIdx.x >= pop_items<NC>(op, pos)) return;
-    run_item<NC>(op, ctrl, (int) blockIdx.x, pos, rb, reinterpret_cast<float*>(smem), red);
+    const int items = pop_items<NC>(op, pos);
+    for (int it = (int) blockIdx.x; it < items; it += (int) gridDim.x)  // uniform over the block
+        run_item<NC>(op, ctrl, it, pos, rb, reinterpret_cast<float*>(smem), red);
 }
 
 }  // namespace rk

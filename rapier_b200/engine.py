@@ -133,6 +133,10 @@ class Engine:
         stats = {f: getattr(st, f) for f, _ in GenStats._fields_}
         return np.frombuffer(out, dtype=np.int32)[:n_out.value].copy(), stats, lg
 
+    def session_fill(self, n_pos: int, seed: int = 1):
+        """A synthetic context of n_pos tokens (rk_engine_session_fill): seeded caches, session after them."""
+        _lib.call("rk_engine_session_fill", self._h, n_pos, seed)
+
     @property
     def session_pos(self) -> int:
         return _lib.lib().rk_engine_session_pos(self._h)
