@@ -356,55 +356,88 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, int row) {
 }
 __host__ __device__ __forceinline__ int argmax_key_row(unsigned long long k) { return (int) (0xffffffffu - (uint32_t) (k & 0xffffffffu)); }
 
-// best[c] (EPI_ARGMAX): the warp's running packed (value, ~row) maximum of column c; the caller issues one
-// atomicMax per warp and column after its last unit (the reference's atomicMax on (monotonic bits, n-1-idx),
-// src/qwythos.cpp:70-84, with the lowest-index tie rule). resv (EPI_RES): lane c < NC holds the residual
-// rows of column c for this unit, loaded by mmvq_res_prefetch when the unit started.
+// The epilogue's warp reduction of a unit's 4 * NC row sums as a reduce-scatter: at xor offsets 16, 8, ...
+// each lane keeps half of its values and adds the partner's copy of that half, until one value is left
+// (then plain butterfly steps). Every step adds the same two partial sums that warp_sum adds for that
+// value (fp32 addition is commutative), so the result is bitwise warp_sum's, with 4 * NC - 1 + (5 -
+// log2(4 * NC)) shuffles instead of 20 * NC. Lane l ends with the sum of value j = c * 4 + r =
+// l >> kRsShift<NC>; 3 columns are reduced as 4 (the fourth column's values are zeros, never stored).
+template <int NC>
+constexpr int kRsShift = NC == 1 ? 3 : NC == 2 ? 2 : 1;
+template <int M>
+__device__ __forceinline__ void rs_step(float* v, int lane, int o) {
+    const bool hi = (lane & o) != 0;
+#pragma unroll
+    for (int i = 0; i < M / 2; ++i) {
+        const float send = hi ? v[i] : v[i + M / 2];
+        const float keep = hi ? v[i + M / 2] : v[i];
+        v[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, o));
+    }
+}
+template <int NC>
+__device__ __forceinline__ float warp_sum_scatter(const float (&acc)[NC][4], int lane) {
+    static_assert(NC >= 1 && NC <= 4, "up to 4 columns");
+    constexpr int M = NC == 3 ? 16 : 4 * NC;
+    float v[M];
+#pragma unroll
+    for (int j = 0; j < M; ++j) v[j] = j < 4 * NC ? acc[j >> 2][j & 3] : 0.0f;
+    rs_step<M>(v, lane, 16);
+    rs_step<M / 2>(v, lane, 8);
+    if constexpr (M >= 8) rs_step<M / 4>(v, lane, 4);
+    if constexpr (M >= 16) rs_step<M / 8>(v, lane, 2);
+#pragma unroll
+    for (int o = 16 >> (5 - kRsShift<NC>); o > 0; o >>= 1) v[0] = __fadd_rn(v[0], __shfl_xor_sync(0xffffffffu, v[0], o));
+    return v[0];
+}
+
+// best[c] (EPI_ARGMAX): the warp's running packed (value, ~row) maximum of column c, held by the lanes
+// whose reduced value is one of column c's rows; lane (4 * c) << kRsShift<NC> issues one atomicMax per
+// column after the warp's last unit (mmvq_argmax_flush; the reference's atomicMax on (monotonic bits,
+// n-1-idx), src/qwythos.cpp:70-84, with the lowest-index tie rule). resv (EPI_RES): lane c < NC holds the
+// residual rows of column c for this unit, loaded by mmvq_res_prefetch when the unit started.
 template <int NC, int EPI>
-__device__ __forceinline__ void mmvq_epilogue(const MmvqParams& p, int unit, int lane, float (&acc)[NC][4],
+__device__ __forceinline__ void mmvq_epilogue(const MmvqParams& p, int unit, int lane, const float (&acc)[NC][4],
                                               unsigned long long (&best)[NC], const float (&resv)[4]) {
-#pragma unroll
-    for (int c = 0; c < NC; ++c)
-#pragma unroll
-        for (int r = 0; r < 4; ++r) acc[c][r] = warp_sum(acc[c][r]);
+    constexpr int SH = kRsShift<NC>;
+    const float out = warp_sum_scatter<NC>(acc, lane);
+    const int j = lane >> SH;  // this lane's value: column j >> 2, row j & 3 of the unit
     const int row0 = unit * 4;
     if constexpr (EPI == EPI_STORE || EPI == EPI_ARGMAX || EPI == EPI_SWIGLU) {
-        if (p.y != nullptr) {
-            float out = 0.0f;
-#pragma unroll
-            for (int c = 0; c < NC; ++c)
-#pragma unroll
-                for (int r = 0; r < 4; ++r)
-                    if (lane == c * 4 + r) out = acc[c][r];
-            if (lane < NC * 4) p.y[(size_t) (lane >> 2) * p.y_stride + row0 + (lane & 3)] = out;
-        }
+        if (p.y != nullptr && (lane & ((1 << SH) - 1)) == 0 && (j >> 2) < NC)
+            p.y[(size_t) (j >> 2) * p.y_stride + row0 + (j & 3)] = out;
         if constexpr (EPI == EPI_ARGMAX) {
+            unsigned long long k = out == out ? argmax_key(out, p.row_off + row0 + (j & 3)) : 0ull;  // NaN never wins
+            unsigned long long o = __shfl_xor_sync(0xffffffffu, k, 1 << SH);
+            k = o > k ? o : k;
+            o = __shfl_xor_sync(0xffffffffu, k, 2 << SH);
+            k = o > k ? o : k;
 #pragma unroll
             for (int c = 0; c < NC; ++c)
-#pragma unroll
-                for (int r = 0; r < 4; ++r)
-                    if (acc[c][r] == acc[c][r]) {  // NaN never wins
-                        const unsigned long long k = argmax_key(acc[c][r], p.row_off + row0 + r);
-                        best[c] = k > best[c] ? k : best[c];
-                    }
+                if ((j >> 2) == c && k > best[c]) best[c] = k;
         }
     } else {  // EPI_RES (y = acc + res) / EPI_STORE_P (y = acc), both with the 4-row partials
+        const int cl = lane < NC ? lane : NC - 1;
+        float rv[4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) rv[r] = __shfl_sync(0xffffffffu, out, (cl * 4 + r) << SH);
         if (lane < NC) {
+            float* y = p.y + (size_t) lane * p.y_stride + row0;
+            float part = 0.0f;
 #pragma unroll
-            for (int c = 0; c < NC; ++c)
-                if (lane == c) {
-                    float* y = p.y + (size_t) c * p.y_stride + row0;
-                    float part = 0.0f;
-#pragma unroll
-                    for (int r = 0; r < 4; ++r) {
-                        const float v = EPI == EPI_RES ? __fadd_rn(acc[c][r], resv[r]) : acc[c][r];
-                        y[r] = v;
-                        part = __fmaf_rn(v, v, part);
-                    }
-                    p.pout[(size_t) c * p.pout_stride + unit] = part;
-                }
+            for (int r = 0; r < 4; ++r) {
+                const float v = EPI == EPI_RES ? __fadd_rn(rv[r], resv[r]) : rv[r];
+                y[r] = v;
+                part = __fmaf_rn(v, v, part);
+            }
+            p.pout[(size_t) lane * p.pout_stride + unit] = part;
         }
     }
+}
+template <int NC>
+__device__ __forceinline__ void mmvq_argmax_flush(const MmvqParams& p, int lane, const unsigned long long (&best)[NC]) {
+#pragma unroll
+    for (int c = 0; c < NC; ++c)
+        if (lane == ((4 * c) << kRsShift<NC>) && best[c] != 0ull) atomicMax(p.amax + c, best[c]);
 }
 
 // EPI_RES: the residual rows of a unit, issued when the unit starts so the load overlaps its tiles.
@@ -480,12 +513,20 @@ __global__ void __launch_bounds__(kMmvqWarps * 32, 2) mmvq_packed_kernel(const M
     }
     __syncwarp();
     const uint64_t pol = policy_evict_first();
-    auto issue = [&](int i) {
-        const int u = ubeg + warp + (i / KC) * kMmvqWarps;
-        const uint8_t* src = p.w + ((size_t) u * KC + (size_t) (i % KC)) * TILE;
-        const int s = i % stages;
-        mbar_arrive_expect_tx(smem_u32(bars + s), TILE);
-        bulk_g2s(smem_u32(ring + (size_t) s * TILE), src, TILE, smem_u32(bars + s), pol);
+    // Producer cursor (lane 0): the next tile to fetch walks the warp's units' tiles in order (a unit's KC
+    // tiles are contiguous; the warp's next unit is kMmvqWarps units further), and tile i + stages goes
+    // into the slot tile i just left, so the refill needs no division.
+    const uint8_t* nsrc = p.w + (size_t) (ubeg + warp) * KC * TILE;
+    int nkc = 0;
+    const size_t unit_skip = (size_t) (kMmvqWarps - 1) * KC * TILE;
+    auto issue = [&](int slot) {
+        mbar_arrive_expect_tx(smem_u32(bars + slot), TILE);
+        bulk_g2s(smem_u32(ring + (size_t) slot * TILE), nsrc, TILE, smem_u32(bars + slot), pol);
+        nsrc += TILE;
+        if (++nkc == KC) {
+            nkc = 0;
+            nsrc += unit_skip;
+        }
     };
     const int npre = ntiles < stages ? ntiles : stages;
     pdl_trigger();
@@ -530,7 +571,7 @@ __global__ void __launch_bounds__(kMmvqWarps * 32, 2) mmvq_packed_kernel(const M
         __syncwarp();
         if (lane == 0 && i + stages < ntiles) {
             fence_proxy_async_smem();
-            issue(i + stages);
+            issue(s);
         }
         if (++s == stages) {
             s = 0;
@@ -548,11 +589,7 @@ __global__ void __launch_bounds__(kMmvqWarps * 32, 2) mmvq_packed_kernel(const M
         }
     }
     if constexpr (EPI == EPI_SWIGLU) mmvq_swiglu_finish<NC>(p, ubeg + warp, kMmvqWarps, unit, lane);
-    if constexpr (EPI == EPI_ARGMAX) {
-#pragma unroll
-        for (int c = 0; c < NC; ++c)
-            if (lane == c && best[c] != 0ull) atomicMax(p.amax + c, best[c]);
-    }
+    if constexpr (EPI == EPI_ARGMAX) mmvq_argmax_flush<NC>(p, lane, best);
 }
 
 // Host-side launcher for one instantiation: sets the smem attribute once, picks the stage count that

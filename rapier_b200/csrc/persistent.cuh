@@ -420,11 +420,7 @@ __device__ __forceinline__ bool p_gemv(const MmvqParams& p, uint8_t* xsm, float*
         return ok;
     }
     if constexpr (EPI == EPI_SWIGLU) mmvq_swiglu_finish<NC>(p, ubeg + warp, kPWarps, unit, lane);
-    if constexpr (EPI == EPI_ARGMAX) {
-#pragma unroll
-        for (int c = 0; c < NC; ++c)
-            if (lane == c && best[c] != 0ull) atomicMax(p.amax + c, best[c]);
-    }
+    if constexpr (EPI == EPI_ARGMAX) mmvq_argmax_flush<NC>(p, lane, best);
     return ok;
 }
 
