@@ -46,6 +46,40 @@ __device__ __forceinline__ int warp_sum_i(int v) {
     return v;
 }
 
+// Warp sums of M values (a power of two) per lane as a reduce-scatter: at xor offsets 16, 8, ... each lane
+// keeps half of its values and adds the partner's copy of that half; once one value is left, plain
+// butterfly steps. Every step adds the same two partial sums that warp_sum adds for that value (fp32
+// addition is commutative), so each sum is bitwise warp_sum's, for M - 1 shuffles (M <= 32) instead of 5 M.
+// Afterwards v[0 .. R), R = max(M / 32, 1), hold sums: v[i] on lane l is the sum of value i + R * l when
+// M >= 32, and of value l >> (5 - log2 M) when M < 32 (the 32 / M lanes of a value agree).
+template <int M>
+__device__ __forceinline__ void rs_step(float* v, int lane, int o) {
+    const bool hi = (lane & o) != 0;
+#pragma unroll
+    for (int i = 0; i < M / 2; ++i) {
+        const float send = hi ? v[i] : v[i + M / 2];
+        const float keep = hi ? v[i + M / 2] : v[i];
+        v[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, o));
+    }
+}
+template <int M, int O>
+__device__ __forceinline__ void rs_level(float* v, int lane) {
+    if constexpr (O > 0) {
+        if constexpr (M > 1) {
+            rs_step<M>(v, lane, O);
+            rs_level<M / 2, O / 2>(v, lane);
+        } else {
+            v[0] = __fadd_rn(v[0], __shfl_xor_sync(0xffffffffu, v[0], O));
+            rs_level<1, O / 2>(v, lane);
+        }
+    }
+}
+template <int M>
+__device__ __forceinline__ void warp_reduce_scatter(float (&v)[M], int lane) {
+    static_assert(M >= 1 && (M & (M - 1)) == 0, "a power of two");
+    rs_level<M, 16>(v, lane);
+}
+
 // ---------------------------------------------------------------------------------------------
 // Q8_1 block rules (the reference's q8_1_finite / q8_1_quant / q8_1_ds are out of its tree; this is
 // the written definition the CPU oracle restates):

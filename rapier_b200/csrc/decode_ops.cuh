@@ -137,7 +137,7 @@ __host__ __device__ __forceinline__ int pop_items(const POp& op, int pos) {
             const int p = pos < 0 ? 0 : (pos > op.at.max_ctx - NC ? op.at.max_ctx - NC : pos);
             return ((p + NC - 1) / attn_chunk_len(p, NC) + 1) * op.at.n_kv;
         }
-        case POP_COMBINE: return op.at.n_head * NC;
+        case POP_COMBINE: return op.at.n_head * NC * (kHdA / 32);
         case POP_DRAFT_PREP: return NC;
         case POP_CTRL: return 1;
         default: return 0;
@@ -415,7 +415,7 @@ __device__ __noinline__ void gdn_quarter_body(const GdnArgs& a, int head, int qu
 // rescaling); K and V rows are loaded several at a time. Partials: o [n_head][NC][max_chunks][256],
 // (m, l) [n_head][NC][max_chunks].
 template <int NC>
-__device__ __noinline__ void attn_chunk_body(const AttnArgs& a, int pos, int chunk, int kvh, float* sm) {
+__device__ __forceinline__ void attn_chunk_impl(const AttnArgs& a, int pos, int chunk, int kvh, float* sm) {
     constexpr int G = kGqa;
     if (pos < 0 || pos + NC > a.max_ctx) {  // uniform over the block
         if (threadIdx.x == 0) atomicOr(&g_rk_status, kStatusBadIndex);
@@ -505,7 +505,8 @@ __device__ __noinline__ void attn_chunk_body(const AttnArgs& a, int pos, int chu
     for (int s0 = t0; s0 < tend; s0 += kSubA) {
         const int ntok = min(kSubA, tend - s0);
         // phase 1: scores, a warp per 4 consecutive tokens (their K rows loaded together), lanes over 8-dim
-        // slices, xor tree per (head, column)
+        // slices; the G * NC * 4 dot products are summed over the lanes by one reduce-scatter (the sums
+        // warp_sum gives), after which each value's lane stores it
         for (int tb = warp * 4; tb < ntok; tb += 32) {
             float kf[4][8];
 #pragma unroll
@@ -520,23 +521,32 @@ __device__ __noinline__ void attn_chunk_body(const AttnArgs& a, int pos, int chu
                     kf[u][2 * i + 1] = f.y;
                 }
             }
+            constexpr int M = G * NC * 4;  // value j = (g * NC + c) * 4 + u
+            float dv[M];
 #pragma unroll
-            for (int g = 0; g < G; ++g)
+            for (int gc = 0; gc < G * NC; ++gc) {
+                const float4* qp = reinterpret_cast<const float4*>(qs + gc * kHdA + lane * 8);
+                const float4 q0 = qp[0], q1 = qp[1];
+                const float qv[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
-                for (int c = 0; c < NC; ++c) {
-                    const float4* qp = reinterpret_cast<const float4*>(qs + (g * NC + c) * kHdA + lane * 8);
-                    const float4 q0 = qp[0], q1 = qp[1];
-                    const float qv[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+                for (int u = 0; u < 4; ++u) {
+                    float d = 0.0f;
 #pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        float d = 0.0f;
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) d = __fmaf_rn(qv[i], kf[u][i], d);
-                        d = warp_sum(d);
-                        const int t = tb + u;
-                        if (lane == 0 && t < ntok) sc[g][c][t] = (s0 + t <= pos + c) ? __fmul_rn(d, a.scale) : -INFINITY;
-                    }
+                    for (int i = 0; i < 8; ++i) d = __fmaf_rn(qv[i], kf[u][i], d);
+                    dv[gc * 4 + u] = d;
                 }
+            }
+            warp_reduce_scatter<M>(dv, lane);
+            constexpr int R = M >= 32 ? M / 32 : 1;
+            constexpr int SH = M >= 32 ? 0 : (M == 16 ? 1 : 2);
+            if ((lane & ((1 << SH) - 1)) == 0) {
+#pragma unroll
+                for (int i = 0; i < R; ++i) {
+                    const int j = M >= 32 ? R * lane + i : lane >> SH;
+                    const int gc = j >> 2, t = tb + (j & 3), c = gc % NC;
+                    if (t < ntok) (&sc[0][0][0])[gc * kSubA + t] = (s0 + t <= pos + c) ? __fmul_rn(dv[i], a.scale) : -INFINITY;
+                }
+            }
         }
         block_sync256();
         // V rows of the pass (thread = output dim), 32 tokens per batch; the first batch goes out now so its
@@ -604,55 +614,59 @@ __device__ __noinline__ void attn_chunk_body(const AttnArgs& a, int pos, int chu
         }
 }
 
-// Combine of head h, column c, then the Q8_1 blocks of o * sigmoid(gate) (sig_mul_quant_kernel,
-// src/qwythos.cpp:692-704; one warp = one 32-dim block). Warp w merges chunks [w n / 8, (w + 1) n / 8)
-// over all 256 dims (lane: dims 8 lane .. 8 lane + 7, four chunks' rows in flight), then thread d merges the
-// eight warp partials in warp order: the same merge for any column count. sm: 8 x 256 + 16 floats.
+// The chunk body as a call (the op kernel and the persistent kernel); attn_kernel inlines the impl.
 template <int NC>
-__device__ __noinline__ void combine_body(const AttnArgs& a, int pos, int h, int c, float* sm) {
+__device__ __noinline__ void attn_chunk_body(const AttnArgs& a, int pos, int chunk, int kvh, float* sm) {
+    attn_chunk_impl<NC>(a, pos, chunk, kvh, sm);
+}
+
+// Combine of head h, column c, dims [32 slice, 32 slice + 32), then that dims' Q8_1 block of
+// o * sigmoid(gate) (sig_mul_quant_kernel, src/qwythos.cpp:692-704; one warp = one 32-dim block). Warp w
+// merges chunks [w n / 8, (w + 1) n / 8) (lane = one dim, eight chunks' rows in flight), then warp 0 merges
+// the eight warp partials in warp order: the same merge for any column count and any slicing, so a dim's
+// result does not depend on which item computed it. sm: 8 x 32 + 16 floats.
+template <int NC>
+__device__ __noinline__ void combine_body(const AttnArgs& a, int pos, int h, int c, int slice, float* sm) {
+    constexpr int kU = 8;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (pos < 0 || pos + NC > a.max_ctx) return;  // recorded by the chunk body
-    float* wnum = sm;           // [8][256]
-    float* wm = sm + 8 * kHdA;  // [8] warp maxima (-inf: the warp had no chunk)
-    float* wden = wm + 8;       // [8]
-    block_sync256();            // scratch reuse across items
+    float* wnum = sm;         // [8][32]
+    float* wm = sm + 8 * 32;  // [8] warp maxima (-inf: the warp had no chunk)
+    float* wden = wm + 8;     // [8]
+    block_sync256();          // scratch reuse across items
     const int n = (pos + c) / attn_chunk_len(pos, NC) + 1;
+    const int d = slice * 32 + lane;
     const float* ml = a.part_ml + ((size_t) h * NC + c) * a.max_chunks * 2;
-    const float* po = a.part_o + ((size_t) h * NC + c) * a.max_chunks * kHdA;
+    const float* po = a.part_o + ((size_t) h * NC + c) * a.max_chunks * kHdA + d;
     const int k0 = warp * n / 8, k1 = (warp + 1) * n / 8;
     float m = -INFINITY;
     for (int k = k0 + lane; k < k1; k += 32) m = fmaxf(m, ld_cg(ml + 2 * k));
     m = warp_max(m);
-    float num[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f}, den = 0.0f;
-    for (int k = k0; k < k1; k += 4) {
-        float mk[4], lk[4];
-        float4 oa[4], ob[4];
+    float num = 0.0f, den = 0.0f;
+    for (int k = k0; k < k1; k += kU) {
+        float mk[kU], lk[kU], ok[kU];
 #pragma unroll
-        for (int u = 0; u < 4; ++u)
+        for (int u = 0; u < kU; ++u)
             if (k + u < k1) {
                 mk[u] = ld_cg(ml + 2 * (k + u));
                 lk[u] = ld_cg(ml + 2 * (k + u) + 1);
-                const float4* row = reinterpret_cast<const float4*>(po + (size_t) (k + u) * kHdA + 8 * lane);
-                oa[u] = __ldcg(row);
-                ob[u] = __ldcg(row + 1);
+                ok[u] = ld_cg(po + (size_t) (k + u) * kHdA);
             }
 #pragma unroll
-        for (int u = 0; u < 4; ++u)
+        for (int u = 0; u < kU; ++u)
             if (k + u < k1) {
                 const float w = expf(__fsub_rn(mk[u], m));
-                const float o8[8] = {oa[u].x, oa[u].y, oa[u].z, oa[u].w, ob[u].x, ob[u].y, ob[u].z, ob[u].w};
-#pragma unroll
-                for (int i = 0; i < 8; ++i) num[i] = __fmaf_rn(w, o8[i], num[i]);
+                num = __fmaf_rn(w, ok[u], num);
                 den = __fmaf_rn(w, lk[u], den);
             }
     }
-#pragma unroll
-    for (int i = 0; i < 8; ++i) wnum[warp * kHdA + 8 * lane + i] = num[i];
+    wnum[warp * 32 + lane] = num;
     if (lane == 0) {
         wm[warp] = k1 > k0 ? m : -INFINITY;
         wden[warp] = den;
     }
     block_sync256();
+    if (warp != 0) return;
     float M = -INFINITY;
 #pragma unroll
     for (int w = 0; w < 8; ++w) M = fmaxf(M, wm[w]);
@@ -661,15 +675,14 @@ __device__ __noinline__ void combine_body(const AttnArgs& a, int pos, int h, int
     for (int w = 0; w < 8; ++w)
         if (wm[w] != -INFINITY) {
             const float sw = expf(__fsub_rn(wm[w], M));
-            nu = __fmaf_rn(sw, wnum[w * kHdA + tid], nu);
+            nu = __fmaf_rn(sw, wnum[w * 32 + lane], nu);
             de = __fmaf_rn(sw, wden[w], de);
         }
     const float ov = __fdiv_rn(nu, de);
-    const size_t oi = ((size_t) c * a.n_head + h) * kHdA + tid;
+    const size_t oi = ((size_t) c * a.n_head + h) * kHdA + d;
     if (a.o) a.o[oi] = ov;
-    const float gate = ld_cg(a.proj + (size_t) c * a.proj_stride + h * 2 * kHdA + kHdA + tid);
-    q8_1_warp_store(sigmul_value(ov, gate), a.q8 + (((size_t) c * a.n_head + h) * (kHdA / 32) + (tid >> 5)) * 36,
-                    lane);
+    const float gate = ld_cg(a.proj + (size_t) c * a.proj_stride + h * 2 * kHdA + kHdA + d);
+    q8_1_warp_store(sigmul_value(ov, gate), a.q8 + (((size_t) c * a.n_head + h) * (kHdA / 32) + slice) * 36, lane);
 }
 
 // MTP draft input of column c: Q8_1 of [enorm(emb(dtok)) | hnorm(h)] (src/qwythos.cpp:1316-1334); the
@@ -769,7 +782,7 @@ __device__ __forceinline__ void run_item(const POp& op, Ctrl* ctrl, int item, in
         case POP_EMBED: embed_body(op.em, ctrl, op.draft, item); break;
         case POP_GDN: gdn_quarter_body<NC>(op.gd, item >> 2, item & 3, pos, rollback != 0, sm); break;
         case POP_ATTN: attn_chunk_body<NC>(op.at, pos, item / op.at.n_kv, item % op.at.n_kv, sm); break;
-        case POP_COMBINE: combine_body<NC>(op.at, pos, item / NC, item % NC, sm); break;
+        case POP_COMBINE: combine_body<NC>(op.at, pos, item / (NC * 8), (item / 8) % NC, item % 8, sm); break;
         case POP_DRAFT_PREP: draft_prep_body(op.dp, ctrl, item, sm, red); break;
         case POP_CTRL:
             if (threadIdx.x == 0) ctrl_body(op.ct, ctrl);

@@ -918,11 +918,23 @@ cudaError_t EngineImpl::launch_op(const POp& op) {
         if (op.epi == EPI_RES) return mmvq_launch<RK_TYPE_Q6_K, NC, PRO_Q8, EPI_RES>(p, s, true);
         return mmvq_launch<RK_TYPE_Q6_K, NC, PRO_Q8, EPI_STORE_P>(p, s, true);
     }
-    // grid: the op's item count, which does not depend on the position, or for the attention chunks (their
-    // count grows with the position) four CTAs per SM taking items in turn
     static int sms = 0;
     if (sms == 0 && cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) sms = 148;
-    const int grid = op.kind == POP_ATTN ? std::min(kMaxChunksA * op.at.n_kv, 4 * sms) : pop_items<NC>(op, 0);
+    if (op.kind == POP_ATTN) {
+        // the chunk items (their count grows with the position): every resident CTA slot takes items in turn
+        const size_t smem = ((size_t) attn_scratch_floats(NC) * 4 + 127) & ~(size_t) 127;
+        static int per_sm[3] = {0, 0, 0};
+        int& occ = per_sm[col_slot(NC)];
+        if (occ == 0) {
+            const cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, attn_kernel<NC>, 256, smem);
+            if (e != cudaSuccess) return e;
+            if (occ < 1) occ = 1;
+        }
+        const int grid = std::min(kMaxChunksA * op.at.n_kv, occ * sms);
+        return launch_pdl(attn_kernel<NC>, dim3((unsigned) grid), dim3(256), smem, s, true, op, ctrl);
+    }
+    // grid: the op's item count, which does not depend on the position
+    const int grid = pop_items<NC>(op, 0);
     const size_t smem = op_scratch_bytes(NC, H);
     static bool attr_set[3] = {false, false, false};
     if (smem > 48 * 1024 && !attr_set[col_slot(NC)]) {

@@ -364,16 +364,6 @@ __host__ __device__ __forceinline__ int argmax_key_row(unsigned long long k) { r
 // l >> kRsShift<NC>; 3 columns are reduced as 4 (the fourth column's values are zeros, never stored).
 template <int NC>
 constexpr int kRsShift = NC == 1 ? 3 : NC == 2 ? 2 : 1;
-template <int M>
-__device__ __forceinline__ void rs_step(float* v, int lane, int o) {
-    const bool hi = (lane & o) != 0;
-#pragma unroll
-    for (int i = 0; i < M / 2; ++i) {
-        const float send = hi ? v[i] : v[i + M / 2];
-        const float keep = hi ? v[i + M / 2] : v[i];
-        v[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, o));
-    }
-}
 template <int NC>
 __device__ __forceinline__ float warp_sum_scatter(const float (&acc)[NC][4], int lane) {
     static_assert(NC >= 1 && NC <= 4, "up to 4 columns");
@@ -381,12 +371,7 @@ __device__ __forceinline__ float warp_sum_scatter(const float (&acc)[NC][4], int
     float v[M];
 #pragma unroll
     for (int j = 0; j < M; ++j) v[j] = j < 4 * NC ? acc[j >> 2][j & 3] : 0.0f;
-    rs_step<M>(v, lane, 16);
-    rs_step<M / 2>(v, lane, 8);
-    if constexpr (M >= 8) rs_step<M / 4>(v, lane, 4);
-    if constexpr (M >= 16) rs_step<M / 8>(v, lane, 2);
-#pragma unroll
-    for (int o = 16 >> (5 - kRsShift<NC>); o > 0; o >>= 1) v[0] = __fadd_rn(v[0], __shfl_xor_sync(0xffffffffu, v[0], o));
+    warp_reduce_scatter<M>(v, lane);
     return v[0];
 }
 

@@ -581,6 +581,22 @@ __global__ void __launch_bounds__(kPWarps * 32, 1)
     }
 }
 
+// The flash-decode chunk items of an attention op as their own launch (graph mode). op_kernel's register
+// allocation covers every op body and leaves one CTA per SM; the chunk body alone keeps kAttnCtas CTAs per
+// SM resident, which the long-context chunk loop (memory latency bound) needs.
+template <int NC>
+constexpr int kAttnCtas = NC == 1 ? 3 : 2;
+template <int NC>
+__global__ void __launch_bounds__(256, kAttnCtas<NC>) attn_kernel(const POp op, Ctrl* ctrl) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    pdl_trigger();
+    pdl_wait();
+    const int pos = ld_cg(op.draft ? &ctrl->dpos : &ctrl->pos);
+    const int items = pop_items<NC>(op, pos);
+    for (int it = (int) blockIdx.x; it < items; it += (int) gridDim.x)  // uniform over the block
+        attn_chunk_impl<NC>(op.at, pos, it / op.at.n_kv, it % op.at.n_kv, reinterpret_cast<float*>(smem));
+}
+
 // One non-GEMV op as its own launch (graph mode).
 template <int NC>
 __global__ void __launch_bounds__(256) op_kernel(const POp op, Ctrl* ctrl) {
