@@ -357,20 +357,23 @@ def run_decode(args, rank, world, local, pg):
 
 def run_pass(args):
     """Four single-token passes of a 9B-shaped model cut to --layers layers (the full lm_head): the small
-    case for an ncu capture of the persistent kernel (the kernel is the one the 32-layer engine runs). Not a
-    bench line: prints the four pass times."""
+    case for an ncu capture of the step kernels (the kernels the 32-layer engine runs); with --ctx-fill N
+    the passes run after a synthetic context of N tokens. Not a bench line: prints the four pass times."""
     import torch
 
     from rapier_b200.engine import Engine, config_9b
 
     torch.cuda.set_device(0)
-    cfg = config_9b(max_ctx=args.ctx, seed=1)
+    fill = args.ctx_fill
+    cfg = config_9b(max_ctx=max(args.ctx, fill + 64) if fill else args.ctx, seed=1)
     cfg.n_layer = args.layers
     eng = Engine(cfg)
+    if fill:
+        eng.session_fill(fill, 7)
     times = []
-    for pos, t in enumerate([5, 17, 99, 1000]):
+    for i, t in enumerate([5, 17, 99, 1000]):
         t0 = time.perf_counter()
-        eng.step([t], pos, want_logits=False)
+        eng.step([t], fill + i, want_logits=False)
         times.append(round((time.perf_counter() - t0) * 1e3, 3))
     print(json.dumps({"workload": "pass", "layers": args.layers, "step_ms_wall": times}), flush=True)
     eng.close()

@@ -16,7 +16,7 @@ namespace rk {
 
 constexpr int kHdA = 256;     // attention head dim
 constexpr int kSubA = 256;    // tokens scored per pass inside a flash-decode chunk (shared-memory scores)
-constexpr int kMaxChunksA = 512;  // flash-decode chunks per kv head at most (bounds the partials)
+constexpr int kMaxChunksA = 512;  // flash-decode chunks per kv head below which chunks stay short (see attn_chunk_len)
 constexpr int kGqa = 4;       // query heads per kv head
 constexpr int kSsm = 128;     // GDN head size
 constexpr float kInvSqrtSsm = 0.08838834764831845f;  // 1/sqrt(128)
@@ -117,12 +117,13 @@ struct alignas(16) POp {  // 16-byte multiple: fetched into shared memory by 16-
 };
 static_assert(sizeof(POp) % 16 == 0 && sizeof(POp) / 16 <= 256, "op records are copied in 16-byte chunks");
 
-// Tokens per flash-decode chunk for a step at positions pos .. pos+nc-1: the smallest of 32, 64, 128, ...
-// that keeps a kv head's chunks at most kMaxChunksA (many small chunks spread any context over many CTAs:
-// 17 chunks of 32 at 512 tokens, 257 of 256 at 65536; the partial buffer stays bounded).
-__host__ __device__ __forceinline__ int attn_chunk_len(int pos, int nc) {
+// Tokens per flash-decode chunk for a step at positions pos .. pos+nc-1: the smallest of 32, 64, 128, 256
+// (kSubA) that keeps a kv head's chunks at most max_chunks (many small chunks spread any context over many
+// CTAs: 17 chunks of 32 at 512 tokens, 257 of 256 at 65536; the engine sizes max_chunks as
+// max(kMaxChunksA, max_ctx / kSubA rounded up), so a chunk is never longer than one pass of kSubA).
+__host__ __device__ __forceinline__ int attn_chunk_len(int pos, int nc, int max_chunks) {
     int len = 32;
-    while ((pos + nc + len - 1) / len > kMaxChunksA) len <<= 1;
+    while ((pos + nc + len - 1) / len > max_chunks && len < kSubA) len <<= 1;
     return len;
 }
 
@@ -135,7 +136,7 @@ __host__ __device__ __forceinline__ int pop_items(const POp& op, int pos) {
         case POP_GDN: return op.gd.hv * 4;
         case POP_ATTN: {  // positions outside the cache are refused by the body; bound the count
             const int p = pos < 0 ? 0 : (pos > op.at.max_ctx - NC ? op.at.max_ctx - NC : pos);
-            return ((p + NC - 1) / attn_chunk_len(p, NC) + 1) * op.at.n_kv;
+            return ((p + NC - 1) / attn_chunk_len(p, NC, op.at.max_chunks) + 1) * op.at.n_kv;
         }
         case POP_COMBINE: return op.at.n_head * NC * (kHdA / 32);
         case POP_DRAFT_PREP: return NC;
@@ -147,7 +148,8 @@ __host__ __device__ __forceinline__ int pop_items(const POp& op, int pos) {
 // Shared-memory scratch (bytes) of the non-GEMV bodies.
 __host__ __device__ constexpr int gdn_scratch_floats(int nc) { return nc * (256 + 32 + 128 + 128 + 8) + 4; }
 __host__ __device__ constexpr int attn_scratch_floats(int nc) {
-    return kGqa * nc * kHdA + kGqa * nc * kSubA + 8 * kHdA + 4 * kGqa * nc;
+    // (max, sum) pairs, then q + scores + the RoPE rows, or the [8][4][256] warp sums of the merge
+    return 64 + (kGqa * nc * (kHdA + kSubA) + 8 * kHdA > 8 * 4 * kHdA ? kGqa * nc * (kHdA + kSubA) + 8 * kHdA : 8 * 4 * kHdA);
 }
 inline size_t op_scratch_bytes(int nc, int H) {
     size_t b = (size_t) gdn_scratch_floats(nc) * 4;
@@ -407,21 +409,23 @@ __device__ __noinline__ void gdn_quarter_body(const GdnArgs& a, int head, int qu
 }
 
 // Flash-decode chunk `chunk` of kv head kvh for NC query columns (gqa_head_kernel, src/qwythos.cpp:380-442,
-// split over chunks of attn_chunk_len tokens), with the attention prologue of the tokens it needs folded
-// in: split of q / gate (split_qg_kernel, :320-327), per-head RMSNorm, NEOX RoPE over n_rot dims from the
-// cos / sin table, and the fp16 K/V store (store_kv2_kernel, :340-345) of the new positions inside this
-// chunk (each position has exactly one owning chunk). Column c attends tokens <= pos + c. The chunk is
-// scored in passes of up to kSubA tokens with a running (max, sum) per head and column (the flash-decode
-// rescaling); K and V rows are loaded several at a time. Partials: o [n_head][NC][max_chunks][256],
+// split over chunks of attn_chunk_len <= kSubA tokens), with the attention prologue of the tokens it needs
+// folded in: split of q / gate (split_qg_kernel, :320-327), per-head RMSNorm, NEOX RoPE over n_rot dims from
+// the cos / sin table, and the fp16 K/V store (store_kv2_kernel, :340-345) of the new positions inside this
+// chunk (each position has exactly one owning chunk). Column c attends tokens <= pos + c. One pass: scores
+// of every (head, column, token) into shared memory, the chunk's max and exponential sum per (head,
+// column), then the weighted V rows, warp w summing tokens [32 w, 32 w + 32) with lane l on dims 8 l ..
+// 8 l + 7, and the eight warp sums added in warp order. The token-to-warp split does not depend on NC, so a
+// column's partial is the same for any column count. Partials: o [n_head][NC][max_chunks][256],
 // (m, l) [n_head][NC][max_chunks].
 template <int NC>
 __device__ __forceinline__ void attn_chunk_impl(const AttnArgs& a, int pos, int chunk, int kvh, float* sm) {
-    constexpr int G = kGqa;
+    constexpr int G = kGqa, GC = G * NC;
     if (pos < 0 || pos + NC > a.max_ctx) {  // uniform over the block
         if (threadIdx.x == 0) atomicOr(&g_rk_status, kStatusBadIndex);
         return;
     }
-    const int len = attn_chunk_len(pos, NC);
+    const int len = attn_chunk_len(pos, NC, a.max_chunks);
     const int t0 = chunk * len;
     if (t0 > pos + NC - 1 || chunk >= a.max_chunks) return;  // beyond every column (uniform over the block)
     const int tend = min(t0 + len, pos + NC);                  // tokens [t0, tend) some column may read
@@ -431,10 +435,11 @@ __device__ __forceinline__ void attn_chunk_impl(const AttnArgs& a, int pos, int 
         asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a.kc + row0), "r"(bytes) : "memory");
         asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a.vc + row0), "r"(bytes) : "memory");
     }
-    float* qs = sm;                                            // [G][NC][256]
-    float (*sc)[NC][kSubA] = reinterpret_cast<float (*)[NC][kSubA]>(sm + G * NC * kHdA);  // [G][NC][kSubA]
-    float* rot = sm + G * NC * kHdA + G * NC * kSubA;          // [8 warps][256]
-    float* run = rot + 8 * kHdA;                               // [G*NC][4]: running max, sum, rescale
+    float* mlc = sm;                    // [GC][2]: the chunk's max and exponential sum (64 floats reserved)
+    float* qs = sm + 64;                // [GC][256]
+    float* scb = qs + GC * kHdA;        // [GC][kSubA]: scores, then their exponentials
+    float* rot = scb + GC * kSubA;      // [8 warps][256]
+    float* wacc = sm + 64;              // [8 warps][4][256]: warp sums in the merge (aliases qs / scb / rot)
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     block_sync256();  // scratch reuse across items
     // ---- prologue: one warp per head vector (lane holds dims j*32 + lane), the block256 order ----
@@ -490,128 +495,137 @@ __device__ __forceinline__ void attn_chunk_impl(const AttnArgs& a, int pos, int 
             }
         }
     }
-    if (tid < G * NC) {
-        run[tid * 4 + 0] = -INFINITY;
-        run[tid * 4 + 1] = 0.0f;
-    }
     block_sync256();  // q in smem; this block's K/V stores visible to its threads
     const __half* kbase = a.kc + (size_t) kvh * a.max_ctx * kHdA;
     const __half* vbase = a.vc + (size_t) kvh * a.max_ctx * kHdA;
-    float acc[G][NC];
+    const int ntok = tend - t0;  // <= kSubA
+    // phase 1: scores, a warp per 4 consecutive tokens (their K rows loaded together), lanes over 8-dim
+    // slices; the G * NC * 4 dot products are summed over the lanes by one reduce-scatter (the sums
+    // warp_sum gives), after which each value's lane stores it
+    for (int tb = warp * 4; tb < ntok; tb += 32) {
+        float kf[4][8];
 #pragma unroll
-    for (int g = 0; g < G; ++g)
+        for (int u = 0; u < 4; ++u) {
+            uint4 kraw = make_uint4(0u, 0u, 0u, 0u);
+            if (tb + u < ntok) kraw = __ldcg(reinterpret_cast<const uint4*>(kbase + (size_t) (t0 + tb + u) * kHdA + lane * 8));
+            const __half2* kh2 = reinterpret_cast<const __half2*>(&kraw);
 #pragma unroll
-        for (int c = 0; c < NC; ++c) acc[g][c] = 0.0f;
-    for (int s0 = t0; s0 < tend; s0 += kSubA) {
-        const int ntok = min(kSubA, tend - s0);
-        // phase 1: scores, a warp per 4 consecutive tokens (their K rows loaded together), lanes over 8-dim
-        // slices; the G * NC * 4 dot products are summed over the lanes by one reduce-scatter (the sums
-        // warp_sum gives), after which each value's lane stores it
-        for (int tb = warp * 4; tb < ntok; tb += 32) {
-            float kf[4][8];
+            for (int i = 0; i < 4; ++i) {
+                const float2 f = __half22float2(kh2[i]);
+                kf[u][2 * i] = f.x;
+                kf[u][2 * i + 1] = f.y;
+            }
+        }
+        constexpr int M = GC * 4;  // value j = (g * NC + c) * 4 + u
+        float dv[M];
+#pragma unroll
+        for (int gc = 0; gc < GC; ++gc) {
+            const float4* qp = reinterpret_cast<const float4*>(qs + gc * kHdA + lane * 8);
+            const float4 q0 = qp[0], q1 = qp[1];
+            const float qv[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
-                uint4 kraw = make_uint4(0u, 0u, 0u, 0u);
-                if (tb + u < ntok) kraw = __ldcg(reinterpret_cast<const uint4*>(kbase + (size_t) (s0 + tb + u) * kHdA + lane * 8));
-                const __half2* kh2 = reinterpret_cast<const __half2*>(&kraw);
+                float d = 0.0f;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) d = __fmaf_rn(qv[i], kf[u][i], d);
+                dv[gc * 4 + u] = d;
+            }
+        }
+        warp_reduce_scatter<M>(dv, lane);
+        constexpr int R = M >= 32 ? M / 32 : 1;
+        constexpr int SH = M >= 32 ? 0 : (M == 16 ? 1 : 2);
+        if ((lane & ((1 << SH) - 1)) == 0) {
+#pragma unroll
+            for (int i = 0; i < R; ++i) {
+                const int j = M >= 32 ? R * lane + i : lane >> SH;
+                const int gc = j >> 2, t = tb + (j & 3), c = gc % NC;
+                if (t < ntok) scb[gc * kSubA + t] = (t0 + t <= pos + c) ? __fmul_rn(dv[i], a.scale) : -INFINITY;
+            }
+        }
+    }
+    block_sync256();
+    // this warp's first V rows go out now, so their round trip overlaps phase 2
+    constexpr int kVB = 4;  // V rows per batch (16 B per lane each)
+    const int tw0 = warp * 32, tw1 = min(tw0 + 32, ntok);
+    uint4 vr[kVB];
+    auto load_v = [&](int tb) {
+#pragma unroll
+        for (int u = 0; u < kVB; ++u)
+            vr[u] = tb + u < tw1 ? __ldcg(reinterpret_cast<const uint4*>(vbase + (size_t) (t0 + tb + u) * kHdA + lane * 8))
+                                 : make_uint4(0u, 0u, 0u, 0u);
+    };
+    load_v(tw0);
+    // phase 2: per (head, column) the chunk's max, the exponentials (masked: 0) and their sum; a warp per pair
+    for (int pair = warp; pair < GC; pair += 8) {
+        float* sp = scb + pair * kSubA;
+        float m = -INFINITY;
+        for (int t = lane; t < ntok; t += 32) m = fmaxf(m, sp[t]);
+        m = warp_max(m);
+        float l = 0.0f;
+        for (int t = lane; t < ntok; t += 32) {
+            const float e = m == -INFINITY ? 0.0f : expf(__fsub_rn(sp[t], m));
+            sp[t] = e;
+            l = __fadd_rn(l, e);
+        }
+        l = warp_sum(l);
+        if (lane == 0) {
+            mlc[pair * 2 + 0] = m;
+            mlc[pair * 2 + 1] = l;
+        }
+    }
+    block_sync256();
+    // phase 3: weighted V rows, this warp's tokens in order
+    float acc[GC][8];
+#pragma unroll
+    for (int gc = 0; gc < GC; ++gc)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[gc][i] = 0.0f;
+    for (int tb = tw0; tb < tw1; tb += kVB) {
+        if (tb > tw0) load_v(tb);
+#pragma unroll
+        for (int u = 0; u < kVB; ++u)
+            if (tb + u < tw1) {
+                const __half2* vh2 = reinterpret_cast<const __half2*>(&vr[u]);
+                float vf[8];
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
-                    const float2 f = __half22float2(kh2[i]);
-                    kf[u][2 * i] = f.x;
-                    kf[u][2 * i + 1] = f.y;
+                    const float2 f = __half22float2(vh2[i]);
+                    vf[2 * i] = f.x;
+                    vf[2 * i + 1] = f.y;
+                }
+#pragma unroll
+                for (int gc = 0; gc < GC; ++gc) {
+                    const float pw = scb[gc * kSubA + tb + u];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) acc[gc][i] = __fmaf_rn(pw, vf[i], acc[gc][i]);
                 }
             }
-            constexpr int M = G * NC * 4;  // value j = (g * NC + c) * 4 + u
-            float dv[M];
-#pragma unroll
-            for (int gc = 0; gc < G * NC; ++gc) {
-                const float4* qp = reinterpret_cast<const float4*>(qs + gc * kHdA + lane * 8);
-                const float4 q0 = qp[0], q1 = qp[1];
-                const float qv[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    float d = 0.0f;
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) d = __fmaf_rn(qv[i], kf[u][i], d);
-                    dv[gc * 4 + u] = d;
-                }
-            }
-            warp_reduce_scatter<M>(dv, lane);
-            constexpr int R = M >= 32 ? M / 32 : 1;
-            constexpr int SH = M >= 32 ? 0 : (M == 16 ? 1 : 2);
-            if ((lane & ((1 << SH) - 1)) == 0) {
-#pragma unroll
-                for (int i = 0; i < R; ++i) {
-                    const int j = M >= 32 ? R * lane + i : lane >> SH;
-                    const int gc = j >> 2, t = tb + (j & 3), c = gc % NC;
-                    if (t < ntok) (&sc[0][0][0])[gc * kSubA + t] = (s0 + t <= pos + c) ? __fmul_rn(dv[i], a.scale) : -INFINITY;
-                }
-            }
-        }
-        block_sync256();
-        // V rows of the pass (thread = output dim), 32 tokens per batch; the first batch goes out now so its
-        // round trip overlaps phase 2
-        __half vh[32];
-#pragma unroll
-        for (int u = 0; u < 32; ++u)
-            vh[u] = u < ntok ? __ldcg(vbase + (size_t) (s0 + u) * kHdA + tid) : __float2half_rn(0.0f);
-        // phase 2: per (head, column) the pass's max, the exponentials against the new running max, the
-        // running sum and the rescale factor of what was accumulated before; one warp per pair
-        for (int pair = warp; pair < G * NC; pair += 8) {
-            const int g = pair / NC, c = pair % NC;
-            float m = -INFINITY;
-            for (int t = lane; t < ntok; t += 32) m = fmaxf(m, sc[g][c][t]);
-            m = warp_max(m);
-            const float m_old = run[pair * 4 + 0];
-            const float m_new = fmaxf(m_old, m);
-            float l = 0.0f;
-            for (int t = lane; t < ntok; t += 32) {
-                const float e = m_new == -INFINITY ? 0.0f : expf(__fsub_rn(sc[g][c][t], m_new));  // masked: 0
-                sc[g][c][t] = e;
-                l = __fadd_rn(l, e);
-            }
-            l = warp_sum(l);
-            if (lane == 0) {
-                const float alpha = m_old == -INFINITY ? 0.0f : expf(__fsub_rn(m_old, m_new));
-                run[pair * 4 + 0] = m_new;
-                run[pair * 4 + 1] = __fmaf_rn(run[pair * 4 + 1], alpha, l);
-                run[pair * 4 + 2] = alpha;
-            }
-        }
-        block_sync256();
-        // phase 3: weighted V, added in token order
-#pragma unroll
-        for (int g = 0; g < G; ++g)
-#pragma unroll
-            for (int c = 0; c < NC; ++c) acc[g][c] = __fmul_rn(acc[g][c], run[(g * NC + c) * 4 + 2]);
-        for (int tb = 0; tb < ntok; tb += 32) {
-            if (tb > 0)
-#pragma unroll
-                for (int u = 0; u < 32; ++u)
-                    vh[u] = tb + u < ntok ? __ldcg(vbase + (size_t) (s0 + tb + u) * kHdA + tid) : __float2half_rn(0.0f);
-#pragma unroll
-            for (int u = 0; u < 32; ++u)
-                if (tb + u < ntok) {
-                    const float vf = __half2float(vh[u]);
-#pragma unroll
-                    for (int g = 0; g < G; ++g)
-#pragma unroll
-                        for (int c = 0; c < NC; ++c) acc[g][c] = __fmaf_rn(sc[g][c][tb + u], vf, acc[g][c]);
-                }
-        }
-        block_sync256();  // sc and run are rewritten by the next pass
     }
+    // merge: 4 (head, column) pairs per round, warp sums added in warp order by thread d = dim
 #pragma unroll
-    for (int g = 0; g < G; ++g)
+    for (int r0 = 0; r0 < GC; r0 += 4) {
+        block_sync256();  // wacc aliases the scores (first round) and the previous round
 #pragma unroll
-        for (int c = 0; c < NC; ++c) {
-            const size_t slot = ((size_t) (kvh * G + g) * NC + c) * a.max_chunks + chunk;
-            a.part_o[slot * kHdA + tid] = acc[g][c];
-            if (tid == 0) {
-                a.part_ml[slot * 2 + 0] = run[(g * NC + c) * 4 + 0];
-                a.part_ml[slot * 2 + 1] = run[(g * NC + c) * 4 + 1];
-            }
+        for (int q = 0; q < 4; ++q) {
+            float4* dst = reinterpret_cast<float4*>(wacc + (warp * 4 + q) * kHdA + lane * 8);
+            dst[0] = make_float4(acc[r0 + q][0], acc[r0 + q][1], acc[r0 + q][2], acc[r0 + q][3]);
+            dst[1] = make_float4(acc[r0 + q][4], acc[r0 + q][5], acc[r0 + q][6], acc[r0 + q][7]);
         }
+        block_sync256();
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            float o = wacc[q * kHdA + tid];
+#pragma unroll
+            for (int w = 1; w < 8; ++w) o = __fadd_rn(o, wacc[(w * 4 + q) * kHdA + tid]);
+            const size_t slot = ((size_t) kvh * GC + r0 + q) * a.max_chunks + chunk;
+            a.part_o[slot * kHdA + tid] = o;
+        }
+    }
+    if (tid < GC) {
+        const size_t slot = ((size_t) kvh * GC + tid) * a.max_chunks + chunk;
+        a.part_ml[slot * 2 + 0] = mlc[tid * 2 + 0];
+        a.part_ml[slot * 2 + 1] = mlc[tid * 2 + 1];
+    }
 }
 
 // The chunk body as a call (the op kernel and the persistent kernel); attn_kernel inlines the impl.
@@ -634,7 +648,7 @@ __device__ __noinline__ void combine_body(const AttnArgs& a, int pos, int h, int
     float* wm = sm + 8 * 32;  // [8] warp maxima (-inf: the warp had no chunk)
     float* wden = wm + 8;     // [8]
     block_sync256();          // scratch reuse across items
-    const int n = (pos + c) / attn_chunk_len(pos, NC) + 1;
+    const int n = (pos + c) / attn_chunk_len(pos, NC, a.max_chunks) + 1;
     const int d = slice * 32 + lane;
     const float* ml = a.part_ml + ((size_t) h * NC + c) * a.max_chunks * 2;
     const float* po = a.part_o + ((size_t) h * NC + c) * a.max_chunks * kHdA + d;

@@ -440,7 +440,8 @@ int EngineImpl::build() {
     qkvzab_rows = 2 * hk * S + 2 * hv * S + 2 * hv;
     qkv3_rows = 2 * nh * kHdA + 2 * nkv * kHdA;
     max_in_rows = qkvzab_rows > qkv3_rows ? qkvzab_rows : qkv3_rows;
-    max_chunks = kMaxChunksA;
+    // chunks of at most kSubA tokens must cover the whole cache (positions up to max_ctx - 1 plus the columns)
+    max_chunks = std::max(kMaxChunksA, (c.max_ctx + kMaxCols + kSubA - 1) / kSubA);
     max_out = c.max_ctx;
     if ((err = cudaSetDevice(dev)) != cudaSuccess) return RK_ECUDA;
     if ((err = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking)) != cudaSuccess) return RK_ECUDA;
@@ -930,7 +931,7 @@ cudaError_t EngineImpl::launch_op(const POp& op) {
             if (e != cudaSuccess) return e;
             if (occ < 1) occ = 1;
         }
-        const int grid = std::min(kMaxChunksA * op.at.n_kv, occ * sms);
+        const int grid = std::min(op.at.max_chunks * op.at.n_kv, occ * sms);
         return launch_pdl(attn_kernel<NC>, dim3((unsigned) grid), dim3(256), smem, s, true, op, ctrl);
     }
     // grid: the op's item count, which does not depend on the position

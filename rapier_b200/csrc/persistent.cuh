@@ -585,7 +585,7 @@ __global__ void __launch_bounds__(kPWarps * 32, 1)
 // allocation covers every op body and leaves one CTA per SM; the chunk body alone keeps kAttnCtas CTAs per
 // SM resident, which the long-context chunk loop (memory latency bound) needs.
 template <int NC>
-constexpr int kAttnCtas = NC == 1 ? 3 : 2;
+constexpr int kAttnCtas = NC == 1 ? 3 : NC == 2 ? 2 : 1;  // 80 / 127 / 255 registers, no spills
 template <int NC>
 __global__ void __launch_bounds__(256, kAttnCtas<NC>) attn_kernel(const POp op, Ctrl* ctrl) {
     extern __shared__ __align__(128) uint8_t smem[];
