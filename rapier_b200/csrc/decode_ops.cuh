@@ -18,6 +18,7 @@ constexpr int kHdA = 256;     // attention head dim
 constexpr int kSubA = 256;    // tokens scored per pass inside a flash-decode chunk (shared-memory scores)
 constexpr int kMaxChunksA = 512;  // flash-decode chunks per kv head below which chunks stay short (see attn_chunk_len)
 constexpr int kGqa = 4;       // query heads per kv head
+constexpr int kDraftParts = 16;  // work items per column of the draft-input op
 constexpr int kSsm = 128;     // GDN head size
 constexpr float kInvSqrtSsm = 0.08838834764831845f;  // 1/sqrt(128)
 constexpr int kRingSlots = 8;  // conv history per channel: the input at position p sits in slot p & 7
@@ -139,7 +140,7 @@ __host__ __device__ __forceinline__ int pop_items(const POp& op, int pos) {
             return ((p + NC - 1) / attn_chunk_len(p, NC, op.at.max_chunks) + 1) * op.at.n_kv;
         }
         case POP_COMBINE: return op.at.n_head * NC * (kHdA / 32);
-        case POP_DRAFT_PREP: return NC;
+        case POP_DRAFT_PREP: return NC * kDraftParts;
         case POP_CTRL: return 1;
         default: return 0;
     }
@@ -700,27 +701,36 @@ __device__ __noinline__ void combine_body(const AttnArgs& a, int pos, int h, int
 }
 
 // MTP draft input of column c: Q8_1 of [enorm(emb(dtok)) | hnorm(h)] (src/qwythos.cpp:1316-1334); the
-// draft's argmax slots are cleared here. sm: H + H/4 floats.
-__device__ __noinline__ void draft_prep_body(const DraftPrepArgs& a, Ctrl* ctrl, int c, float* sm, float* red) {
+// draft's argmax slots are cleared here. Item `part` (kDraftParts per column) quantizes 32-value blocks
+// [part * H / 256, (part + 1) * H / 256): parts 0..7 the embedding half (each dequantizes the whole row
+// for its RMS), parts 8..15 the hidden half; the scales are those of one whole-row pass. sm: H + H/4 floats.
+__device__ __noinline__ void draft_prep_body(const DraftPrepArgs& a, Ctrl* ctrl, int c, int part, float* sm,
+                                             float* red) {
     const int H = a.H;
     float* e = sm;
     float* ep = sm + H;
     block_sync256();  // scratch reuse across items
-    if (c == 0 && threadIdx.x == 0) {
+    if (c == 0 && part == 0 && threadIdx.x == 0) {
         ctrl->damax[0] = 0ull;
         ctrl->damax[1] = 0ull;
     }
-    const int tok = read_token(ctrl, 1, c, a.V);
-    dequant_row(a.emb + (size_t) tok * ((size_t) (H / 256) * 210), H, e, ep);
-    block_sync256();
-    const float inv_e = rms_inv(block256_partials_sum<true>(ep, H / 4, red), H, a.eps);
-    const float inv_h = rms_inv(block256_partials_sum(a.hsave_p + (size_t) c * (H / 4), H / 4, red), H, a.eps);
+    const bool emb_half = part < kDraftParts / 2;  // uniform over the block
+    float inv;
+    if (emb_half) {
+        const int tok = read_token(ctrl, 1, c, a.V);
+        dequant_row(a.emb + (size_t) tok * ((size_t) (H / 256) * 210), H, e, ep);
+        block_sync256();
+        inv = rms_inv(block256_partials_sum<true>(ep, H / 4, red), H, a.eps);
+    } else {
+        inv = rms_inv(block256_partials_sum(a.hsave_p + (size_t) c * (H / 4), H / 4, red), H, a.eps);
+    }
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nb = (2 * H / 32) / kDraftParts;
     const float* hc = a.hsave + (size_t) c * H;
     uint8_t* out = a.eh_q8 + (size_t) c * (2 * H / 32) * 36;
-    for (int blk = warp; blk < 2 * H / 32; blk += 8) {
+    for (int blk = part * nb + warp; blk < (part + 1) * nb; blk += 8) {
         const int i = blk * 32 + lane;
-        const float v = i < H ? rms_value(e[i], a.enorm[i], inv_e) : rms_value(ld_cg(hc + i - H), a.hnorm[i - H], inv_h);
+        const float v = i < H ? rms_value(e[i], a.enorm[i], inv) : rms_value(ld_cg(hc + i - H), a.hnorm[i - H], inv);
         q8_1_warp_store(v, out + (size_t) blk * 36, lane);
     }
 }
@@ -797,7 +807,7 @@ __device__ __forceinline__ void run_item(const POp& op, Ctrl* ctrl, int item, in
         case POP_GDN: gdn_quarter_body<NC>(op.gd, item >> 2, item & 3, pos, rollback != 0, sm); break;
         case POP_ATTN: attn_chunk_body<NC>(op.at, pos, item / op.at.n_kv, item % op.at.n_kv, sm); break;
         case POP_COMBINE: combine_body<NC>(op.at, pos, item / (NC * 8), (item / 8) % NC, item % 8, sm); break;
-        case POP_DRAFT_PREP: draft_prep_body(op.dp, ctrl, item, sm, red); break;
+        case POP_DRAFT_PREP: draft_prep_body(op.dp, ctrl, item / kDraftParts, item % kDraftParts, sm, red); break;
         case POP_CTRL:
             if (threadIdx.x == 0) ctrl_body(op.ct, ctrl);
             break;
