@@ -134,6 +134,9 @@ def barrier(pg, device):
 # gemv workload (config 1)
 # ------------------------------------------------------------------------------------------------------
 GEMV_N_IN, GEMV_N_OUT, GEMV_NCOLS, GEMV_COPIES = 4096, 12288, 2, 8
+# DRAM bytes of one config-1 launch (12288 x 4096, 2 columns) from an ncu capture of this kernel: 41,328,384
+# read + 9,216 written, equal to the algorithmic bytes (no re-reads).
+GEMV_CONFIG1_NCU_TRAFFIC = 41_337_600
 
 
 def gemv_algorithmic_bytes(n_in, n_out, ncols):
@@ -216,8 +219,10 @@ def run_gemv(args, rank, world, local, pg):
                    "weights": "Q6_K packed tiles, 8 rotating copies (330 MB) > L2 126 MB",
                    "parallelism": f"replicas x{world}"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "traffic": None, "peak_source": peak_kind,
-                     "algorithmic_bytes_per_launch": algo},
+                     "frac": round(achieved / peak, 4), "traffic": GEMV_CONFIG1_NCU_TRAFFIC if nc == 2 else None,
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch "
+                                       "(profiles/mmvq_packed_config1_gemv.md)" if nc == 2 else None,
+                     "peak_source": peak_kind, "algorithmic_bytes_per_launch": algo},
         "e2e": {"value": round(algo * args.steps * world / (e2e_ms / 1e3) / 1e9, 1), "unit": "GB/s",
                 "h2d_bytes_per_step": n_in * nc * 4, "d2h_bytes_per_step": n_out * nc * 4},
         "gpu_launches": args.steps,
