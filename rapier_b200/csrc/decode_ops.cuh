@@ -244,7 +244,7 @@ __device__ __noinline__ void embed_body(const EmbedArgs& a, Ctrl* ctrl, int draf
 // channel xor trees added in order. History: 8 slots per channel; this launch writes slots pos, pos+1
 // and reads pos-3 .. pos-1 (mod 8), so no write of any block can meet a read of another.
 template <int NC>
-__device__ __noinline__ void gdn_quarter_body(const GdnArgs& a, int head, int quarter, int pos, bool from_snap,
+__device__ __forceinline__ void gdn_quarter_impl(const GdnArgs& a, int head, int quarter, int pos, bool from_snap,
                                                  float* sm) {
     constexpr int S = kSsm;
     float* kq = sm;                     // [NC][256]: normalized k (0..127) | q (128..255)
@@ -409,6 +409,13 @@ __device__ __noinline__ void gdn_quarter_body(const GdnArgs& a, int head, int qu
     }
 }
 
+// The GDN item as a call (the op kernel and the persistent kernel); gdn_kernel inlines the impl.
+template <int NC>
+__device__ __noinline__ void gdn_quarter_body(const GdnArgs& a, int head, int quarter, int pos, bool from_snap,
+                                                 float* sm) {
+    gdn_quarter_impl<NC>(a, head, quarter, pos, from_snap, sm);
+}
+
 // Flash-decode chunk `chunk` of kv head kvh for NC query columns (gqa_head_kernel, src/qwythos.cpp:380-442,
 // split over chunks of attn_chunk_len <= kSubA tokens), with the attention prologue of the tokens it needs
 // folded in: split of q / gate (split_qg_kernel, :320-327), per-head RMSNorm, NEOX RoPE over n_rot dims from
@@ -430,11 +437,10 @@ __device__ __forceinline__ void attn_chunk_impl(const AttnArgs& a, int pos, int 
     const int t0 = chunk * len;
     if (t0 > pos + NC - 1 || chunk >= a.max_chunks) return;  // beyond every column (uniform over the block)
     const int tend = min(t0 + len, pos + NC);                  // tokens [t0, tend) some column may read
-    if (threadIdx.x == 0) {  // the chunk's K and V rows (contiguous per kv head) head for L2 now
+    if (threadIdx.x == 0) {  // the chunk's K rows (contiguous per kv head) head for L2 now; V after the scores
         const uint32_t bytes = (uint32_t) (tend - t0) * kHdA * 2;
         const size_t row0 = ((size_t) kvh * a.max_ctx + t0) * kHdA;
         asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a.kc + row0), "r"(bytes) : "memory");
-        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a.vc + row0), "r"(bytes) : "memory");
     }
     float* mlc = sm;                    // [GC][2]: the chunk's max and exponential sum (64 floats reserved)
     float* qs = sm + 64;                // [GC][256]
@@ -545,6 +551,11 @@ __device__ __forceinline__ void attn_chunk_impl(const AttnArgs& a, int pos, int 
         }
     }
     block_sync256();
+    if (threadIdx.x == 0) {  // V rows head for L2 only now: fewer prefetched lines wait (and get evicted) in L2
+        const uint32_t bytes = (uint32_t) (tend - t0) * kHdA * 2;
+        const size_t row0 = ((size_t) kvh * a.max_ctx + t0) * kHdA;
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a.vc + row0), "r"(bytes) : "memory");
+    }
     // this warp's first V rows go out now, so their round trip overlaps phase 2
     constexpr int kVB = 4;  // V rows per batch (16 B per lane each)
     const int tw0 = warp * 32, tw1 = min(tw0 + 32, ntok);
@@ -637,12 +648,12 @@ __device__ __noinline__ void attn_chunk_body(const AttnArgs& a, int pos, int chu
 
 // Combine of head h, column c, dims [32 slice, 32 slice + 32), then that dims' Q8_1 block of
 // o * sigmoid(gate) (sig_mul_quant_kernel, src/qwythos.cpp:692-704; one warp = one 32-dim block). Warp w
-// merges chunks [w n / 8, (w + 1) n / 8) (lane = one dim, eight chunks' rows in flight), then warp 0 merges
+// merges chunks [w n / 8, (w + 1) n / 8) (lane = one dim, 16 chunks' rows in flight), then warp 0 merges
 // the eight warp partials in warp order: the same merge for any column count and any slicing, so a dim's
 // result does not depend on which item computed it. sm: 8 x 32 + 16 floats.
 template <int NC>
 __device__ __noinline__ void combine_body(const AttnArgs& a, int pos, int h, int c, int slice, float* sm) {
-    constexpr int kU = 8;
+    constexpr int kU = 16;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (pos < 0 || pos + NC > a.max_ctx) return;  // recorded by the chunk body
     float* wnum = sm;         // [8][32]

@@ -597,6 +597,20 @@ __global__ void __launch_bounds__(256, kAttnCtas<NC>) attn_kernel(const POp op, 
         attn_chunk_impl<NC>(op.at, pos, it / op.at.n_kv, it % op.at.n_kv, reinterpret_cast<float*>(smem));
 }
 
+// The GDN op as its own launch (graph mode): a kernel of its own instead of the generic op kernel, whose
+// code covers every op body (instruction-cache misses) and whose register allocation is the largest body's.
+template <int NC>
+__global__ void __launch_bounds__(256) gdn_kernel(const POp op, Ctrl* ctrl) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    pdl_trigger();
+    pdl_wait();
+    const int pos = ld_cg(op.draft ? &ctrl->dpos : &ctrl->pos);
+    const int rb = ld_cg(&ctrl->rollback);
+    const int items = pop_items<NC>(op, pos);
+    for (int it = (int) blockIdx.x; it < items; it += (int) gridDim.x)  // uniform over the block
+        gdn_quarter_impl<NC>(op.gd, it >> 2, it & 3, pos, rb != 0, reinterpret_cast<float*>(smem));
+}
+
 // One non-GEMV op as its own launch (graph mode).
 template <int NC>
 __global__ void __launch_bounds__(256) op_kernel(const POp op, Ctrl* ctrl) {
