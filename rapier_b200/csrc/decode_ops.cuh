@@ -16,7 +16,7 @@ namespace rk {
 
 constexpr int kHdA = 256;     // attention head dim
 constexpr int kSubA = 256;    // tokens scored per pass inside a flash-decode chunk (shared-memory scores)
-constexpr int kMaxChunksA = 512;  // flash-decode chunks per kv head below which chunks stay short (see attn_chunk_len)
+constexpr int kMaxChunksA = 512;  // flash-decode chunks per kv head the chunk length aims for (see attn_chunk_len)
 constexpr int kGqa = 4;       // query heads per kv head
 constexpr int kDraftParts = 16;  // work items per column of the draft-input op
 constexpr int kSsm = 128;     // GDN head size
@@ -79,6 +79,7 @@ struct AttnArgs {
     int proj_stride;
     const float *qn, *kn, *rope;
     int n_rot, n_head, n_kv, max_ctx, max_chunks;
+    int chunk_len;  // tokens per flash-decode chunk (attn_chunk_len of max_ctx)
     float eps, scale;
     __half *kc, *vc;
     float *part_o, *part_ml;
@@ -118,13 +119,15 @@ struct alignas(16) POp {  // 16-byte multiple: fetched into shared memory by 16-
 };
 static_assert(sizeof(POp) % 16 == 0 && sizeof(POp) / 16 <= 256, "op records are copied in 16-byte chunks");
 
-// Tokens per flash-decode chunk for a step at positions pos .. pos+nc-1: the smallest of 32, 64, 128, 256
-// (kSubA) that keeps a kv head's chunks at most max_chunks (many small chunks spread any context over many
-// CTAs: 17 chunks of 32 at 512 tokens, 257 of 256 at 65536; the engine sizes max_chunks as
-// max(kMaxChunksA, max_ctx / kSubA rounded up), so a chunk is never longer than one pass of kSubA).
-__host__ __device__ __forceinline__ int attn_chunk_len(int pos, int nc, int max_chunks) {
+// Tokens per flash-decode chunk of an engine with cache capacity max_ctx: the smallest of 32, 64, 128, 256
+// (kSubA) that splits the whole cache into at most kMaxChunksA chunks (256 beyond 131072 positions), so a
+// chunk is one pass of at most kSubA tokens and short contexts spread over many CTAs (17 chunks of 32 at
+// 512 tokens when max_ctx <= 16384). The length depends on the engine only, never on the position or the
+// column count: column c of a multi-column step is chunked exactly as a single-token step at position
+// pos + c, which keeps the MTP verify bitwise equal to single-token decoding at every position.
+__host__ __device__ __forceinline__ int attn_chunk_len(int max_ctx) {
     int len = 32;
-    while ((pos + nc + len - 1) / len > max_chunks && len < kSubA) len <<= 1;
+    while ((max_ctx + len - 1) / len > kMaxChunksA && len < kSubA) len <<= 1;
     return len;
 }
 
@@ -137,7 +140,7 @@ __host__ __device__ __forceinline__ int pop_items(const POp& op, int pos) {
         case POP_GDN: return op.gd.hv * 4;
         case POP_ATTN: {  // positions outside the cache are refused by the body; bound the count
             const int p = pos < 0 ? 0 : (pos > op.at.max_ctx - NC ? op.at.max_ctx - NC : pos);
-            return ((p + NC - 1) / attn_chunk_len(p, NC, op.at.max_chunks) + 1) * op.at.n_kv;
+            return ((p + NC - 1) / op.at.chunk_len + 1) * op.at.n_kv;
         }
         case POP_COMBINE: return op.at.n_head * NC * (kHdA / 32);
         case POP_DRAFT_PREP: return NC * kDraftParts;
@@ -417,7 +420,7 @@ __device__ __noinline__ void gdn_quarter_body(const GdnArgs& a, int head, int qu
 }
 
 // Flash-decode chunk `chunk` of kv head kvh for NC query columns (gqa_head_kernel, src/qwythos.cpp:380-442,
-// split over chunks of attn_chunk_len <= kSubA tokens), with the attention prologue of the tokens it needs
+// split over chunks of a.chunk_len <= kSubA tokens), with the attention prologue of the tokens it needs
 // folded in: split of q / gate (split_qg_kernel, :320-327), per-head RMSNorm, NEOX RoPE over n_rot dims from
 // the cos / sin table, and the fp16 K/V store (store_kv2_kernel, :340-345) of the new positions inside this
 // chunk (each position has exactly one owning chunk). Column c attends tokens <= pos + c. One pass: scores
@@ -433,7 +436,7 @@ __device__ __forceinline__ void attn_chunk_impl(const AttnArgs& a, int pos, int 
         if (threadIdx.x == 0) atomicOr(&g_rk_status, kStatusBadIndex);
         return;
     }
-    const int len = attn_chunk_len(pos, NC, a.max_chunks);
+    const int len = a.chunk_len;
     const int t0 = chunk * len;
     if (t0 > pos + NC - 1 || chunk >= a.max_chunks) return;  // beyond every column (uniform over the block)
     const int tend = min(t0 + len, pos + NC);                  // tokens [t0, tend) some column may read
@@ -660,7 +663,7 @@ __device__ __noinline__ void combine_body(const AttnArgs& a, int pos, int h, int
     float* wm = sm + 8 * 32;  // [8] warp maxima (-inf: the warp had no chunk)
     float* wden = wm + 8;     // [8]
     block_sync256();          // scratch reuse across items
-    const int n = (pos + c) / attn_chunk_len(pos, NC, a.max_chunks) + 1;
+    const int n = (pos + c) / a.chunk_len + 1;
     const int d = slice * 32 + lane;
     const float* ml = a.part_ml + ((size_t) h * NC + c) * a.max_chunks * 2;
     const float* po = a.part_o + ((size_t) h * NC + c) * a.max_chunks * kHdA + d;

@@ -196,7 +196,7 @@ struct EngineImpl {
     // FF, hk, hv, nh, nkv and V (lm_head rows) are this rank's shares; Vg is the vocabulary.
     int tp_rank = 0, tp_size = 1;
     int H = 0, FF = 0, V = 0, Vg = 0, hk = 0, hv = 0, nh = 0, nkv = 0;
-    int qkvzab_rows = 0, qkv3_rows = 0, max_in_rows = 0, max_chunks = 0;
+    int qkvzab_rows = 0, qkv3_rows = 0, max_in_rows = 0, max_chunks = 0, chunk_len = 32;
     std::vector<Layer> layers;
     Layer draft;
     float *enorm = nullptr, *hnorm = nullptr, *shnorm = nullptr, *out_norm = nullptr;
@@ -440,8 +440,9 @@ int EngineImpl::build() {
     qkvzab_rows = 2 * hk * S + 2 * hv * S + 2 * hv;
     qkv3_rows = 2 * nh * kHdA + 2 * nkv * kHdA;
     max_in_rows = qkvzab_rows > qkv3_rows ? qkvzab_rows : qkv3_rows;
-    // chunks of at most kSubA tokens must cover the whole cache (positions up to max_ctx - 1 plus the columns)
-    max_chunks = std::max(kMaxChunksA, (c.max_ctx + kMaxCols + kSubA - 1) / kSubA);
+    // one flash-decode chunk length for the engine (attn_chunk_len); its chunks cover the whole cache
+    chunk_len = attn_chunk_len(c.max_ctx);
+    max_chunks = (c.max_ctx + chunk_len - 1) / chunk_len;
     max_out = c.max_ctx;
     if ((err = cudaSetDevice(dev)) != cudaSuccess) return RK_ECUDA;
     if ((err = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking)) != cudaSuccess) return RK_ECUDA;
@@ -708,6 +709,7 @@ POp EngineImpl::attn_op(int kind, const Layer& L, int draft_flag) {
     a.n_kv = nkv;
     a.max_ctx = cfg.max_ctx;
     a.max_chunks = max_chunks;
+    a.chunk_len = chunk_len;
     a.eps = cfg.eps;
     a.scale = kAttnScale;
     a.kc = L.kc;

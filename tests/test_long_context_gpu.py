@@ -1,6 +1,8 @@
-"""Decode after a long synthetic context (rk_engine_session_fill: seeded fp16 K/V and GDN states): chunks of
-512 tokens scored in two 256-token passes each, the MTP stream equal to the greedy stream, and the two
-executors bit for bit, at a 20000-token context."""
+"""Decode after a long synthetic context (rk_engine_session_fill: seeded fp16 K/V and GDN states) in an engine
+of 20256 positions (flash-decode chunks of 64 tokens): the MTP stream equal to the greedy stream, the two
+executors bit for bit, and a 2-column step bitwise equal to two single-token steps at position 16383, where
+a chunk length chosen from the position (32 tokens below 16384, 64 above) would have split the two columns'
+keys differently."""
 import numpy as np
 import pytest
 
@@ -51,3 +53,24 @@ def test_fill_is_deterministic_and_seeded(pair):
     g.session_fill(FILL, 12)
     _, _, lc = g.session_run(P, 1, first_logits=True)
     assert np.array_equal(la, lb) and not np.array_equal(la, lc)
+
+
+def test_two_columns_equal_singles_at_former_chunk_boundary(pair):
+    g, _ = pair
+    pos = 16383
+    g.session_fill(pos, 4)
+    lg2, _ = g.step([7, 8], pos)
+    g.session_fill(pos, 4)
+    s0, _ = g.step([7], pos)
+    s1, _ = g.step([8], pos + 1)
+    assert np.array_equal(lg2[0].view(np.uint32), s0[0].view(np.uint32))
+    assert np.array_equal(lg2[1].view(np.uint32), s1[0].view(np.uint32))
+
+
+def test_mtp_equals_greedy_across_former_chunk_boundary(pair):
+    g, _ = pair
+    g.session_fill(16370, 6)
+    a, _, _ = g.session_run(P, 40, mtp=False)
+    g.session_fill(16370, 6)
+    b, st, _ = g.session_run(P, 40, mtp=True)
+    assert list(a) == list(b) and st["mtp_steps"] > 0
