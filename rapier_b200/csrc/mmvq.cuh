@@ -514,7 +514,6 @@ __global__ void __launch_bounds__(kMmvqWarps * 32, 2) mmvq_packed_kernel(const M
         }
     };
     const int npre = ntiles < stages ? ntiles : stages;
-    pdl_trigger();
     if (p.prefetch_before_wait && lane == 0)
         for (int i = 0; i < npre; ++i) issue(i);
     pdl_wait();
@@ -573,6 +572,10 @@ __global__ void __launch_bounds__(kMmvqWarps * 32, 2) mmvq_packed_kernel(const M
             if (unit < uend) mmvq_res_prefetch<NC, EPI>(p, unit, lane, resv);
         }
     }
+    // The next launch may start only now: its CTAs would otherwise queue their own bulk copies (and the
+    // launches after it theirs) ahead of this launch's last refills, which gate the whole step (measured:
+    // 1 % per token; with ring depths that let two GEMV CTAs share an SM, early starts cost up to 20 %).
+    pdl_trigger();
     if constexpr (EPI == EPI_SWIGLU) mmvq_swiglu_finish<NC>(p, ubeg + warp, kMmvqWarps, unit, lane);
     if constexpr (EPI == EPI_ARGMAX) mmvq_argmax_flush<NC>(p, lane, best);
 }
