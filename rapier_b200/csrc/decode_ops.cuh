@@ -655,7 +655,7 @@ __device__ __noinline__ void attn_chunk_body(const AttnArgs& a, int pos, int chu
 // the eight warp partials in warp order: the same merge for any column count and any slicing, so a dim's
 // result does not depend on which item computed it. sm: 8 x 32 + 16 floats.
 template <int NC>
-__device__ __noinline__ void combine_body(const AttnArgs& a, int pos, int h, int c, int slice, float* sm) {
+__device__ __forceinline__ void combine_impl(const AttnArgs& a, int pos, int h, int c, int slice, float* sm) {
     constexpr int kU = 16;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (pos < 0 || pos + NC > a.max_ctx) return;  // recorded by the chunk body
@@ -712,6 +712,12 @@ __device__ __noinline__ void combine_body(const AttnArgs& a, int pos, int h, int
     if (a.o) a.o[oi] = ov;
     const float gate = ld_cg(a.proj + (size_t) c * a.proj_stride + h * 2 * kHdA + kHdA + d);
     q8_1_warp_store(sigmul_value(ov, gate), a.q8 + (((size_t) c * a.n_head + h) * (kHdA / 32) + slice) * 36, lane);
+}
+
+// The combine item as a call (the op kernel and the persistent kernel); combine_kernel inlines the impl.
+template <int NC>
+__device__ __noinline__ void combine_body(const AttnArgs& a, int pos, int h, int c, int slice, float* sm) {
+    combine_impl<NC>(a, pos, h, c, slice, sm);
 }
 
 // MTP draft input of column c: Q8_1 of [enorm(emb(dtok)) | hnorm(h)] (src/qwythos.cpp:1316-1334); the

@@ -936,6 +936,10 @@ cudaError_t EngineImpl::launch_op(const POp& op) {
         const int grid = std::min(op.at.max_chunks * op.at.n_kv, occ * sms);
         return launch_pdl(attn_kernel<NC>, dim3((unsigned) grid), dim3(256), smem, s, true, op, ctrl);
     }
+    if (op.kind == POP_COMBINE) {  // sm: 8 x 32 + 16 floats
+        return launch_pdl(combine_kernel<NC>, dim3((unsigned) pop_items<NC>(op, 0)), dim3(256), (size_t) 2048, s, true, op,
+                          ctrl);
+    }
     if (op.kind == POP_GDN) {
         const size_t smem = ((size_t) gdn_scratch_floats(NC) * 4 + 127) & ~(size_t) 127;
         return launch_pdl(gdn_kernel<NC>, dim3((unsigned) pop_items<NC>(op, 0)), dim3(256), smem, s, true, op, ctrl);

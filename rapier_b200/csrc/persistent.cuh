@@ -611,6 +611,19 @@ __global__ void __launch_bounds__(256) gdn_kernel(const POp op, Ctrl* ctrl) {
         gdn_quarter_impl<NC>(op.gd, it >> 2, it & 3, pos, rb != 0, reinterpret_cast<float*>(smem));
 }
 
+// The attention combine as its own launch (graph mode): n_head x NC x 8 items of 32 dims, small enough per
+// block that they run in one wave (the generic op kernel's registers leave one block per SM).
+template <int NC>
+__global__ void __launch_bounds__(256, 2) combine_kernel(const POp op, Ctrl* ctrl) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    pdl_trigger();
+    pdl_wait();
+    const int pos = ld_cg(op.draft ? &ctrl->dpos : &ctrl->pos);
+    const int items = pop_items<NC>(op, pos);
+    for (int it = (int) blockIdx.x; it < items; it += (int) gridDim.x)  // uniform over the block
+        combine_impl<NC>(op.at, pos, it / (NC * 8), (it / 8) % NC, it % 8, reinterpret_cast<float*>(smem));
+}
+
 // One non-GEMV op as its own launch (graph mode).
 template <int NC>
 __global__ void __launch_bounds__(256) op_kernel(const POp op, Ctrl* ctrl) {
