@@ -1,8 +1,10 @@
 // persistent.cuh — the two executors of a decode op program (decode_ops.cuh).
 //
-// * op_kernel<NC>: one launch per non-GEMV op (grid = the op's largest item count, one item per block,
-//   blocks past the op's live item count return); GEMV ops launch mmvq_packed_kernel. The engine
-//   captures the launches of a program in a CUDA graph.
+// * Graph executor: one launch per op, captured in a CUDA graph. GEMV ops launch mmvq_packed_kernel; the GDN
+//   step, the flash-decode chunks and the attention combine have kernels of their own (gdn_kernel,
+//   attn_kernel, combine_kernel: each compiled for its body alone, so its register count allows several
+//   blocks per SM and its code stays small); the remaining small ops (embedding, draft input, control) run
+//   in op_kernel<NC> (grid = the op's largest item count, blocks past the live item count return).
 // * persistent_kernel<NC>: the whole program in one cooperative launch, one 512-thread CTA per SM. Ops
 //   run in program order separated by grid barriers. All 16 warps consume GEMV tiles (16 warps per SM
 //   hide the latency of the tile decode) against one staged copy of the activations; the 256-thread
