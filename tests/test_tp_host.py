@@ -4,7 +4,6 @@ before rk_engine_tp_connect (a stand-in engine records what it is handed)."""
 import os
 import socket
 
-import pytest
 import torch.multiprocessing as mp
 
 
