@@ -2,7 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl rapier|reference] [--workload gemv|decode]
 
-Workloads (BASELINE.json configs; synthetic seeded data, no model file):
+Workloads (synthetic seeded data, no model file):
   decode  config 5 (default): the 9B-shaped qwen35 hybrid (24 GDN + 8 GQA layers, MTP block), random-init
           weights quantized to Q6_K, greedy decode of 400 tokens from a seeded 32-token prompt with exact
           MTP (--no-mtp: config 4). A step is one 400-token generation; tok/s = generated tokens / device
@@ -269,65 +269,11 @@ def tp_layout(world: int) -> tuple:
     return 1, world
 
 
-def run_decode(args, rank, world, local, pg):
-    import torch
-
-    from rapier_b200.engine import Engine, config_9b
-
-    dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
+def decode_config(args, world: int) -> dict:
+    """The decode line's `config`, from the arguments only (the same dict on both arms)."""
     tp, groups = tp_layout(world)
-    grp, tp_rank = rank // tp, rank % tp
-    group = None
-    if tp > 1:
-        subgroups = [pg.new_group(list(range(g * tp, (g + 1) * tp))) for g in range(groups)]
-        group = subgroups[grp]
-    fill = args.ctx_fill
-    cfg = config_9b(max_ctx=max(args.ctx, fill + N_PROMPT + args.gen + 64) if fill else args.ctx, seed=1 + grp)
-    eng = Engine(cfg, device=local, tp_rank=tp_rank, tp_size=tp)
-    if tp > 1:
-        eng.connect_tp(group)
-        barrier(pg, dev)
-    prompt = [int(t) for t in np.random.default_rng(1234 + grp).integers(0, cfg.n_vocab, N_PROMPT)]
-    mtp = not args.no_mtp
-    n_gen = args.gen
-
-    def one_generation():
-        if fill:  # decode after a synthetic context of `fill` tokens (seeded caches, rk_engine_session_fill)
-            eng.session_fill(fill, 7 + grp)
-            ids, st, _ = eng.session_run(prompt, n_gen, mtp=mtp)
-            return ids, st
-        return eng.generate(prompt, n_gen, mtp=mtp)
-
-    for _ in range(args.warmup):
-        one_generation()
-    barrier(pg, dev)
-    gen_ms, stats = 0.0, None
-    t0 = time.perf_counter()
-    with ClockSampler(local) as clk:
-        for _ in range(args.steps):
-            ids, st = one_generation()
-            gen_ms += st["gen_ms"]
-            stats = st
-        barrier(pg, dev)
-    wall_s = time.perf_counter() - t0
-    gen_ms = max_over_ranks(gen_ms, pg, dev)
-    wall_s = max_over_ranks(wall_s, pg, dev)
-    tokens = n_gen * args.steps * groups
-    probe = eng.probe_gemv(ncols=2 if mtp else 1, iters=20)
-    persistent = eng.mode == "persistent"
-    eng.close()
-    peak, peak_kind = measured_peaks()
-    per_launch_s = probe["ms"] / 1e3 / (probe["iters"] * probe["launches"])
-    algo_per_launch = probe["algo_bytes"] / probe["launches"]
-    achieved = algo_per_launch / per_launch_s / 1e9
-    rounds = stats["mtp_steps"]
-    if persistent:  # one kernel per program run (a whole greedy generation is one run)
-        launches_per_gen = stats["graph_launches"]
-    else:
-        launches_per_gen = ((stats["graph_launches"] - rounds) * stats["kernels_per_single_step"] +
-                            rounds * stats["kernels_per_round"])
-    par = "single GPU" if world == 1 else (f"tensor parallel x{tp}" + (f", {groups} independent groups" if groups > 1 else ""))
+    fill, mtp = args.ctx_fill, not args.no_mtp
+    cfgd = decode_config(args, world)
     line = {
         "metric": "greedy decode tok/s (1 B200, exact MTP)" if mtp else "greedy decode tok/s (1 B200, no MTP)",
         "value": round(tokens / (gen_ms / 1e3), 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
@@ -335,15 +281,11 @@ def run_decode(args, rank, world, local, pg):
         "scaling": "strong" if (world > 1 and groups == 1) else "weak", "vs_baseline": None,
         "dtype": "q6_k x q8_1 int8 dp4a, fp32 accumulate, fp16 KV",
         "data": "synthetic (random-init weights, seeded prompt)",
-        "config": {"workload": "config5-decode-mtp" if mtp else "config4-decode", "model": "qwen35-9b-shaped",
-                   "layers": "24 GDN + 8 GQA (+1 MTP block)", "n_prompt": N_PROMPT, "n_gen": n_gen,
-                   "ctx": (fill + N_PROMPT + n_gen) if fill else args.ctx, "kv_context": fill + N_PROMPT if fill else N_PROMPT,
-                   "parallelism": par, "tensor_parallel": tp, "groups": groups,
-                   "executor": "persistent" if persistent else "graph",
-                   "l2": "6.5 GB of weights per token > 126 MB L2"},
+        "config": cfgd,
+        "executor": "persistent" if persistent else "graph",
         "mtp": {"rounds": rounds, "accepted": stats["mtp_accepted"],
                 "acceptance": round(stats["mtp_accepted"] / rounds, 4) if rounds else None,
-                "single_steps": stats["single_steps"]} if mtp else None,
+                "single_steps": stats["single_steps"], "forced_acceptance_1": forced} if mtp else None,
         "roofline": {"bound": "hbm",
                      "kernel": ("persistent_kernel (the GEMV ops of one trunk step, one launch)" if persistent else
                                 "mmvq_packed_kernel (all GEMVs of one trunk step, graph replay)"),
@@ -384,72 +326,54 @@ def run_pass(args):
     eng.close()
 
 
-def cpu_baseline_decode(budget_s=20.0):
-    """The oracle (C restatement, OpenMP over the host cores) on one GDN layer, one attention layer and the
-    lm_head of the 9B shape; token time extrapolated as 24 x GDN + 8 x attention + head."""
+def cpu_baseline_decode(budget_s=20.0, mtp=True):
+    """The oracle (C restatement, OpenMP over the host cores) on one GDN layer, one attention layer, the MTP
+    block and the lm_head of the 9B shape; a token's time is extrapolated as 24 x GDN + 8 x attention +
+    head. With exact MTP at this model's acceptance of 0 (random weights), every round emits one token and
+    costs two trunk columns and two draft columns; the oracle runs columns one after the other."""
     from oracle import oracle as O
-    from oracle.model import Model
-    from rapier_b200.engine import config_9b
+    from oracle.model import Model, config_9b
 
-    cfg = config_9b(max_ctx=64, seed=1)
-    cfg.n_layer, cfg.attn_interval = 4, 4  # layers 0..2 GDN, 3 attention; layers 0 and 3 are timed
+    cfg = config_9b(max_ctx=64, seed=1, n_layer=4)  # layers 0..2 GDN, 3 attention; layers 0 and 3 are timed
     t_gen = time.perf_counter()
-    m = Model(cfg, only_layers=(0, 3), with_embed=False)
+    m = Model(cfg, only_layers=(0, 3), with_embed=False, with_draft=mtp)
     t_gen = time.perf_counter() - t_gen
     H = cfg.n_embd
     x = O.synth_normal(3, H)
-    timings = {"gdn": [], "attn": [], "head": []}
+    xp = O.row_sumsq_partials(x)
+    timings = {"gdn": [], "attn": [], "head": [], "draft": []}
     t_end = time.perf_counter() + budget_s
     pos = 0
     while (time.perf_counter() < t_end or pos < 2) and pos < cfg.max_ctx:
         for kind, il in (("gdn", 0), ("attn", 3)):
             t0 = time.perf_counter()
-            one_layer_forward(m, il, x, pos)
+            m.layer(il, x, xp, pos)
             timings[kind].append(time.perf_counter() - t0)
         t0 = time.perf_counter()
-        xq = O.rms_quant_q8_1(x, m.out_norm, O.row_sumsq_partials(x), np.float32(cfg.eps))
-        O.mmvq(O.TYPE_Q6_K, m.lm_head, xq, H, cfg.n_vocab)
+        m.head(x, xp)
         timings["head"].append(time.perf_counter() - t0)
+        if mtp:  # the draft without its embedding row: eh_proj, the nextn layer, the head
+            t0 = time.perf_counter()
+            ehq = O.quantize_q8_1(np.concatenate([x, x]), 2 * H, 1)
+            dx = O.mmvq(O.TYPE_Q6_K, m.eh_proj, ehq, 2 * H, H)
+            dx, dxp = m._attention(m.draft_layer, m.draft_kv, dx, O.row_sumsq_partials(dx), pos)
+            dx, dxp = m._ffn(m.draft_layer, dx, dxp)
+            O.mmvq(O.TYPE_Q6_K, m.lm_head, O.rms_quant_q8_1(dx, m.shnorm, dxp, m.eps), H, cfg.n_vocab)
+            timings["draft"].append(time.perf_counter() - t0)
         pos += 1
-    med = {k: statistics.median(v) for k, v in timings.items()}
+    med = {k: statistics.median(v) for k, v in timings.items() if v}
     t_tok = 24 * med["gdn"] + 8 * med["attn"] + med["head"]
-    return {"value": round(1.0 / t_tok, 4), "unit": "tok/s", "cores": O.num_threads(), "kind": "port",
-            "sample": f"{pos} tokens through 1 GDN + 1 attention layer + lm_head of the 9B shape (no MTP); token "
-                      f"time extrapolated as 24 GDN + 8 attention + head = {t_tok * 1e3:.1f} ms "
-                      f"(weights generated in {t_gen:.1f} s, untimed)"}
-
-
-def one_layer_forward(model, il, x, pos):
-    """Layer il of oracle.model.Model.forward (mixer + FFN) on hidden x at position pos."""
-    from oracle import oracle as O
-
-    H, L, st, eps, Q6 = model.H, model.layers[il], model.state[il], model.eps, O.TYPE_Q6_K
-    xp = O.row_sumsq_partials(x)
-    xq = O.rms_quant_q8_1(x, L["attn_norm"], xp, eps)
-    if L["gdn"]:
-        hk, hv, C, KS = model.hk, model.hv, model.C, 128
-        proj = O.mmvq(Q6, L["in_proj"], xq, H, 2 * hk * KS + 2 * hv * KS + 2 * hv)
-        z = proj[C:C + hv * KS]
-        beta, g = O.beta_gate(proj[C + hv * KS:C + hv * KS + hv], proj[C + hv * KS + hv:], L["dt"], L["ssm_a"])
-        st["ring"], h = O.gdn_conv_l2(st["ring"], proj[:C], L["conv_w"], C, 2 * hk, eps, pos)
-        st["ssm"], _, q8 = O.gdn_step_norm_silu_q8(st["ssm"], h[:hk * KS], h[hk * KS:2 * hk * KS], h[2 * hk * KS:C],
-                                                   g, beta, z, L["ssm_norm"], eps, hk, hv)
-        x2, xp = O.mmvq_res(Q6, L["out_proj"], q8, x, hv * KS, H)
+    if mtp:
+        t_out = 2 * (t_tok + med["draft"])
+        how = (f"exact MTP at acceptance 0: a round = 2 trunk columns + 2 draft columns = "
+               f"2 x ({t_tok * 1e3:.1f} + {med['draft'] * 1e3:.1f}) ms per emitted token")
     else:
-        nh, nkv, HD = model.nh, model.nkv, 256
-        q3 = O.mmvq(Q6, L["in_proj"], xq, H, 2 * nh * HD + 2 * nkv * HD)
-        q, gate = O.split_qg(q3[:2 * nh * HD], nh, HD)
-        k = q3[2 * nh * HD:2 * nh * HD + nkv * HD]
-        v = q3[2 * nh * HD + nkv * HD:]
-        q = O.rope_apply(O.rms_norm_rows(q, L["q_norm"], nh, HD, eps), nh, HD, 64, model.rope, pos)
-        k = O.rope_apply(O.rms_norm_rows(k, L["k_norm"], nkv, HD, eps), nkv, HD, 64, model.rope, pos)
-        st["k"][pos] = O.f32_to_f16(k).reshape(nkv, HD)
-        st["v"][pos] = O.f32_to_f16(v).reshape(nkv, HD)
-        o = O.gqa_decode_f16(q, st["k"].ravel(), st["v"].ravel(), nh, nkv, HD, pos + 1, 0.0625)
-        x2, xp = O.mmvq_res(Q6, L["out_proj"], O.sigmul_q8_1(o, gate), x, nh * HD, H)
-    xq = O.rms_quant_q8_1(x2, L["post_norm"], xp, eps)
-    ug = O.mmvq(Q6, L["upgate"], xq, H, 2 * model.FF)
-    return O.mmvq_res(Q6, L["down"], O.swiglu_q8_1(ug[:model.FF], ug[model.FF:]), x2, model.FF, H)[0]
+        t_out = t_tok
+        how = f"no MTP: {t_tok * 1e3:.1f} ms per token"
+    return {"value": round(1.0 / t_out, 4), "unit": "tok/s", "cores": O.num_threads(), "kind": "port",
+            "sample": f"{pos} positions through 1 GDN + 1 attention layer + lm_head (+ the MTP block) of the 9B "
+                      f"shape; token time extrapolated as 24 GDN + 8 attention + head; {how} (weights generated "
+                      f"in {t_gen:.1f} s, untimed)"}
 
 
 def main():
@@ -481,10 +405,9 @@ def main():
         if rank != 0:
             return
         if args.workload == "decode":
-            base = cpu_baseline_decode()
-            metric = "greedy decode tok/s (1 B200, exact MTP)" if not args.no_mtp else "greedy decode tok/s (no MTP)"
-            cfgd = {"workload": "config5-decode-mtp" if not args.no_mtp else "config4-decode",
-                    "model": "qwen35-9b-shaped", "n_prompt": N_PROMPT, "n_gen": N_GEN, "ctx": args.ctx}
+            base = cpu_baseline_decode(mtp=not args.no_mtp)
+            metric = "greedy decode tok/s (1 B200, exact MTP)" if not args.no_mtp else "greedy decode tok/s (1 B200, no MTP)"
+            cfgd = decode_config(args, args.gpus)
         else:
             base = cpu_baseline_gemv()
             metric = "Q6_K x Q8_1 GEMV HBM GB/s (12288x4096, ncols 2)"
@@ -504,7 +427,8 @@ def main():
     line = (run_decode if args.workload == "decode" else run_gemv)(args, rank, world, local, pg)
     if rank == 0:
         if world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline_decode() if args.workload == "decode" else cpu_baseline_gemv()
+            line["cpu_baseline"] = (cpu_baseline_decode(mtp=not args.no_mtp) if args.workload == "decode"
+                                    else cpu_baseline_gemv())
         print(json.dumps(line), flush=True)
     if pg is not None:
         pg.destroy_process_group()

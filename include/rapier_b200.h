@@ -130,6 +130,10 @@ int rk_beta_gate(float* beta, const float* alpha, const float* dt, const float* 
 /* Strata rms_norm_weighted (called at src/qwythos.cpp:1206-1207): per row x = x * rsqrt(mean(x^2) + eps) * w,
  * in place. */
 int rk_rms_norm_rows(float* x, const float* w, int rows, int cols, float eps, void* stream);
+/* Parity probe, no reference counterpart: y[i] = f(x[i]) with the exactly specified fp32 sequences every
+ * kernel here uses in place of the vendor library (fn 0 exp, 1 log, 2 log1p, 3 sigmoid, 4 silu,
+ * 5 1/sqrt as two correctly rounded operations; 6 the CUDA library's expf, for comparison only). */
+int rk_math_probe(int fn, const float* x, float* y, int n, void* stream);
 /* Greedy argmax of forward_token (src/qwythos.cpp:1803-1811) / argmax_kernel (:70-84): out[j] receives
  * the index of the largest of x[j*n .. j*n+n) (lowest index on ties). */
 int rk_argmax(const float* x, int n, int ncols, int* out, void* stream);
@@ -178,7 +182,7 @@ int rk_store_kv_f16(uint16_t* kcache, uint16_t* vcache, const float* k, const fl
  * (0 <= c < ncols) of q [ncols][n_head][hd] attends tokens 0..*pos + c (device) and writes
  * o [ncols][n_head][hd] = softmax(q . K^T * scale) V. The chunk partials go to `scratch` (caller-owned,
  * like the reference's `scores` buffer), at least rk_gqa_scratch_bytes(n_head, ncols, max_ctx) bytes,
- * max_ctx > *pos + ncols - 1. hd == 256, n_head % n_kv == 0, 1 <= ncols <= 2. */
+ * max_ctx > *pos + ncols - 1. hd == 256, n_head == 4 * n_kv, 1 <= ncols <= 2. */
 size_t rk_gqa_scratch_bytes(int n_head, int ncols, int max_ctx);
 int rk_gqa_decode_f16(const float* q, const uint16_t* kcache, const uint16_t* vcache, float* o, int n_head,
                       int n_kv, int hd, int ncols, const int* pos, int max_ctx, float scale, void* scratch,
@@ -284,6 +288,18 @@ int rk_engine_generate(rk_engine* e, const int* prompt, int n_prompt, int n_gen,
  * positions pos, pos+1: updates the caches and states like a decode step and copies the logits
  * (ncols x n_vocab floats) and argmax ids to the host (either may be NULL). */
 int rk_engine_step(rk_engine* e, const int* tokens, int ncols, int pos, float* logits, int* argmax);
+/* The MTP draft alone (draft_predict, src/qwythos.cpp:1316-1406): the nextn block at draft position pos
+ * (it writes the draft KV slot pos) on [enorm(emb(tok)) | hnorm(h)], h = the final-normed hidden of the
+ * last trunk pass's column 0, or h = 0 when h_zero != 0 (the slot-0 seed, src/qwythos.cpp:2955-2958; this
+ * also zeroes the saved hidden), then the shared head norm, the lm_head and argmax. Copies the draft
+ * logits (n_vocab floats, may be NULL) and the argmax id (may be NULL). A parity hook for the draft. */
+int rk_engine_draft_step(rk_engine* e, int tok, int pos, int h_zero, float* logits, int* argmax);
+/* Test hook, no reference counterpart: forced MTP draft candidates by position. tokens[p] (p < n), when
+ * >= 0, replaces the draft's own prediction as the candidate verified at position p; -1 keeps the draft's.
+ * n == 0 clears every entry. The emitted stream does not depend on the candidate (acceptance is exact),
+ * so this drives the accept branch with known tokens (e.g. a previous greedy stream) to test it, the way
+ * the reference's QWYTHOS_NOACCEPT knob (src/qwythos.cpp:3210) drives the reject branch. Synchronous. */
+int rk_engine_force_candidates(rk_engine* e, const int* tokens, int n);
 /* Serving session (the reference's --serve loop, src/qwythos.cpp:2593-2812): the engine keeps a context
  * across runs. rk_engine_session_reset clears it (op "reset"; same as rk_engine_reset). A run (op "run")
  * ingests the previous run's last emitted token (still pending) and then tokens[0..n_tokens), all but the
@@ -292,7 +308,11 @@ int rk_engine_step(rk_engine* e, const int* tokens, int ncols, int pos, float* l
  * first run after a reset seeds the draft's slot 0. Every emitted token except a final eos_id belongs to the
  * context afterwards. first_logits (n_vocab floats, may be NULL) receives the logits of the first generated
  * token. RK_ERANGE when the context cannot hold the run ("context full; send op reset"). rk_engine_generate
- * leaves a session positioned after its generation. */
+ * leaves a session positioned after its generation. The draft's own cache is filled only by MTP runs: an
+ * MTP run after non-MTP runs drafts from an empty cache for the earlier positions, which lowers its
+ * acceptance (never its tokens). A run that fails after it has started (a CUDA error, a device-side wait
+ * that gave up) leaves the caches and states partly advanced, so every later run returns RK_ECUDA until
+ * rk_engine_session_reset (or rk_engine_reset). */
 int rk_engine_session_reset(rk_engine* e);
 int rk_engine_session_run(rk_engine* e, const int* tokens, int n_tokens, int n_gen, int use_mtp, int eos_id,
                           int* out_ids, int* n_out, float* first_logits, rk_gen_stats* stats);

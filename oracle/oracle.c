@@ -21,9 +21,9 @@
  *     (or_rms_norm_rows, or_rope_*). PARITY UNPINNED for these rules.
  *
  * Arithmetic conventions: every fp32 operation is written explicitly (fmaf where the reference's
- * compiler contracts a multiply-add in the reference expression); transcendental functions use the C
- * library (expf, log1pf, sqrtf), so kernel outputs that pass through them are compared within the
- * stated tolerance, while integer sums and Q8_1 bytes of identical fp32 inputs are bit-exact.
+ * compiler contracts a multiply-add in the reference expression; -ffp-contract=off everywhere else);
+ * exp, log1p and 1/sqrt are the exactly specified sequences below (or_expf, or_log1pf, 1/sqrtf), the
+ * same sequences the CUDA kernels run, so outputs that pass through them are bit-exact too.
  */
 #include "oracle.h"
 
@@ -98,6 +98,95 @@ void or_f32_to_f16_n(const float* x, uint16_t* y, size_t n) {
 }
 void or_f16_to_f32_n(const uint16_t* x, float* y, size_t n) {
     for (size_t i = 0; i < n; ++i) y[i] = or_f16_to_f32(x[i]);
+}
+
+/* ------------------------------------------------------------------------------------------------ */
+/* Transcendentals with an exactly specified operation sequence (the CUDA kernels write the same      */
+/* sequence, rapier_b200/csrc/common.cuh): every step is one IEEE-754 fp32 operation rounded to        */
+/* nearest even (fmaf is the correctly rounded fused multiply-add), so both sides get the same bits.  */
+/* The reference uses the vendor library (expf / __expf / log1pf / rsqrtf), whose last ulp is not      */
+/* specified; these stay within ~1 ulp of the true value (tests compare with float64).               */
+/*                                                                                                    */
+/* or_expf: Cody-Waite reduction + Taylor polynomial (Cody & Waite, "Software Manual for the          */
+/* Elementary Functions", 1980, ch. 6): n = rint(x log2 e); r = x - n C1 - n C2, C1 = 355/512 (exact    */
+/* product), C2 = ln2 - C1; exp(r) = sum_{k<=7} r^k/k! by Horner with fmaf; times 2^(n/2) 2^(n - n/2).   */
+/* or_logf: x = m 2^e, m in [sqrt(1/2), sqrt(2)); s = (m-1)/(m+1); log m = 2s(1 + s^2/3 + ... + s^10/11).  */
+/* or_log1pf: u = 1 + t; t if u == 1 else log(u) t / (u - 1) (Goldberg 1991, Theorem 4).                */
+/* ------------------------------------------------------------------------------------------------ */
+static float f_from_bits(uint32_t b) {
+    float f;
+    memcpy(&f, &b, 4);
+    return f;
+}
+static uint32_t f_bits(float f) {
+    uint32_t b;
+    memcpy(&b, &f, 4);
+    return b;
+}
+static float or_pow2i(int e) { return f_from_bits((uint32_t) (e + 127) << 23); }
+float or_expf(float x) {
+    if (x != x) return x;
+    if (x > 88.8f) return f_from_bits(0x7f800000u);
+    if (x < -104.0f) return 0.0f;
+    const float n = rintf(x * 1.44269502f);
+    float r = fmaf(-n, 0.693359375f, x);
+    r = fmaf(-n, -2.12194440e-4f, r);
+    float p = 1.98412698e-4f;
+    p = fmaf(p, r, 1.38888889e-3f);
+    p = fmaf(p, r, 8.33333333e-3f);
+    p = fmaf(p, r, 4.16666667e-2f);
+    p = fmaf(p, r, 1.66666667e-1f);
+    p = fmaf(p, r, 0.5f);
+    p = fmaf(p, r, 1.0f);
+    p = fmaf(p, r, 1.0f);
+    const int ni = (int) n, n1 = ni / 2;
+    return (p * or_pow2i(n1)) * or_pow2i(ni - n1);
+}
+float or_logf(float x) {
+    int bias = 0;
+    if (x < 1.17549435e-38f) {
+        x = x * 16777216.0f;
+        bias = -24;
+    }
+    const uint32_t bits = f_bits(x);
+    int e = (int) ((bits >> 23) & 0xffu) - 127;
+    float m = f_from_bits((bits & 0x007fffffu) | 0x3f800000u);
+    if (m > 1.41421354f) {
+        m = m * 0.5f;
+        e += 1;
+    }
+    e += bias;
+    const float s = (m - 1.0f) / (m + 1.0f);
+    const float s2 = s * s;
+    float q = 9.09090909e-2f;
+    q = fmaf(q, s2, 1.11111111e-1f);
+    q = fmaf(q, s2, 1.42857143e-1f);
+    q = fmaf(q, s2, 2.00000000e-1f);
+    q = fmaf(q, s2, 3.33333333e-1f);
+    const float lm = fmaf((2.0f * s) * s2, q, 2.0f * s);
+    const float fe = (float) e;
+    return fmaf(fe, 0.693359375f, fmaf(fe, -2.12194440e-4f, lm));
+}
+float or_log1pf(float t) {
+    if (t != t || t == f_from_bits(0x7f800000u)) return t;
+    const float u = 1.0f + t;
+    if (u == 1.0f) return t;
+    return (or_logf(u) * t) / (u - 1.0f);
+}
+static float or_rsqrtf(float x) { return 1.0f / sqrtf(x); }
+static float or_sigmoidf(float x) { return 1.0f / (1.0f + or_expf(-x)); }
+static float or_siluf(float x) { return x / (1.0f + or_expf(-x)); }
+void or_math_n(int fn, const float* x, float* y, size_t n) {
+    for (size_t i = 0; i < n; ++i) {
+        switch (fn) {
+            case 0: y[i] = or_expf(x[i]); break;
+            case 1: y[i] = or_logf(x[i]); break;
+            case 2: y[i] = or_log1pf(x[i]); break;
+            case 3: y[i] = or_sigmoidf(x[i]); break;
+            case 4: y[i] = or_siluf(x[i]); break;
+            default: y[i] = or_rsqrtf(x[i]); break;
+        }
+    }
 }
 
 /* ------------------------------------------------------------------------------------------------ */
@@ -790,7 +879,7 @@ void or_swiglu_q8_1(const float* up, const float* gate, void* y, int n) {
     for (int b = 0; b < n / 32; ++b) {
         for (int l = 0; l < 32; ++l) {
             const float g = gate[32 * b + l];
-            v[l] = g / (1.0f + expf(-g)) * up[32 * b + l];
+            v[l] = or_siluf(g) * up[32 * b + l];
         }
         or_q8_1_block(v, (uint8_t*) y + (size_t) b * 36);
     }
@@ -799,7 +888,7 @@ void or_swiglu_q8_1(const float* up, const float* gate, void* y, int n) {
 void or_sigmul_q8_1(const float* o, const float* g, void* y, int n) {
     float v[32];
     for (int b = 0; b < n / 32; ++b) {
-        for (int l = 0; l < 32; ++l) v[l] = o[32 * b + l] * (1.0f / (1.0f + expf(-g[32 * b + l])));
+        for (int l = 0; l < 32; ++l) v[l] = o[32 * b + l] * or_sigmoidf(g[32 * b + l]);
         or_q8_1_block(v, (uint8_t*) y + (size_t) b * 36);
     }
 }
@@ -807,9 +896,9 @@ void or_sigmul_q8_1(const float* o, const float* g, void* y, int n) {
  * passes v through above 20. */
 void or_beta_gate(float* beta, const float* alpha, const float* dt, const float* ssm_a, float* gate, int n) {
     for (int i = 0; i < n; ++i) {
-        beta[i] = 1.0f / (1.0f + expf(-beta[i]));
+        beta[i] = or_sigmoidf(beta[i]);
         const float v = alpha[i] + dt[i];
-        gate[i] = (v > 20.0f ? v : log1pf(expf(v))) * ssm_a[i];
+        gate[i] = (v > 20.0f ? v : or_log1pf(or_expf(v))) * ssm_a[i];
     }
 }
 /* rms_norm_weighted (Strata, out of tree; called at src/qwythos.cpp:1206-1207): written definition —
@@ -845,7 +934,7 @@ void or_gdn_conv_l2(float* ring, const float* qkv, const float* conv_w, float* h
         sum = fmaf(v1, w[1], sum);
         sum = fmaf(v2, w[2], sum);
         sum = fmaf(x, w[3], sum);
-        y[c] = sum / (1.0f + expf(-sum));
+        y[c] = or_siluf(sum);
     }
     for (int c = 0; c < channels; ++c) ring[(size_t) c * 4 + (pos & 3)] = qkv[c];
     for (int hh = 0; hh < channels / 128; ++hh) {
@@ -878,7 +967,7 @@ void or_gdn_step_norm_silu_q8(float* state, const float* q, const float* k, cons
         const int qh = head % h_k;
         const float* sk = k + (size_t) qh * S;
         const float* sq = q + (size_t) qh * S;
-        const float g = expf(gate[head]);
+        const float g = or_expf(gate[head]);
         float oc[128];
         for (int col = 0; col < S; ++col) {
             float kv[4], o[4];
@@ -915,7 +1004,7 @@ void or_gdn_step_norm_silu_q8(float* state, const float* q, const float* k, cons
         float yv[128];
         for (int col = 0; col < S; ++col) {
             const float zz = z[(size_t) head * S + col];
-            const float gate_z = zz / (1.0f + expf(-zz));
+            const float gate_z = or_siluf(zz);
             yv[col] = oc[col] * scale * gamma[col] * gate_z;
             y[(size_t) head * S + col] = yv[col];
         }
@@ -962,7 +1051,7 @@ void or_split_qg(const float* qg, float* q, float* g, int heads, int hd) {
             g[(size_t) h * hd + i] = qg[(size_t) h * 2 * hd + hd + i];
         }
 }
-/* store_kv2_kernel :340-345, with an fp16 cache: cache[pos * n + i]. */
+/* store_kv2_kernel :340-345, with an fp16 cache (the flash-decode workload's KV type): cache[pos * n + i]. */
 void or_store_kv_f16(uint16_t* kcache, uint16_t* vcache, const float* k, const float* v, int pos, int n) {
     for (int i = 0; i < n; ++i) {
         kcache[(size_t) pos * n + i] = or_f32_to_f16(k[i]);
@@ -991,7 +1080,7 @@ void or_gqa_decode_f16(const float* q, const uint16_t* kc, const uint16_t* vc, f
         }
         double sum = 0.0;
         for (int t = 0; t < n_tok; ++t) {
-            sc[t] = expf(sc[t] - mx);
+            sc[t] = or_expf(sc[t] - mx);
             sum += sc[t];
         }
         const float inv = (float) (1.0 / sum);
@@ -1002,6 +1091,169 @@ void or_gqa_decode_f16(const float* q, const uint16_t* kc, const uint16_t* vc, f
         }
     }
     free(sc);
+}
+
+/* The same attention step in the summation order of the decode engine's flash-decode kernels, so
+ * the engine's outputs can be compared bit for bit (the reference's own order is a HIP block reduction
+ * that no other machine reproduces; or_gqa_decode_f16 above restates it in float64, and the tests check
+ * that both agree within the fp32 tolerance). Per column c (position pos + c) of proj [c][proj_stride]
+ * = [n_head x (q 256 | gate 256) | k n_kv x 256 | v n_kv x 256]:
+ *  - per head vector: ss = sum over j = 0..7 (in order) of the 32-lane xor-tree sum of x[32j + l]^2;
+ *    inv = 1/sqrt(ss/256 + eps); x = (x * inv) * w; NEOX RoPE over the first n_rot dims (the table's
+ *    cos / sin at pos + c); k and v stored as fp16 at pos + c (caches [max_ctx][n_kv][256]);
+ *  - chunks of chunk_len tokens; chunk ch covers [ch*len, min(ch*len + len, pos + ncols)), tokens
+ *    after pos + c scored -inf; score = xor-tree sum over lanes l of the fma chain over dims 8l..8l+7,
+ *    times scale; m = max; e_t = exp(s_t - m); l = xor-tree sum over lanes of each lane's sum of e_t for
+ *    t = lane, lane + 32, ...; o = sum over warps w = 0..7 in order of the fma chain over tokens
+ *    [32w, 32w + 32) of e_t * v_t;
+ *  - combine over the (pos + c)/len + 1 chunks: warp w takes chunks [w n/8, (w+1) n/8), m_w = their max,
+ *    fma chains of exp(m_k - m_w) * o_k and * l_k; then over the warps with chunks, in order, fma chains
+ *    of exp(m_w - M); o = num / den;
+ *  - q8 (may be NULL): the Q8_1 blocks of o * sigmoid(gate) per column. */
+static void attn_norm_rope(float* x, const float* w, const float* rope, int n_rot, int p, float eps) {
+    float ss = 0.0f;
+    for (int j = 0; j < 8; ++j) {
+        float sq[32];
+        for (int l = 0; l < 32; ++l) sq[l] = x[32 * j + l] * x[32 * j + l];
+        const float pj = or_xor_sum32(sq);
+        ss = j == 0 ? pj : ss + pj;
+    }
+    const float inv = 1.0f / sqrtf(ss / 256.0f + eps);
+    float r[256];
+    for (int d = 0; d < 256; ++d) r[d] = (x[d] * inv) * w[d];
+    const int half = n_rot / 2;
+    for (int d = 0; d < 256; ++d) {
+        if (d < n_rot) {
+            const int i = d < half ? d : d - half;
+            const float cs = rope[((size_t) p * half + i) * 2 + 0];
+            const float sn = rope[((size_t) p * half + i) * 2 + 1];
+            const float x0 = r[i], x1 = r[i + half];
+            x[d] = d < half ? x0 * cs - x1 * sn : x0 * sn + x1 * cs;
+        } else {
+            x[d] = r[d];
+        }
+    }
+}
+void or_attn_flash_f16(const float* proj, int ncols, int proj_stride, const float* qn, const float* kn,
+                       const float* rope, int n_rot, int n_head, int n_kv, uint16_t* kc, uint16_t* vc, int pos,
+                       int chunk_len, float eps, float scale, float* o, void* q8) {
+    const int HD = 256, G = n_head / n_kv;
+    float* qs = (float*) malloc(sizeof(float) * (size_t) ncols * n_head * HD);
+    for (int c = 0; c < ncols; ++c) {
+        const float* col = proj + (size_t) c * proj_stride;
+        for (int h = 0; h < n_head; ++h) {
+            float* x = qs + ((size_t) c * n_head + h) * HD;
+            memcpy(x, col + (size_t) h * 2 * HD, sizeof(float) * HD);
+            attn_norm_rope(x, qn, rope, n_rot, pos + c, eps);
+        }
+        for (int kv = 0; kv < n_kv; ++kv) {
+            float k[256];
+            memcpy(k, col + (size_t) n_head * 2 * HD + (size_t) kv * HD, sizeof k);
+            attn_norm_rope(k, kn, rope, n_rot, pos + c, eps);
+            const float* v = col + (size_t) n_head * 2 * HD + (size_t) n_kv * HD + (size_t) kv * HD;
+            for (int d = 0; d < HD; ++d) {
+                kc[((size_t) (pos + c) * n_kv + kv) * HD + d] = or_f32_to_f16(k[d]);
+                vc[((size_t) (pos + c) * n_kv + kv) * HD + d] = or_f32_to_f16(v[d]);
+            }
+        }
+    }
+    const int len = chunk_len, last = pos + ncols;
+#pragma omp parallel for collapse(2) schedule(dynamic)
+    for (int c = 0; c < ncols; ++c)
+        for (int h = 0; h < n_head; ++h) {
+            const int kv = h / G;
+            const float* q = qs + ((size_t) c * n_head + h) * HD;
+            const int n = (pos + c) / len + 1;
+            float* cm = (float*) malloc(sizeof(float) * (size_t) n * (2 + HD));
+            float* cl = cm + n;
+            float* co = cl + n;
+            float sc[256];
+            for (int ch = 0; ch < n; ++ch) {
+                const int t0 = ch * len;
+                const int ntok = (t0 + len < last ? t0 + len : last) - t0;
+                float m = -INFINITY;
+                for (int t = 0; t < ntok; ++t) {
+                    if (t0 + t > pos + c) {
+                        sc[t] = -INFINITY;
+                        continue;
+                    }
+                    const uint16_t* kk = kc + ((size_t) (t0 + t) * n_kv + kv) * HD;
+                    float lanes[32];
+                    for (int l = 0; l < 32; ++l) {
+                        float d = 0.0f;
+                        for (int i = 0; i < 8; ++i) d = fmaf(q[8 * l + i], or_f16_to_f32(kk[8 * l + i]), d);
+                        lanes[l] = d;
+                    }
+                    sc[t] = or_xor_sum32(lanes) * scale;
+                    m = fmaxf(m, sc[t]);
+                }
+                float lane_l[32];
+                for (int l = 0; l < 32; ++l) lane_l[l] = 0.0f;
+                for (int t = 0; t < ntok; ++t) {
+                    const float e = m == -INFINITY ? 0.0f : or_expf(sc[t] - m);
+                    sc[t] = e;
+                    lane_l[t & 31] = lane_l[t & 31] + e;
+                }
+                cm[ch] = m;
+                cl[ch] = or_xor_sum32(lane_l);
+                for (int d = 0; d < HD; ++d) {
+                    float acc = 0.0f;
+                    for (int w = 0; w < 8; ++w) {
+                        float a = 0.0f;
+                        for (int t = 32 * w; t < 32 * w + 32 && t < ntok; ++t) {
+                            const float vv = or_f16_to_f32(vc[((size_t) (t0 + t) * n_kv + kv) * HD + d]);
+                            a = fmaf(sc[t], vv, a);
+                        }
+                        acc = w == 0 ? a : acc + a;
+                    }
+                    co[(size_t) ch * HD + d] = acc;
+                }
+            }
+            float wm[8], wden[8];
+            float* wnum = (float*) malloc(sizeof(float) * 8 * HD);
+            for (int w = 0; w < 8; ++w) {
+                const int k0 = w * n / 8, k1 = (w + 1) * n / 8;
+                float mw = -INFINITY;
+                for (int k = k0; k < k1; ++k) mw = fmaxf(mw, cm[k]);
+                float den = 0.0f;
+                for (int d = 0; d < HD; ++d) wnum[w * HD + d] = 0.0f;
+                for (int k = k0; k < k1; ++k) {
+                    const float wk = or_expf(cm[k] - mw);
+                    for (int d = 0; d < HD; ++d) wnum[w * HD + d] = fmaf(wk, co[(size_t) k * HD + d], wnum[w * HD + d]);
+                    den = fmaf(wk, cl[k], den);
+                }
+                wm[w] = k1 > k0 ? mw : -INFINITY;
+                wden[w] = den;
+            }
+            float M = -INFINITY;
+            for (int w = 0; w < 8; ++w) M = fmaxf(M, wm[w]);
+            for (int d = 0; d < HD; ++d) {
+                float nu = 0.0f, de = 0.0f;
+                for (int w = 0; w < 8; ++w)
+                    if (wm[w] != -INFINITY) {
+                        const float sw = or_expf(wm[w] - M);
+                        nu = fmaf(sw, wnum[w * HD + d], nu);
+                        de = fmaf(sw, wden[w], de);
+                    }
+                o[((size_t) c * n_head + h) * HD + d] = nu / de;
+            }
+            free(wnum);
+            free(cm);
+        }
+    if (q8)
+        for (int c = 0; c < ncols; ++c) {
+            const float* col = proj + (size_t) c * proj_stride;
+            for (int h = 0; h < n_head; ++h)
+                for (int b = 0; b < HD / 32; ++b) {
+                    float v[32];
+                    for (int l = 0; l < 32; ++l) {
+                        const int d = 32 * b + l;
+                        v[l] = o[((size_t) c * n_head + h) * HD + d] * or_sigmoidf(col[(size_t) h * 2 * HD + HD + d]);
+                    }
+                    or_q8_1_block(v, (uint8_t*) q8 + (((size_t) c * n_head + h) * (HD / 32) + b) * 36);
+                }
+        }
+    free(qs);
 }
 
 /* Host argmax of forward_token (src/qwythos.cpp:1803-1811): strict greater, lowest index wins ties. */

@@ -84,9 +84,17 @@ void or_gqa_decode_f16(const float* q, const uint16_t* kc, const uint16_t* vc, f
                        int hd, int n_tok, float scale);
 
 /* ---- greedy ---- */
+void or_attn_flash_f16(const float* proj, int ncols, int proj_stride, const float* qn, const float* kn,
+                       const float* rope, int n_rot, int n_head, int n_kv, uint16_t* kc, uint16_t* vc, int pos,
+                       int chunk_len, float eps, float scale, float* o, void* q8);
 int or_argmax(const float* x, int n);
 
 /* ---- timing helper for the CPU baseline ---- */
+/* The exactly specified transcendentals (fn 0 exp, 1 log, 2 log1p, 3 sigmoid, 4 silu, 5 1/sqrt). */
+float or_expf(float x);
+float or_logf(float x);
+float or_log1pf(float t);
+void or_math_n(int fn, const float* x, float* y, size_t n);
 int or_num_threads(void);
 
 #ifdef __cplusplus

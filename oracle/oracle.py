@@ -82,6 +82,9 @@ def _declare(L):
         "or_store_kv_f16": (None, [_u16p, _u16p, _f32p, _f32p, _i, _i]),
         "or_gqa_decode_f16": (None, [_f32p, _u16p, _u16p, _f32p, _i, _i, _i, _i, _f]),
         "or_argmax": (_i, [_f32p, _i]),
+        "or_math_n": (None, [_i, _f32p, _f32p, _sz]),
+        "or_attn_flash_f16": (None, [_f32p, _i, _i, _f32p, _f32p, _f32p, _i, _i, _i, _u16p, _u16p, _i, _i, _f, _f,
+                                     _f32p, _u8p]),
         "or_num_threads": (_i, []),
     }
     for name, (res, args) in sig.items():
@@ -319,6 +322,29 @@ def gqa_decode_f16(q, kc, vc, n_head, n_kv, hd, n_tok, scale):
     return o
 
 
+def attn_chunk_len(max_ctx: int) -> int:
+    """Tokens per flash-decode chunk of a cache of max_ctx positions: the smallest of 32, 64, 128, 256 that
+    splits the cache into at most 512 chunks (the decode engine's rule)."""
+    n = 32
+    while (max_ctx + n - 1) // n > 512 and n < 256:
+        n *= 2
+    return n
+
+
+def attn_flash_f16(proj, ncols, proj_stride, qn, kn, rope, n_rot, n_head, n_kv, kc, vc, pos, chunk_len, eps,
+                   scale=0.0625):
+    """The attention step in the decode engine's flash-decode order (q/k norm, RoPE, fp16 K/V store at
+    pos .. pos+ncols-1 into kc / vc [max_ctx][n_kv][256] in place, chunked softmax, combine). Returns
+    (o [ncols][n_head][256], Q8_1 of o * sigmoid(gate) per column)."""
+    assert kc.dtype == np.uint16 and kc.flags.c_contiguous and vc.dtype == np.uint16 and vc.flags.c_contiguous
+    o = np.empty(ncols * n_head * 256, np.float32)
+    q8 = np.empty(ncols * n_head * 8 * 36, np.uint8)
+    lib().or_attn_flash_f16(_c(proj, np.float32), ncols, proj_stride, _c(qn, np.float32), _c(kn, np.float32),
+                            _c(rope, np.float32), n_rot, n_head, n_kv, kc.reshape(-1), vc.reshape(-1), pos, chunk_len,
+                            eps, scale, o, q8)
+    return o, q8
+
+
 def argmax(x):
     x = _c(x, np.float32)
     return lib().or_argmax(x, x.size)
@@ -326,3 +352,14 @@ def argmax(x):
 
 def num_threads():
     return lib().or_num_threads()
+
+
+# ---- exactly specified transcendentals (the sequences the CUDA kernels run) ----
+MATH_FNS = {"exp": 0, "log": 1, "log1p": 2, "sigmoid": 3, "silu": 4, "rsqrt": 5}
+
+
+def math(fn: str, x):
+    x = _c(x, np.float32)
+    y = np.empty_like(x)
+    lib().or_math_n(MATH_FNS[fn], x.ravel(), y.ravel(), x.size)
+    return y

@@ -79,6 +79,7 @@ SIGNATURES = {
     "rk_beta_gate": (i32, [vp, vp, vp, vp, vp, i32, vp]),
     "rk_rms_norm_rows": (i32, [vp, vp, i32, i32, f32, vp]),
     "rk_argmax": (i32, [vp, i32, i32, vp, vp]),
+    "rk_math_probe": (i32, [i32, vp, vp, i32, vp]),
     "rk_gdn_conv_l2": (i32, [vp, vp, vp, vp, i32, i32, f32, vp, vp]),
     "rk_gdn_step_norm_silu_q8": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, f32, vp, vp, i32, i32, vp]),
     "rk_split_qg": (i32, [vp, vp, vp, i32, i32, vp]),
@@ -94,6 +95,8 @@ SIGNATURES = {
     "rk_engine_reset": (i32, [vp]),
     "rk_engine_generate": (i32, [vp, C.POINTER(C.c_int), i32, i32, i32, C.POINTER(C.c_int), C.POINTER(GenStats)]),
     "rk_engine_step": (i32, [vp, C.POINTER(C.c_int), i32, i32, vp, C.POINTER(C.c_int)]),
+    "rk_engine_draft_step": (i32, [vp, i32, i32, i32, vp, C.POINTER(C.c_int)]),
+    "rk_engine_force_candidates": (i32, [vp, C.POINTER(C.c_int), i32]),
     "rk_engine_session_reset": (i32, [vp]),
     "rk_engine_session_run": (i32, [vp, C.POINTER(C.c_int), i32, i32, i32, i32, C.POINTER(C.c_int),
                                     C.POINTER(C.c_int), vp, C.POINTER(GenStats)]),

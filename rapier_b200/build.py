@@ -21,7 +21,9 @@ LIB = os.path.join(PKG, "librapier_b200.so")
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
+# --fmad=false: device code never fuses a multiply and an add unless it says so (__fmaf_rn), the same rule as
+# the CPU oracle's -ffp-contract=off, so both compute every fp32 expression with the same roundings.
+FLAGS = ["-O3", "-lineinfo", "-std=c++17", "--fmad=false", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
          "-Xcompiler", "-ffp-contract=off",
          "--expt-relaxed-constexpr", "-I" + os.path.join(ROOT, "include")]
 

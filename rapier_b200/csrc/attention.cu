@@ -140,7 +140,7 @@ __global__ void __launch_bounds__(256) gqa_chunk_kernel(const float* __restrict_
         m = warp_max(m);
         float l = 0.0f;
         for (int t = lane; t < ntok; t += 32) {
-            const float e = m == -INFINITY ? 0.0f : expf(__fsub_rn(sc[g][c][t], m));  // masked: exp(-inf) = 0
+            const float e = m == -INFINITY ? 0.0f : rk_expf(__fsub_rn(sc[g][c][t], m));  // masked: exp(-inf) = 0
             sc[g][c][t] = e;
             l = __fadd_rn(l, e);
         }
@@ -194,7 +194,7 @@ __global__ void __launch_bounds__(256) gqa_combine_kernel(const float* __restric
     for (int k = 0; k < nchunks; ++k) M = fmaxf(M, ml[2 * k]);
     float num = 0.0f, den = 0.0f;
     for (int k = 0; k < nchunks; ++k) {
-        const float w = expf(__fsub_rn(ml[2 * k], M));
+        const float w = rk_expf(__fsub_rn(ml[2 * k], M));
         num = __fmaf_rn(w, po[(size_t) k * kHd + d], num);
         den = __fmaf_rn(w, ml[2 * k + 1], den);
     }

@@ -81,6 +81,87 @@ __device__ __forceinline__ void warp_reduce_scatter(float (&v)[M], int lane) {
 }
 
 // ---------------------------------------------------------------------------------------------
+// Transcendentals with an exactly specified operation sequence. Every step is one IEEE-754 fp32
+// operation rounded to nearest even (or an exact bit manipulation), so the CPU oracle, which writes the
+// same sequence in C, gets the same bits. The reference computes these with the vendor library's expf /
+// __expf / log1pf / rsqrtf, whose last-ulp behaviour is not specified; these stay within ~1 ulp of the
+// true value (tests compare with float64).
+//
+// rk_expf: Cody-Waite argument reduction and a Taylor polynomial (W. J. Cody, W. Waite, "Software
+// Manual for the Elementary Functions", 1980, ch. 6): n = rint(x * log2 e); r = x - n * C1 - n * C2
+// with C1 = 355/512 (9 significant bits, so n * C1 is exact inside the fma) and C2 = ln 2 - C1;
+// exp(r) = sum_{k<=7} r^k / k! by Horner's rule with fused multiply-adds (|r| <= 0.35: the first
+// omitted term is below 6e-9 relative); the result is p * 2^n, applied as two exact power-of-two
+// factors 2^(n/2) and 2^(n - n/2) so that overflow gives inf and underflow rounds once.
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ float rk_pow2i(int e) { return __int_as_float((e + 127) << 23); }  // -126 <= e <= 127
+__device__ __forceinline__ float rk_expf(float x) {
+    if (x != x) return x;
+    if (x > 88.8f) return __int_as_float(0x7f800000);
+    if (x < -104.0f) return 0.0f;
+    const float n = rintf(__fmul_rn(x, 1.44269502f));
+    float r = __fmaf_rn(-n, 0.693359375f, x);
+    r = __fmaf_rn(-n, -2.12194440e-4f, r);
+    float p = 1.98412698e-4f;
+    p = __fmaf_rn(p, r, 1.38888889e-3f);
+    p = __fmaf_rn(p, r, 8.33333333e-3f);
+    p = __fmaf_rn(p, r, 4.16666667e-2f);
+    p = __fmaf_rn(p, r, 1.66666667e-1f);
+    p = __fmaf_rn(p, r, 0.5f);
+    p = __fmaf_rn(p, r, 1.0f);
+    p = __fmaf_rn(p, r, 1.0f);
+    const int ni = (int) n, n1 = ni / 2;
+    return __fmul_rn(__fmul_rn(p, rk_pow2i(n1)), rk_pow2i(ni - n1));
+}
+// rk_logf for x > 0 finite: x = m * 2^e with m in [sqrt(1/2), sqrt(2)); s = (m - 1) / (m + 1);
+// log m = 2 s (1 + s^2/3 + s^4/5 + ... + s^10/11) (the atanh series, |s| <= 0.172); log x = e * ln2 + log m
+// with ln 2 split in two parts. Subnormal x is scaled by 2^24 first.
+__device__ __forceinline__ float rk_logf(float x) {
+    int bias = 0;
+    if (x < 1.17549435e-38f) {
+        x = __fmul_rn(x, 16777216.0f);
+        bias = -24;
+    }
+    const int bits = __float_as_int(x);
+    int e = ((bits >> 23) & 0xff) - 127;
+    float m = __int_as_float((bits & 0x007fffff) | 0x3f800000);
+    if (m > 1.41421354f) {
+        m = __fmul_rn(m, 0.5f);
+        e += 1;
+    }
+    e += bias;
+    const float s = __fdiv_rn(__fsub_rn(m, 1.0f), __fadd_rn(m, 1.0f));
+    const float s2 = __fmul_rn(s, s);
+    float q = 9.09090909e-2f;
+    q = __fmaf_rn(q, s2, 1.11111111e-1f);
+    q = __fmaf_rn(q, s2, 1.42857143e-1f);
+    q = __fmaf_rn(q, s2, 2.00000000e-1f);
+    q = __fmaf_rn(q, s2, 3.33333333e-1f);
+    const float lm = __fmaf_rn(__fmul_rn(__fmul_rn(2.0f, s), s2), q, __fmul_rn(2.0f, s));
+    const float fe = (float) e;
+    return __fmaf_rn(fe, 0.693359375f, __fmaf_rn(fe, -2.12194440e-4f, lm));
+}
+// rk_log1pf for t >= 0 (softplus only feeds it exp values): u = 1 + t; t when u == 1, else
+// log(u) * t / (u - 1), which cancels the rounding error of 1 + t (D. Goldberg, "What every computer
+// scientist should know about floating-point arithmetic", 1991, Theorem 4).
+__device__ __forceinline__ float rk_log1pf(float t) {
+    if (t != t || t == __int_as_float(0x7f800000)) return t;
+    const float u = __fadd_rn(1.0f, t);
+    if (u == 1.0f) return t;
+    return __fdiv_rn(__fmul_rn(rk_logf(u), t), __fsub_rn(u, 1.0f));
+}
+// 1 / sqrt(x), two correctly rounded operations (the reference uses rsqrtf, an approximation).
+__device__ __forceinline__ float rk_rsqrtf(float x) { return __fdiv_rn(1.0f, __fsqrt_rn(x)); }
+__device__ __forceinline__ float rk_sigmoidf(float x) { return __fdiv_rn(1.0f, __fadd_rn(1.0f, rk_expf(-x))); }
+__device__ __forceinline__ float rk_siluf(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, rk_expf(-x))); }
+// The GDN decay input softplus(alpha + dt) * ssm_a, softplus passing v through above 20 (beta_gate_kernel,
+// src/qwythos.cpp:707-715).
+__device__ __forceinline__ float rk_softplus_gate(float alpha, float dt, float ssm_a) {
+    const float v = __fadd_rn(alpha, dt);
+    return __fmul_rn(v > 20.0f ? v : rk_log1pf(rk_expf(v)), ssm_a);
+}
+
+// ---------------------------------------------------------------------------------------------
 // Q8_1 block rules (the reference's q8_1_finite / q8_1_quant / q8_1_ds are out of its tree; this is
 // the written definition the CPU oracle restates):
 //   d = amax / 127, clamped to 65504 when NaN, infinite or above the fp16 maximum;

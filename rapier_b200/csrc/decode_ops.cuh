@@ -97,6 +97,8 @@ struct CtrlArgs {
     int kind;
     int* out;
     int max_out;
+    const int* force;  // forced draft candidate per position (-1: the draft's own argmax); a test hook
+    int n_force;
 };
 struct XArgmaxArgs {  // tensor parallelism: the global argmax over the ranks' vocabulary shards
     const XchDesc* xch;
@@ -166,11 +168,10 @@ inline size_t op_scratch_bytes(int nc, int H) {
 // ------------------------------------------------------------------------------------------------
 // Shared helpers
 // ------------------------------------------------------------------------------------------------
-__device__ __forceinline__ float silu_dev(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x))); }
-__device__ __forceinline__ float sigmoid_dev(float x) { return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x))); }
+__device__ __forceinline__ float silu_dev(float x) { return rk_siluf(x); }
+__device__ __forceinline__ float sigmoid_dev(float x) { return rk_sigmoidf(x); }
 __device__ __forceinline__ float softplus_gate_dev(float alpha, float dt, float ssm_a) {
-    const float v = __fadd_rn(alpha, dt);
-    return __fmul_rn(v > 20.0f ? v : log1pf(expf(v)), ssm_a);
+    return rk_softplus_gate(alpha, dt, ssm_a);
 }
 // conv taps oldest first: sum = v0*w0, then fma(v1,w1), fma(v2,w2), fma(x,w3)
 __device__ __forceinline__ float conv4_dev(float v0, float v1, float v2, float x, const float4 w) {
@@ -332,7 +333,7 @@ __device__ __forceinline__ void gdn_quarter_impl(const GdnArgs& a, int head, int
         const float ssq = __fadd_rn(__fadd_rn(__fadd_rn(p[0], p[1]), p[2]), p[3]);
         const float ssk = __fadd_rn(__fadd_rn(__fadd_rn(p[4], p[5]), p[6]), p[7]);
         const int idx = tid < S ? S + tid : tid - S;
-        kq[c * 256 + idx] = __fmul_rn(kq[c * 256 + idx], rsqrtf(__fadd_rn(tid < S ? ssq : ssk, a.eps)));
+        kq[c * 256 + idx] = __fmul_rn(kq[c * 256 + idx], rk_rsqrtf(__fadd_rn(tid < S ? ssq : ssk, a.eps)));
     }
     // ---- the state step ----
     block_sync256();
@@ -346,7 +347,7 @@ __device__ __forceinline__ void gdn_quarter_impl(const GdnArgs& a, int head, int
         float beta = 0.0f, g = 0.0f;
         if (stepper) {
             beta = sigmoid_dev(beta_in[c]);
-            g = expf(softplus_gate_dev(alpha_in[c], a.dt[head], a.ssm_a[head]));
+            g = rk_expf(softplus_gate_dev(alpha_in[c], a.dt[head], a.ssm_a[head]));
             float kv = 0.0f;
 #pragma unroll
             for (int r = 0; r < 32; ++r) kv = __fmaf_rn(s[r], kk[rg * 32 + r], kv);
@@ -402,7 +403,7 @@ __device__ __forceinline__ void gdn_quarter_impl(const GdnArgs& a, int head, int
                 const float ss = __fadd_rn(__fadd_rn(__fadd_rn(ld_cg(q4), ld_cg(q4 + 1)), ld_cg(q4 + 2)), ld_cg(q4 + 3));
                 const float ocj = ld_cg(a.o_scr + ((size_t) c * hv + head) * S + j);
                 const float z = z_in[c];
-                const float scale = rsqrtf(__fadd_rn(__fdiv_rn(ss, (float) S), a.eps));
+                const float scale = rk_rsqrtf(__fadd_rn(__fdiv_rn(ss, (float) S), a.eps));
                 const float yv = __fmul_rn(__fmul_rn(__fmul_rn(ocj, scale), a.gamma[j]), silu_dev(z));
                 if (a.y) a.y[(size_t) c * hv * S + head * S + j] = yv;
                 q8_1_warp_store(yv, a.q8 + ((size_t) c * hv * 4 + head * 4 + wid) * 36, lane);
@@ -470,7 +471,7 @@ __device__ __forceinline__ void attn_chunk_impl(const AttnArgs& a, int pos, int 
             const float pj = warp_sum(__fmul_rn(x[j], x[j]));
             ss = j == 0 ? pj : __fadd_rn(ss, pj);
         }
-        const float inv = rsqrtf(__fadd_rn(__fdiv_rn(ss, (float) kHdA), a.eps));
+        const float inv = rk_rsqrtf(__fadd_rn(__fdiv_rn(ss, (float) kHdA), a.eps));
         const float* nw = is_q ? a.qn : a.kn;
         float* r = rot + warp * kHdA;
 #pragma unroll
@@ -578,7 +579,7 @@ __device__ __forceinline__ void attn_chunk_impl(const AttnArgs& a, int pos, int 
         m = warp_max(m);
         float l = 0.0f;
         for (int t = lane; t < ntok; t += 32) {
-            const float e = m == -INFINITY ? 0.0f : expf(__fsub_rn(sp[t], m));
+            const float e = m == -INFINITY ? 0.0f : rk_expf(__fsub_rn(sp[t], m));
             sp[t] = e;
             l = __fadd_rn(l, e);
         }
@@ -684,7 +685,7 @@ __device__ __forceinline__ void combine_impl(const AttnArgs& a, int pos, int h, 
 #pragma unroll
         for (int u = 0; u < kU; ++u)
             if (k + u < k1) {
-                const float w = expf(__fsub_rn(mk[u], m));
+                const float w = rk_expf(__fsub_rn(mk[u], m));
                 num = __fmaf_rn(w, ok[u], num);
                 den = __fmaf_rn(w, lk[u], den);
             }
@@ -703,7 +704,7 @@ __device__ __forceinline__ void combine_impl(const AttnArgs& a, int pos, int h, 
 #pragma unroll
     for (int w = 0; w < 8; ++w)
         if (wm[w] != -INFINITY) {
-            const float sw = expf(__fsub_rn(wm[w], M));
+            const float sw = rk_expf(__fsub_rn(wm[w], M));
             nu = __fmaf_rn(sw, wnum[w * 32 + lane], nu);
             de = __fmaf_rn(sw, wden[w], de);
         }
@@ -808,11 +809,17 @@ __device__ __noinline__ void ctrl_body(const CtrlArgs& a, Ctrl* ctrl) {
         v->accept = acc;
         v->steps = v->steps + 1;
         v->accepted = v->accepted + acc;
-    } else if (a.kind == CTRL_ROUND) {
-        // the next candidate: the draft column that predicts the position after the last emitted token
-        v->tok[1] = argmax_key_row(v->damax[v->accept ? 1 : 0]);
-    } else if (a.kind == CTRL_DRAFT1) {
-        v->tok[1] = argmax_key_row(v->damax[0]);
+    } else if (a.kind == CTRL_ROUND || a.kind == CTRL_DRAFT1) {
+        // the next candidate, for position pos + 1: the draft column that predicts the position after the
+        // last emitted token, unless the host forced one for that position (a test hook that drives the
+        // accept branch with known tokens; the emitted stream does not depend on the candidate)
+        int cand = argmax_key_row(v->damax[a.kind == CTRL_ROUND && v->accept ? 1 : 0]);
+        const int p1 = v->pos + 1;
+        if (a.force != nullptr && p1 >= 0 && p1 < a.n_force) {
+            const int f = a.force[p1];
+            if (f >= 0) cand = f;
+        }
+        v->tok[1] = cand;
     }
     __threadfence();
 }

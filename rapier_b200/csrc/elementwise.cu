@@ -71,10 +71,9 @@ __global__ void __launch_bounds__(256) gate_quant_kernel(const float* __restrict
 
 // beta_gate_kernel (:707-715).
 __device__ __forceinline__ float softplus_gate(float alpha, float dt, float ssm_a) {
-    const float v = __fadd_rn(alpha, dt);
-    return __fmul_rn(v > 20.0f ? v : log1pf(expf(v)), ssm_a);
+    return rk_softplus_gate(alpha, dt, ssm_a);
 }
-__device__ __forceinline__ float sigmoidf_(float x) { return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x))); }
+__device__ __forceinline__ float sigmoidf_(float x) { return rk_sigmoidf(x); }
 
 __global__ void beta_gate_kernel(float* __restrict__ beta, const float* __restrict__ alpha, const float* __restrict__ dt,
                                  const float* __restrict__ ssm_a, float* __restrict__ gate, int n) {
@@ -84,6 +83,24 @@ __global__ void beta_gate_kernel(float* __restrict__ beta, const float* __restri
     if (i >= n) return;
     beta[i] = sigmoidf_(beta[i]);
     gate[i] = softplus_gate(alpha[i], dt[i], ssm_a[i]);
+}
+
+// The exactly specified transcendentals of common.cuh, one value per thread (a parity probe).
+__global__ void math_probe_kernel(int fn, const float* __restrict__ x, float* __restrict__ y, int n) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const float v = x[i];
+    float r;
+    switch (fn) {
+        case 0: r = rk_expf(v); break;
+        case 1: r = rk_logf(v); break;
+        case 2: r = rk_log1pf(v); break;
+        case 3: r = rk_sigmoidf(v); break;
+        case 4: r = rk_siluf(v); break;
+        case 5: r = rk_rsqrtf(v); break;
+        default: r = expf(v); break;  // the CUDA library's expf, for the error-bound comparison only
+    }
+    y[i] = r;
 }
 
 // rms_norm_weighted (Strata; written definition): per row, ss by each thread's strided fma partial,
@@ -100,7 +117,7 @@ __global__ void __launch_bounds__(128) rms_rows_kernel(float* __restrict__ x, co
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = part;
     __syncthreads();
     const float ss = __fadd_rn(__fadd_rn(__fadd_rn(red[0], red[1]), red[2]), red[3]);
-    const float inv = rsqrtf(__fadd_rn(__fdiv_rn(ss, (float) cols), eps));
+    const float inv = rk_rsqrtf(__fadd_rn(__fdiv_rn(ss, (float) cols), eps));
     for (int i = threadIdx.x; i < cols; i += 128) p[i] = __fmul_rn(__fmul_rn(p[i], inv), w[i]);
 }
 
@@ -249,6 +266,16 @@ int rk_beta_gate(float* beta, const float* alpha, const float* dt, const float* 
     return launched(launch_pdl(beta_gate_kernel, dim3((n + 255) / 256), dim3(256), 0, (cudaStream_t) stream, true, beta,
                                alpha, dt, ssm_a, gate, n),
                     what);
+}
+
+int rk_math_probe(int fn, const float* x, float* y, int n, void* stream) {
+    const char* what = "rk_math_probe";
+    if (n <= 0 || fn < 0 || fn > 6) return set_error(RK_EINVAL, "%s: requires n > 0 and 0 <= fn <= 6", what);
+    if (int rc = check_ptr(x, what)) return rc;
+    if (int rc = check_ptr(y, what)) return rc;
+    if (int rc = check_stream(stream, what)) return rc;
+    math_probe_kernel<<<(n + 255) / 256, 256, 0, (cudaStream_t) stream>>>(fn, x, y, n);
+    return check_launch(what);
 }
 
 int rk_rms_norm_rows(float* x, const float* w, int rows, int cols, float eps, void* stream) {

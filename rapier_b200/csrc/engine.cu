@@ -175,7 +175,7 @@ struct Program {
     cudaGraphExec_t graph = nullptr;
     int kernels = 0;  // kernels one run launches
 };
-enum : int { P_SINGLE = 0, P_TRUNK2, P_ROUND, P_DRAFT1, P_SEED, P_PROBE1, P_PROBE2, P_PREFILL, P_COUNT };
+enum : int { P_SINGLE = 0, P_TRUNK2, P_ROUND, P_DRAFT1, P_SEED, P_PROBE1, P_PROBE2, P_PREFILL, P_DRAFTX, P_COUNT };
 // executor slot of a column count (1, 2, 4)
 inline int col_slot(int nc) { return nc >= 4 ? 2 : nc - 1; }
 
@@ -217,12 +217,16 @@ struct EngineImpl {
     Ctrl* ctrl = nullptr;
     int* out = nullptr;
     int max_out = 0;
+    int* force = nullptr;  // test hook: forced draft candidate per position (-1: the draft's own), max_ctx + 2
     Ctrl* ctrl_stage = nullptr;  // pinned host staging, one slot per queued host write
     int stage_slots = 0, stage_next = 0;
     // session (rk_engine_session_*): the next position to write, the last emitted token not yet ingested
     // (-1: none), the GDN rollback the next pass must honour, and whether the draft slot 0 was seeded
     int s_pos = 0, s_pending = -1, s_rollback = 0;
     bool s_primed = false;
+    // a run failed after it had started to change the caches and states in place: the session's bookkeeping
+    // no longer describes them, so runs are refused until a reset
+    bool s_poisoned = false;
     // programs and executors
     Program progs[P_COUNT];
     bool persistent = false;
@@ -290,7 +294,7 @@ struct EngineImpl {
     void add_ffn(std::vector<POp>& v, const Layer& L, float* xres, float* part);
     POp attn_op(int kind, const Layer& L, int draft_flag);
     void add_trunk(std::vector<POp>& v, bool head = true);
-    void add_draft(std::vector<POp>& v, bool head);
+    void add_draft(std::vector<POp>& v, bool head, float* logits_out = nullptr);
     void add_ctrl(std::vector<POp>& v, int kind);
     void add_xargmax(std::vector<POp>& v, int draft_flag);
     void add_probe(std::vector<POp>& v, int nc);
@@ -612,6 +616,8 @@ int EngineImpl::build() {
     eh_q8 = alloc<uint8_t>(2 * rk_q8_1_bytes(2 * H, 1));
     ctrl = alloc<Ctrl>(1);
     out = alloc<int>((size_t) max_out);
+    force = alloc<int>((size_t) c.max_ctx + 2);
+    if (force && err == cudaSuccess) err = cudaMemsetAsync(force, 0xff, sizeof(int) * ((size_t) c.max_ctx + 2), s);
     psync = alloc<PSync>(1);
     xdesc = alloc<XchDesc>(1);
     stage_slots = 4096;  // plus one slot after them for the emitted-count readback
@@ -773,7 +779,7 @@ void EngineImpl::add_trunk(std::vector<POp>& v, bool head) {
 
 // The MTP draft (draft_predict, src/qwythos.cpp:1316-1406): [enorm(emb) | hnorm(h)] -> eh_proj -> the
 // nextn attention block -> (with_head) shnorm + the shared lm_head + argmax.
-void EngineImpl::add_draft(std::vector<POp>& v, bool head) {
+void EngineImpl::add_draft(std::vector<POp>& v, bool head, float* logits_out) {
     POp d = make_op(POP_DRAFT_PREP);
     d.draft = 1;
     d.dp.emb = tok_embd;
@@ -798,7 +804,7 @@ void EngineImpl::add_draft(std::vector<POp>& v, bool head) {
     add_rowpar(v, q8_params(D.out_proj, q8_attn, dx, dx, dxp));
     add_ffn(v, D, dx, dxp);
     if (head) {
-        MmvqParams p = rms_params(lm_head, dx, shnorm, dxp, nullptr, V);
+        MmvqParams p = rms_params(lm_head, dx, shnorm, dxp, logits_out, V);
         p.amax = &ctrl->damax[0];
         p.row_off = tp_rank * V;
         add_gemv(v, PRO_RMS, EPI_ARGMAX, p);
@@ -811,6 +817,8 @@ void EngineImpl::add_ctrl(std::vector<POp>& v, int kind) {
     c.ct.kind = kind;
     c.ct.out = out;
     c.ct.max_out = max_out;
+    c.ct.force = force;
+    c.ct.n_force = cfg.max_ctx + 2;
     v.push_back(c);
 }
 
@@ -1218,6 +1226,10 @@ static int create_engine(const rk_model_config* cfg, int device, int tp_rank, in
             E.add_draft(E.progs[P_SEED].ops, false);
             rc = E.finalize(E.progs[P_SEED], 1);
         }
+        if (rc == RK_OK) {  // rk_engine_draft_step: the draft with its logits kept
+            E.add_draft(E.progs[P_DRAFTX].ops, true, E.logits);
+            rc = E.finalize(E.progs[P_DRAFTX], 1);
+        }
     }
     if (rc == RK_OK) {
         E.add_probe(E.progs[P_PROBE1].ops, 1);
@@ -1340,6 +1352,7 @@ int rk_engine_reset(rk_engine* e) {
     E.s_pending = -1;
     E.s_rollback = 0;
     E.s_primed = false;
+    E.s_poisoned = false;
     return RK_OK;
 }
 
@@ -1367,6 +1380,52 @@ int rk_engine_step(rk_engine* e, const int* tokens, int ncols, int pos, float* l
     if (int rc = E.check_abort(what)) return rc;
     if (argmax)
         for (int c = 0; c < ncols; ++c) argmax[c] = argmax_key_row(back.amax[c]);
+    return RK_OK;
+}
+
+// The MTP draft alone (draft_predict, src/qwythos.cpp:1316-1406) at draft position pos with input token tok
+// and the hidden of the last trunk pass's column 0 (or h = 0, the slot-0 seed), logits kept.
+int rk_engine_draft_step(rk_engine* e, int tok, int pos, int h_zero, float* logits, int* argmax) {
+    const char* what = "rk_engine_draft_step";
+    if (!e) return set_error(RK_EINVAL, "%s: null engine", what);
+    EngineImpl& E = e->impl;
+    if (!E.cfg.has_mtp) return set_error(RK_EINVAL, "%s: model built without the MTP block", what);
+    if (E.tp_size > 1 && !E.tp_connected) return set_error(RK_EINVAL, "%s: call rk_engine_tp_connect first", what);
+    if (pos < 0 || pos + 1 > E.cfg.max_ctx) return set_error(RK_ERANGE, "%s: position out of range", what);
+    if (tok < 0 || tok >= E.Vg) return set_error(RK_ERANGE, "%s: token out of range", what);
+    cudaError_t ce = cudaSuccess;
+    if (h_zero) {
+        ce = cudaMemsetAsync(E.hsave, 0, sizeof(float) * E.H, E.s);
+        if (ce == cudaSuccess) ce = cudaMemsetAsync(E.hsave_p, 0, sizeof(float) * E.H / 4, E.s);
+    }
+    Ctrl h = {};
+    h.dpos = pos;
+    h.dtok[0] = tok;
+    if (ce == cudaSuccess) E.set_ctrl(h);
+    if (ce == cudaSuccess) ce = E.run(E.progs[P_DRAFTX], 0);
+    if (ce == cudaSuccess && logits)
+        ce = cudaMemcpyAsync(logits, E.logits, sizeof(float) * (size_t) E.V, cudaMemcpyDeviceToHost, E.s);
+    Ctrl back;
+    if (ce == cudaSuccess) ce = cudaMemcpyAsync(&back, E.ctrl, sizeof(Ctrl), cudaMemcpyDeviceToHost, E.s);
+    if (ce == cudaSuccess) ce = cudaStreamSynchronize(E.s);
+    if (ce != cudaSuccess) return set_error(RK_ECUDA, "%s: %s", what, cudaGetErrorString(ce));
+    if (int rc = E.check_abort(what)) return rc;
+    if (argmax) *argmax = argmax_key_row(back.damax[0]);
+    return RK_OK;
+}
+
+int rk_engine_force_candidates(rk_engine* e, const int* tokens, int n) {
+    const char* what = "rk_engine_force_candidates";
+    if (!e || (n > 0 && !tokens)) return set_error(RK_EINVAL, "%s: null argument", what);
+    EngineImpl& E = e->impl;
+    const int cap = E.cfg.max_ctx + 2;
+    if (n < 0 || n > cap) return set_error(RK_EINVAL, "%s: n must be in [0, max_ctx + 2]", what);
+    for (int i = 0; i < n; ++i)
+        if (tokens[i] < -1 || tokens[i] >= E.Vg) return set_error(RK_ERANGE, "%s: token out of range", what);
+    cudaError_t ce = cudaStreamSynchronize(E.s);
+    if (ce == cudaSuccess) ce = cudaMemset(E.force, 0xff, sizeof(int) * (size_t) cap);
+    if (ce == cudaSuccess && n > 0) ce = cudaMemcpy(E.force, tokens, sizeof(int) * (size_t) n, cudaMemcpyHostToDevice);
+    if (ce != cudaSuccess) return set_error(RK_ECUDA, "%s: %s", what, cudaGetErrorString(ce));
     return RK_OK;
 }
 
@@ -1462,14 +1521,16 @@ int rk_engine_generate(rk_engine* e, const int* prompt, int n_prompt, int n_gen,
         cudaEventElapsedTime(&gen, ev[1], ev[2]);
     }
     for (auto& v : ev) cudaEventDestroy(v);
+    E.s_poisoned = true;  // until the generation is known to be complete
     if (ce != cudaSuccess) return set_error(RK_ECUDA, "%s: %s", what, cudaGetErrorString(ce));
     if (int rc2 = E.check_abort(what)) return rc2;
     if (back.bad) return set_error(RK_ERANGE, "%s: a token outside the vocabulary reached the device", what);
     if (back.n_emitted < n_gen) return set_error(RK_ECUDA, "%s: generation stopped early (%d of %d)", what, back.n_emitted, n_gen);
+    E.s_poisoned = false;
     E.s_pos = back.pos;  // a session may continue the generation (its last token is pending)
     E.s_pending = back.tok[0];
     E.s_rollback = back.rollback;
-    E.s_primed = true;
+    E.s_primed = use_mtp != 0;
     if (stats) {
         stats->prefill_ms = pre;
         stats->gen_ms = gen;
@@ -1535,6 +1596,8 @@ int rk_engine_session_run(rk_engine* e, const int* tokens, int n_tokens, int n_g
     if (n_tokens < 0 || n_gen < 1) return set_error(RK_EINVAL, "%s: needs n_tokens >= 0 and n_gen >= 1", what);
     if (use_mtp && !E.cfg.has_mtp) return set_error(RK_EINVAL, "%s: model built without the MTP block", what);
     if (eos_id < -1 || eos_id >= E.Vg) return set_error(RK_ERANGE, "%s: eos_id out of range", what);
+    if (E.s_poisoned)
+        return set_error(RK_ECUDA, "%s: a previous run failed part way; call rk_engine_session_reset", what);
     std::vector<int> list;
     if (E.s_pending >= 0) list.push_back(E.s_pending);
     for (int i = 0; i < n_tokens; ++i) {
@@ -1568,7 +1631,7 @@ int rk_engine_session_run(rk_engine* e, const int* tokens, int n_tokens, int n_g
         ce = E.run(E.progs[P_SEED], 0);
         ++launches;
     }
-    E.s_primed = true;
+    if (use_mtp) E.s_primed = true;  // the draft's cache is kept only by MTP runs
     E.set_ctrl_eos(eos_id);
     cudaEventRecord(ev[1], E.s);
     {  // the seed pass: the last ingested token, the first generated one
@@ -1627,9 +1690,18 @@ int rk_engine_session_run(rk_engine* e, const int* tokens, int n_tokens, int n_g
         cudaEventElapsedTime(&gen, ev[1], ev[2]);
     }
     for (auto& v : ev) cudaEventDestroy(v);
-    if (ce != cudaSuccess) return set_error(RK_ECUDA, "%s: %s", what, cudaGetErrorString(ce));
-    if (int rc = E.check_abort(what)) return rc;
-    if (back.bad) return set_error(RK_ERANGE, "%s: a token outside the vocabulary reached the device", what);
+    if (ce != cudaSuccess) {
+        E.s_poisoned = true;
+        return set_error(RK_ECUDA, "%s: %s", what, cudaGetErrorString(ce));
+    }
+    if (int rc = E.check_abort(what)) {
+        E.s_poisoned = true;
+        return rc;
+    }
+    if (back.bad) {
+        E.s_poisoned = true;
+        return set_error(RK_ERANGE, "%s: a token outside the vocabulary reached the device", what);
+    }
     *n_out = std::min(back.n_emitted, n_gen);
     E.s_pos = back.pos;
     E.s_pending = back.stop ? -1 : back.tok[0];

@@ -27,11 +27,10 @@ namespace {
 constexpr int S = 128;                              // state size
 constexpr float kInvSqrtS = 0.08838834764831845f;   // 1/sqrt(128)
 
-__device__ __forceinline__ float silu_f(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x))); }
-__device__ __forceinline__ float sigmoid_f(float x) { return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x))); }
+__device__ __forceinline__ float silu_f(float x) { return rk_siluf(x); }
+__device__ __forceinline__ float sigmoid_f(float x) { return rk_sigmoidf(x); }
 __device__ __forceinline__ float softplus_gate(float alpha, float dt, float ssm_a) {
-    const float v = __fadd_rn(alpha, dt);
-    return __fmul_rn(v > 20.0f ? v : log1pf(expf(v)), ssm_a);
+    return rk_softplus_gate(alpha, dt, ssm_a);
 }
 __device__ __forceinline__ float pick4(const float4 t, int i) {
     return i == 0 ? t.x : (i == 1 ? t.y : (i == 2 ? t.z : t.w));
@@ -66,7 +65,7 @@ __global__ void __launch_bounds__(S) conv_l2_kernel(float* __restrict__ ring, co
         if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = sq;
         __syncthreads();
         const float ss = __fadd_rn(__fadd_rn(__fadd_rn(part[0], part[1]), part[2]), part[3]);
-        y = __fmul_rn(y, rsqrtf(__fadd_rn(ss, eps)));
+        y = __fmul_rn(y, rk_rsqrtf(__fadd_rn(ss, eps)));
     }
     h[c] = y;
 }
@@ -99,7 +98,7 @@ __device__ __forceinline__ float state_step(float (&s)[32], const float* kk, con
 
 // y = oc * rsqrt(ss/128 + eps) * gamma * silu(z), evaluated left to right.
 __device__ __forceinline__ float gated_out(float oc, float ss, float eps, float gamma, float z) {
-    const float scale = rsqrtf(__fadd_rn(__fdiv_rn(ss, (float) S), eps));
+    const float scale = rk_rsqrtf(__fadd_rn(__fdiv_rn(ss, (float) S), eps));
     return __fmul_rn(__fmul_rn(__fmul_rn(oc, scale), gamma), silu_f(z));
 }
 
@@ -128,7 +127,7 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(128)
 #pragma unroll
     for (int r = 0; r < 32; ++r) s[r] = base[r * rs];
     __syncthreads();
-    const float g = expf(gate[head]);
+    const float g = rk_expf(gate[head]);
     const float oc = state_step(s, kq, kq + S, v[head * S + quarter * 32 + col], g, beta[head], red_kv, red_o, col, rg);
 #pragma unroll
     for (int r = 0; r < 32; ++r) base[r * rs] = s[r];
@@ -239,8 +238,8 @@ __global__ void __cluster_dims__(8, 1, 1) __launch_bounds__(128)
     for (int c = 0; c < NC; ++c) {
         const float ssq = __fadd_rn(__fadd_rn(__fadd_rn(qk_ss[c][0], qk_ss[c][1]), qk_ss[c][2]), qk_ss[c][3]);
         const float ssk = __fadd_rn(__fadd_rn(__fadd_rn(qk_ss[c][4], qk_ss[c][5]), qk_ss[c][6]), qk_ss[c][7]);
-        kq[c][S + tid] = __fmul_rn(qk_raw[c][tid], rsqrtf(__fadd_rn(ssq, eps)));       // q
-        kq[c][tid] = __fmul_rn(qk_raw[c][S + tid], rsqrtf(__fadd_rn(ssk, eps)));       // k
+        kq[c][S + tid] = __fmul_rn(qk_raw[c][tid], rk_rsqrtf(__fadd_rn(ssq, eps)));       // q
+        kq[c][tid] = __fmul_rn(qk_raw[c][S + tid], rk_rsqrtf(__fadd_rn(ssk, eps)));       // k
     }
     // ---- the state step, column by column, state in registers ----
     float s[32];
@@ -253,7 +252,7 @@ __global__ void __cluster_dims__(8, 1, 1) __launch_bounds__(128)
     for (int c = 0; c < NC; ++c) {
         const float* pc = proj + (size_t) c * proj_stride;
         const float beta = sigmoid_f(pc[off_beta + head]);
-        const float g = expf(softplus_gate(pc[off_alpha + head], dt_bias[head], ssm_a[head]));
+        const float g = rk_expf(softplus_gate(pc[off_alpha + head], dt_bias[head], ssm_a[head]));
         oc[c] = state_step(s, kq[c], kq[c] + S, vloc[c][lane], g, beta, red_kv[c], red_o[c], lane, wid);
         if (NC > 1 && c == 0) {
 #pragma unroll

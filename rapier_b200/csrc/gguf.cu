@@ -139,7 +139,11 @@ bool GgufFile::open(const char* path, std::string& err) {
         t.name = r.string();
         t.n_dims = (int) r.get<uint32_t>();
         if (t.n_dims < 1 || t.n_dims > 4) r.ok = false;
-        for (int d = 0; d < t.n_dims && r.ok; ++d) t.ne[d] = (int64_t) r.get<uint64_t>();
+        for (int d = 0; d < t.n_dims && r.ok; ++d) {
+            const uint64_t ne = r.get<uint64_t>();
+            if (ne < 1 || ne > (1ull << 40)) r.ok = false;  // also keeps every product below 2^128
+            t.ne[d] = (int64_t) ne;
+        }
         t.type = (int) r.get<uint32_t>();
         offs[(size_t) i] = r.get<uint64_t>();
     }
@@ -151,9 +155,16 @@ bool GgufFile::open(const char* path, std::string& err) {
     for (size_t i = 0; i < tensors_.size(); ++i) {
         GgufTensor& t = tensors_[i];
         const size_t row = ggml_row_bytes(t.type, t.ne[0]);
-        const double rows = (double) t.ne[1] * (double) t.ne[2] * (double) t.ne[3];
-        t.bytes = row ? (size_t) ((double) row * rows) : 0;
-        if (row && (offs[i] > size_ || data0 + offs[i] > size_ || t.bytes > size_ - data0 - offs[i]))
+        // bytes = row * ne1 * ne2 * ne3 in exact integer arithmetic (each factor < 2^41 here)
+        unsigned __int128 bytes = row;
+        bool big = false;
+        for (int d = 1; d < 4; ++d) {
+            bytes *= (unsigned __int128) (uint64_t) t.ne[d];
+            if (bytes > (unsigned __int128) size_) big = true;  // larger than the file: refused below
+            if (big) break;
+        }
+        t.bytes = big ? size_ + 1 : (size_t) bytes;
+        if (row && (big || offs[i] > size_ || data0 + offs[i] > size_ || t.bytes > size_ - data0 - offs[i]))
             return err = "tensor " + t.name + " extends past the end of the file", false;
         t.data = row ? map_ + data0 + offs[i] : nullptr;
         index_[t.name] = i;

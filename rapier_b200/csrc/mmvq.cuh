@@ -103,16 +103,16 @@ __device__ __forceinline__ float block256_partials_sum(const float* partials, in
     return ss;
 }
 __device__ __forceinline__ float rms_inv(float ss, int cols, float eps) {
-    return rsqrtf(__fadd_rn(__fdiv_rn(ss, (float) cols), eps));
+    return rk_rsqrtf(__fadd_rn(__fdiv_rn(ss, (float) cols), eps));
 }
 // The fused-quantize producers (one value per lane), shared with the standalone kernels so a fused
 // prologue writes the same bits the standalone kernel writes.
 __device__ __forceinline__ float rms_value(float x, float w, float inv) { return __fmul_rn(__fmul_rn(x, w), inv); }
 __device__ __forceinline__ float swiglu_value(float up, float g) {
-    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), up);
+    return __fmul_rn(rk_siluf(g), up);
 }
 __device__ __forceinline__ float sigmul_value(float o, float g) {
-    return __fmul_rn(o, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g))));
+    return __fmul_rn(o, rk_sigmoidf(g));
 }
 
 // Staged activation group in shared memory: codes 0..15 in the lo plane, 16..31 in the hi plane

@@ -179,6 +179,22 @@ class Engine:
                   logits.ctypes.data_as(C.c_void_p) if want_logits else None, am)
         return (logits.reshape(n, -1) if want_logits else None), list(am)
 
+    def draft_step(self, tok: int, pos: int, h_zero: bool = False, want_logits: bool = True):
+        """The MTP draft alone at draft position pos on (emb(tok), the last trunk pass's normed hidden, or 0)
+        (rk_engine_draft_step). Returns (logits or None, argmax id)."""
+        logits = np.empty(self.cfg.n_vocab // self.tp_size, np.float32) if want_logits else None
+        am = C.c_int(0)
+        _lib.call("rk_engine_draft_step", self._h, int(tok), int(pos), 1 if h_zero else 0,
+                  logits.ctypes.data_as(C.c_void_p) if want_logits else None, C.byref(am))
+        return logits, am.value
+
+    def force_candidates(self, tokens_by_pos=None):
+        """Forced MTP draft candidates by position (rk_engine_force_candidates; -1 keeps the draft's own);
+        None clears them."""
+        toks = [] if tokens_by_pos is None else [int(t) for t in tokens_by_pos]
+        arr = (C.c_int * max(1, len(toks)))(*toks)
+        _lib.call("rk_engine_force_candidates", self._h, arr, len(toks))
+
     def read_tensor(self, tid: int) -> np.ndarray:
         L = _lib.lib()
         n = L.rk_engine_read_tensor(self._h, tid, None, 0)

@@ -189,6 +189,14 @@ def rms_norm_weighted(x, w, rows, cols, eps, stream=None):
     _call("rk_rms_norm_rows", _ptr(x), _ptr(w), rows, cols, eps, _stream(stream))
 
 
+MATH_FNS = {"exp": 0, "log": 1, "log1p": 2, "sigmoid": 3, "silu": 4, "rsqrt": 5, "cuda_expf": 6}
+
+
+def math_probe(fn: str, x, y, n, stream=None):
+    """y = f(x) with the kernels' exactly specified fp32 sequence (rk_math_probe)."""
+    _call("rk_math_probe", MATH_FNS[fn], _ptr(x), _ptr(y), n, _stream(stream))
+
+
 def argmax(x, n, ncols, out, stream=None):
     _call("rk_argmax", _ptr(x), n, ncols, _ptr(out), _stream(stream))
 

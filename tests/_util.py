@@ -47,16 +47,14 @@ def rel_err(got, want) -> float:
     return float(np.max(np.abs(got - want)) / max(np.max(np.abs(want)), 1e-30))
 
 
-def q8_1_codes_close(got: np.ndarray, want: np.ndarray, max_code_diff: int = 1, min_equal: float = 0.99):
-    """Q8_1 blocks produced through a transcendental function (rsqrt, exp) on GPU vs CPU: the fp32
-    input can differ in the last ulp, so a code may round the other way. Codes differ by at most
-    `max_code_diff` and at least `min_equal` of them are identical; the scales agree within 1e-3."""
-    g = got.reshape(-1, 36)
-    w = want.reshape(-1, 36)
-    gd = g[:, 0:2].copy().view(np.float16).astype(np.float32)
-    wd = w[:, 0:2].copy().view(np.float16).astype(np.float32)
-    assert np.allclose(gd, wd, rtol=2e-3, atol=0), "Q8_1 scales differ"
-    gc = g[:, 4:].view(np.int8).astype(np.int32)
-    wc = w[:, 4:].view(np.int8).astype(np.int32)
-    assert np.max(np.abs(gc - wc)) <= max_code_diff, "Q8_1 codes differ by more than 1"
-    assert np.mean(gc == wc) >= min_equal, f"only {np.mean(gc == wc):.4f} of Q8_1 codes identical"
+def assert_bits(got, want, what: str = ""):
+    """Bit-for-bit equality of fp32 arrays (the kernels and the oracle run the same operation sequence)."""
+    got = np.ascontiguousarray(got, np.float32).ravel()
+    want = np.ascontiguousarray(want, np.float32).ravel()
+    assert got.shape == want.shape, (got.shape, want.shape)
+    same = got.view(np.uint32) == want.view(np.uint32)
+    if not same.all():
+        d = np.abs(got.astype(np.float64) - want)
+        i = int(np.argmax(d))
+        raise AssertionError(f"{what}: {int((~same).sum())}/{same.size} values differ in their bits; worst index "
+                             f"{i}: got {got[i]!r} want {want[i]!r}")

@@ -111,6 +111,24 @@ def test_refusals(tmp_path):
     assert _config(tmp_path / "missing.gguf")[0] == _lib.RK_EINVAL
 
 
+@pytest.mark.parametrize("ne1", [0, 2**63 + 5, 2**41])
+def test_refuses_bad_tensor_dims(tmp_path, ne1):
+    """A tensor directory entry with a zero, negative-as-int64 or absurd dimension is refused (the byte
+    count is computed in exact integer arithmetic, so no overflow lets a tensor pass the end-of-file check)."""
+    from rapier_b200 import _lib
+
+    good = tmp_path / "m.gguf"
+    _tiny_gguf(good)
+    data = bytearray(good.read_bytes())
+    name = b"token_embd.weight"
+    at = data.index(name) + len(name)  # the directory entry: n_dims u32, ne[0] u64, ne[1] u64, ...
+    assert int.from_bytes(data[at:at + 4], "little") == 2
+    data[at + 12:at + 20] = int(ne1).to_bytes(8, "little")
+    bad = tmp_path / "dims.gguf"
+    bad.write_bytes(bytes(data))
+    assert _config(bad)[0] == _lib.RK_EINVAL
+
+
 def _table(n_rot, base, factor, orig, n_pos):
     from rapier_b200 import _lib
 

@@ -175,7 +175,7 @@ def test_gguf_layout_res(cuda, oracle, t):
 
 
 def test_config1_full_shape(cuda, oracle):
-    """W 12288x4096 ~ N(0, 0.02) -> Q6_K, x ~ N(0, 1) -> Q8_1, ncols 1 and 2."""
+    """The single-GEMV workload: W 12288x4096 ~ N(0, 0.02) -> Q6_K, x ~ N(0, 1) -> Q8_1, ncols 1 and 2."""
     from rapier_b200 import ops
 
     n_in, n_out = 4096, 12288

@@ -161,3 +161,32 @@ def test_gdn_oracle_matches_unfused_restatement(oracle):
         y64[h * S:(h + 1) * S] = o * inv * gamma * zz / (1 + np.exp(-zz))
     assert np.max(np.abs(st2 - s64)) < 1e-5
     assert np.max(np.abs(y - y64)) < 1e-4 * np.max(np.abs(y64))
+
+
+@pytest.mark.parametrize("ncols", [1, 2])
+def test_flash_order_attention_matches_reference_form(oracle, ncols):
+    """The attention restated in the decode engine's flash-decode order (chunks, per-chunk softmax, combine)
+    agrees with the reference-form restatement (one softmax over all tokens, float64 sums) within fp32
+    rounding, at chunk boundaries and over several chunks; column c attends 0..pos+c."""
+    nh, nkv, HD, n_rot, eps = 16, 4, 256, 64, 1e-6
+    max_ctx = 300
+    rope = oracle.rope_table(max_ctx, n_rot, 1e7)
+    qn = oracle.synth_normal(11, HD, std=0.02, mean=1.0)
+    kn = oracle.synth_normal(12, HD, std=0.02, mean=1.0)
+    kc = np.zeros((max_ctx, nkv, HD), np.uint16)
+    vc = np.zeros_like(kc)
+    stride = nh * 2 * HD + 2 * nkv * HD
+    for pos in range(0, 260, ncols):
+        proj = oracle.synth_normal(100 + pos, ncols * stride)
+        o, q8 = oracle.attn_flash_f16(proj, ncols, stride, qn, kn, rope, n_rot, nh, nkv, kc, vc, pos, 32, eps)
+        if pos % 31 and pos not in (32, 64, 256):
+            continue
+        for c in range(ncols):
+            col = proj[c * stride:(c + 1) * stride]
+            q, g = oracle.split_qg(col[:nh * 2 * HD], nh, HD)
+            q = oracle.rope_apply(oracle.rms_norm_rows(q, qn, nh, HD, eps), nh, HD, n_rot, rope, pos + c)
+            want = oracle.gqa_decode_f16(q, kc.ravel(), vc.ravel(), nh, nkv, HD, pos + c + 1, 0.0625)
+            got = o[c * nh * HD:(c + 1) * nh * HD]
+            assert np.max(np.abs(got - want)) <= 2e-6 * np.max(np.abs(want)), (pos, c)
+            assert np.array_equal(q8[c * nh * 8 * 36:(c + 1) * nh * 8 * 36],
+                                  oracle.sigmul_q8_1(got, g))
