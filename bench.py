@@ -273,6 +273,93 @@ def decode_config(args, world: int) -> dict:
     """The decode line's `config`, from the arguments only (the same dict on both arms)."""
     tp, groups = tp_layout(world)
     fill, mtp = args.ctx_fill, not args.no_mtp
+    par = "single GPU" if world == 1 else (f"tensor parallel x{tp}" + (f", {groups} independent groups" if groups > 1 else ""))
+    return {"workload": "config5-decode-mtp" if mtp else "config4-decode", "model": "qwen35-9b-shaped",
+            "layers": "24 GDN + 8 GQA (+1 MTP block)", "n_prompt": N_PROMPT, "n_gen": args.gen,
+            "ctx": (fill + N_PROMPT + args.gen) if fill else args.ctx,
+            "kv_context": fill + N_PROMPT if fill else N_PROMPT, "parallelism": par, "tensor_parallel": tp,
+            "groups": groups, "l2": "6.5 GB of weights per token > 126 MB L2"}
+
+
+def run_decode(args, rank, world, local, pg):
+    import torch
+
+    from rapier_b200.engine import Engine, config_9b
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    tp, groups = tp_layout(world)
+    grp, tp_rank = rank // tp, rank % tp
+    group = None
+    if tp > 1:
+        subgroups = [pg.new_group(list(range(g * tp, (g + 1) * tp))) for g in range(groups)]
+        group = subgroups[grp]
+    fill = args.ctx_fill
+    cfg = config_9b(max_ctx=max(args.ctx, fill + N_PROMPT + args.gen + 64) if fill else args.ctx, seed=1 + grp)
+    eng = Engine(cfg, device=local, tp_rank=tp_rank, tp_size=tp)
+    if tp > 1:
+        eng.connect_tp(group)
+        barrier(pg, dev)
+    prompt = [int(t) for t in np.random.default_rng(1234 + grp).integers(0, cfg.n_vocab, N_PROMPT)]
+    mtp = not args.no_mtp
+    n_gen = args.gen
+
+    def one_generation():
+        if fill:  # decode after a synthetic context of `fill` tokens (seeded caches, rk_engine_session_fill)
+            eng.session_fill(fill, 7 + grp)
+            ids, st, _ = eng.session_run(prompt, n_gen, mtp=mtp)
+            return ids, st
+        return eng.generate(prompt, n_gen, mtp=mtp)
+
+    for _ in range(args.warmup):
+        ids0, _ = one_generation()
+    barrier(pg, dev)
+    gen_ms, stats = 0.0, None
+    t0 = time.perf_counter()
+    with ClockSampler(local) as clk:
+        for _ in range(args.steps):
+            ids, st = one_generation()
+            gen_ms += st["gen_ms"]
+            stats = st
+        barrier(pg, dev)
+    wall_s = time.perf_counter() - t0
+    gen_ms = max_over_ranks(gen_ms, pg, dev)
+    wall_s = max_over_ranks(wall_s, pg, dev)
+    tokens = n_gen * args.steps * groups
+    forced = None
+    if mtp:
+        # the same generations with every draft candidate forced to the token the greedy stream has at its
+        # position (rk_engine_force_candidates): acceptance 1.0, the stream unchanged; what exact MTP gives
+        # once the draft is right, on this engine
+        seq = list(prompt) + [int(t) for t in ids0]
+        if fill:
+            seq = [-1] * fill + seq
+        eng.force_candidates(seq)
+        f_ms, f_st = 0.0, None
+        for _ in range(args.steps):
+            ids_f, st_f = one_generation()
+            assert np.array_equal(ids_f, ids0), "forced-candidate stream differs from the greedy stream"
+            f_ms += st_f["gen_ms"]
+            f_st = st_f
+        eng.force_candidates(None)
+        f_ms = max_over_ranks(f_ms, pg, dev)
+        forced = {"tok_s": round(tokens / (f_ms / 1e3), 2), "ms_per_generation": round(f_ms / args.steps, 3),
+                  "rounds": f_st["mtp_steps"], "accepted": f_st["mtp_accepted"],
+                  "acceptance": round(f_st["mtp_accepted"] / max(1, f_st["mtp_steps"]), 4),
+                  "note": "candidates forced to the greedy stream's tokens (test hook); same tokens emitted"}
+    probe = eng.probe_gemv(ncols=2 if mtp else 1, iters=20)
+    persistent = eng.mode == "persistent"
+    eng.close()
+    peak, peak_kind = measured_peaks()
+    per_launch_s = probe["ms"] / 1e3 / (probe["iters"] * probe["launches"])
+    algo_per_launch = probe["algo_bytes"] / probe["launches"]
+    achieved = algo_per_launch / per_launch_s / 1e9
+    rounds = stats["mtp_steps"]
+    if persistent:  # one kernel per program run (a whole greedy generation is one run)
+        launches_per_gen = stats["graph_launches"]
+    else:
+        launches_per_gen = ((stats["graph_launches"] - rounds) * stats["kernels_per_single_step"] +
+                            rounds * stats["kernels_per_round"])
     cfgd = decode_config(args, world)
     line = {
         "metric": "greedy decode tok/s (1 B200, exact MTP)" if mtp else "greedy decode tok/s (1 B200, no MTP)",

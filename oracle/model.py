@@ -9,9 +9,11 @@ This module imports nothing from the product package: the geometry is a plain ob
 the `Config` fields works, e.g. the engine's own rk_model_config) and the tensor ids below are restated
 constants (tests check them against the engine's).
 
-Attention runs in the decode engine's flash-decode summation order (oracle.attn_flash_f16, chunk length
-by the engine's rule for max_ctx), so the model's logits can be compared bit for bit; the reference-form
-attention (float64 sums) agrees with it within fp32 rounding (tests/test_oracle_golden.py).
+The GEMVs run in the packed-tile kernel's fp32 summation order (oracle.mmvq_packed: the same integer
+sums as the reference's lane order, oracle.mmvq, with a different fp32 rounding sequence) and attention
+in the decode engine's flash-decode order (oracle.attn_flash_f16, chunk length by the engine's rule for
+max_ctx), so the model's logits can be compared bit for bit; the reference-order restatements agree with
+them within fp32 rounding (tests/test_oracle_golden.py).
 """
 from __future__ import annotations
 
@@ -194,18 +196,18 @@ class Model:
         H, nh, nkv, eps = self.H, self.nh, self.nkv, self.eps
         xq = O.rms_quant_q8_1(x, L["attn_norm"], xp, eps)
         rows = 2 * nh * KHD + 2 * nkv * KHD
-        q3 = O.mmvq(O.TYPE_Q6_K, L["in_proj"], xq, H, rows)
+        q3 = O.mmvq_packed(O.TYPE_Q6_K, L["in_proj"], xq, H, rows)
         _, oq = O.attn_flash_f16(q3, 1, rows, L["q_norm"], L["k_norm"], self.rope, self.cfg.n_rot, nh, nkv,
                                  kv["k"], kv["v"], pos, self.chunk_len, eps)
-        return O.mmvq_res(O.TYPE_Q6_K, L["out_proj"], oq, x, nh * KHD, H)
+        return O.mmvq_packed(O.TYPE_Q6_K, L["out_proj"], oq, nh * KHD, H, res=x)
 
     def _ffn(self, L, x, xp):
         """ffn (src/qwythos.cpp:1011-1042): post_norm + Q8_1, up||gate, swiglu + Q8_1, down + residual."""
         H, FF = self.H, self.FF
         xq = O.rms_quant_q8_1(x, L["post_norm"], xp, self.eps)
-        ug = O.mmvq(O.TYPE_Q6_K, L["upgate"], xq, H, 2 * FF)
+        ug = O.mmvq_packed(O.TYPE_Q6_K, L["upgate"], xq, H, 2 * FF)
         sq = O.swiglu_q8_1(ug[:FF], ug[FF:])
-        return O.mmvq_res(O.TYPE_Q6_K, L["down"], sq, x, FF, H)
+        return O.mmvq_packed(O.TYPE_Q6_K, L["down"], sq, FF, H, res=x)
 
     def layer(self, il: int, x, xp, pos: int):
         """Trunk layer il (its mixer, then the FFN) on hidden x with partials xp at position pos; returns
@@ -216,14 +218,14 @@ class Model:
         if L["gdn"]:  # forward_gdn (src/qwythos.cpp:1074-1149)
             xq = O.rms_quant_q8_1(x, L["attn_norm"], xp, eps)
             rows = 2 * hk * KS + 2 * hv * KS + 2 * hv
-            proj = O.mmvq(Q6, L["in_proj"], xq, H, rows)
+            proj = O.mmvq_packed(Q6, L["in_proj"], xq, H, rows)
             C = self.C
             z = proj[C:C + hv * KS]
             beta, g = O.beta_gate(proj[C + hv * KS:C + hv * KS + hv], proj[C + hv * KS + hv:], L["dt"], L["ssm_a"])
             st["ring"], h = O.gdn_conv_l2(st["ring"], proj[:C], L["conv_w"], C, 2 * hk, eps, pos)
             st["ssm"], _, q8 = O.gdn_step_norm_silu_q8(st["ssm"], h[:hk * KS], h[hk * KS:2 * hk * KS],
                                                        h[2 * hk * KS:C], g, beta, z, L["ssm_norm"], eps, hk, hv)
-            x, xp = O.mmvq_res(Q6, L["out_proj"], q8, x, hv * KS, H)
+            x, xp = O.mmvq_packed(Q6, L["out_proj"], q8, hv * KS, H, res=x)
         else:
             x, xp = self._attention(L, st, x, xp, pos)
         return self._ffn(L, x, xp)
@@ -234,7 +236,7 @@ class Model:
         self.h = O.rms_norm_out(x, self.out_norm, xp, self.eps)
         self.hp = O.row_sumsq_partials(self.h)
         xq = O.rms_quant_q8_1(x, self.out_norm, xp, self.eps)
-        return O.mmvq(O.TYPE_Q6_K, self.lm_head, xq, self.H, self.V)
+        return O.mmvq_packed(O.TYPE_Q6_K, self.lm_head, xq, self.H, self.V)
 
     def forward(self, tok: int, pos: int) -> np.ndarray:
         """One teacher-forced token: returns the logits (n_vocab) and updates the caches."""
@@ -258,14 +260,14 @@ class Model:
         ep = O.row_sumsq_partials(e)
         eh = np.concatenate([O.rms_norm_out(e, self.enorm, ep, eps), O.rms_norm_out(h, self.hnorm, hp, eps)])
         ehq = O.quantize_q8_1(eh, 2 * H, 1)
-        dx = O.mmvq(Q6, self.eh_proj, ehq, 2 * H, H)
+        dx = O.mmvq_packed(Q6, self.eh_proj, ehq, 2 * H, H)
         dxp = O.row_sumsq_partials(dx)
         dx, dxp = self._attention(D, self.draft_kv, dx, dxp, pos)
         dx, dxp = self._ffn(D, dx, dxp)
         if not with_head:
             return None
         xq = O.rms_quant_q8_1(dx, self.shnorm, dxp, eps)
-        return O.mmvq(Q6, self.lm_head, xq, H, self.V)
+        return O.mmvq_packed(Q6, self.lm_head, xq, H, self.V)
 
     def generate(self, prompt, n_gen: int):
         """Greedy decoding (the reference's CLI loop without MTP, src/qwythos.cpp:2905-2952, :3184-3192):

@@ -762,6 +762,69 @@ void or_mmvq_res(int type, const void* w, const void* xq, float* y, const float*
     }
 }
 
+/* The same GEMV in the summation order of the packed-tile kernel (rk_pack_weights' tiles of 4 rows x 1024
+ * values): lane l of the row's warp takes 32-value group g = 32 kc + l of every 1024-value chunk kc; per
+ * group the two 16-value sub-block sums (code - 32) * x times their int8 scales are added as integers
+ * (exact), then acc = fmaf((float) isum, d8 * d, acc) over kc in order (d8 the group's Q8_1 scale, d the
+ * row's super-block scale; Q8_0: the 32-value integer dot, d its block scale); the lanes are added by the
+ * 32-lane xor tree. Same integers as the reference order above, different fp32 rounding (a few ulp):
+ * this is the order the decode engine's GEMVs run in. Q6_K and Q8_0, n_in % 1024 == 0. */
+static float packed_row_dot(int type, const uint8_t* wrow, const uint8_t* xcol, int n_in) {
+    float lanes[32];
+    for (int l = 0; l < 32; ++l) {
+        float acc = 0.0f;
+        for (int kc = 0; kc < n_in / 1024; ++kc) {
+            const int g = 32 * kc + l;
+            const uint8_t* xb = xcol + (size_t) g * 36;
+            const int8_t* xq = (const int8_t*) (xb + 4);
+            const float d8 = q81_d(xb);
+            int isum;
+            float d;
+            if (type == 14) {
+                const uint8_t* blk = wrow + (size_t) (g / 8) * 210;
+                const int v0 = (g % 8) * 32;
+                int s0 = 0, s1 = 0;
+                for (int i = 0; i < 16; ++i) s0 += (q6k_code(blk, v0 + i) - 32) * xq[i];
+                for (int i = 16; i < 32; ++i) s1 += (q6k_code(blk, v0 + i) - 32) * xq[i];
+                isum = s0 * (int) (int8_t) blk[192 + (g % 8) * 2] + s1 * (int) (int8_t) blk[192 + (g % 8) * 2 + 1];
+                d = q6k_d(blk);
+            } else {
+                const uint8_t* blk = wrow + (size_t) g * 34;
+                int sd = 0;
+                for (int i = 0; i < 32; ++i) sd += (int) (int8_t) blk[2 + i] * xq[i];
+                isum = sd;
+                uint16_t hb;
+                memcpy(&hb, blk, 2);
+                d = or_f16_to_f32(hb);
+            }
+            acc = fmaf((float) isum, d8 * d, acc);
+        }
+        lanes[l] = acc;
+    }
+    return or_xor_sum32(lanes);
+}
+void or_mmvq_packed(int type, const void* w, const void* xq, float* y, const float* res, float* partials, int n_in,
+                    int n_out, int ncols) {
+    const size_t rb = or_weight_bytes(type, n_in, 1);
+    const size_t xb = or_q8_1_bytes(n_in, 1);
+    const int nslots = (n_out + 3) / 4;
+    for (int j = 0; j < ncols; ++j) {
+#pragma omp parallel for schedule(static)
+        for (int s = 0; s < nslots; ++s) {
+            float p = 0.0f;
+            for (int i = 0; i < 4; ++i) {
+                const int r = 4 * s + i;
+                if (r >= n_out) break;
+                float v = packed_row_dot(type, (const uint8_t*) w + rb * r, (const uint8_t*) xq + xb * j, n_in);
+                if (res) v = v + res[(size_t) j * n_out + r];
+                y[(size_t) j * n_out + r] = v;
+                p = fmaf(v, v, p);
+            }
+            if (partials) partials[(size_t) j * nslots + s] = p;
+        }
+    }
+}
+
 /* Exact integer sums, the bit-exact parity target. Layout out[((j * n_out) + r) * nsub + s]:
  *   Q6_K: nsub = n_in/16, s = 16-value sub-block: sum over its 16 values of (code-32) * x_code * scale
  *         (the sum of the reference's per-lane dp4a(vi, u) * sc over the four lanes that cover it);

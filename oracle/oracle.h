@@ -55,6 +55,10 @@ int or_unpack_weights(int type, const void* src, void* dst, int n_in, int n_out)
 void or_mmvq(int type, const void* w, const void* xq, float* y, int n_in, int n_out, int ncols);
 void or_mmvq_res(int type, const void* w, const void* xq, float* y, const float* res, float* partials,
                  int n_in, int n_out, int ncols);
+/* The GEMV in the packed-tile kernel's order (y = W x (+ res), optional 4-row partials; res and partials
+ * may be NULL). */
+void or_mmvq_packed(int type, const void* w, const void* xq, float* y, const float* res, float* partials, int n_in,
+                    int n_out, int ncols);
 void or_mmvq_isums(int type, const void* w, const void* xq, int32_t* out, int n_in, int n_out, int ncols);
 
 /* ---- norms / elementwise ---- */

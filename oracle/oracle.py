@@ -42,7 +42,7 @@ _f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
 _u8p = np.ctypeslib.ndpointer(np.uint8, flags="C_CONTIGUOUS")
 _u16p = np.ctypeslib.ndpointer(np.uint16, flags="C_CONTIGUOUS")
 _i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
-_i, _f, _d, _sz, _u64 = C.c_int, C.c_float, C.c_double, C.c_size_t, C.c_uint64
+_i, _f, _d, _sz, _u64, _vp = C.c_int, C.c_float, C.c_double, C.c_size_t, C.c_uint64, C.c_void_p
 
 
 def _declare(L):
@@ -63,6 +63,7 @@ def _declare(L):
         "or_unpack_weights": (_i, [_i, _u8p, _u8p, _i, _i]),
         "or_mmvq": (None, [_i, _u8p, _u8p, _f32p, _i, _i, _i]),
         "or_mmvq_res": (None, [_i, _u8p, _u8p, _f32p, _f32p, _f32p, _i, _i, _i]),
+        "or_mmvq_packed": (None, [_i, _u8p, _u8p, _f32p, _vp, _vp, _i, _i, _i]),
         "or_mmvq_isums": (None, [_i, _u8p, _u8p, _i32p, _i, _i, _i]),
         "or_row_sumsq_partials": (None, [_f32p, _f32p, _i]),
         "or_add_partials": (None, [_f32p, _f32p, _f32p, _i]),
@@ -207,6 +208,20 @@ def mmvq_res(t, w, xq, res, n_in, n_out, ncols=1):
     partials = np.empty(nslots * ncols, np.float32)
     lib().or_mmvq_res(t, _c(w, np.uint8), _c(xq, np.uint8), y, _c(res, np.float32), partials, n_in, n_out, ncols)
     return y, partials
+
+
+def mmvq_packed(t, w, xq, n_in, n_out, ncols=1, res=None):
+    """The GEMV in the packed-tile kernel's summation order (the decode engine's GEMVs): y, or with `res`
+    (y = W x + res) the pair (y, 4-row partials)."""
+    y = np.empty(ncols * n_out, np.float32)
+    if res is None:
+        lib().or_mmvq_packed(t, _c(w, np.uint8), _c(xq, np.uint8), y, None, None, n_in, n_out, ncols)
+        return y
+    res = _c(res, np.float32)
+    p = np.empty(ncols * ((n_out + 3) // 4), np.float32)
+    lib().or_mmvq_packed(t, _c(w, np.uint8), _c(xq, np.uint8), y, res.ctypes.data_as(C.c_void_p),
+                         p.ctypes.data_as(C.c_void_p), n_in, n_out, ncols)
+    return y, p
 
 
 def mmvq_isums(t, w, xq, n_in, n_out, ncols=1):

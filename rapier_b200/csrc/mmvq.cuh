@@ -574,7 +574,8 @@ __global__ void __launch_bounds__(kMmvqWarps * 32, 2) mmvq_packed_kernel(const M
     }
     // The next launch may start only now: its CTAs would otherwise queue their own bulk copies (and the
     // launches after it theirs) ahead of this launch's last refills, which gate the whole step (measured:
-    // 1 % per token; with ring depths that let two GEMV CTAs share an SM, early starts cost up to 20 %).
+    // 1 % per token; with rings sized so two launches' CTAs share an SM and the next launch triggered once
+    // every warp has issued its last copy, the decode step ran 20-25 % slower).
     pdl_trigger();
     if constexpr (EPI == EPI_SWIGLU) mmvq_swiglu_finish<NC>(p, ubeg + warp, kMmvqWarps, unit, lane);
     if constexpr (EPI == EPI_ARGMAX) mmvq_argmax_flush<NC>(p, lane, best);
@@ -607,6 +608,7 @@ cudaError_t mmvq_launch(MmvqParams p, cudaStream_t s, bool pdl) {
     int ctas = 1;
     int stages = (int) (((long long) max_optin - 2048 - (long long) fixed) / (long long) (kMmvqWarps * tile));
     if (stages > 5) stages = 5;
+
     if (mmvq_env_stages() > 0) stages = mmvq_env_stages();
     if (mmvq_env_ctas() > 0) ctas = mmvq_env_ctas();
     if (stages < 2 || stages > kMmvqMaxStages) return cudaErrorInvalidValue;

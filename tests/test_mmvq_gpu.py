@@ -1,14 +1,16 @@
 """GPU parity of the quantized GEMVs against the CPU oracle, through the C-ABI (rapier_b200.ops).
 
-Bit-exact: Q8_1 bytes of the quantizer, the packed layout, and the integer sub-block sums. fp32 outputs:
-within RTOL = 1e-3 (tests/_util.py) of the oracle's restatement of the reference's order. Columns of a
-multi-column call: bitwise equal to single-column calls (the reference's invariant, src/native_mmvq.cu:902-920).
+Bit-exact: Q8_1 bytes of the quantizer, the packed layout, the integer sub-block sums, and the packed
+GEMV's fp32 outputs against the oracle's restatement of the packed kernel's summation order
+(oracle.mmvq_packed). fp32 outputs are also within RTOL = 1e-3 (tests/_util.py) of the oracle's
+restatement of the reference's lane order. Columns of a multi-column call: bitwise equal to single-column
+calls (the reference's invariant, src/native_mmvq.cu:902-920).
 """
 import numpy as np
 import pytest
 import torch
 
-from tests._util import assert_close, empty_dev, to_dev, to_np
+from tests._util import assert_bits, assert_close, empty_dev, to_dev, to_np
 
 pytestmark = pytest.mark.gpu
 
@@ -94,6 +96,7 @@ def test_packed_gemv_vs_oracle(cuda, oracle, t, shape):
     y2 = empty_dev(2 * n_out, torch.float32)
     ops.mmvq_packed(t, dp, dx, y2, n_in, n_out, 2)
     assert_close(to_np(y2), want, what=f"packed gemv {t} {shape}")
+    assert_bits(to_np(y2), oracle.mmvq_packed(t, raw, xq, n_in, n_out, 2), what=f"packed gemv {t} {shape}")
     # each column of the 2-column call is bitwise the single-column call
     y1 = empty_dev(n_out, torch.float32)
     xcol = ops.native_q8_1_bytes(n_in, 1)
@@ -114,6 +117,7 @@ def test_packed_gemv_many_columns_bitwise(cuda, oracle, ncols):
     ops.mmvq_packed(Q6, dp, dx, yn, n_in, n_out, ncols)
     got = to_np(yn)
     assert_close(got, oracle.mmvq(Q6, raw, xq, n_in, n_out, ncols), what="many columns")
+    assert_bits(got, oracle.mmvq_packed(Q6, raw, xq, n_in, n_out, ncols), what="many columns")
     y1 = empty_dev(n_out, torch.float32)
     xcol = ops.native_q8_1_bytes(n_in, 1)
     for j in range(ncols):
@@ -139,6 +143,9 @@ def test_packed_res_epilogue(cuda, oracle, t, ncols):
     ops.mmvq_packed_res(t, dp, dx, dy, dy, part, n_in, n_out, ncols)
     assert_close(to_np(dy), want_y, what="res y")
     assert_close(to_np(part), want_p, what="res partials")
+    py, pp = oracle.mmvq_packed(t, raw, xq, n_in, n_out, ncols, res=res)
+    assert_bits(to_np(dy), py, what="res y")
+    assert_bits(to_np(part), pp, what="res partials")
 
 
 @pytest.mark.parametrize("t", [Q6, Q8])
@@ -191,6 +198,7 @@ def test_config1_full_shape(cuda, oracle):
     ops.mmvq_packed(Q6, dp, dq, y, n_in, n_out, 2)
     want = oracle.mmvq(Q6, raw, xq, n_in, n_out, 2)
     assert_close(to_np(y), want, what="config 1")
+    assert_bits(to_np(y), oracle.mmvq_packed(Q6, raw, xq, n_in, n_out, 2), what="config 1")
     # against the float64 product of the dequantized operands (scale of the quantization error)
     wd = oracle.dequantize_weights(Q6, raw, n_in, n_out).reshape(n_out, n_in).astype(np.float64)
     xd = oracle.dequantize_q8_1(xq, 2 * n_in).reshape(2, n_in).astype(np.float64)

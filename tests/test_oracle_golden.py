@@ -190,3 +190,19 @@ def test_flash_order_attention_matches_reference_form(oracle, ncols):
             assert np.max(np.abs(got - want)) <= 2e-6 * np.max(np.abs(want)), (pos, c)
             assert np.array_equal(q8[c * nh * 8 * 36:(c + 1) * nh * 8 * 36],
                                   oracle.sigmul_q8_1(got, g))
+
+
+@pytest.mark.parametrize("t", [14, 8])
+def test_packed_order_gemv_matches_reference_order(oracle, t):
+    """The GEMV in the packed kernel's summation order uses the same integer sums as the reference's lane
+    order; the fp32 results differ only by rounding (a few ulp of the row's scale)."""
+    n_in, n_out = 8192, 96
+    raw = oracle.quantize_weights(t, oracle.synth_normal(31, n_in * n_out, std=0.02), n_in, n_out)
+    xq = oracle.quantize_q8_1(oracle.synth_normal(32, n_in * 2), n_in, 2)
+    a = oracle.mmvq(t, raw, xq, n_in, n_out, 2)
+    b = oracle.mmvq_packed(t, raw, xq, n_in, n_out, 2)
+    assert np.max(np.abs(a - b)) <= 1e-6 * np.max(np.abs(a))
+    res = oracle.synth_normal(33, 2 * n_out)
+    y, p = oracle.mmvq_packed(t, raw, xq, n_in, n_out, 2, res=res)
+    assert np.array_equal(y, b + res)
+    assert np.array_equal(p, np.concatenate([oracle.row_sumsq_partials(y[:n_out]), oracle.row_sumsq_partials(y[n_out:])]))
