@@ -390,9 +390,10 @@ def run_decode(args, rank, world, local, pg):
 
 
 def run_pass(args):
-    """Four single-token passes of a 9B-shaped model cut to --layers layers (the full lm_head): the small
-    case for an ncu capture of the step kernels (the kernels the 32-layer engine runs); with --ctx-fill N
-    the passes run after a synthetic context of N tokens. Not a bench line: prints the four pass times."""
+    """Four passes (--cols 1: single tokens; 2: the verify's two columns) of a 9B-shaped model cut to
+    --layers layers (the full lm_head): the small case for an ncu capture of the step kernels (the kernels the
+    32-layer engine runs); with --ctx-fill N the passes run after a synthetic context of N tokens. Not a
+    bench line: prints the four pass times."""
     import torch
 
     from rapier_b200.engine import Engine, config_9b
@@ -405,11 +406,12 @@ def run_pass(args):
     if fill:
         eng.session_fill(fill, 7)
     times = []
-    for i, t in enumerate([5, 17, 99, 1000]):
+    toks = [5, 17, 99, 1000, 7, 250, 31, 4096]
+    for i in range(4):
         t0 = time.perf_counter()
-        eng.step([t], fill + i, want_logits=False)
+        eng.step(toks[args.cols * i:args.cols * (i + 1)], fill + args.cols * i, want_logits=False)
         times.append(round((time.perf_counter() - t0) * 1e3, 3))
-    print(json.dumps({"workload": "pass", "layers": args.layers, "step_ms_wall": times}), flush=True)
+    print(json.dumps({"workload": "pass", "layers": args.layers, "cols": args.cols, "step_ms_wall": times}), flush=True)
     eng.close()
 
 
@@ -472,6 +474,7 @@ def main():
     ap.add_argument("--workload", default="decode", choices=["decode", "gemv", "pass"],
                     help="pass: four single-token steps of a --layers model (a small case for ncu captures)")
     ap.add_argument("--layers", type=int, default=8, help="pass: decoder layers of the 9B-shaped model")
+    ap.add_argument("--cols", type=int, default=1, choices=[1, 2], help="pass: tokens per pass")
     ap.add_argument("--ctx", type=int, default=512, help="decode: KV capacity (512 or 65536)")
     ap.add_argument("--ctx-fill", type=int, default=0,
                     help="decode: start each generation after a synthetic context of this many tokens (65536: "

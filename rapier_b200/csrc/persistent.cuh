@@ -592,6 +592,23 @@ template <int NC>
 __global__ void __launch_bounds__(256, kAttnCtas<NC>) attn_kernel(const POp op, Ctrl* ctrl) {
     extern __shared__ __align__(128) uint8_t smem[];
     pdl_trigger();
+    if (threadIdx.x == 0) {
+        // The K rows of this block's first chunk (all but the new positions written long before) head for
+        // L2 while the projection GEMV upstream still runs; the position as it reads now is only a hint
+        // for this prefetch, bounds-checked like the body's.
+        const int ph = ld_cg(op.draft ? &ctrl->dpos : &ctrl->pos);
+        const AttnArgs& a = op.at;
+        if (ph >= 0 && ph + NC <= a.max_ctx && (int) blockIdx.x < pop_items<NC>(op, ph)) {
+            const int chunk = (int) blockIdx.x / a.n_kv, kvh = (int) blockIdx.x % a.n_kv;
+            const int t0 = chunk * a.chunk_len;
+            const int tend = min(t0 + a.chunk_len, ph + NC);
+            if (chunk < a.max_chunks && t0 < tend) {
+                const uint32_t bytes = (uint32_t) (tend - t0) * kHdA * 2;
+                const size_t row0 = ((size_t) kvh * a.max_ctx + t0) * kHdA;
+                asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a.kc + row0), "r"(bytes) : "memory");
+            }
+        }
+    }
     pdl_wait();
     const int pos = ld_cg(op.draft ? &ctrl->dpos : &ctrl->pos);
     const int items = pop_items<NC>(op, pos);
@@ -605,6 +622,18 @@ template <int NC>
 __global__ void __launch_bounds__(256) gdn_kernel(const POp op, Ctrl* ctrl) {
     extern __shared__ __align__(128) uint8_t smem[];
     pdl_trigger();
+    // The state slice this block steps was written by the same layer's GDN op one step earlier, long
+    // complete; its lines are asked of L2 now, while the projection GEMV upstream still runs (from the
+    // snapshot when the rollback flag, as it reads now, says so). A prefetch only warms L2: the loads
+    // after the wait read the current values from wherever the flag then points.
+    if (threadIdx.x < 128 && (int) blockIdx.x < op.gd.hv * 4) {
+        const int head = (int) blockIdx.x >> 2, quarter = (int) blockIdx.x & 3;
+        const size_t off = ((size_t) ((threadIdx.x >> 5) * 32) * op.gd.hv + head) * kSsm + quarter * 32 + (threadIdx.x & 31);
+        const size_t rs = (size_t) op.gd.hv * kSsm;
+        const float* src = (ld_cg(&ctrl->rollback) != 0 ? op.gd.snap : op.gd.state) + off;
+#pragma unroll 8
+        for (int r = 0; r < 32; ++r) asm volatile("prefetch.global.L2 [%0];" ::"l"(src + r * rs));
+    }
     pdl_wait();
     const int pos = ld_cg(op.draft ? &ctrl->dpos : &ctrl->pos);
     const int rb = ld_cg(&ctrl->rollback);
