@@ -258,10 +258,9 @@ N_PROMPT, N_GEN = 32, 400
 
 
 def tp_layout(world: int) -> tuple:
-    """(tensor-parallel size, groups) for `world` GPUs: one tensor-parallel group of up to 4 ranks (the 9B
-    geometry's row-parallel inputs split into whole 1024-value tiles over 2 and 4 ranks), groups of 4
-    (independent streams) beyond that."""
-    if world in (1, 2, 4):
+    """(tensor-parallel size, groups) for `world` GPUs: one tensor-parallel group of 1, 2, 4 or 8 ranks (the
+    9B geometry's head and row-parallel splits), else groups of 4 or 2 (independent streams)."""
+    if world in (1, 2, 4, 8):
         return world, 1
     for tp in (4, 2):
         if world % tp == 0:

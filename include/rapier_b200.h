@@ -264,8 +264,11 @@ int rk_engine_create(const rk_model_config* cfg, int device, rk_engine** out);
  * paired with them (GDN), its q and kv heads (attention), its FF rows of up||gate, its vocabulary shard of
  * the lm_head; the row-parallel GEMVs (ssm_out, wo, down, eh_proj) take its share of their inputs and
  * sum the ranks' partials over NVLink peer memory inside the decode kernel, so every rank keeps the same
- * residual stream; the argmax is global. Every rank's share of a row-parallel input must be a multiple of
- * 1024 (the 9B geometry: 2 and 4 ranks) else RK_EUNSUPPORTED. Needs the persistent executor. After all
+ * residual stream; the argmax is global. k-heads and q heads split evenly over the ranks; kv heads too, or,
+ * with more ranks than kv heads, each rank keeps the kv head its 2 or 4 q heads use (the 9B geometry at 8
+ * ranks); every rank's share of a row-parallel input must be a multiple of 256 (it is padded with zero
+ * weight blocks to whole 1024-value tiles) else RK_EUNSUPPORTED. The 9B geometry runs at 2, 4 and 8 ranks.
+ * Needs the persistent executor. After all
  * ranks have created their engines: rk_engine_tp_export on each, an exchange of the handles between the
  * processes, rk_engine_tp_connect on each with all handles (rank-major, rk_tp_handle_bytes each). All
  * ranks then call generate / step / probe in lockstep; logits hold the rank's vocabulary shard. No
@@ -274,6 +277,12 @@ int rk_engine_create_tp(const rk_model_config* cfg, int device, int tp_rank, int
 size_t rk_tp_handle_bytes(void);
 int rk_engine_tp_export(rk_engine* e, void* handle, size_t bytes);
 int rk_engine_tp_connect(rk_engine* e, const void* handles, size_t bytes_per_rank);
+/* Recovery after a failed tensor-parallel call (a rank that did not take part in a step leaves the others'
+ * cross-rank waits to give up after RK_TP_WAIT_MS, default 5000, with RK_ECUDA and status bit 3): every rank
+ * calls this while none of the group's kernels runs, the ranks meet on the host, then every rank calls
+ * rk_engine_reset before the next step. It clears this rank's exchange epochs and flags. No reference
+ * counterpart (the reference's row split has no failure path). */
+int rk_engine_tp_resync(rk_engine* e);
 int rk_engine_destroy(rk_engine* e);
 /* Clears KV caches, GDN states, conv rings and the draft cache (the reference's op:reset,
  * src/qwythos.cpp:2533-2549). */

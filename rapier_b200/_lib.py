@@ -112,6 +112,7 @@ SIGNATURES = {
     "rk_tp_handle_bytes": (sz, []),
     "rk_engine_tp_export": (i32, [vp, vp, sz]),
     "rk_engine_tp_connect": (i32, [vp, vp, sz]),
+    "rk_engine_tp_resync": (i32, [vp]),
     "rk_engine_trace": (i32, [vp, i32, C.POINTER(C.c_double), C.POINTER(C.c_int), i32, C.POINTER(C.c_double), i32]),
     "rk_engine_probe_gemv": (i32, [vp, i32, i32, C.POINTER(ProbeResult)]),
 }

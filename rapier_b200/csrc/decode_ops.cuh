@@ -430,9 +430,10 @@ __device__ __noinline__ void gdn_quarter_body(const GdnArgs& a, int head, int qu
 // 8 l + 7, and the eight warp sums added in warp order. The token-to-warp split does not depend on NC, so a
 // column's partial is the same for any column count. Partials: o [n_head][NC][max_chunks][256],
 // (m, l) [n_head][NC][max_chunks].
-template <int NC>
+template <int NC, int G = kGqa>
 __device__ __forceinline__ void attn_chunk_impl(const AttnArgs& a, int pos, int chunk, int kvh, float* sm) {
-    constexpr int G = kGqa, GC = G * NC;
+    static_assert(G == 2 || G == 4, "2 or 4 q heads per kv head");
+    constexpr int GC = G * NC;
     if (pos < 0 || pos + NC > a.max_ctx) {  // uniform over the block
         if (threadIdx.x == 0) atomicOr(&g_rk_status, kStatusBadIndex);
         return;
@@ -617,19 +618,20 @@ __device__ __forceinline__ void attn_chunk_impl(const AttnArgs& a, int pos, int 
                 }
             }
     }
-    // merge: 4 (head, column) pairs per round, warp sums added in warp order by thread d = dim
+    // merge: up to 4 (head, column) pairs per round, warp sums added in warp order by thread d = dim
+    constexpr int QR = GC < 4 ? GC : 4;
 #pragma unroll
-    for (int r0 = 0; r0 < GC; r0 += 4) {
+    for (int r0 = 0; r0 < GC; r0 += QR) {
         block_sync256();  // wacc aliases the scores (first round) and the previous round
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
+        for (int q = 0; q < QR; ++q) {
             float4* dst = reinterpret_cast<float4*>(wacc + (warp * 4 + q) * kHdA + lane * 8);
             dst[0] = make_float4(acc[r0 + q][0], acc[r0 + q][1], acc[r0 + q][2], acc[r0 + q][3]);
             dst[1] = make_float4(acc[r0 + q][4], acc[r0 + q][5], acc[r0 + q][6], acc[r0 + q][7]);
         }
         block_sync256();
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
+        for (int q = 0; q < QR; ++q) {
             float o = wacc[q * kHdA + tid];
 #pragma unroll
             for (int w = 1; w < 8; ++w) o = __fadd_rn(o, wacc[(w * 4 + q) * kHdA + tid]);
@@ -647,7 +649,8 @@ __device__ __forceinline__ void attn_chunk_impl(const AttnArgs& a, int pos, int 
 // The chunk body as a call (the op kernel and the persistent kernel); attn_kernel inlines the impl.
 template <int NC>
 __device__ __noinline__ void attn_chunk_body(const AttnArgs& a, int pos, int chunk, int kvh, float* sm) {
-    attn_chunk_impl<NC>(a, pos, chunk, kvh, sm);
+    if (a.n_head == 2 * a.n_kv) attn_chunk_impl<NC, 2>(a, pos, chunk, kvh, sm);  // 8-way tensor parallelism
+    else attn_chunk_impl<NC>(a, pos, chunk, kvh, sm);
 }
 
 // Combine of head h, column c, dims [32 slice, 32 slice + 32), then that dims' Q8_1 block of

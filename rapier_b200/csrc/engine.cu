@@ -70,10 +70,11 @@ __global__ void fill_float_kernel(float* dst, long long n, uint64_t seed, float 
 // d = half((max_j amax_j / 31) / 127), scale_j = clamp(roundf((amax_j / 31) / d), 0, 127),
 // code = clamp(roundf(x / (d * scale_j)), -32, 31) + 32. One thread per 256-value block of a slice of the
 // tensor: local rows are global rows grow0 + r, local column blocks are global column blocks
-// [cb_a, cb_a + ncb_a) then [cb_b, cb_b + ncb_b) (nb_full blocks per global row); block bg of the global
+// [cb_a, cb_a + ncb_a) then [cb_b, cb_b + ncb_b) (nb_full blocks per global row), written into local rows
+// of row_blocks >= ncb_a + ncb_b blocks (the rest left as the caller zeroed it); block bg of the global
 // tensor holds values bg*256 .. bg*256+255, so a slice holds exactly the global tensor's values.
 __global__ void gen_q6k_kernel(uint64_t seed, float scale, long long rows, long long grow0, int nb_full, int ncb_a,
-                               int cb_a, int ncb_b, int cb_b, uint8_t* __restrict__ out) {
+                               int cb_a, int ncb_b, int cb_b, int row_blocks, uint8_t* __restrict__ out) {
     const long long b = (long long) blockIdx.x * blockDim.x + threadIdx.x;
     const int ncb = ncb_a + ncb_b;
     if (b >= rows * ncb) return;
@@ -99,7 +100,7 @@ __global__ void gen_q6k_kernel(uint64_t seed, float scale, long long rows, long 
     uint8_t ql[128], qh[64];
     for (int i = 0; i < 128; ++i) ql[i] = 0;
     for (int i = 0; i < 64; ++i) qh[i] = 0;
-    uint8_t* blk = out + (size_t) b * 210;
+    uint8_t* blk = out + ((size_t) lr * row_blocks + lcb) * 210;  // local rows are row_blocks blocks wide
     for (int j = 0; j < 16; ++j) {
         int sc = 0;
         if (dh > 0.0f) {
@@ -197,6 +198,7 @@ struct EngineImpl {
     int tp_rank = 0, tp_size = 1;
     int H = 0, FF = 0, V = 0, Vg = 0, hk = 0, hv = 0, nh = 0, nkv = 0;
     int qkvzab_rows = 0, qkv3_rows = 0, max_in_rows = 0, max_chunks = 0, chunk_len = 32;
+    int kv0 = 0;  // global index of this rank's first kv head
     std::vector<Layer> layers;
     Layer draft;
     float *enorm = nullptr, *hnorm = nullptr, *shnorm = nullptr, *out_norm = nullptr;
@@ -270,7 +272,7 @@ struct EngineImpl {
     void gen_f32(int tid, float* dst, size_t n, double std, double mean, int kind,
                  const std::vector<long long>* pick = nullptr);
     void gen_q6k(int tid, Mat& group, int row_off, int n_in_full, int grow0, int rows, int cb_a, int ncb_a, int cb_b,
-                 int ncb_b, uint8_t* scratch);
+                 int ncb_b, uint8_t* scratch, int row_blocks = 0);
     void gen_q6k_into(int tid, Mat& group, int row_off, int n_in, int n_out, uint8_t* scratch) {
         gen_q6k(tid, group, row_off, n_in, 0, n_out, 0, n_in / 256, 0, 0, scratch);
     }
@@ -283,12 +285,14 @@ struct EngineImpl {
         if (err == cudaSuccess) err = cudaErrorInvalidValue;
         return false;
     }
+    // the input width a row-parallel GEMV over a share of `cols` values runs at: whole 1024-value tiles
+    static int tp_in(int cols) { return (cols + 1023) / 1024 * 1024; }
     int gdn_vhead(int j) const {  // global v-head of local v-head j (the v-heads paired with this rank's k-heads)
         return j < hk ? tp_rank * hk + j : cfg.ssm_h_k + tp_rank * hk + (j - hk);
     }
     // programs
     MmvqParams rms_params(const Mat& m, const float* x_, const float* w, const float* part, float* y, int y_stride);
-    MmvqParams q8_params(const Mat& m, const uint8_t* xq, float* y, const float* res, float* part);
+    MmvqParams q8_params(const Mat& m, const uint8_t* xq, float* y, const float* res, float* part, int x_cols = 0);
     void add_gemv(std::vector<POp>& v, int pro, int epi, const MmvqParams& p);
     void add_rowpar(std::vector<POp>& v, MmvqParams p);
     void add_ffn(std::vector<POp>& v, const Layer& L, float* xres, float* part);
@@ -399,11 +403,16 @@ void EngineImpl::gen_f32(int tid, float* dst, size_t n, double std, double mean,
 
 // Q6_K rows [grow0, grow0 + rows) of tensor tid (n_in_full columns), keeping the 256-column blocks
 // [cb_a, cb_a + ncb_a) then [cb_b, cb_b + ncb_b) of each row: generated as GGUF rows, then repacked into
-// rows [row_off, row_off + rows) of a packed group whose rows are (ncb_a + ncb_b) * 256 wide.
+// rows [row_off, row_off + rows) of a packed group whose rows are row_blocks * 256 wide (default
+// ncb_a + ncb_b; wider rows end in all-zero blocks: d = 0, so they add exactly nothing to a dot product,
+// whatever the activations they meet).
 void EngineImpl::gen_q6k(int tid, Mat& group, int row_off, int n_in_full, int grow0, int rows, int cb_a, int ncb_a,
-                         int cb_b, int ncb_b, uint8_t* scratch) {
-    const int n_in = (ncb_a + ncb_b) * 256;
+                         int cb_b, int ncb_b, uint8_t* scratch, int row_blocks) {
+    if (row_blocks < ncb_a + ncb_b) row_blocks = ncb_a + ncb_b;
+    const int n_in = row_blocks * 256;
     const long long nb = (long long) rows * (ncb_a + ncb_b);
+    if (row_blocks > ncb_a + ncb_b && err == cudaSuccess)
+        err = cudaMemsetAsync(scratch, 0, (size_t) rows * row_blocks * 210, s);
     if (gg) {  // the GGUF rows' bytes (this slice's column blocks), then the same repack
         const std::string name = gguf_name(tid);
         const GgufTensor* t = gg->find(name);
@@ -413,8 +422,8 @@ void EngineImpl::gen_q6k(int tid, Mat& group, int row_off, int n_in_full, int gr
                                                         "; the engine's GEMVs take Q6_K (14)");
         if (t->ne[0] != n_in_full || t->ne[1] < (int64_t) grow0 + rows)
             return (void) src_fail(RK_EINVAL, "tensor " + name + " has an unexpected shape");
-        const size_t rb = ggml_row_bytes(kGgmlQ6_K, n_in_full), lrb = (size_t) (ncb_a + ncb_b) * 210;
-        stage.resize((size_t) rows * lrb);
+        const size_t rb = ggml_row_bytes(kGgmlQ6_K, n_in_full), lrb = (size_t) row_blocks * 210;
+        stage.assign((size_t) rows * lrb, 0);
         for (int r = 0; r < rows; ++r) {
             const uint8_t* src = t->data + (size_t) (grow0 + r) * rb;
             std::memcpy(stage.data() + (size_t) r * lrb, src + (size_t) cb_a * 210, (size_t) ncb_a * 210);
@@ -425,7 +434,7 @@ void EngineImpl::gen_q6k(int tid, Mat& group, int row_off, int n_in_full, int gr
     } else {
         const uint64_t st = hash64(cfg.seed, (uint64_t) tid);
         gen_q6k_kernel<<<(unsigned) ((nb + 127) / 128), 128, 0, s>>>(st, synth_scale(0.02), rows, grow0, n_in_full / 256,
-                                                                     ncb_a, cb_a, ncb_b, cb_b, scratch);
+                                                                     ncb_a, cb_a, ncb_b, cb_b, row_blocks, scratch);
         if (err == cudaSuccess) err = cudaGetLastError();
     }
     if (err != cudaSuccess) return;
@@ -440,6 +449,10 @@ int EngineImpl::build() {
     const int N = tp_size, g = tp_rank;
     H = c.n_embd, Vg = c.n_vocab;
     FF = c.n_ff / N, V = c.n_vocab / N, hk = c.ssm_h_k / N, hv = c.ssm_h_v / N, nh = c.n_head / N, nkv = c.n_head_kv / N;
+    // more ranks than kv heads (8 ranks, 4 kv heads): each rank keeps the one kv head its q heads use,
+    // computed on every rank that shares it (GQA group of nh q heads per kv head on the rank)
+    if (nkv == 0) nkv = 1;
+    kv0 = (g * nh) / (c.n_head / c.n_head_kv);
     const int hkg = c.ssm_h_k, hvg = c.ssm_h_v, S = kSsm;
     qkvzab_rows = 2 * hk * S + 2 * hv * S + 2 * hv;
     qkv3_rows = 2 * nh * kHdA + 2 * nkv * kHdA;
@@ -471,9 +484,10 @@ int EngineImpl::build() {
     auto rows_of = [&](int tid, Mat& m, int row_off, int n_in, int grow0, int rows) {
         gen_q6k(tid, m, row_off, n_in, grow0, rows, 0, n_in / 256, 0, 0, scratch);
     };
-    // this rank's column share [col0, col0 + cols) of every row (a row-parallel weight)
+    // this rank's column share [col0, col0 + cols) of every row (a row-parallel weight), in rows padded with
+    // zero blocks to a whole number of 1024-value tiles (tp_in)
     auto cols_of = [&](int tid, Mat& m, int n_in_full, int n_out, int col0, int cols) {
-        gen_q6k(tid, m, 0, n_in_full, 0, n_out, col0 / 256, cols / 256, 0, 0, scratch);
+        gen_q6k(tid, m, 0, n_in_full, 0, n_out, col0 / 256, cols / 256, 0, 0, scratch, tp_in(cols) / 256);
     };
     // globals: the embedding table is replicated; the lm_head is vocabulary-sharded
     tok_embd = alloc<uint8_t>(rk_weight_bytes(RK_TYPE_Q6_K, H, Vg));
@@ -487,7 +501,7 @@ int EngineImpl::build() {
     } else if (tok_embd) {
         const long long nb = (long long) Vg * (H / 256);
         gen_q6k_kernel<<<(unsigned) ((nb + 127) / 128), 128, 0, s>>>(hash64(c.seed, T_TOK_EMBD), synth_scale(0.02), Vg,
-                                                                     0, H / 256, H / 256, 0, 0, 0, tok_embd);
+                                                                     0, H / 256, H / 256, 0, 0, 0, H / 256, tok_embd);
         tensors.push_back({T_TOK_EMBD, true, H, Vg, tok_embd, 0, true});
     }
     out_norm = norm(T_OUT_NORM, H);
@@ -507,7 +521,7 @@ int EngineImpl::build() {
             rows_of(layer_tid(il, L_FFN_UP), L.upgate, 0, H, g * FF, FF);
             rows_of(layer_tid(il, L_FFN_GATE), L.upgate, FF, H, g * FF, FF);
         }
-        L.down = mat(FF, H);
+        L.down = mat(tp_in(FF), H);
         if (L.down.w) cols_of(layer_tid(il, L_FFN_DOWN), L.down, c.n_ff, H, g * FF, FF);
         if (L.gdn) {
             // this rank's k-heads [g*hk, (g+1)*hk) and the v-heads paired with them (h and h + hkg):
@@ -536,10 +550,10 @@ int EngineImpl::build() {
                 rows_of(layer_tid(il, L_GDN_ALPHA), L.in_proj, b0 + hv + hk, H, hkg + g * hk, hk);
             }
             // ssm_out row-parallel over this rank's v-head outputs (two column ranges)
-            L.out_proj = mat(hv * S, H);
+            L.out_proj = mat(tp_in(hv * S), H);
             if (L.out_proj.w)
                 gen_q6k(layer_tid(il, L_GDN_OUT), L.out_proj, 0, hvg * S, 0, H, va / 256, n / 256, vb / 256, n / 256,
-                        scratch);
+                        scratch, tp_in(hv * S) / 256);
             const int C = 2 * hk * S + hv * S;
             std::vector<long long> chans;  // global conv channel of each local channel
             for (int i = 0; i < n; ++i) chans.push_back(qa + i);
@@ -561,14 +575,14 @@ int EngineImpl::build() {
             L.snap = alloc<float>((size_t) S * hv * S);
             L.ring = alloc<float>((size_t) C * kRingSlots);
         } else {
-            // this rank's q heads [g*nh, (g+1)*nh) and kv heads [g*nkv, (g+1)*nkv)
+            // this rank's q heads [g*nh, (g+1)*nh) and kv heads [kv0, kv0 + nkv)
             L.in_proj = mat(H, qkv3_rows);
             if (L.in_proj.w) {
                 rows_of(layer_tid(il, L_ATT_Q), L.in_proj, 0, H, g * nh * 2 * kHdA, nh * 2 * kHdA);
-                rows_of(layer_tid(il, L_ATT_K), L.in_proj, 2 * nh * kHdA, H, g * nkv * kHdA, nkv * kHdA);
-                rows_of(layer_tid(il, L_ATT_V), L.in_proj, 2 * nh * kHdA + nkv * kHdA, H, g * nkv * kHdA, nkv * kHdA);
+                rows_of(layer_tid(il, L_ATT_K), L.in_proj, 2 * nh * kHdA, H, kv0 * kHdA, nkv * kHdA);
+                rows_of(layer_tid(il, L_ATT_V), L.in_proj, 2 * nh * kHdA + nkv * kHdA, H, kv0 * kHdA, nkv * kHdA);
             }
-            L.out_proj = mat(nh * kHdA, H);  // wo row-parallel over this rank's heads
+            L.out_proj = mat(tp_in(nh * kHdA), H);  // wo row-parallel over this rank's heads
             if (L.out_proj.w) cols_of(layer_tid(il, L_ATT_O), L.out_proj, c.n_head * kHdA, H, g * nh * kHdA, nh * kHdA);
             L.q_norm = norm(layer_tid(il, L_ATT_QN), kHdA);
             L.k_norm = norm(layer_tid(il, L_ATT_KN), kHdA);
@@ -580,7 +594,7 @@ int EngineImpl::build() {
         enorm = norm(T_ENORM, H);
         hnorm = norm(T_HNORM, H);
         shnorm = norm(T_SHNORM, H);
-        eh_proj = mat(2 * H / N, H);  // row-parallel over this rank's share of [emb | h]
+        eh_proj = mat(tp_in(2 * H / N), H);  // row-parallel over this rank's share of [emb | h]
         if (eh_proj.w) cols_of(T_EH_PROJ, eh_proj, 2 * H, H, g * 2 * H / N, 2 * H / N);
     }
     cudaStreamSynchronize(s);
@@ -600,13 +614,17 @@ int EngineImpl::build() {
     xp = alloc<float>(K * (size_t) H / 4);
     proj = alloc<float>(K * (size_t) max_in_rows);
     ug = alloc<float>(K * 2 * (size_t) FF);
-    q8 = alloc<uint8_t>(K * rk_q8_1_bytes(hv * S, 1));
+    // Q8_1 inputs of the row-parallel GEMVs: a padded GEMV (tp_in > the share) reads past each column into
+    // the next one, or for the last column into the slack after them (zeros): finite blocks that meet
+    // all-zero weight blocks
+    const size_t slack = rk_q8_1_bytes(2048, 1);
+    q8 = alloc<uint8_t>(K * rk_q8_1_bytes(hv * S, 1) + slack);
     gdn_o = alloc<float>(K * (size_t) hv * S);
     gdn_ss = alloc<float>(K * (size_t) hv * 4);
     gdn_cnt = alloc<unsigned>((size_t) hv);
     attn_scratch = alloc<float>((size_t) nh * K * max_chunks * (kHdA + 2));
-    q8_ff = alloc<uint8_t>(K * rk_q8_1_bytes(FF, 1));
-    q8_attn = alloc<uint8_t>(K * rk_q8_1_bytes(nh * kHdA, 1));
+    q8_ff = alloc<uint8_t>(K * rk_q8_1_bytes(FF, 1) + slack);
+    q8_attn = alloc<uint8_t>(K * rk_q8_1_bytes(nh * kHdA, 1) + slack);
     swiglu_cnt = alloc<unsigned>((size_t) FF / 32);
     hsave = alloc<float>(2 * (size_t) H);
     hsave_p = alloc<float>(2 * (size_t) H / 4);
@@ -650,7 +668,8 @@ MmvqParams EngineImpl::rms_params(const Mat& m, const float* x_, const float* w,
 }
 
 // y = W . xq (+ res) with the 4-row partials (the reference's residual epilogue; y == res in place).
-MmvqParams EngineImpl::q8_params(const Mat& m, const uint8_t* xq, float* y, const float* res, float* part) {
+// x_cols: the width of one column of xq (its producer's stride) when the matrix is wider (tp_in padding)
+MmvqParams EngineImpl::q8_params(const Mat& m, const uint8_t* xq, float* y, const float* res, float* part, int x_cols) {
     MmvqParams p = {};
     p.w = m.w;
     p.n_in = m.n_in;
@@ -663,6 +682,7 @@ MmvqParams EngineImpl::q8_params(const Mat& m, const uint8_t* xq, float* y, cons
     p.res_stride = m.n_out;
     p.pout = part;
     p.pout_stride = m.n_out / 4;
+    if (x_cols > 0) p.xq_stride = (int) rk_q8_1_bytes(x_cols, 1);
     return p;
 }
 
@@ -698,7 +718,7 @@ void EngineImpl::add_xargmax(std::vector<POp>& v, int draft_flag) {
 // down + residual.
 void EngineImpl::add_ffn(std::vector<POp>& v, const Layer& L, float* xres, float* part) {
     add_gemv(v, PRO_RMS, EPI_SWIGLU, rms_params(L.upgate, xres, L.post_norm, part, ug, 2 * FF));
-    add_rowpar(v, q8_params(L.down, q8_ff, xres, xres, part));
+    add_rowpar(v, q8_params(L.down, q8_ff, xres, xres, part, FF));
 }
 
 POp EngineImpl::attn_op(int kind, const Layer& L, int draft_flag) {
@@ -758,11 +778,11 @@ void EngineImpl::add_trunk(std::vector<POp>& v, bool head) {
             a.hv = hv;
             a.eps = cfg.eps;
             v.push_back(g);
-            add_rowpar(v, q8_params(L.out_proj, q8, x, x, xp));
+            add_rowpar(v, q8_params(L.out_proj, q8, x, x, xp, hv * kSsm));
         } else {
             v.push_back(attn_op(POP_ATTN, L, 0));
             v.push_back(attn_op(POP_COMBINE, L, 0));
-            add_rowpar(v, q8_params(L.out_proj, q8_attn, x, x, xp));
+            add_rowpar(v, q8_params(L.out_proj, q8_attn, x, x, xp, nh * kHdA));
         }
         add_ffn(v, L, x, xp);
     }
@@ -793,7 +813,7 @@ void EngineImpl::add_draft(std::vector<POp>& v, bool head, float* logits_out) {
     d.dp.eh_q8 = eh_q8;
     v.push_back(d);
     {  // no residual; under tensor parallelism this rank's share of the [emb | h] input columns
-        MmvqParams p = q8_params(eh_proj, eh_q8 + (size_t) tp_rank * (eh_proj.n_in / 32) * 36, dx, nullptr, dxp);
+        MmvqParams p = q8_params(eh_proj, eh_q8 + (size_t) tp_rank * (2 * H / tp_size / 32) * 36, dx, nullptr, dxp);
         p.xq_stride = (int) rk_q8_1_bytes(2 * H, 1);
         add_rowpar(v, p);
     }
@@ -801,7 +821,7 @@ void EngineImpl::add_draft(std::vector<POp>& v, bool head, float* logits_out) {
     add_gemv(v, PRO_RMS, EPI_STORE, rms_params(D.in_proj, dx, D.attn_norm, dxp, proj, D.in_proj.n_out));
     v.push_back(attn_op(POP_ATTN, D, 1));
     v.push_back(attn_op(POP_COMBINE, D, 1));
-    add_rowpar(v, q8_params(D.out_proj, q8_attn, dx, dx, dxp));
+    add_rowpar(v, q8_params(D.out_proj, q8_attn, dx, dx, dxp, nh * kHdA));
     add_ffn(v, D, dx, dxp);
     if (head) {
         MmvqParams p = rms_params(lm_head, dx, shnorm, dxp, logits_out, V);
@@ -836,7 +856,7 @@ void EngineImpl::add_probe(std::vector<POp>& v, int nc) {
     for (const Layer& L : layers) {
         add_gemv(v, PRO_RMS, EPI_STORE, rms_params(L.in_proj, x, L.attn_norm, xp, proj, L.in_proj.n_out));
         count(L.in_proj, true, false);
-        add_rowpar(v, q8_params(L.out_proj, L.gdn ? q8 : q8_attn, x, x, xp));
+        add_rowpar(v, q8_params(L.out_proj, L.gdn ? q8 : q8_attn, x, x, xp, L.gdn ? hv * kSsm : nh * kHdA));
         count(L.out_proj, false, true);
         add_ffn(v, L, x, xp);
         count(L.upgate, true, false);
@@ -942,6 +962,8 @@ cudaError_t EngineImpl::launch_op(const POp& op) {
             if (occ < 1) occ = 1;
         }
         const int grid = std::min(op.at.max_chunks * op.at.n_kv, occ * sms);
+        if (op.at.n_head == 2 * op.at.n_kv)  // 2 q heads per kv head (8-way tensor parallelism)
+            return launch_pdl(attn_kernel<NC, 2>, dim3((unsigned) grid), dim3(256), smem, s, true, op, ctrl);
         return launch_pdl(attn_kernel<NC>, dim3((unsigned) grid), dim3(256), smem, s, true, op, ctrl);
     }
     if (op.kind == POP_COMBINE) {  // sm: 8 x 32 + 16 floats
@@ -1142,14 +1164,17 @@ static int create_engine(const rk_model_config* cfg, int device, int tp_rank, in
     if (tp_size < 1 || tp_size > kMaxRanks || tp_rank < 0 || tp_rank >= tp_size)
         return set_error(RK_EINVAL, "%s: bad tensor-parallel rank / size", what);
     if (tp_size > 1) {
-        // every rank's share of a row-parallel input must be a whole number of 1024-value tiles; kv heads
-        // and k-heads split evenly
+        // k-heads and q heads split evenly; kv heads split evenly, or each rank keeps the one its q heads use
+        // (2 or 4 q heads per rank); every rank's share of a row-parallel input is a whole number of 256-value
+        // Q6_K blocks (padded to 1024-value tiles with zero blocks)
         const int N = tp_size;
-        if (c.ssm_h_k % N || c.n_head_kv % N || c.n_ff % (1024 * N) || (c.ssm_h_v * kSsm) % (1024 * N) ||
-            (c.n_head * kHdA) % (1024 * N) || (2 * c.n_embd) % (1024 * N) || c.n_vocab % (4 * N))
+        const bool kv_split = c.n_head_kv % N == 0;
+        const bool kv_repl = N % c.n_head_kv == 0 && c.n_head % N == 0 && (c.n_head / N == 2 || c.n_head / N == 4);
+        if (c.ssm_h_k % N || c.n_head % N || !(kv_split || kv_repl) || c.n_ff % (256 * N) ||
+            (c.ssm_h_v * kSsm) % (256 * N) || (2 * c.n_embd) % (256 * N) || c.n_vocab % (4 * N))
             return set_error(RK_EUNSUPPORTED,
-                             "%s: tensor parallelism over %d ranks needs k-heads and kv-heads divisible by it and "
-                             "every rank's row-parallel input a multiple of 1024",
+                             "%s: tensor parallelism over %d ranks needs k-heads and q heads divisible by it, 2 or 4 "
+                             "q heads per kv head on a rank, and every rank's row-parallel input a multiple of 256",
                              what, N);
         const char* mode = std::getenv("RK_ENGINE_MODE");
         if (mode && std::strcmp(mode, "graph") == 0)
@@ -1292,6 +1317,10 @@ int rk_engine_tp_connect(rk_engine* e, const void* handles, size_t bytes_per_ran
     d.n = E.tp_size;
     d.rows = E.H;
     d.slots = E.p_grid + 1;
+    // RK_TP_WAIT_MS bounds every cross-rank wait (default 5000 ms; a test uses a short bound)
+    const char* wenv = std::getenv("RK_TP_WAIT_MS");
+    const long long wms = wenv ? std::atoll(wenv) : 0;
+    d.wait_ns = wms > 0 ? (unsigned long long) wms * 1000000ull : kPeerSpinNs;
     E.peer_maps.assign(E.tp_size, nullptr);
     for (int q = 0; q < E.tp_size; ++q) {
         uint8_t* base = nullptr;
@@ -1314,6 +1343,23 @@ int rk_engine_tp_connect(rk_engine* e, const void* handles, size_t bytes_per_ran
     const cudaError_t ce = cudaMemcpy(E.xdesc, &d, sizeof d, cudaMemcpyHostToDevice);
     if (ce != cudaSuccess) return set_error(RK_ECUDA, "%s: %s", what, cudaGetErrorString(ce));
     E.tp_connected = true;
+    return RK_OK;
+}
+
+// After a failed step (a peer that never signalled), the ranks' exchange epochs and flags disagree; every
+// rank clears its own (the peers write only into this rank's flag and key arrays, and none of them runs).
+int rk_engine_tp_resync(rk_engine* e) {
+    const char* what = "rk_engine_tp_resync";
+    if (!e) return set_error(RK_EINVAL, "%s: null engine", what);
+    EngineImpl& E = e->impl;
+    if (E.tp_size < 2 || !E.tp_connected) return set_error(RK_EINVAL, "%s: not a connected tensor-parallel engine", what);
+    cudaError_t ce = cudaSetDevice(E.dev);
+    if (ce == cudaSuccess) ce = cudaStreamSynchronize(E.s);
+    if (ce == cudaSuccess) ce = cudaMemset(E.xmem + E.xoff_flags, 0, E.xmem_bytes - E.xoff_flags);
+    if (ce == cudaSuccess) ce = cudaMemset(E.psync, 0, sizeof(PSync));
+    if (ce == cudaSuccess) ce = cudaDeviceSynchronize();
+    if (ce != cudaSuccess) return set_error(RK_ECUDA, "%s: %s", what, cudaGetErrorString(ce));
+    E.s_poisoned = true;  // the caches and states may be partly advanced: a reset comes next
     return RK_OK;
 }
 

@@ -57,6 +57,7 @@ struct XchDesc {
     int rank, n;  // this rank, number of ranks
     int rows;     // rows of a partial column (the hidden size)
     int slots;    // flag slots: one per persistent CTA + one for the argmax exchange
+    unsigned long long wait_ns;            // a cross-rank wait gives up after this long
     float* buf[kMaxRanks];                 // per rank: partials [2 parity][kMaxRanks source][2 columns][rows]
     unsigned long long* flags[kMaxRanks];  // per rank: [slots][kMaxRanks] epochs, written by the peers
     unsigned long long* keys[kMaxRanks];   // per rank: argmax keys [2 parity][kMaxRanks][2 columns]
@@ -73,7 +74,7 @@ constexpr int kMaxGemvOps = 256;
 constexpr int kPWarps = 16;  // warps of a persistent CTA; all consume GEMV tiles
 
 constexpr unsigned long long kGridSpinNs = 1000000000ull;  // a grid barrier gives up after 1 s
-constexpr unsigned long long kPeerSpinNs = 5000000000ull;  // a cross-rank wait after 5 s (a peer's host may lag)
+constexpr unsigned long long kPeerSpinNs = 5000000000ull;  // default cross-rank wait bound (a peer's host may lag)
 
 __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p) {
     unsigned long long v;
@@ -142,7 +143,7 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned 
 
 // One thread: signal flag slot `slot` of every peer with `epoch` (after a system-scope fence that makes
 // this CTA's preceding writes visible), then wait until every peer has signalled this rank's slot. The
-// wait gives up after 5 s (status bit, abort). Returns false when the program must stop.
+// wait gives up after x->wait_ns (status bit, abort). Returns false when the program must stop.
 __device__ __noinline__ bool xch_signal_wait(const XchDesc* x, int slot, unsigned long long epoch, PSync* sync) {
     const int me = x->rank, n = x->n;
     __threadfence_system();
@@ -154,7 +155,7 @@ __device__ __noinline__ bool xch_signal_wait(const XchDesc* x, int slot, unsigne
         if (q == me) continue;
         for (uint32_t it = 0; ld_acquire_sys_u64(mine + q) < epoch; ++it) {
             if (ld_volatile_u32(&sync->abort)) return false;
-            if ((it & 63u) == 63u && globaltimer_ns() - t0 > kPeerSpinNs) {
+            if ((it & 63u) == 63u && globaltimer_ns() - t0 > x->wait_ns) {
                 atomicOr(&g_rk_status, kStatusGridTimeout);
                 atomicExch(&sync->abort, 1u);
                 return false;
@@ -588,7 +589,7 @@ __global__ void __launch_bounds__(kPWarps * 32, 1)
 // SM resident, which the long-context chunk loop (memory latency bound) needs.
 template <int NC>
 constexpr int kAttnCtas = NC == 1 ? 3 : NC == 2 ? 2 : 1;  // 80 / 127 / 255 registers, no spills
-template <int NC>
+template <int NC, int G = kGqa>
 __global__ void __launch_bounds__(256, kAttnCtas<NC>) attn_kernel(const POp op, Ctrl* ctrl) {
     extern __shared__ __align__(128) uint8_t smem[];
     pdl_trigger();
@@ -613,7 +614,7 @@ __global__ void __launch_bounds__(256, kAttnCtas<NC>) attn_kernel(const POp op, 
     const int pos = ld_cg(op.draft ? &ctrl->dpos : &ctrl->pos);
     const int items = pop_items<NC>(op, pos);
     for (int it = (int) blockIdx.x; it < items; it += (int) gridDim.x)  // uniform over the block
-        attn_chunk_impl<NC>(op.at, pos, it / op.at.n_kv, it % op.at.n_kv, reinterpret_cast<float*>(smem));
+        attn_chunk_impl<NC, G>(op.at, pos, it / op.at.n_kv, it % op.at.n_kv, reinterpret_cast<float*>(smem));
 }
 
 // The GDN op as its own launch (graph mode): a kernel of its own instead of the generic op kernel, whose

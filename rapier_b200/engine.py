@@ -157,6 +157,11 @@ class Engine:
         buf = (C.c_uint8 * len(blob)).from_buffer_copy(blob)
         _lib.call("rk_engine_tp_connect", self._h, buf, n)
 
+    def tp_resync(self) -> None:
+        """After a failed tensor-parallel call: clear this rank's exchange epochs and flags
+        (rk_engine_tp_resync). Call on every rank with no kernel running, meet on the host, then reset."""
+        _lib.call("rk_engine_tp_resync", self._h)
+
     def connect_tp(self, group=None) -> None:
         """Exchange the handles over torch.distributed (any backend; `group` spans this engine's ranks, in
         tensor-parallel rank order) and connect."""

@@ -21,7 +21,7 @@ def test_bench_entry_points_and_shared_config():
     c1 = bench.decode_config(args, 1)
     assert c1 == bench.decode_config(args, 1)
     assert c1["workload"] == "config5-decode-mtp" and c1["parallelism"] == "single GPU"
-    assert bench.tp_layout(8) == (4, 2) and bench.tp_layout(4) == (4, 1)
+    assert bench.tp_layout(8) == (8, 1) and bench.tp_layout(4) == (4, 1)
 
 
 def test_reference_arm_prints_one_line():

@@ -13,7 +13,7 @@ def test_tp_layout():
     assert bench.tp_layout(1) == (1, 1)
     assert bench.tp_layout(2) == (2, 1)
     assert bench.tp_layout(4) == (4, 1)
-    assert bench.tp_layout(8) == (4, 2)
+    assert bench.tp_layout(8) == (8, 1)
     assert bench.tp_layout(6) == (2, 3)
     assert bench.tp_layout(3) == (1, 3)
 

@@ -1,9 +1,16 @@
-"""One rank of the tensor-parallel decode check (launched by tests/test_tp_gpu.py through
+"""One rank of the tensor-parallel decode checks (launched by tests/test_tp_gpu.py through
 torch.distributed.run, one process per GPU). Rank 0 writes the results to the JSON path in argv[1].
 
-The model is a 4-layer, 2048-wide geometry (the smallest whose row-parallel inputs split over 2 ranks
-into whole 1024-value tiles). Every rank: teacher-forced steps (its logits shard and the global argmax),
-then greedy and MTP generations. Rank 0 also runs the same steps on a single-GPU engine for reference."""
+argv[2] = "check" (default): teacher-forced steps (every rank's logits shard and the global argmax), then
+greedy and MTP generations; rank 0 also runs the same steps on a single-GPU engine for reference.
+argv[2] = "fail": after a reference generation, rank 0 runs one step that rank 1 skips, so rank 0's
+cross-rank waits give up (RK_TP_WAIT_MS, set short by the launcher); then every rank resyncs and resets
+and the generation is repeated. The host barriers are gloo's; no rank leaves a kernel in flight.
+
+argv[3] = geometry: "mid" (2048 wide, 4 layers: splits over 2 ranks into whole tiles), "tiny" (1024 wide, 4
+q heads and 1 kv head: over 2 ranks each keeps the shared kv head and pads its 512-value row-parallel
+inputs to a tile, the 8-rank layout of the 9B geometry on 2 GPUs) or "9b4" (the 9B geometry cut to 4
+layers and a 32768-token vocabulary: splits over 2, 4 and 8 ranks, with replicated kv heads at 8)."""
 import json
 import os
 import sys
@@ -16,24 +23,62 @@ import torch.distributed as dist
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 sys.path.insert(0, ROOT)
 
+from rapier_b200 import ops  # noqa: E402
+from rapier_b200._lib import RK_ECUDA, RkError  # noqa: E402
 from rapier_b200.engine import Engine, config_9b  # noqa: E402
 
 
-def mid_config(max_ctx=512, seed=3):
+def geometry(name, max_ctx=512, seed=3):
     c = config_9b(max_ctx, seed)
-    c.n_layer, c.n_embd, c.n_ff, c.n_vocab = 4, 2048, 4096, 4096
-    c.ssm_h_k, c.ssm_h_v, c.n_head, c.n_head_kv = 8, 16, 8, 2
+    if name == "mid":
+        c.n_layer, c.n_embd, c.n_ff, c.n_vocab = 4, 2048, 4096, 4096
+        c.ssm_h_k, c.ssm_h_v, c.n_head, c.n_head_kv = 8, 16, 8, 2
+    elif name == "tiny":
+        c.n_layer, c.n_embd, c.n_ff, c.n_vocab = 4, 1024, 2048, 4096
+        c.ssm_h_k, c.ssm_h_v, c.n_head, c.n_head_kv = 4, 8, 4, 1
+    else:
+        c.n_layer, c.n_vocab = 4, 32768
     return c
 
 
 def main():
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    mode = sys.argv[2] if len(sys.argv) > 2 else "check"
+    geo = sys.argv[3] if len(sys.argv) > 3 else "mid"
     torch.cuda.set_device(rank)
     dist.init_process_group("gloo", timeout=timedelta(seconds=120))
-    cfg = mid_config()
+    cfg = geometry(geo)
     eng = Engine(cfg, device=rank, tp_rank=rank, tp_size=world)
     eng.connect_tp()
     dist.barrier()
+    prompt = [int(t) for t in np.random.default_rng(6).integers(0, cfg.n_vocab, 16)]
+    if mode == "fail":
+        g0, _ = eng.generate(prompt, 24, mtp=False)
+        dist.barrier()
+        err, status = None, 0
+        if rank == 0:  # rank 1 skips this step: rank 0's waits for its partial sums give up
+            try:
+                eng.step([5], 0, want_logits=False)
+            except RkError as e:
+                err = e.code
+            status = ops.device_status()
+        dist.barrier()
+        eng.tp_resync()
+        dist.barrier()
+        eng.reset()
+        g1, _ = eng.generate(prompt, 24, mtp=False)
+        g2, st = eng.generate(prompt, 24, mtp=True)
+        mine = {"rank": rank, "err": err, "status": status, "before": g0.tolist(), "after": g1.tolist(),
+                "after_mtp": g2.tolist(), "final_status": ops.device_status()}
+        gathered = [None] * world
+        dist.all_gather_object(gathered, mine)
+        eng.close()
+        if rank == 0:
+            with open(sys.argv[1], "w") as f:
+                json.dump({"ranks": gathered, "ecuda": RK_ECUDA}, f)
+        dist.barrier()
+        dist.destroy_process_group()
+        return
     toks = [int(t) for t in np.random.default_rng(5).integers(0, cfg.n_vocab, 24)]
     eng.reset()
     shards, ams = [], []
@@ -41,11 +86,10 @@ def main():
         lg, am = eng.step([t], pos)
         shards.append(lg[0].tolist())
         ams.append(am[0])
-    prompt = [int(t) for t in np.random.default_rng(6).integers(0, cfg.n_vocab, 16)]
     g0, _ = eng.generate(prompt, 96, mtp=False)
     g1, st = eng.generate(prompt, 96, mtp=True)
     mine = {"rank": rank, "shards": shards, "argmax": ams, "greedy": g0.tolist(), "mtp": g1.tolist(),
-            "mtp_steps": st["mtp_steps"]}
+            "mtp_steps": st["mtp_steps"], "status": ops.device_status()}
     gathered = [None] * world
     dist.all_gather_object(gathered, mine)
     eng.close()
