@@ -255,6 +255,10 @@ def cpu_baseline_gemv(sample_rows=4096):
 # decode workload (configs 4 / 5)
 # ------------------------------------------------------------------------------------------------------
 N_PROMPT, N_GEN = 32, 400
+# DRAM bytes per GEMV launch of one 2-column (verify) trunk step, 32 layers + lm_head, from an ncu capture of
+# the 4-layer 2-column pass (profiles/mmvq_packed_decode_2col_pass.md): 24 x GDN layer + 8 x attention layer
+# + lm_head, / 129 launches.
+DECODE_2COL_NCU_TRAFFIC = 51_161_749
 
 
 def tp_layout(world: int) -> tuple:
@@ -376,7 +380,11 @@ def run_decode(args, rank, world, local, pg):
                      "kernel": ("persistent_kernel (the GEMV ops of one trunk step, one launch)" if persistent else
                                 "mmvq_packed_kernel (all GEMVs of one trunk step, graph replay)"),
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
-                     "traffic": None, "peak_source": peak_kind, "algorithmic_bytes_per_launch": round(algo_per_launch),
+                     "traffic": DECODE_2COL_NCU_TRAFFIC if (mtp and not persistent and tp == 1) else None,
+                     "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum of the 4-layer 2-column pass, "
+                                        "scaled to 32 layers (profiles/mmvq_packed_decode_2col_pass.md)")
+                     if (mtp and not persistent and tp == 1) else None,
+                     "peak_source": peak_kind, "algorithmic_bytes_per_launch": round(algo_per_launch),
                      "gemv_ops": probe["launches"], "avg_gemv_us": round(per_launch_s * 1e6, 3),
                      "per_gpu": tp > 1},
         "e2e": {"value": round(tokens / wall_s, 2), "unit": "tok/s",

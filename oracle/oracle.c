@@ -441,17 +441,16 @@ static void q6k_pack_tile(const uint8_t* raw, int n_in, int rt, int kc, uint8_t*
             const uint8_t* blk = raw + ((size_t) (4 * rt + r) * nb + sb) * 210;
             int code[32];
             for (int e = 0; e < 32; ++e) code[e] = q6k_code(blk, 32 * gi + e);
-            uint8_t* ql = tile + (size_t) (r * 32 + g) * 16;
+            /* A (16 B): byte 4t + b = code[4t + b] (6 bits) | (code[16 + 4t + b] >> 4) << 6;
+             * B (8 B): byte 4u + b = low nibble of code[16 + 8u + b] | low nibble of code[20 + 8u + b] << 4 */
+            uint8_t* qa = tile + (size_t) (r * 32 + g) * 16;
             for (int t = 0; t < 4; ++t)
                 for (int b = 0; b < 4; ++b)
-                    ql[4 * t + b] = (uint8_t) ((code[4 * t + b] & 15) | ((code[16 + 4 * t + b] & 15) << 4));
-            uint8_t* qh = tile + 2048 + (size_t) (r * 32 + g) * 8;
+                    qa[4 * t + b] = (uint8_t) ((code[4 * t + b] & 63) | ((code[16 + 4 * t + b] >> 4) << 6));
+            uint8_t* qb = tile + 2048 + (size_t) (r * 32 + g) * 8;
             for (int u = 0; u < 2; ++u)
-                for (int b = 0; b < 4; ++b) {
-                    int byte = 0;
-                    for (int s = 0; s < 4; ++s) byte |= ((code[4 * (4 * u + s) + b] >> 4) & 3) << (2 * s);
-                    qh[4 * u + b] = (uint8_t) byte;
-                }
+                for (int b = 0; b < 4; ++b)
+                    qb[4 * u + b] = (uint8_t) ((code[16 + 8 * u + b] & 15) | ((code[20 + 8 * u + b] & 15) << 4));
             uint8_t* sc = tile + 3072 + (size_t) (g * 4 + r) * 2;
             sc[0] = blk[192 + 2 * gi];
             sc[1] = blk[192 + 2 * gi + 1];
@@ -469,13 +468,17 @@ static void q6k_unpack_tile(const uint8_t* tile, int n_in, int rt, int kc, uint8
         for (int g = 0; g < 32; ++g) {
             const int sb = 4 * kc + g / 8, gi = g % 8;
             uint8_t* blk = raw + ((size_t) (4 * rt + r) * nb + sb) * 210;
-            const uint8_t* ql = tile + (size_t) (r * 32 + g) * 16;
-            const uint8_t* qh = tile + 2048 + (size_t) (r * 32 + g) * 8;
+            const uint8_t* qa = tile + (size_t) (r * 32 + g) * 16;
+            const uint8_t* qb = tile + 2048 + (size_t) (r * 32 + g) * 8;
             for (int e = 0; e < 32; ++e) {
-                const int T = e / 4, b = e % 4;
-                const int lo = T < 4 ? (ql[4 * T + b] & 15) : (ql[4 * (T - 4) + b] >> 4);
-                const int hi = (qh[4 * (T / 4) + b] >> (2 * (T % 4))) & 3;
-                q6k_set_code(blk, 32 * gi + e, lo | (hi << 4));
+                int code;
+                if (e < 16) {
+                    code = qa[e] & 63;
+                } else {
+                    const int T = (e - 16) / 4, b = e % 4;
+                    code = ((qb[4 * (T / 2) + b] >> (4 * (T % 2))) & 15) | ((qa[4 * T + b] >> 6) << 4);
+                }
+                q6k_set_code(blk, 32 * gi + e, code);
             }
             const uint8_t* sc = tile + 3072 + (size_t) (g * 4 + r) * 2;
             blk[192 + 2 * gi] = sc[0];

@@ -51,6 +51,10 @@ int mmvq_env_ctas() {
     static const int v = env_int("RK_MMVQ_CTAS");
     return v;
 }
+int mmvq_env_warps() {
+    static const int v = env_int("RK_MMVQ_WARPS");
+    return v;
+}
 
 int num_sms() {
     static int n = 0;

@@ -217,22 +217,20 @@ __global__ void pack_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict
         int code[32];
 #pragma unroll
         for (int e = 0; e < 32; ++e) code[e] = q6k_code(blk, 32 * gi + e);
-        uint8_t* ql = t + (r * 32 + g) * 16;
+        // A (16 B): byte 4tt + b = code[4tt + b] (6 bits) | (code[16 + 4tt + b] >> 4) << 6;
+        // B (8 B): byte 4u + b = low nibbles of code[16 + 8u + b] | code[20 + 8u + b] << 4 (q6_decode)
+        uint8_t* qa = t + (r * 32 + g) * 16;
 #pragma unroll
         for (int tt = 0; tt < 4; ++tt)
 #pragma unroll
             for (int b = 0; b < 4; ++b)
-                ql[4 * tt + b] = (uint8_t) ((code[4 * tt + b] & 15) | ((code[16 + 4 * tt + b] & 15) << 4));
-        uint8_t* qh = t + 2048 + (r * 32 + g) * 8;
+                qa[4 * tt + b] = (uint8_t) ((code[4 * tt + b] & 63) | ((code[16 + 4 * tt + b] >> 4) << 6));
+        uint8_t* qb = t + 2048 + (r * 32 + g) * 8;
 #pragma unroll
         for (int u = 0; u < 2; ++u)
 #pragma unroll
-            for (int b = 0; b < 4; ++b) {
-                int byte = 0;
-#pragma unroll
-                for (int s = 0; s < 4; ++s) byte |= ((code[4 * (4 * u + s) + b] >> 4) & 3) << (2 * s);
-                qh[4 * u + b] = (uint8_t) byte;
-            }
+            for (int b = 0; b < 4; ++b)
+                qb[4 * u + b] = (uint8_t) ((code[16 + 8 * u + b] & 15) | ((code[20 + 8 * u + b] & 15) << 4));
         t[3072 + (g * 4 + r) * 2 + 0] = blk[192 + 2 * gi];
         t[3072 + (g * 4 + r) * 2 + 1] = blk[192 + 2 * gi + 1];
         if (gi == 0) {
@@ -271,17 +269,17 @@ __global__ void unpack_kernel(const uint8_t* __restrict__ src, uint8_t* __restri
         // the four groups that share them: the group with gi % 4 == 0 of each half writes its half.
         if ((gi & 3) != 0) return;
         const int h = gi >> 2;  // values 128h .. 128h + 127 (groups gi..gi+3)
-        const uint8_t* qlp[4];
-        const uint8_t* qhp[4];
+        const uint8_t* qap[4];
+        const uint8_t* qbp[4];
         for (int j = 0; j < 4; ++j) {
-            qlp[j] = t + (r * 32 + g + j) * 16;
-            qhp[j] = t + 2048 + (r * 32 + g + j) * 8;
+            qap[j] = t + (r * 32 + g + j) * 16;
+            qbp[j] = t + 2048 + (r * 32 + g + j) * 8;
         }
-        auto code_of = [&](int j, int e) {  // group gi + j, value e
-            const int T = e >> 2, b = e & 3;
-            const int lo = T < 4 ? (qlp[j][4 * T + b] & 15) : (qlp[j][4 * (T - 4) + b] >> 4);
-            const int hi = (qhp[j][4 * (T >> 2) + b] >> (2 * (T & 3))) & 3;
-            return lo | (hi << 4);
+        auto code_of = [&](int j, int e) {  // group gi + j, value e (the layout pack_kernel writes)
+            if (e < 16) return qap[j][e] & 63;
+            const int T = (e - 16) >> 2, b = e & 3;
+            const int nib = (qbp[j][4 * (T >> 1) + b] >> (4 * (T & 1))) & 15;
+            return nib | ((qap[j][4 * T + b] >> 6) << 4);
         };
         for (int l = 0; l < 32; ++l) {
             // ql[64h + l]      : low nibble j=0 (group gi), high nibble j=2 (group gi+2)

@@ -2,7 +2,8 @@
 // the decode engine (engine.cu), which instantiates its fused prologue / epilogue variants.
 //
 // Weight layout: rk_pack_weights' tiles of 4 rows x 1024 values (3360 B for Q6_K, 4352 B for Q8_0,
-// byte-for-byte the GGUF bytes, reordered so each lane's 32-value group is one 16-byte vector).
+// the GGUF block's codes and scales, rearranged so each lane's 32-value group is one 16-byte and one 8-byte
+// vector: q6_decode below gives the layout of the 6-bit codes).
 // A "unit" is one row tile over the whole input (n_in/1024 tiles, contiguous in memory). Units are
 // split into contiguous ranges per CTA (balanced per SM) and dealt round-robin to the CTA's warps.
 // Each warp streams its tiles through a private ring of `stages` shared-memory slots filled by 1-D
@@ -74,11 +75,10 @@ struct MmvqParams {
     const XchDesc* xch;  // EPI_XRES: the ranks' exchange buffers
 };
 
-// Smem bytes a launch needs for the activation staging and the rings.
-inline size_t mmvq_smem_bytes(int type, int n_in, int ncols, int stages) {
+// Smem bytes a launch of `warps` consumer warps needs for the activation staging and the rings.
+inline size_t mmvq_smem_bytes(int type, int n_in, int ncols, int stages, int warps = kMmvqWarps) {
     const size_t tile = type == RK_TYPE_Q6_K ? kQ6Tile : kQ80Tile;
-    return (size_t) kMmvqWarps * kMmvqMaxStages * 8 + (size_t) ncols * (n_in / 32) * 48 +
-           (size_t) kMmvqWarps * stages * tile;
+    return (size_t) warps * kMmvqMaxStages * 8 + (size_t) ncols * (n_in / 32) * 48 + (size_t) warps * stages * tile;
 }
 
 // ---------------------------------------------------------------------------------------------------
@@ -272,17 +272,20 @@ __device__ __noinline__ void mmvq_build_x(const MmvqParams& p, uint8_t* xsm, flo
     }
 }
 
-// The 6-bit codes of one row of a group as eight ints (byte b of int T = code of value 4T + b),
-// from the packed ql (16 B) and qh (8 B) of that row.
-__device__ __forceinline__ void q6_decode(const uint4 ql, const uint2 qh, int v[8]) {
-    v[0] = (int) ((ql.x & 0x0f0f0f0fu) | ((qh.x << 4) & 0x30303030u));
-    v[1] = (int) ((ql.y & 0x0f0f0f0fu) | ((qh.x << 2) & 0x30303030u));
-    v[2] = (int) ((ql.z & 0x0f0f0f0fu) | (qh.x & 0x30303030u));
-    v[3] = (int) ((ql.w & 0x0f0f0f0fu) | ((qh.x >> 2) & 0x30303030u));
-    v[4] = (int) (((ql.x >> 4) & 0x0f0f0f0fu) | ((qh.y << 4) & 0x30303030u));
-    v[5] = (int) (((ql.y >> 4) & 0x0f0f0f0fu) | ((qh.y << 2) & 0x30303030u));
-    v[6] = (int) (((ql.z >> 4) & 0x0f0f0f0fu) | (qh.y & 0x30303030u));
-    v[7] = (int) (((ql.w >> 4) & 0x0f0f0f0fu) | ((qh.y >> 2) & 0x30303030u));
+// The 6-bit codes of one row of a group as eight ints (byte b of int T = code of value 4T + b), from the
+// packed A (16 B: byte 4T + b holds the code of value 4T + b in its low 6 bits and the top 2 bits of
+// value 16 + 4T + b above them) and B (8 B: byte 4u + b holds the low nibbles of values 16 + 8u + b and
+// 20 + 8u + b). The first four ints are one mask each; the last four take a nibble plane and the top bits
+// of an A word.
+__device__ __forceinline__ void q6_decode(const uint4 a, const uint2 b, int v[8]) {
+    v[0] = (int) (a.x & 0x3f3f3f3fu);
+    v[1] = (int) (a.y & 0x3f3f3f3fu);
+    v[2] = (int) (a.z & 0x3f3f3f3fu);
+    v[3] = (int) (a.w & 0x3f3f3f3fu);
+    v[4] = (int) ((b.x & 0x0f0f0f0fu) | ((a.x >> 2) & 0x30303030u));
+    v[5] = (int) (((b.x >> 4) & 0x0f0f0f0fu) | ((a.y >> 2) & 0x30303030u));
+    v[6] = (int) ((b.y & 0x0f0f0f0fu) | ((a.z >> 2) & 0x30303030u));
+    v[7] = (int) (((b.y >> 4) & 0x0f0f0f0fu) | ((a.w >> 2) & 0x30303030u));
 }
 // sum over each 16-value sub-block of (code - 32) * x, exactly.
 __device__ __forceinline__ void q6_subsums(const int v[8], const int4 xa, const int4 xb, int b0, int b1, int& s0,
@@ -296,7 +299,10 @@ __device__ __forceinline__ void q6_subsums(const int v[8], const int4 xa, const 
     s1 = __dp4a(v[6], xb.z, s1);
     s1 = __dp4a(v[7], xb.w, s1);
 }
-__device__ __forceinline__ int sext8(uint32_t w, int byte) { return ((int) (w << (24 - 8 * byte))) >> 24; }
+// Byte `byte` of w, sign-extended: one byte permute (selector nibbles: the byte, then its sign replicated).
+__device__ __forceinline__ int sext8(uint32_t w, int byte) {
+    return (int) __byte_perm(w, 0u, (unsigned) (byte | ((8 | byte) << 4) | ((8 | byte) << 8) | ((8 | byte) << 12)));
+}
 
 // One Q6_K tile (4 rows x this lane's group) against NC staged columns.
 template <int NC>
@@ -473,8 +479,8 @@ __device__ __forceinline__ void mmvq_swiglu_finish(const MmvqParams& p, int firs
     }
 }
 
-template <int TYPE, int NC, int PRO, int EPI>
-__global__ void __launch_bounds__(kMmvqWarps * 32, 2) mmvq_packed_kernel(const MmvqParams p) {
+template <int TYPE, int NC, int PRO, int EPI, int W = kMmvqWarps>
+__global__ void __launch_bounds__(W * 32, 16 / W) mmvq_packed_kernel(const MmvqParams p) {
     constexpr int TILE = TYPE == RK_TYPE_Q6_K ? kQ6Tile : kQ80Tile;
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ float red[kRedCols * 8];
@@ -483,13 +489,13 @@ __global__ void __launch_bounds__(kMmvqWarps * 32, 2) mmvq_packed_kernel(const M
     const int ng = p.n_in >> 5;
     const int stages = p.stages;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem) + warp * kMmvqMaxStages;
-    uint8_t* xsm = smem + kMmvqWarps * kMmvqMaxStages * 8;
+    uint8_t* xsm = smem + W * kMmvqMaxStages * 8;
     uint8_t* ring = xsm + (size_t) NC * ng * 48 + (size_t) warp * stages * TILE;
 
     const int units = p.n_out >> 2;
     const int ubeg = (int) (((long long) blockIdx.x * units) / gridDim.x);
     const int uend = (int) (((long long) (blockIdx.x + 1) * units) / gridDim.x);
-    const int my_units = (uend - ubeg > warp) ? (uend - ubeg - warp + kMmvqWarps - 1) / kMmvqWarps : 0;
+    const int my_units = (uend - ubeg > warp) ? (uend - ubeg - warp + W - 1) / W : 0;
     const int ntiles = my_units * KC;
 
     if (lane == 0) {
@@ -499,11 +505,11 @@ __global__ void __launch_bounds__(kMmvqWarps * 32, 2) mmvq_packed_kernel(const M
     __syncwarp();
     const uint64_t pol = policy_evict_first();
     // Producer cursor (lane 0): the next tile to fetch walks the warp's units' tiles in order (a unit's KC
-    // tiles are contiguous; the warp's next unit is kMmvqWarps units further), and tile i + stages goes
+    // tiles are contiguous; the warp's next unit is W units further), and tile i + stages goes
     // into the slot tile i just left, so the refill needs no division.
     const uint8_t* nsrc = p.w + (size_t) (ubeg + warp) * KC * TILE;
     int nkc = 0;
-    const size_t unit_skip = (size_t) (kMmvqWarps - 1) * KC * TILE;
+    const size_t unit_skip = (size_t) (W - 1) * KC * TILE;
     auto issue = [&](int slot) {
         mbar_arrive_expect_tx(smem_u32(bars + slot), TILE);
         bulk_g2s(smem_u32(ring + (size_t) slot * TILE), nsrc, TILE, smem_u32(bars + slot), pol);
@@ -568,7 +574,7 @@ __global__ void __launch_bounds__(kMmvqWarps * 32, 2) mmvq_packed_kernel(const M
 #pragma unroll
                 for (int r = 0; r < 4; ++r) acc[c][r] = 0.0f;
             kc = 0;
-            unit += kMmvqWarps;
+            unit += W;
             if (unit < uend) mmvq_res_prefetch<NC, EPI>(p, unit, lane, resv);
         }
     }
@@ -577,7 +583,7 @@ __global__ void __launch_bounds__(kMmvqWarps * 32, 2) mmvq_packed_kernel(const M
     // 1 % per token; with rings sized so two launches' CTAs share an SM and the next launch triggered once
     // every warp has issued its last copy, the decode step ran 20-25 % slower).
     pdl_trigger();
-    if constexpr (EPI == EPI_SWIGLU) mmvq_swiglu_finish<NC>(p, ubeg + warp, kMmvqWarps, unit, lane);
+    if constexpr (EPI == EPI_SWIGLU) mmvq_swiglu_finish<NC>(p, ubeg + warp, W, unit, lane);
     if constexpr (EPI == EPI_ARGMAX) mmvq_argmax_flush<NC>(p, lane, best);
 }
 
@@ -587,9 +593,10 @@ __global__ void __launch_bounds__(kMmvqWarps * 32, 2) mmvq_packed_kernel(const M
 // src/native_mmvq.cu:3648-3651): RK_MMVQ_STAGES forces the ring depth, RK_MMVQ_CTAS the CTAs per SM.
 int mmvq_env_stages();
 int mmvq_env_ctas();
+int mmvq_env_warps();
 
-template <int TYPE, int NC, int PRO, int EPI>
-cudaError_t mmvq_launch(MmvqParams p, cudaStream_t s, bool pdl) {
+template <int TYPE, int NC, int PRO, int EPI, int W>
+cudaError_t mmvq_launch_w(MmvqParams p, cudaStream_t s, bool pdl) {
     static int configured_smem = -1;
     static int max_optin = 0;
     if (max_optin == 0) {
@@ -599,23 +606,22 @@ cudaError_t mmvq_launch(MmvqParams p, cudaStream_t s, bool pdl) {
         if (max_optin <= 0) max_optin = 227 * 1024;
     }
     const size_t tile = TYPE == RK_TYPE_Q6_K ? kQ6Tile : kQ80Tile;
-    const size_t fixed = mmvq_smem_bytes(TYPE, p.n_in, NC, 0);
+    const size_t fixed = mmvq_smem_bytes(TYPE, p.n_in, NC, 0, W);
     // One CTA per SM (8 warps) with a ring of up to 5 slots: measured best on B200 for config 1 (12288 x
     // 4096, 2 columns: 2.8 vs 2.4-2.6 TB/s) and for a decode step of one GEMV launch per op (2.45 vs
     // 2.59 ms). Two 3-slot CTAs per SM leave the busiest warp 8 tiles where the average is 5 (units are
     // dealt to warps whole), with 16 warps sharing the SM's issue slots, and let the next op's CTAs become
     // resident and start their weight prefetch while this one still runs.
     int ctas = 1;
-    int stages = (int) (((long long) max_optin - 2048 - (long long) fixed) / (long long) (kMmvqWarps * tile));
+    int stages = (int) (((long long) max_optin - 2048 - (long long) fixed) / (long long) (W * tile));
     if (stages > 5) stages = 5;
-
     if (mmvq_env_stages() > 0) stages = mmvq_env_stages();
     if (mmvq_env_ctas() > 0) ctas = mmvq_env_ctas();
     if (stages < 2 || stages > kMmvqMaxStages) return cudaErrorInvalidValue;
     p.stages = stages;
-    const size_t smem = mmvq_smem_bytes(TYPE, p.n_in, NC, stages);
+    const size_t smem = mmvq_smem_bytes(TYPE, p.n_in, NC, stages, W);
     if ((int) smem > configured_smem) {
-        cudaError_t e = cudaFuncSetAttribute(mmvq_packed_kernel<TYPE, NC, PRO, EPI>,
+        cudaError_t e = cudaFuncSetAttribute(mmvq_packed_kernel<TYPE, NC, PRO, EPI, W>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
         if (e != cudaSuccess) return e;
         configured_smem = (int) smem;
@@ -623,7 +629,13 @@ cudaError_t mmvq_launch(MmvqParams p, cudaStream_t s, bool pdl) {
     const int units = p.n_out / 4;
     int grid = num_sms() * ctas;
     if (grid > units) grid = units;
-    return launch_pdl(mmvq_packed_kernel<TYPE, NC, PRO, EPI>, dim3(grid), dim3(kMmvqWarps * 32), smem, s, pdl, p);
+    return launch_pdl(mmvq_packed_kernel<TYPE, NC, PRO, EPI, W>, dim3(grid), dim3(W * 32), smem, s, pdl, p);
+}
+// RK_MMVQ_WARPS=16: 16 consumer warps per CTA (512 threads, shallower rings) instead of 8.
+template <int TYPE, int NC, int PRO, int EPI>
+cudaError_t mmvq_launch(MmvqParams p, cudaStream_t s, bool pdl) {
+    if (mmvq_env_warps() == 16) return mmvq_launch_w<TYPE, NC, PRO, EPI, 16>(p, s, pdl);
+    return mmvq_launch_w<TYPE, NC, PRO, EPI, kMmvqWarps>(p, s, pdl);
 }
 
 }  // namespace rk
