@@ -769,14 +769,22 @@ void or_mmvq_res(int type, const void* w, const void* xq, float* y, const float*
  * values): lane l of the row's warp takes 32-value group g = 32 kc + l of every 1024-value chunk kc; per
  * group the two 16-value sub-block sums (code - 32) * x times their int8 scales are added as integers
  * (exact), then acc = fmaf((float) isum, d8 * d, acc) over kc in order (d8 the group's Q8_1 scale, d the
- * row's super-block scale; Q8_0: the 32-value integer dot, d its block scale); the lanes are added by the
- * 32-lane xor tree. Same integers as the reference order above, different fp32 rounding (a few ulp):
- * this is the order the decode engine's GEMVs run in. Q6_K and Q8_0, n_in % 1024 == 0. */
+ * row's super-block scale; Q8_0: the 32-value integer dot, d its block scale). With an even chunk count
+ * KC >= 2 the chain runs separately over each half, kc < KC/2 and kc >= KC/2 (two warps can take the
+ * halves), and the lane's value is lo + hi. The lanes are added by the 32-lane xor tree. Same integers as
+ * the reference order above, different fp32 rounding (a few ulp): this is the order the decode engine's
+ * GEMVs run in. Q6_K and Q8_0, n_in % 1024 == 0. */
 static float packed_row_dot(int type, const uint8_t* wrow, const uint8_t* xcol, int n_in) {
     float lanes[32];
+    const int KC = n_in / 1024;
+    const int split = KC >= 2 && KC % 2 == 0 ? KC / 2 : KC;
     for (int l = 0; l < 32; ++l) {
-        float acc = 0.0f;
-        for (int kc = 0; kc < n_in / 1024; ++kc) {
+        float acc = 0.0f, lo = 0.0f;
+        for (int kc = 0; kc < KC; ++kc) {
+            if (kc == split) {
+                lo = acc;
+                acc = 0.0f;
+            }
             const int g = 32 * kc + l;
             const uint8_t* xb = xcol + (size_t) g * 36;
             const int8_t* xq = (const int8_t*) (xb + 4);
@@ -802,7 +810,7 @@ static float packed_row_dot(int type, const uint8_t* wrow, const uint8_t* xcol, 
             }
             acc = fmaf((float) isum, d8 * d, acc);
         }
-        lanes[l] = acc;
+        lanes[l] = split < KC ? lo + acc : acc;
     }
     return or_xor_sum32(lanes);
 }

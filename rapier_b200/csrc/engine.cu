@@ -941,13 +941,14 @@ template <int NC>
 cudaError_t EngineImpl::launch_op(const POp& op) {
     if (op.kind == POP_GEMV) {
         const MmvqParams& p = op.g;
+        const int w = NC == 2 ? 16 : kMmvqWarps;  // the 2-column GEMVs with 16 warps per CTA (mmvq_launch)
         if (op.pro == PRO_RMS) {
-            if (op.epi == EPI_STORE) return mmvq_launch<RK_TYPE_Q6_K, NC, PRO_RMS, EPI_STORE>(p, s, true);
-            if (op.epi == EPI_SWIGLU) return mmvq_launch<RK_TYPE_Q6_K, NC, PRO_RMS, EPI_SWIGLU>(p, s, true);
-            return mmvq_launch<RK_TYPE_Q6_K, NC, PRO_RMS, EPI_ARGMAX>(p, s, true);
+            if (op.epi == EPI_STORE) return mmvq_launch<RK_TYPE_Q6_K, NC, PRO_RMS, EPI_STORE>(p, s, true, w);
+            if (op.epi == EPI_SWIGLU) return mmvq_launch<RK_TYPE_Q6_K, NC, PRO_RMS, EPI_SWIGLU>(p, s, true, w);
+            return mmvq_launch<RK_TYPE_Q6_K, NC, PRO_RMS, EPI_ARGMAX>(p, s, true, w);
         }
-        if (op.epi == EPI_RES) return mmvq_launch<RK_TYPE_Q6_K, NC, PRO_Q8, EPI_RES>(p, s, true);
-        return mmvq_launch<RK_TYPE_Q6_K, NC, PRO_Q8, EPI_STORE_P>(p, s, true);
+        if (op.epi == EPI_RES) return mmvq_launch<RK_TYPE_Q6_K, NC, PRO_Q8, EPI_RES>(p, s, true, w);
+        return mmvq_launch<RK_TYPE_Q6_K, NC, PRO_Q8, EPI_STORE_P>(p, s, true, w);
     }
     static int sms = 0;
     if (sms == 0 && cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) sms = 148;

@@ -299,10 +299,7 @@ __device__ __forceinline__ void q6_subsums(const int v[8], const int4 xa, const 
     s1 = __dp4a(v[6], xb.z, s1);
     s1 = __dp4a(v[7], xb.w, s1);
 }
-// Byte `byte` of w, sign-extended: one byte permute (selector nibbles: the byte, then its sign replicated).
-__device__ __forceinline__ int sext8(uint32_t w, int byte) {
-    return (int) __byte_perm(w, 0u, (unsigned) (byte | ((8 | byte) << 4) | ((8 | byte) << 8) | ((8 | byte) << 12)));
-}
+__device__ __forceinline__ int sext8(uint32_t w, int byte) { return ((int) (w << (24 - 8 * byte))) >> 24; }
 
 // One Q6_K tile (4 rows x this lane's group) against NC staged columns.
 template <int NC>
@@ -479,42 +476,90 @@ __device__ __forceinline__ void mmvq_swiglu_finish(const MmvqParams& p, int firs
     }
 }
 
+// The per-lane fp32 chain of a row runs over each half of an even chunk count separately (kc < KC/2 and
+// kc >= KC/2), and the halves are added lo + hi: two warps can then take the halves of a unit. mmvq_split
+// is the first chunk of the second half (KC when there is one chain).
+__host__ __device__ __forceinline__ int mmvq_split(int KC) { return KC >= 2 && (KC & 1) == 0 ? KC >> 1 : KC; }
+template <int NC>
+__device__ __forceinline__ void mmvq_stash_half(float (&acc)[NC][4], float (&lo)[NC][4]) {
+#pragma unroll
+    for (int c = 0; c < NC; ++c)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            lo[c][r] = acc[c][r];
+            acc[c][r] = 0.0f;
+        }
+}
+template <int NC>
+__device__ __forceinline__ void mmvq_join_halves(float (&acc)[NC][4], const float (&lo)[NC][4]) {
+#pragma unroll
+    for (int c = 0; c < NC; ++c)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) acc[c][r] = __fadd_rn(lo[c][r], acc[c][r]);
+}
+// Bounded spin on a shared-memory word written by another warp of the block (warp pairs below).
+__device__ __forceinline__ bool smem_wait_at_least(const volatile int* w, int v) {
+    for (uint32_t it = 0; it < (1u << 24); ++it) {
+        if (*w >= v) return true;
+        if (it >= 64u) __nanosleep(32);
+    }
+    atomicOr(&g_rk_status, kStatusWaitTimeout);
+    return false;
+}
+// Bytes of the warp-pair exchange slots of a 16-warp launch (two slots per pair of warps, NC x 4 floats per lane).
+__host__ __device__ __forceinline__ size_t mmvq_pair_bytes(int ncols, int warps) { return warps == 16 ? (size_t) 8 * 2 * ncols * 4 * 32 * 4 : 0; }
+
 template <int TYPE, int NC, int PRO, int EPI, int W = kMmvqWarps>
 __global__ void __launch_bounds__(W * 32, 16 / W) mmvq_packed_kernel(const MmvqParams p) {
     constexpr int TILE = TYPE == RK_TYPE_Q6_K ? kQ6Tile : kQ80Tile;
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ float red[kRedCols * 8];
+    __shared__ int pair_flag[8][2], pair_ack[8][2];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int KC = p.n_in >> 10;
     const int ng = p.n_in >> 5;
     const int stages = p.stages;
+    const int split = mmvq_split(KC);
+    // Warp pairs (16 warps, an even chunk count): warps 2m and 2m + 1 take the two halves of the same units,
+    // so a unit's tiles are consumed by two warps at once; the odd warp hands its half's chains to the even
+    // one through a shared-memory slot, and the even warp adds them (lo + hi) and runs the epilogue.
+    const bool paired = W == 16 && split < KC;
+    const int PW = paired ? W / 2 : W;           // units in flight per CTA
+    const int ul = paired ? warp >> 1 : warp;    // this warp's unit lane
+    const int half = paired ? warp & 1 : 0;      // which half of each unit this warp consumes
+    const int KT = paired ? split : KC;          // tiles per unit for this warp
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem) + warp * kMmvqMaxStages;
-    uint8_t* xsm = smem + W * kMmvqMaxStages * 8;
+    float* pslots = reinterpret_cast<float*>(smem + W * kMmvqMaxStages * 8);
+    uint8_t* xsm = smem + W * kMmvqMaxStages * 8 + mmvq_pair_bytes(NC, W);
     uint8_t* ring = xsm + (size_t) NC * ng * 48 + (size_t) warp * stages * TILE;
 
     const int units = p.n_out >> 2;
     const int ubeg = (int) (((long long) blockIdx.x * units) / gridDim.x);
     const int uend = (int) (((long long) (blockIdx.x + 1) * units) / gridDim.x);
-    const int my_units = (uend - ubeg > warp) ? (uend - ubeg - warp + W - 1) / W : 0;
-    const int ntiles = my_units * KC;
+    const int my_units = (uend - ubeg > ul) ? (uend - ubeg - ul + PW - 1) / PW : 0;
+    const int ntiles = my_units * KT;
 
     if (lane == 0) {
         for (int s = 0; s < stages; ++s) mbar_init(smem_u32(bars + s), 1);
         fence_mbar_init();
     }
+    if (threadIdx.x < 16) {
+        pair_flag[threadIdx.x >> 1][threadIdx.x & 1] = 0;
+        pair_ack[threadIdx.x >> 1][threadIdx.x & 1] = 0;
+    }
     __syncwarp();
     const uint64_t pol = policy_evict_first();
-    // Producer cursor (lane 0): the next tile to fetch walks the warp's units' tiles in order (a unit's KC
-    // tiles are contiguous; the warp's next unit is W units further), and tile i + stages goes
-    // into the slot tile i just left, so the refill needs no division.
-    const uint8_t* nsrc = p.w + (size_t) (ubeg + warp) * KC * TILE;
+    // Producer cursor (lane 0): the next tile to fetch walks this warp's tiles in order (a unit's tiles are
+    // contiguous: KT of them from this warp's half; the next unit is PW units further), and tile i + stages
+    // goes into the slot tile i just left, so the refill needs no division.
+    const uint8_t* nsrc = p.w + ((size_t) (ubeg + ul) * KC + (size_t) half * KT) * TILE;
     int nkc = 0;
-    const size_t unit_skip = (size_t) (W - 1) * KC * TILE;
+    const size_t unit_skip = (size_t) (PW * KC - KT) * TILE;
     auto issue = [&](int slot) {
         mbar_arrive_expect_tx(smem_u32(bars + slot), TILE);
         bulk_g2s(smem_u32(ring + (size_t) slot * TILE), nsrc, TILE, smem_u32(bars + slot), pol);
         nsrc += TILE;
-        if (++nkc == KC) {
+        if (++nkc == KT) {
             nkc = 0;
             nsrc += unit_skip;
         }
@@ -529,26 +574,31 @@ __global__ void __launch_bounds__(W * 32, 16 / W) mmvq_packed_kernel(const MmvqP
     mmvq_build_x<NC, PRO>(p, xsm, red);
     __syncthreads();
 
-    float acc[NC][4];
+    float acc[NC][4], lo[NC][4];
     unsigned long long best[NC];
 #pragma unroll
     for (int c = 0; c < NC; ++c) {
         best[c] = 0ull;
 #pragma unroll
-        for (int r = 0; r < 4; ++r) acc[c][r] = 0.0f;
+        for (int r = 0; r < 4; ++r) {
+            acc[c][r] = 0.0f;
+            lo[c][r] = 0.0f;
+        }
     }
 
-    int s = 0, kc = 0, unit = ubeg + warp;
+    int s = 0, kc = 0, unit = ubeg + ul, seq = 0;
     uint32_t parity = 0;
     float resv[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    if (ntiles > 0) mmvq_res_prefetch<NC, EPI>(p, unit, lane, resv);
+    if (ntiles > 0 && half == 0) mmvq_res_prefetch<NC, EPI>(p, unit, lane, resv);
+    const int kbase = half * KT;  // this warp's first chunk of a unit
     for (int i = 0; i < ntiles; ++i) {
         const bool landed = mbar_wait_bounded(smem_u32(bars + s), parity);
         if (!__all_sync(0xffffffffu, landed)) break;
+        if (!paired && kc == split) mmvq_stash_half<NC>(acc, lo);
         const uint8_t* t = ring + (size_t) s * TILE;
         int4 xa[NC], xb[NC];
         float4 xm[NC];
-        const int g = (kc << 5) + lane;
+        const int g = ((kbase + kc) << 5) + lane;
 #pragma unroll
         for (int c = 0; c < NC; ++c) {
             const XStage xs = xstage_col(xsm, ng, c);
@@ -567,15 +617,42 @@ __global__ void __launch_bounds__(W * 32, 16 / W) mmvq_packed_kernel(const MmvqP
             s = 0;
             parity ^= 1u;
         }
-        if (++kc == KC) {
-            mmvq_epilogue<NC, EPI>(p, unit, lane, acc, best, resv);
+        if (++kc == KT) {
+            if (!paired) {
+                if (split < KC) mmvq_join_halves<NC>(acc, lo);
+                mmvq_epilogue<NC, EPI>(p, unit, lane, acc, best, resv);
+            } else {
+                float* slot = pslots + ((size_t) (ul * 2 + (seq & 1)) * NC * 4) * 32;
+                if (half == 1) {  // hand the hi half over: slot free once the even warp took seq - 2
+                    if (seq >= 2) smem_wait_at_least(&pair_ack[ul][seq & 1], seq - 1);
+#pragma unroll
+                    for (int c = 0; c < NC; ++c)
+#pragma unroll
+                        for (int r = 0; r < 4; ++r) slot[(c * 4 + r) * 32 + lane] = acc[c][r];
+                    __syncwarp();
+                    __threadfence_block();
+                    if (lane == 0) *reinterpret_cast<volatile int*>(&pair_flag[ul][seq & 1]) = seq + 1;
+                } else {
+                    smem_wait_at_least(&pair_flag[ul][seq & 1], seq + 1);
+                    __threadfence_block();
+#pragma unroll
+                    for (int c = 0; c < NC; ++c)
+#pragma unroll
+                        for (int r = 0; r < 4; ++r) acc[c][r] = __fadd_rn(acc[c][r], slot[(c * 4 + r) * 32 + lane]);
+                    __syncwarp();
+                    __threadfence_block();  // the slot is read before the odd warp may refill it
+                    if (lane == 0) *reinterpret_cast<volatile int*>(&pair_ack[ul][seq & 1]) = seq + 1;
+                    mmvq_epilogue<NC, EPI>(p, unit, lane, acc, best, resv);
+                }
+            }
 #pragma unroll
             for (int c = 0; c < NC; ++c)
 #pragma unroll
                 for (int r = 0; r < 4; ++r) acc[c][r] = 0.0f;
             kc = 0;
-            unit += W;
-            if (unit < uend) mmvq_res_prefetch<NC, EPI>(p, unit, lane, resv);
+            ++seq;
+            unit += PW;
+            if (unit < uend && half == 0) mmvq_res_prefetch<NC, EPI>(p, unit, lane, resv);
         }
     }
     // The next launch may start only now: its CTAs would otherwise queue their own bulk copies (and the
@@ -583,8 +660,10 @@ __global__ void __launch_bounds__(W * 32, 16 / W) mmvq_packed_kernel(const MmvqP
     // 1 % per token; with rings sized so two launches' CTAs share an SM and the next launch triggered once
     // every warp has issued its last copy, the decode step ran 20-25 % slower).
     pdl_trigger();
-    if constexpr (EPI == EPI_SWIGLU) mmvq_swiglu_finish<NC>(p, ubeg + warp, W, unit, lane);
-    if constexpr (EPI == EPI_ARGMAX) mmvq_argmax_flush<NC>(p, lane, best);
+    if (half == 0) {
+        if constexpr (EPI == EPI_SWIGLU) mmvq_swiglu_finish<NC>(p, ubeg + ul, PW, unit, lane);
+        if constexpr (EPI == EPI_ARGMAX) mmvq_argmax_flush<NC>(p, lane, best);
+    }
 }
 
 // Host-side launcher for one instantiation: sets the smem attribute once, picks the stage count that
@@ -606,7 +685,7 @@ cudaError_t mmvq_launch_w(MmvqParams p, cudaStream_t s, bool pdl) {
         if (max_optin <= 0) max_optin = 227 * 1024;
     }
     const size_t tile = TYPE == RK_TYPE_Q6_K ? kQ6Tile : kQ80Tile;
-    const size_t fixed = mmvq_smem_bytes(TYPE, p.n_in, NC, 0, W);
+    const size_t fixed = mmvq_smem_bytes(TYPE, p.n_in, NC, 0, W) + mmvq_pair_bytes(NC, W);
     // One CTA per SM (8 warps) with a ring of up to 5 slots: measured best on B200 for config 1 (12288 x
     // 4096, 2 columns: 2.8 vs 2.4-2.6 TB/s) and for a decode step of one GEMV launch per op (2.45 vs
     // 2.59 ms). Two 3-slot CTAs per SM leave the busiest warp 8 tiles where the average is 5 (units are
@@ -619,7 +698,7 @@ cudaError_t mmvq_launch_w(MmvqParams p, cudaStream_t s, bool pdl) {
     if (mmvq_env_ctas() > 0) ctas = mmvq_env_ctas();
     if (stages < 2 || stages > kMmvqMaxStages) return cudaErrorInvalidValue;
     p.stages = stages;
-    const size_t smem = mmvq_smem_bytes(TYPE, p.n_in, NC, stages, W);
+    const size_t smem = mmvq_smem_bytes(TYPE, p.n_in, NC, stages, W) + mmvq_pair_bytes(NC, W);
     if ((int) smem > configured_smem) {
         cudaError_t e = cudaFuncSetAttribute(mmvq_packed_kernel<TYPE, NC, PRO, EPI, W>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
@@ -631,10 +710,14 @@ cudaError_t mmvq_launch_w(MmvqParams p, cudaStream_t s, bool pdl) {
     if (grid > units) grid = units;
     return launch_pdl(mmvq_packed_kernel<TYPE, NC, PRO, EPI, W>, dim3(grid), dim3(W * 32), smem, s, pdl, p);
 }
-// RK_MMVQ_WARPS=16: 16 consumer warps per CTA (512 threads, shallower rings) instead of 8.
+// warps: consumer warps per CTA, 8 (256 threads, 5-slot rings) or 16 (512 threads, 3-4 slots).
+// Measured on B200: the decode engine's 2-column GEMVs (the MTP verify and draft) run 8 % faster with 16
+// warps (the integer chains of two columns per tile leave 2 warps per scheduler idle on dependencies),
+// single-column ones 1 % slower, and a lone repeated 41 MB GEMV 10 % slower. RK_MMVQ_WARPS=8|16 overrides.
 template <int TYPE, int NC, int PRO, int EPI>
-cudaError_t mmvq_launch(MmvqParams p, cudaStream_t s, bool pdl) {
-    if (mmvq_env_warps() == 16) return mmvq_launch_w<TYPE, NC, PRO, EPI, 16>(p, s, pdl);
+cudaError_t mmvq_launch(MmvqParams p, cudaStream_t s, bool pdl, int warps = kMmvqWarps) {
+    if (mmvq_env_warps() == 8 || mmvq_env_warps() == 16) warps = mmvq_env_warps();
+    if (warps == 16) return mmvq_launch_w<TYPE, NC, PRO, EPI, 16>(p, s, pdl);
     return mmvq_launch_w<TYPE, NC, PRO, EPI, kMmvqWarps>(p, s, pdl);
 }
 

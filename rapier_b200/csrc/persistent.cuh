@@ -351,7 +351,10 @@ __device__ __forceinline__ bool p_gemv(const MmvqParams& p, uint8_t* xsm, float*
             for (int r = 0; r < 4; ++r) acc[c][r] = 0.0f;
         float resv[4] = {0.0f, 0.0f, 0.0f, 0.0f};
         mmvq_res_prefetch<NC, EPI>(p, unit, lane, resv);
+        float lo[NC][4];  // the first half's chains (an even chunk count runs two chains, mmvq_packed_kernel)
+        const int split = mmvq_split(KC);
         for (int kc = 0; kc < KC; ++kc) {
+            if (kc == split) mmvq_stash_half<NC>(acc, lo);
             if (!pipe_wait(w, 0)) {
                 ok = false;
                 break;
@@ -370,6 +373,7 @@ __device__ __forceinline__ bool p_gemv(const MmvqParams& p, uint8_t* xsm, float*
             pipe_release(w, warp, lane);
         }
         if (!ok) break;
+        if (split < KC) mmvq_join_halves<NC>(acc, lo);
         if constexpr (EPI == EPI_XRES) {  // this rank's partial rows
 #pragma unroll
             for (int c = 0; c < NC; ++c)
