@@ -55,6 +55,10 @@ int mmvq_env_warps() {
     static const int v = env_int("RK_MMVQ_WARPS");
     return v;
 }
+int mmvq_env_pair() {
+    static const int v = env_int("RK_MMVQ_PAIR");
+    return v;
+}
 
 int num_sms() {
     static int n = 0;

@@ -48,6 +48,7 @@ struct MmvqParams {
     const uint8_t* w;  // packed tiles
     int n_in, n_out;
     int stages;
+    int pair;                  // 16-warp launches: warp pairs share units (RK_MMVQ_PAIR=1; set by the launcher)
     int prefetch_before_wait;  // 1: weights are static, stream them before waiting on the upstream grid
     // prologue inputs
     const uint8_t* xq;  // PRO_Q8: Q8_1 blocks, column stride xq_stride bytes (0: rk_q8_1_bytes(n_in, 1))
@@ -520,17 +521,19 @@ __global__ void __launch_bounds__(W * 32, 16 / W) mmvq_packed_kernel(const MmvqP
     const int ng = p.n_in >> 5;
     const int stages = p.stages;
     const int split = mmvq_split(KC);
-    // Warp pairs (16 warps, an even chunk count): warps 2m and 2m + 1 take the two halves of the same units,
-    // so a unit's tiles are consumed by two warps at once; the odd warp hands its half's chains to the even
-    // one through a shared-memory slot, and the even warp adds them (lo + hi) and runs the epilogue.
-    const bool paired = W == 16 && split < KC;
+    // Warp pairs (16 warps, an even chunk count, RK_MMVQ_PAIR=1): warps 2m and 2m + 1 take the two halves of
+    // the same units, so a unit's tiles are consumed by two warps at once; the odd warp hands its half's
+    // chains to the even one through a shared-memory slot, and the even warp adds them (lo + hi) and runs
+    // the epilogue. Measured on the decode's 2-column GEMVs: 4 % slower than 16 unpaired warps (the slots
+    // cost a ring slot per warp and the handoff waits), so off by default.
+    const bool paired = W == 16 && split < KC && p.pair != 0;
     const int PW = paired ? W / 2 : W;           // units in flight per CTA
     const int ul = paired ? warp >> 1 : warp;    // this warp's unit lane
     const int half = paired ? warp & 1 : 0;      // which half of each unit this warp consumes
     const int KT = paired ? split : KC;          // tiles per unit for this warp
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem) + warp * kMmvqMaxStages;
     float* pslots = reinterpret_cast<float*>(smem + W * kMmvqMaxStages * 8);
-    uint8_t* xsm = smem + W * kMmvqMaxStages * 8 + mmvq_pair_bytes(NC, W);
+    uint8_t* xsm = smem + W * kMmvqMaxStages * 8 + (p.pair ? mmvq_pair_bytes(NC, W) : 0);
     uint8_t* ring = xsm + (size_t) NC * ng * 48 + (size_t) warp * stages * TILE;
 
     const int units = p.n_out >> 2;
@@ -673,6 +676,7 @@ __global__ void __launch_bounds__(W * 32, 16 / W) mmvq_packed_kernel(const MmvqP
 int mmvq_env_stages();
 int mmvq_env_ctas();
 int mmvq_env_warps();
+int mmvq_env_pair();  // RK_MMVQ_PAIR > 0: warp pairs in 16-warp launches
 
 template <int TYPE, int NC, int PRO, int EPI, int W>
 cudaError_t mmvq_launch_w(MmvqParams p, cudaStream_t s, bool pdl) {
@@ -685,7 +689,8 @@ cudaError_t mmvq_launch_w(MmvqParams p, cudaStream_t s, bool pdl) {
         if (max_optin <= 0) max_optin = 227 * 1024;
     }
     const size_t tile = TYPE == RK_TYPE_Q6_K ? kQ6Tile : kQ80Tile;
-    const size_t fixed = mmvq_smem_bytes(TYPE, p.n_in, NC, 0, W) + mmvq_pair_bytes(NC, W);
+    p.pair = mmvq_env_pair() > 0 ? 1 : 0;
+    const size_t fixed = mmvq_smem_bytes(TYPE, p.n_in, NC, 0, W) + (p.pair ? mmvq_pair_bytes(NC, W) : 0);
     // One CTA per SM (8 warps) with a ring of up to 5 slots: measured best on B200 for config 1 (12288 x
     // 4096, 2 columns: 2.8 vs 2.4-2.6 TB/s) and for a decode step of one GEMV launch per op (2.45 vs
     // 2.59 ms). Two 3-slot CTAs per SM leave the busiest warp 8 tiles where the average is 5 (units are
@@ -698,7 +703,7 @@ cudaError_t mmvq_launch_w(MmvqParams p, cudaStream_t s, bool pdl) {
     if (mmvq_env_ctas() > 0) ctas = mmvq_env_ctas();
     if (stages < 2 || stages > kMmvqMaxStages) return cudaErrorInvalidValue;
     p.stages = stages;
-    const size_t smem = mmvq_smem_bytes(TYPE, p.n_in, NC, stages, W) + mmvq_pair_bytes(NC, W);
+    const size_t smem = mmvq_smem_bytes(TYPE, p.n_in, NC, stages, W) + (p.pair ? mmvq_pair_bytes(NC, W) : 0);
     if ((int) smem > configured_smem) {
         cudaError_t e = cudaFuncSetAttribute(mmvq_packed_kernel<TYPE, NC, PRO, EPI, W>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
@@ -711,9 +716,10 @@ cudaError_t mmvq_launch_w(MmvqParams p, cudaStream_t s, bool pdl) {
     return launch_pdl(mmvq_packed_kernel<TYPE, NC, PRO, EPI, W>, dim3(grid), dim3(W * 32), smem, s, pdl, p);
 }
 // warps: consumer warps per CTA, 8 (256 threads, 5-slot rings) or 16 (512 threads, 3-4 slots).
-// Measured on B200: the decode engine's 2-column GEMVs (the MTP verify and draft) run 8 % faster with 16
-// warps (the integer chains of two columns per tile leave 2 warps per scheduler idle on dependencies),
-// single-column ones 1 % slower, and a lone repeated 41 MB GEMV 10 % slower. RK_MMVQ_WARPS=8|16 overrides.
+// Measured on B200 (same box, alternating): the decode engine's 2-column GEMVs (the MTP verify and draft)
+// run 9 % faster with 16 warps (the integer chains of two columns per tile leave 2 warps per scheduler
+// idle on dependencies; the MTP decode +5.4 %), single-column ones 6 % slower (the no-MTP decode -5 %), and
+// a lone repeated 41 MB GEMV 10 % slower. RK_MMVQ_WARPS=8|16 overrides.
 template <int TYPE, int NC, int PRO, int EPI>
 cudaError_t mmvq_launch(MmvqParams p, cudaStream_t s, bool pdl, int warps = kMmvqWarps) {
     if (mmvq_env_warps() == 8 || mmvq_env_warps() == 16) warps = mmvq_env_warps();
