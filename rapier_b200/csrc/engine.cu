@@ -272,7 +272,7 @@ struct EngineImpl {
     void gen_f32(int tid, float* dst, size_t n, double std, double mean, int kind,
                  const std::vector<long long>* pick = nullptr);
     void gen_q6k(int tid, Mat& group, int row_off, int n_in_full, int grow0, int rows, int cb_a, int ncb_a, int cb_b,
-                 int ncb_b, uint8_t* scratch, int row_blocks = 0);
+                 int ncb_b, uint8_t* scratch, int row_blocks = 0, int grow1 = 0, int rows1 = 0);
     void gen_q6k_into(int tid, Mat& group, int row_off, int n_in, int n_out, uint8_t* scratch) {
         gen_q6k(tid, group, row_off, n_in, 0, n_out, 0, n_in / 256, 0, 0, scratch);
     }
@@ -407,41 +407,47 @@ void EngineImpl::gen_f32(int tid, float* dst, size_t n, double std, double mean,
 // ncb_a + ncb_b; wider rows end in all-zero blocks: d = 0, so they add exactly nothing to a dot product,
 // whatever the activations they meet).
 void EngineImpl::gen_q6k(int tid, Mat& group, int row_off, int n_in_full, int grow0, int rows, int cb_a, int ncb_a,
-                         int cb_b, int ncb_b, uint8_t* scratch, int row_blocks) {
+                         int cb_b, int ncb_b, uint8_t* scratch, int row_blocks, int grow1, int rows1) {
     if (row_blocks < ncb_a + ncb_b) row_blocks = ncb_a + ncb_b;
     const int n_in = row_blocks * 256;
-    const long long nb = (long long) rows * (ncb_a + ncb_b);
+    const size_t lrb = (size_t) row_blocks * 210;
     if (row_blocks > ncb_a + ncb_b && err == cudaSuccess)
-        err = cudaMemsetAsync(scratch, 0, (size_t) rows * row_blocks * 210, s);
-    if (gg) {  // the GGUF rows' bytes (this slice's column blocks), then the same repack
-        const std::string name = gguf_name(tid);
-        const GgufTensor* t = gg->find(name);
-        if (!t) return (void) src_fail(RK_EINVAL, "tensor " + name + " missing");
-        if (t->type != kGgmlQ6_K)
-            return (void) src_fail(RK_EUNSUPPORTED, "tensor " + name + " is ggml type " + std::to_string(t->type) +
-                                                        "; the engine's GEMVs take Q6_K (14)");
-        if (t->ne[0] != n_in_full || t->ne[1] < (int64_t) grow0 + rows)
-            return (void) src_fail(RK_EINVAL, "tensor " + name + " has an unexpected shape");
-        const size_t rb = ggml_row_bytes(kGgmlQ6_K, n_in_full), lrb = (size_t) row_blocks * 210;
-        stage.assign((size_t) rows * lrb, 0);
-        for (int r = 0; r < rows; ++r) {
-            const uint8_t* src = t->data + (size_t) (grow0 + r) * rb;
-            std::memcpy(stage.data() + (size_t) r * lrb, src + (size_t) cb_a * 210, (size_t) ncb_a * 210);
-            if (ncb_b) std::memcpy(stage.data() + (size_t) r * lrb + (size_t) ncb_a * 210, src + (size_t) cb_b * 210, (size_t) ncb_b * 210);
+        err = cudaMemsetAsync(scratch, 0, (size_t) (rows + rows1) * lrb, s);
+    // rows [grow0, grow0 + rows), then (optional) rows [grow1, grow1 + rows1), staged back to back
+    const int gr[2] = {grow0, grow1}, nr[2] = {rows, rows1};
+    for (int k = 0; k < 2 && nr[k] > 0; ++k) {
+        uint8_t* out = scratch + (size_t) (k == 0 ? 0 : rows) * lrb;
+        if (gg) {  // the GGUF rows' bytes (this slice's column blocks), then the same repack
+            const std::string name = gguf_name(tid);
+            const GgufTensor* t = gg->find(name);
+            if (!t) return (void) src_fail(RK_EINVAL, "tensor " + name + " missing");
+            if (t->type != kGgmlQ6_K)
+                return (void) src_fail(RK_EUNSUPPORTED, "tensor " + name + " is ggml type " + std::to_string(t->type) +
+                                                            "; the engine's GEMVs take Q6_K (14)");
+            if (t->ne[0] != n_in_full || t->ne[1] < (int64_t) gr[k] + nr[k])
+                return (void) src_fail(RK_EINVAL, "tensor " + name + " has an unexpected shape");
+            const size_t rb = ggml_row_bytes(kGgmlQ6_K, n_in_full);
+            stage.assign((size_t) nr[k] * lrb, 0);
+            for (int r = 0; r < nr[k]; ++r) {
+                const uint8_t* src = t->data + (size_t) (gr[k] + r) * rb;
+                std::memcpy(stage.data() + (size_t) r * lrb, src + (size_t) cb_a * 210, (size_t) ncb_a * 210);
+                if (ncb_b) std::memcpy(stage.data() + (size_t) r * lrb + (size_t) ncb_a * 210, src + (size_t) cb_b * 210, (size_t) ncb_b * 210);
+            }
+            if (err == cudaSuccess) err = cudaMemcpyAsync(out, stage.data(), stage.size(), cudaMemcpyHostToDevice, s);
+            if (err == cudaSuccess) err = cudaStreamSynchronize(s);
+        } else {
+            const uint64_t st = hash64(cfg.seed, (uint64_t) tid);
+            const long long nb = (long long) nr[k] * (ncb_a + ncb_b);
+            gen_q6k_kernel<<<(unsigned) ((nb + 127) / 128), 128, 0, s>>>(st, synth_scale(0.02), nr[k], gr[k], n_in_full / 256,
+                                                                         ncb_a, cb_a, ncb_b, cb_b, row_blocks, out);
+            if (err == cudaSuccess) err = cudaGetLastError();
         }
-        if (err == cudaSuccess) err = cudaMemcpyAsync(scratch, stage.data(), stage.size(), cudaMemcpyHostToDevice, s);
-        if (err == cudaSuccess) err = cudaStreamSynchronize(s);
-    } else {
-        const uint64_t st = hash64(cfg.seed, (uint64_t) tid);
-        gen_q6k_kernel<<<(unsigned) ((nb + 127) / 128), 128, 0, s>>>(st, synth_scale(0.02), rows, grow0, n_in_full / 256,
-                                                                     ncb_a, cb_a, ncb_b, cb_b, row_blocks, scratch);
-        if (err == cudaSuccess) err = cudaGetLastError();
     }
     if (err != cudaSuccess) return;
     uint8_t* dst = group.w + (size_t) (row_off / 4) * (n_in / 1024) * kQ6Tile;
-    const int rc = rk_pack_weights(RK_TYPE_Q6_K, scratch, dst, n_in, rows, s);
+    const int rc = rk_pack_weights(RK_TYPE_Q6_K, scratch, dst, n_in, rows + rows1, s);
     if (rc != RK_OK && err == cudaSuccess) err = cudaErrorInvalidValue;
-    tensors.push_back({tid, true, n_in, rows, group.w, (size_t) row_off, false});
+    tensors.push_back({tid, true, n_in, rows + rows1, group.w, (size_t) row_off, false});
 }
 
 int EngineImpl::build() {
@@ -544,10 +550,11 @@ int EngineImpl::build() {
                 rows_of(layer_tid(il, L_GDN_Z), L.in_proj, z0, H, va, n);
                 rows_of(layer_tid(il, L_GDN_Z), L.in_proj, z0 + n, H, vb, n);
                 const int b0 = z0 + hv * S;
-                rows_of(layer_tid(il, L_GDN_BETA), L.in_proj, b0, H, g * hk, hk);
-                rows_of(layer_tid(il, L_GDN_BETA), L.in_proj, b0 + hk, H, hkg + g * hk, hk);
-                rows_of(layer_tid(il, L_GDN_ALPHA), L.in_proj, b0 + hv, H, g * hk, hk);
-                rows_of(layer_tid(il, L_GDN_ALPHA), L.in_proj, b0 + hv + hk, H, hkg + g * hk, hk);
+                // beta / alpha rows of both v-head ranges in one repack each (hk may be 2: a 4-row tile spans both)
+                gen_q6k(layer_tid(il, L_GDN_BETA), L.in_proj, b0, H, g * hk, hk, 0, H / 256, 0, 0, scratch, 0,
+                        hkg + g * hk, hk);
+                gen_q6k(layer_tid(il, L_GDN_ALPHA), L.in_proj, b0 + hv, H, g * hk, hk, 0, H / 256, 0, 0, scratch, 0,
+                        hkg + g * hk, hk);
             }
             // ssm_out row-parallel over this rank's v-head outputs (two column ranges)
             L.out_proj = mat(tp_in(hv * S), H);
@@ -1171,10 +1178,11 @@ static int create_engine(const rk_model_config* cfg, int device, int tp_rank, in
         const int N = tp_size;
         const bool kv_split = c.n_head_kv % N == 0;
         const bool kv_repl = N % c.n_head_kv == 0 && c.n_head % N == 0 && (c.n_head / N == 2 || c.n_head / N == 4);
-        if (c.ssm_h_k % N || c.n_head % N || !(kv_split || kv_repl) || c.n_ff % (256 * N) ||
+        if (c.ssm_h_k % (2 * N) || c.n_head % N || !(kv_split || kv_repl) || c.n_ff % (256 * N) ||
             (c.ssm_h_v * kSsm) % (256 * N) || (2 * c.n_embd) % (256 * N) || c.n_vocab % (4 * N))
             return set_error(RK_EUNSUPPORTED,
-                             "%s: tensor parallelism over %d ranks needs k-heads and q heads divisible by it, 2 or 4 "
+                             "%s: tensor parallelism over %d ranks needs an even number of k-heads per rank, q heads "
+                             "divisible by the ranks, 2 or 4 "
                              "q heads per kv head on a rank, and every rank's row-parallel input a multiple of 256",
                              what, N);
         const char* mode = std::getenv("RK_ENGINE_MODE");
