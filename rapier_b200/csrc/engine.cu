@@ -242,7 +242,7 @@ struct EngineImpl {
     // tensor parallelism: this rank's exchange memory (exported by CUDA IPC), the peers' mappings, and the
     // descriptor the kernels read
     uint8_t* xmem = nullptr;
-    size_t xmem_bytes = 0, xoff_flags = 0, xoff_keys = 0;
+    size_t xmem_bytes = 0, xoff_flags = 0, xoff_keys = 0, xoff_ep = 0;
     XchDesc* xdesc = nullptr;
     std::vector<void*> peer_maps;
     bool tp_connected = false;
@@ -891,9 +891,10 @@ int EngineImpl::setup_executor() {
     // kernel (its row-parallel exchanges run inside it). RK_ENGINE_MODE=graph|persistent overrides.
     const char* mode = std::getenv("RK_ENGINE_MODE");
     persistent = mode ? std::strcmp(mode, "graph") != 0 : tp_size > 1;
-    if (!persistent) return RK_OK;
     int sms = 0, optin = 0;
     if ((err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return RK_ECUDA;
+    p_grid = sms;  // also the exchange's flag slots in graph mode (one GEMV CTA per SM)
+    if (!persistent) return RK_OK;
     if ((err = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) != cudaSuccess)
         return RK_ECUDA;
     // Two slots per warp (32 tiles, 107 KB in flight per SM) keep HBM busy; deeper rings only queue more
@@ -955,7 +956,13 @@ cudaError_t EngineImpl::launch_op(const POp& op) {
             return mmvq_launch<RK_TYPE_Q6_K, NC, PRO_RMS, EPI_ARGMAX>(p, s, true, w);
         }
         if (op.epi == EPI_RES) return mmvq_launch<RK_TYPE_Q6_K, NC, PRO_Q8, EPI_RES>(p, s, true, w);
+        if constexpr (NC <= 2)  // the exchange buffers hold two columns (tensor parallelism has no prefill program)
+            if (op.epi == EPI_XRES) return mmvq_launch<RK_TYPE_Q6_K, NC, PRO_Q8, EPI_XRES>(p, s, true, w);
         return mmvq_launch<RK_TYPE_Q6_K, NC, PRO_Q8, EPI_STORE_P>(p, s, true, w);
+    }
+    if (op.kind == POP_XARGMAX) {
+        if constexpr (NC <= 2) return launch_pdl(xargmax_kernel<NC>, dim3(1), dim3(32), 0, s, true, op, ctrl);
+        return cudaErrorInvalidValue;
     }
     static int sms = 0;
     if (sms == 0 && cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) sms = 148;
@@ -1118,9 +1125,10 @@ void EngineImpl::set_ctrl_eos(int eos_id) {
     if (e != cudaSuccess && err == cudaSuccess) err = e;
 }
 
-// After a synchronized run: a persistent launch that gave up on a wait leaves the sticky abort word.
+// After a synchronized run: a persistent launch that gave up on a wait, or (graph mode, tensor parallelism)
+// an exchange that gave up on a peer, leaves the sticky abort word.
 int EngineImpl::check_abort(const char* what) {
-    if (!persistent) return RK_OK;
+    if (!persistent && tp_size == 1) return RK_OK;
     PSync h = {};
     if (cudaMemcpy(&h, psync, sizeof h, cudaMemcpyDeviceToHost) != cudaSuccess)
         return set_error(RK_ECUDA, "%s: reading the executor state failed", what);
@@ -1185,9 +1193,6 @@ static int create_engine(const rk_model_config* cfg, int device, int tp_rank, in
                              "divisible by the ranks, 2 or 4 "
                              "q heads per kv head on a rank, and every rank's row-parallel input a multiple of 256",
                              what, N);
-        const char* mode = std::getenv("RK_ENGINE_MODE");
-        if (mode && std::strcmp(mode, "graph") == 0)
-            return set_error(RK_EUNSUPPORTED, "%s: tensor parallelism needs the persistent executor", what);
     }
     if (c.n_layer < 1 || c.n_embd <= 0 || c.n_embd % 1024 || c.n_ff <= 0 || c.n_ff % 1024 || c.n_vocab <= 0 ||
         c.n_vocab % 4)
@@ -1214,12 +1219,13 @@ static int create_engine(const rk_model_config* cfg, int device, int tp_rank, in
         return set_error(rc, "%s: %s", what, msg.c_str());
     }
     if (rc == RK_OK) rc = E.setup_executor();
-    if (rc == RK_OK && tp_size > 1 && !E.persistent) rc = RK_EUNSUPPORTED;
     if (rc == RK_OK && tp_size > 1) {
-        // this rank's exchange memory: partials [2][8][2][H] floats | flags [grid + 1][8] | keys [2][8][2]
+        // this rank's exchange memory: partials [2][8][2][H] floats | flags [grid + 1][8] | keys [2][8][2] |
+        // the graph executor's epoch per flag slot [grid + 1] (local only; the peers write flags and keys)
         E.xoff_flags = (size_t) 2 * kMaxRanks * 2 * E.H * sizeof(float);
         E.xoff_keys = E.xoff_flags + (size_t) (E.p_grid + 1) * kMaxRanks * 8;
-        E.xmem_bytes = E.xoff_keys + (size_t) 2 * kMaxRanks * 2 * 8;
+        E.xoff_ep = E.xoff_keys + (size_t) 2 * kMaxRanks * 2 * 8;
+        E.xmem_bytes = E.xoff_ep + (size_t) (E.p_grid + 1) * 8;
         void* p = nullptr;
         if ((E.err = cudaMalloc(&p, E.xmem_bytes)) != cudaSuccess) rc = RK_ENOMEM;
         if (rc == RK_OK) {
@@ -1279,8 +1285,6 @@ static int create_engine(const rk_model_config* cfg, int device, int tp_rank, in
         if (rc == RK_ENOMEM || ce == cudaErrorMemoryAllocation)
             return set_error(RK_ENOMEM, "%s: out of device memory", what);
         if (rc == RK_EINVAL) return set_error(RK_EINVAL, "%s: unsupported GEMV prologue/epilogue pair", what);
-        if (rc == RK_EUNSUPPORTED)
-            return set_error(RK_EUNSUPPORTED, "%s: tensor parallelism needs the persistent executor", what);
         return set_error(RK_ECUDA, "%s: %s", what, cudaGetErrorString(ce));
     }
     *out = e;
@@ -1349,6 +1353,8 @@ int rk_engine_tp_connect(rk_engine* e, const void* handles, size_t bytes_per_ran
         d.flags[q] = reinterpret_cast<unsigned long long*>(base + E.xoff_flags);
         d.keys[q] = reinterpret_cast<unsigned long long*>(base + E.xoff_keys);
     }
+    d.ep = reinterpret_cast<unsigned long long*>(E.xmem + E.xoff_ep);
+    d.sync = E.psync;
     const cudaError_t ce = cudaMemcpy(E.xdesc, &d, sizeof d, cudaMemcpyHostToDevice);
     if (ce != cudaSuccess) return set_error(RK_ECUDA, "%s: %s", what, cudaGetErrorString(ce));
     E.tp_connected = true;

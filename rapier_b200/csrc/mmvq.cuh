@@ -26,6 +26,7 @@
 #pragma once
 
 #include "common.cuh"
+#include "xch.cuh"
 
 namespace rk {
 
@@ -41,8 +42,6 @@ enum MmvqPro { PRO_Q8 = 0, PRO_RMS = 1 };
 // EPI_XRES (persistent decode kernel under tensor parallelism): a row-parallel GEMV's partial sums are
 // summed over the ranks (peer memory), then as EPI_RES (res != null) or EPI_STORE_P (res == null).
 enum MmvqEpi { EPI_STORE = 0, EPI_RES = 1, EPI_ARGMAX = 2, EPI_STORE_P = 3, EPI_SWIGLU = 4, EPI_XRES = 5 };
-
-struct XchDesc;  // persistent.cuh
 
 struct MmvqParams {
     const uint8_t* w;  // packed tiles
@@ -152,7 +151,7 @@ __device__ __forceinline__ void xstage_put_warp(const XStage& s, int g, int code
 // as block256_partials_sum does (threads 0..255, then the 8 warp totals in order), every column at once,
 // with one block-wide barrier; `red` holds NC * 8 floats.
 template <int NC, int PRO>
-__device__ __noinline__ void mmvq_build_x(const MmvqParams& p, uint8_t* xsm, float* red) {
+__device__ __forceinline__ void mmvq_build_x_body(const MmvqParams& p, uint8_t* xsm, float* red) {
     static_assert(PRO != PRO_RMS || NC <= kRedCols, "red holds kRedCols columns of warp totals");
     const int ng = p.n_in >> 5;
     if constexpr (PRO == PRO_Q8) {
@@ -271,6 +270,13 @@ __device__ __noinline__ void mmvq_build_x(const MmvqParams& p, uint8_t* xsm, flo
             }
         }
     }
+}
+// The same as a call (the persistent kernel, whose op bodies stay out of line). mmvq_packed_kernel inlines
+// the body: a call that takes the kernel's parameter block by reference makes every thread copy the block
+// (184 bytes) to its stack at entry.
+template <int NC, int PRO>
+__device__ __noinline__ void mmvq_build_x(const MmvqParams& p, uint8_t* xsm, float* red) {
+    mmvq_build_x_body<NC, PRO>(p, xsm, red);
 }
 
 // The 6-bit codes of one row of a group as eight ints (byte b of int T = code of value 4T + b), from the
@@ -441,6 +447,67 @@ __device__ __forceinline__ void mmvq_res_prefetch(const MmvqParams& p, int unit,
     }
 }
 
+// EPI_XRES (tensor parallelism, both executors): a unit's 4 x NC row sums of this rank's share of the input
+// (the xor butterfly per value) go into this rank's slot of every rank's partial buffer (posted peer
+// stores); `yoff` (xres_offset) selects the slot and the epoch's parity half.
+__device__ __forceinline__ size_t xres_offset(const XchDesc* x, unsigned long long ep) {
+    return (((size_t) (ep & 1ull) * kMaxRanks + x->rank) * 2) * x->rows;
+}
+template <int NC>
+__device__ __forceinline__ void xres_push(const XchDesc* x, size_t yoff, int unit, int lane, float (&acc)[NC][4]) {
+#pragma unroll
+    for (int c = 0; c < NC; ++c)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) acc[c][r] = warp_sum(acc[c][r]);
+    float out = 0.0f;
+#pragma unroll
+    for (int c = 0; c < NC; ++c)
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+            if (lane == c * 4 + r) out = acc[c][r];
+    if (lane < NC * 4) {
+        const size_t o = yoff + (size_t) (lane >> 2) * x->rows + (size_t) unit * 4 + (lane & 3);
+        for (int q = 0; q < x->n; ++q) x->buf[q][o] = out;
+    }
+}
+// After a CTA's units (all threads call it): signal flag slot `slot` of every peer and wait for theirs, then
+// sum the CTA's rows [4 ubeg, 4 uend) over the ranks in rank order (every rank gets the same bits), add the
+// residual and write y and the 4-row partials as EPI_RES does (EPI_STORE_P without a residual). A CTA with
+// a failed part (`ok` false in any thread) does not signal, so its peers' waits give up too.
+template <int NC>
+__device__ __forceinline__ bool xres_finish(const MmvqParams& p, int ubeg, int uend, int slot, unsigned long long ep,
+                                            PSync* sync, int* sflag, bool ok) {
+    __threadfence_system();  // this thread's pushed partials, before the CTA's signal
+    const int all_ok = __syncthreads_and(ok ? 1 : 0);
+    if (threadIdx.x == 0) *sflag = all_ok && xch_signal_wait(p.xch, slot, ep, sync);
+    __syncthreads();
+    if (!*sflag) return false;
+    const XchDesc* x = p.xch;
+    const int n = x->n;
+    const float* mine = x->buf[x->rank] + (size_t) (ep & 1ull) * kMaxRanks * 2 * x->rows;
+    const size_t src_stride = (size_t) 2 * x->rows;
+    for (int idx = (int) threadIdx.x; idx < (uend - ubeg) * NC; idx += (int) blockDim.x) {
+        const int u = ubeg + idx / NC, c = idx % NC;
+        float part = 0.0f;
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const size_t off = (size_t) c * x->rows + (size_t) u * 4 + r;
+            float pq[kMaxRanks];
+#pragma unroll
+            for (int q = 0; q < kMaxRanks; ++q) pq[q] = q < n ? __ldcg(mine + q * src_stride + off) : 0.0f;
+            float v = pq[0];
+#pragma unroll
+            for (int q = 1; q < kMaxRanks; ++q)
+                if (q < n) v = __fadd_rn(v, pq[q]);
+            if (p.res != nullptr) v = __fadd_rn(v, __ldcg(p.res + (size_t) c * p.res_stride + (size_t) u * 4 + r));
+            p.y[(size_t) c * p.y_stride + (size_t) u * 4 + r] = v;
+            part = __fmaf_rn(v, v, part);
+        }
+        p.pout[(size_t) c * p.pout_stride + u] = part;
+    }
+    return true;
+}
+
 // EPI_SWIGLU, after a warp's units [first, end) (stride `stride`) are written: one fence, then one arrival
 // per unit (issued by different lanes at once); for every 32-position block whose 16 units (8 up + 8 gate)
 // are done, the warp whose arrival completed it writes the Q8_1 block of silu(gate) * up (the down GEMV's
@@ -526,7 +593,7 @@ __global__ void __launch_bounds__(W * 32, 16 / W) mmvq_packed_kernel(const MmvqP
     // chains to the even one through a shared-memory slot, and the even warp adds them (lo + hi) and runs
     // the epilogue. Measured on the decode's 2-column GEMVs: 4 % slower than 16 unpaired warps (the slots
     // cost a ring slot per warp and the handoff waits), so off by default.
-    const bool paired = W == 16 && split < KC && p.pair != 0;
+    const bool paired = EPI != EPI_XRES && W == 16 && split < KC && p.pair != 0;
     const int PW = paired ? W / 2 : W;           // units in flight per CTA
     const int ul = paired ? warp >> 1 : warp;    // this warp's unit lane
     const int half = paired ? warp & 1 : 0;      // which half of each unit this warp consumes
@@ -573,9 +640,22 @@ __global__ void __launch_bounds__(W * 32, 16 / W) mmvq_packed_kernel(const MmvqP
     pdl_wait();
     if (!p.prefetch_before_wait && lane == 0)
         for (int i = 0; i < npre; ++i) issue(i);
+    // EPI_XRES (the graph executor under tensor parallelism): this CTA's exchange epoch, from the counter
+    // of its flag slot (the previous exchange on this slot was written back by a launch now complete)
+    __shared__ unsigned long long xep_sh;
+    __shared__ int xflag_sh;
+    if constexpr (EPI == EPI_XRES)
+        if (threadIdx.x == 0) xep_sh = xch_epoch_next(p.xch, (int) blockIdx.x);
 
-    mmvq_build_x<NC, PRO>(p, xsm, red);
+    mmvq_build_x_body<NC, PRO>(p, xsm, red);
     __syncthreads();
+    unsigned long long xep = 0ull;
+    size_t yoff = 0;
+    if constexpr (EPI == EPI_XRES) {
+        xep = xep_sh;
+        yoff = xres_offset(p.xch, xep);
+    }
+    bool ok = true;
 
     float acc[NC][4], lo[NC][4];
     unsigned long long best[NC];
@@ -596,7 +676,10 @@ __global__ void __launch_bounds__(W * 32, 16 / W) mmvq_packed_kernel(const MmvqP
     const int kbase = half * KT;  // this warp's first chunk of a unit
     for (int i = 0; i < ntiles; ++i) {
         const bool landed = mbar_wait_bounded(smem_u32(bars + s), parity);
-        if (!__all_sync(0xffffffffu, landed)) break;
+        if (!__all_sync(0xffffffffu, landed)) {
+            ok = false;
+            break;
+        }
         if (!paired && kc == split) mmvq_stash_half<NC>(acc, lo);
         const uint8_t* t = ring + (size_t) s * TILE;
         int4 xa[NC], xb[NC];
@@ -623,7 +706,8 @@ __global__ void __launch_bounds__(W * 32, 16 / W) mmvq_packed_kernel(const MmvqP
         if (++kc == KT) {
             if (!paired) {
                 if (split < KC) mmvq_join_halves<NC>(acc, lo);
-                mmvq_epilogue<NC, EPI>(p, unit, lane, acc, best, resv);
+                if constexpr (EPI == EPI_XRES) xres_push<NC>(p.xch, yoff, unit, lane, acc);
+                else mmvq_epilogue<NC, EPI>(p, unit, lane, acc, best, resv);
             } else {
                 float* slot = pslots + ((size_t) (ul * 2 + (seq & 1)) * NC * 4) * 32;
                 if (half == 1) {  // hand the hi half over: slot free once the even warp took seq - 2
@@ -667,6 +751,12 @@ __global__ void __launch_bounds__(W * 32, 16 / W) mmvq_packed_kernel(const MmvqP
         if constexpr (EPI == EPI_SWIGLU) mmvq_swiglu_finish<NC>(p, ubeg + ul, PW, unit, lane);
         if constexpr (EPI == EPI_ARGMAX) mmvq_argmax_flush<NC>(p, lane, best);
     }
+    if constexpr (EPI == EPI_XRES) {
+        PSync* sync = p.xch->sync;
+        if (!xres_finish<NC>(p, ubeg, uend, (int) blockIdx.x, xep, sync, &xflag_sh, ok) && threadIdx.x == 0)
+            atomicExch(&sync->abort, 1u);  // for the host, and so that later waits of this rank end at once
+        if (threadIdx.x == 0) xch_epoch_done(p.xch, (int) blockIdx.x, xep);
+    }
 }
 
 // Host-side launcher for one instantiation: sets the smem attribute once, picks the stage count that
@@ -700,7 +790,7 @@ cudaError_t mmvq_launch_w(MmvqParams p, cudaStream_t s, bool pdl) {
     int stages = (int) (((long long) max_optin - 2048 - (long long) fixed) / (long long) (W * tile));
     if (stages > 5) stages = 5;
     if (mmvq_env_stages() > 0) stages = mmvq_env_stages();
-    if (mmvq_env_ctas() > 0) ctas = mmvq_env_ctas();
+    if (mmvq_env_ctas() > 0 && EPI != EPI_XRES) ctas = mmvq_env_ctas();  // an exchange CTA owns a flag slot per SM
     if (stages < 2 || stages > kMmvqMaxStages) return cudaErrorInvalidValue;
     p.stages = stages;
     const size_t smem = mmvq_smem_bytes(TYPE, p.n_in, NC, stages, W) + (p.pair ? mmvq_pair_bytes(NC, W) : 0);

@@ -38,31 +38,6 @@
 
 namespace rk {
 
-struct PSync {
-    unsigned long long arrive;  // grid-barrier arrivals of the running launch
-    unsigned exits;             // CTAs of the running launch that have finished
-    unsigned abort;             // sticky give-up flag, cleared by the host
-    unsigned long long xepoch;  // tensor parallelism: exchanges done so far (monotonic, never cleared)
-};
-
-// Tensor parallelism: every rank's exchange memory, mapped into this rank's address space (CUDA IPC over
-// NVLink). A rank pushes its row-parallel partial sums into its own slot of every rank's buffer (posted
-// peer stores), then signals each peer by a system-scope release store of the exchange's epoch into the
-// peer's flag slot; a rank that has acquired all the signals of a slot sums the partials from its own
-// memory. Epochs only grow, the flag words of a slot only grow, so no flag is ever cleared; buffers
-// alternate by epoch parity, and a rank starts an exchange only after every peer has signalled the
-// previous one (which a peer does after reading), so no buffer is rewritten while read.
-constexpr int kMaxRanks = 8;
-struct XchDesc {
-    int rank, n;  // this rank, number of ranks
-    int rows;     // rows of a partial column (the hidden size)
-    int slots;    // flag slots: one per persistent CTA + one for the argmax exchange
-    unsigned long long wait_ns;            // a cross-rank wait gives up after this long
-    float* buf[kMaxRanks];                 // per rank: partials [2 parity][kMaxRanks source][2 columns][rows]
-    unsigned long long* flags[kMaxRanks];  // per rank: [slots][kMaxRanks] epochs, written by the peers
-    unsigned long long* keys[kMaxRanks];   // per rank: argmax keys [2 parity][kMaxRanks][2 columns]
-};
-
 // One GEMV of a program, as the weight cursors see it (built by the host in program order).
 struct GemvEnt {
     const uint8_t* w;  // packed tiles
@@ -73,24 +48,8 @@ static_assert(sizeof(GemvEnt) == 16, "GemvEnt is copied in 16-byte chunks");
 constexpr int kMaxGemvOps = 256;
 constexpr int kPWarps = 16;  // warps of a persistent CTA; all consume GEMV tiles
 
-constexpr unsigned long long kGridSpinNs = 1000000000ull;  // a grid barrier gives up after 1 s
-constexpr unsigned long long kPeerSpinNs = 5000000000ull;  // default cross-rank wait bound (a peer's host may lag)
-
-__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p) {
-    unsigned long long v;
-    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-    return v;
-}
-__device__ __forceinline__ unsigned ld_volatile_u32(const unsigned* p) {
-    return *reinterpret_cast<const volatile unsigned*>(p);
-}
 __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ unsigned long long globaltimer_ns() {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
 }
 
 // Grid barrier: the counter starts at 0 in every launch and every barrier adds gridDim.x arrivals. A CTA
@@ -130,66 +89,6 @@ __device__ __forceinline__ bool grid_sync(PSync* sync, unsigned long long& targe
     // the acquire above and this bar.sync order the whole CTA's later reads after every arrival
     __syncthreads();
     return *flag != 0;
-}
-
-__device__ __forceinline__ void st_release_sys_u64(unsigned long long* p, unsigned long long v) {
-    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
-    unsigned long long v;
-    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-    return v;
-}
-
-// One thread: signal flag slot `slot` of every peer with `epoch` (after a system-scope fence that makes
-// this CTA's preceding writes visible), then wait until every peer has signalled this rank's slot. The
-// wait gives up after x->wait_ns (status bit, abort). Returns false when the program must stop.
-__device__ __noinline__ bool xch_signal_wait(const XchDesc* x, int slot, unsigned long long epoch, PSync* sync) {
-    const int me = x->rank, n = x->n;
-    __threadfence_system();
-    for (int q = 0; q < n; ++q)
-        if (q != me) st_release_sys_u64(x->flags[q] + (size_t) slot * kMaxRanks + me, epoch);
-    const unsigned long long* mine = x->flags[me] + (size_t) slot * kMaxRanks;
-    const unsigned long long t0 = globaltimer_ns();
-    for (int q = 0; q < n; ++q) {
-        if (q == me) continue;
-        for (uint32_t it = 0; ld_acquire_sys_u64(mine + q) < epoch; ++it) {
-            if (ld_volatile_u32(&sync->abort)) return false;
-            if ((it & 63u) == 63u && globaltimer_ns() - t0 > x->wait_ns) {
-                atomicOr(&g_rk_status, kStatusGridTimeout);
-                atomicExch(&sync->abort, 1u);
-                return false;
-            }
-            if (it >= 256u) __nanosleep(32);
-        }
-    }
-    return true;
-}
-
-// The global argmax of the ranks' vocabulary shards (thread 0 of CTA 0): every rank's per-column keys
-// (value, ~global row) go to every rank, and the maximum replaces this rank's slot, so all ranks continue
-// with the same token.
-template <int NC>
-__device__ __noinline__ bool xch_argmax(const XchDesc* x, unsigned long long* slots, unsigned long long epoch,
-                                        PSync* sync) {
-    const int me = x->rank, n = x->n, par = (int) (epoch & 1ull);
-    volatile unsigned long long* vs = slots;
-    unsigned long long mine[NC];
-#pragma unroll
-    for (int c = 0; c < NC; ++c) mine[c] = vs[c];
-    for (int q = 0; q < n; ++q)
-#pragma unroll
-        for (int c = 0; c < NC; ++c) x->keys[q][((size_t) par * kMaxRanks + me) * 2 + c] = mine[c];
-    if (!xch_signal_wait(x, x->slots - 1, epoch, sync)) return false;
-    const volatile unsigned long long* k = x->keys[me] + (size_t) par * kMaxRanks * 2;
-#pragma unroll
-    for (int c = 0; c < NC; ++c) {
-        unsigned long long best = 0ull;
-        for (int q = 0; q < n; ++q) best = k[q * 2 + c] > best ? k[q * 2 + c] : best;
-        vs[c] = best;
-    }
-    __threadfence();
-    return true;
 }
 
 // ---------------------------------------------------------------------------------------------------
@@ -327,7 +226,7 @@ __device__ __forceinline__ bool p_gemv(const MmvqParams& p, uint8_t* xsm, float*
     size_t yoff = 0;  // this rank's slot in every rank's partial buffer for this exchange
     if constexpr (EPI == EPI_XRES) {
         ep = ++xep;
-        yoff = (((size_t) (ep & 1ull) * kMaxRanks + p.xch->rank) * 2) * p.xch->rows;
+        yoff = xres_offset(p.xch, ep);
     }
     mmvq_build_x<NC, PRO>(p, xsm, red);
     __syncthreads();
@@ -374,58 +273,13 @@ __device__ __forceinline__ bool p_gemv(const MmvqParams& p, uint8_t* xsm, float*
         }
         if (!ok) break;
         if (split < KC) mmvq_join_halves<NC>(acc, lo);
-        if constexpr (EPI == EPI_XRES) {  // this rank's partial rows
-#pragma unroll
-            for (int c = 0; c < NC; ++c)
-#pragma unroll
-                for (int r = 0; r < 4; ++r) acc[c][r] = warp_sum(acc[c][r]);
-            float out = 0.0f;
-#pragma unroll
-            for (int c = 0; c < NC; ++c)
-#pragma unroll
-                for (int r = 0; r < 4; ++r)
-                    if (lane == c * 4 + r) out = acc[c][r];
-            if (lane < NC * 4) {  // pushed to every rank (peer stores are posted)
-                const size_t o = yoff + (size_t) (lane >> 2) * p.xch->rows + unit * 4 + (lane & 3);
-                for (int q = 0; q < p.xch->n; ++q) p.xch->buf[q][o] = out;
-            }
+        if constexpr (EPI == EPI_XRES) {  // this rank's partial rows, pushed to every rank
+            xres_push<NC>(p.xch, yoff, unit, lane, acc);
         } else {
             mmvq_epilogue<NC, EPI>(p, unit, lane, acc, best, resv);
         }
     }
-    if constexpr (EPI == EPI_XRES) {
-        // sum this CTA's rows over the ranks (the same rows on every rank: same grid, same split), in rank
-        // order, then the residual add and the 4-row partials as EPI_RES (or EPI_STORE_P without res)
-        __threadfence_system();  // this thread's pushed partials, before the CTA's signal
-        __syncthreads();
-        if (threadIdx.x == 0) *sflag = ok && xch_signal_wait(p.xch, (int) blockIdx.x, ep, sync);
-        __syncthreads();
-        if (!*sflag) return false;
-        const XchDesc* x = p.xch;
-        const int n = x->n;
-        const float* mine = x->buf[x->rank] + (size_t) (ep & 1ull) * kMaxRanks * 2 * x->rows;
-        const size_t src_stride = (size_t) 2 * x->rows;
-        for (int idx = (int) threadIdx.x; idx < (uend - ubeg) * NC; idx += (int) blockDim.x) {
-            const int u = ubeg + idx / NC, c = idx % NC;
-            float part = 0.0f;
-#pragma unroll
-            for (int r = 0; r < 4; ++r) {
-                const size_t off = (size_t) c * x->rows + (size_t) u * 4 + r;
-                float pq[kMaxRanks];
-#pragma unroll
-                for (int q = 0; q < kMaxRanks; ++q) pq[q] = q < n ? __ldcg(mine + q * src_stride + off) : 0.0f;
-                float v = pq[0];
-#pragma unroll
-                for (int q = 1; q < kMaxRanks; ++q)
-                    if (q < n) v = __fadd_rn(v, pq[q]);
-                if (p.res != nullptr) v = __fadd_rn(v, __ldcg(p.res + (size_t) c * p.res_stride + (size_t) u * 4 + r));
-                p.y[(size_t) c * p.y_stride + (size_t) u * 4 + r] = v;
-                part = __fmaf_rn(v, v, part);
-            }
-            p.pout[(size_t) c * p.pout_stride + u] = part;
-        }
-        return ok;
-    }
+    if constexpr (EPI == EPI_XRES) return xres_finish<NC>(p, ubeg, uend, (int) blockIdx.x, ep, sync, sflag, ok);
     if constexpr (EPI == EPI_SWIGLU) mmvq_swiglu_finish<NC>(p, ubeg + warp, kPWarps, unit, lane);
     if constexpr (EPI == EPI_ARGMAX) mmvq_argmax_flush<NC>(p, lane, best);
     return ok;
@@ -658,6 +512,20 @@ __global__ void __launch_bounds__(256, 2) combine_kernel(const POp op, Ctrl* ctr
     const int items = pop_items<NC>(op, pos);
     for (int it = (int) blockIdx.x; it < items; it += (int) gridDim.x)  // uniform over the block
         combine_impl<NC>(op.at, pos, it / (NC * 8), (it / 8) % NC, it % 8, reinterpret_cast<float*>(smem));
+}
+
+// Tensor parallelism, graph mode: the global argmax after an lm_head over this rank's vocabulary shard
+// (one thread; the keys exchange of xch_argmax on the argmax flag slot, whose epoch counter it advances).
+template <int NC>
+__global__ void __launch_bounds__(32) xargmax_kernel(const POp op, Ctrl* ctrl) {
+    pdl_trigger();
+    pdl_wait();
+    if (threadIdx.x != 0) return;
+    const XchDesc* x = op.xa.xch;
+    const int slot = x->slots - 1;
+    const unsigned long long ep = xch_epoch_next(x, slot);
+    if (!xch_argmax<NC>(x, op.draft ? ctrl->damax : ctrl->amax, ep, x->sync)) atomicExch(&x->sync->abort, 1u);
+    xch_epoch_done(x, slot, ep);
 }
 
 // One non-GEMV op as its own launch (graph mode).

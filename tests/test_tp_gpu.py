@@ -81,8 +81,38 @@ def test_tp8_9b_geometry(tmp_path_factory):
     _check(_run(tmp_path_factory, 8, "check", "9b4", 29520))
 
 
-def test_tp2_peer_wait_runs_out_and_recovers(tmp_path_factory):
-    res = _run(tmp_path_factory, 2, "fail", "mid", 29521, {"RK_TP_WAIT_MS": "300"})
+def _check_executors(res):
+    """The graph executor (the exchange inside the row-parallel GEMV kernels and a one-thread argmax kernel)
+    gives the persistent executor's bits under tensor parallelism: same summation order of the partials."""
+    for r in res["ranks"]:
+        p, g = r["persistent"], r["graph"]
+        assert p["mode"] == "persistent" and g["mode"] == "graph"
+        assert p["bits"] == g["bits"]
+        assert p["argmax"] == g["argmax"]
+        assert p["greedy"] == g["greedy"] == p["mtp"] == g["mtp"]
+        assert p["status"] == 0 and g["status"] == 0
+        assert g["mtp_steps"] > 0
+    first = res["ranks"][0]["graph"]
+    for r in res["ranks"][1:]:
+        assert r["graph"]["argmax"] == first["argmax"] and r["graph"]["greedy"] == first["greedy"]
+
+
+def test_tp2_graph_executor_bitwise_persistent(tmp_path_factory):
+    _check_executors(_run(tmp_path_factory, 2, "exec", "9b4", 29523))
+
+
+def test_tp2_graph_executor_replicated_kv(tmp_path_factory):
+    _check_executors(_run(tmp_path_factory, 2, "exec", "tiny", 29524))
+
+
+def test_tp8_graph_executor_bitwise_persistent(tmp_path_factory):
+    _check_executors(_run(tmp_path_factory, 8, "exec", "9b4", 29525))
+
+
+@pytest.mark.parametrize("executor", ["persistent", "graph"])
+def test_tp2_peer_wait_runs_out_and_recovers(tmp_path_factory, executor):
+    port = 29521 if executor == "persistent" else 29526
+    res = _run(tmp_path_factory, 2, "fail", "mid", port, {"RK_TP_WAIT_MS": "300", "RK_ENGINE_MODE": executor})
     r0, r1 = res["ranks"]
     assert r0["err"] == res["ecuda"]
     assert r0["status"] & 8  # a cross-rank wait gave up

@@ -7,6 +7,9 @@ argv[2] = "fail": after a reference generation, rank 0 runs one step that rank 1
 cross-rank waits give up (RK_TP_WAIT_MS, set short by the launcher); then every rank resyncs and resets
 and the generation is repeated. The host barriers are gloo's; no rank leaves a kernel in flight.
 
+argv[2] = "exec": the same teacher-forced steps and generations on the persistent executor and on the graph
+executor (one kernel per op; the exchange inside the GEMV and argmax kernels); rank 0 writes both.
+
 argv[3] = geometry: "mid" (2048 wide, 4 layers: splits over 2 ranks into whole tiles), "tiny" (1024 wide, 4
 q heads and 1 kv head: over 2 ranks each keeps the shared kv head and pads its 512-value row-parallel
 inputs to a tile, the 8-rank layout of the 9B geometry on 2 GPUs) or "9b4" (the 9B geometry cut to 4
@@ -41,6 +44,36 @@ def geometry(name, max_ctx=512, seed=3):
     return c
 
 
+def run_executors(cfg, rank, world):
+    toks = [int(t) for t in np.random.default_rng(5).integers(0, cfg.n_vocab, 16)]
+    prompt = [int(t) for t in np.random.default_rng(6).integers(0, cfg.n_vocab, 16)]
+    mine = {"rank": rank}
+    for ex in ("persistent", "graph"):
+        eng = Engine(cfg, device=rank, mode=ex, tp_rank=rank, tp_size=world)
+        eng.connect_tp()
+        dist.barrier()
+        eng.reset()
+        bits, ams = [], []
+        for pos, t in enumerate(toks):
+            lg, am = eng.step([t], pos)
+            bits.append(np.ascontiguousarray(lg[0], np.float32).view(np.uint32).tolist())
+            ams.append(am[0])
+        g0, _ = eng.generate(prompt, 48, mtp=False)
+        g1, st = eng.generate(prompt, 48, mtp=True)
+        mine[ex] = {"mode": eng.mode, "bits": bits, "argmax": ams, "greedy": g0.tolist(), "mtp": g1.tolist(),
+                    "mtp_steps": st["mtp_steps"], "status": ops.device_status()}
+        dist.barrier()
+        eng.close()
+        dist.barrier()
+    gathered = [None] * world
+    dist.all_gather_object(gathered, mine)
+    if rank == 0:
+        with open(sys.argv[1], "w") as f:
+            json.dump({"ranks": gathered}, f)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def main():
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     mode = sys.argv[2] if len(sys.argv) > 2 else "check"
@@ -48,6 +81,9 @@ def main():
     torch.cuda.set_device(rank)
     dist.init_process_group("gloo", timeout=timedelta(seconds=120))
     cfg = geometry(geo)
+    if mode == "exec":
+        run_executors(cfg, rank, world)
+        return
     eng = Engine(cfg, device=rank, tp_rank=rank, tp_size=world)
     eng.connect_tp()
     dist.barrier()
