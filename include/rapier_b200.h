@@ -268,8 +268,8 @@ int rk_engine_create(const rk_model_config* cfg, int device, rk_engine** out);
  * with more ranks than kv heads, each rank keeps the kv head its 2 or 4 q heads use (the 9B geometry at 8
  * ranks); every rank's share of a row-parallel input must be a multiple of 256 (it is padded with zero
  * weight blocks to whole 1024-value tiles) else RK_EUNSUPPORTED. The 9B geometry runs at 2, 4 and 8 ranks.
- * Needs the persistent executor. After all
- * ranks have created their engines: rk_engine_tp_export on each, an exchange of the handles between the
+ * Either executor: the exchange runs inside the row-parallel GEMV kernels (graph) or inside the persistent
+ * kernel. After all ranks have created their engines: rk_engine_tp_export on each, an exchange of the handles between the
  * processes, rk_engine_tp_connect on each with all handles (rank-major, rk_tp_handle_bytes each). All
  * ranks then call generate / step / probe in lockstep; logits hold the rank's vocabulary shard. No
  * reference counterpart for the API shape. */
@@ -351,10 +351,10 @@ int rk_engine_probe_gemv(rk_engine* e, int ncols, int iters, rk_probe_result* ou
 /* Device bytes the engine holds. */
 size_t rk_engine_device_bytes(const rk_engine* e);
 /* The executor the engine runs its step programs with: RK_ENGINE_GRAPH (one kernel per op, replayed from
- * CUDA graphs; the single-GPU default) or RK_ENGINE_PERSISTENT (one cooperative kernel per program, a
- * whole generation in one launch; the tensor-parallel default, required there). The environment variable
- * RK_ENGINE_MODE=graph|persistent, read at rk_engine_create, overrides. Both produce the same bits. No
- * reference counterpart (the reference replays a CUDA graph). */
+ * CUDA graphs; the default) or RK_ENGINE_PERSISTENT (one cooperative kernel per program, a whole greedy
+ * generation in one launch). The environment variable RK_ENGINE_MODE=graph|persistent, read at
+ * rk_engine_create, chooses. Both produce the same bits, with or without tensor parallelism. No reference
+ * counterpart (the reference replays a CUDA graph). */
 #define RK_ENGINE_GRAPH 0
 #define RK_ENGINE_PERSISTENT 1
 int rk_engine_mode(const rk_engine* e);

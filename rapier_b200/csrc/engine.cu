@@ -5,9 +5,10 @@
 // Every step kind is an op program (decode_ops.cuh): one token; the trunk over 2 columns; an MTP round
 // (2-column verify -> accept -> 2-column draft -> next candidate); the first draft; the draft seed. Every
 // op reads its tokens, positions and the rollback flag from the device Ctrl block, so no step needs a
-// host round trip. Two executors (persistent.cuh) run a program: by default one persistent cooperative
-// kernel (a whole generation in one launch); with RK_ENGINE_MODE=graph one kernel per op, replayed from
-// a CUDA graph. Both write the same bits.
+// host round trip. Two executors (persistent.cuh) run a program: one kernel per op, replayed from a CUDA
+// graph (the single-GPU default), or one persistent cooperative kernel (a whole generation in one launch);
+// RK_ENGINE_MODE=graph|persistent chooses. Both write the same bits, under tensor parallelism too (the
+// row-parallel exchange runs inside the GEMV op in either, xch.cuh).
 //
 // Ops per trunk layer:
 //   GDN  : GEMV qkv||z||beta||alpha (RMSNorm+Q8_1 prologue) -> GDN (conv / L2 / delta rule / gated norm /
@@ -880,17 +881,17 @@ void EngineImpl::add_probe(std::vector<POp>& v, int nc) {
     probe_gemvs = n;
 }
 
-// The persistent executor (the tensor-parallel default, or RK_ENGINE_MODE=persistent), unless the device
+// The persistent executor (RK_ENGINE_MODE=persistent), unless the device
 // cannot hold one 512-thread CTA per SM with at least two ring slots per warp. The shared-memory region (staged activations or op
 // scratch) and the ring depth are set per column count. Tuning knobs (like the reference's
 // QWYTHOS_Q6ROWS sweep knob, src/native_mmvq.cu:3648-3651): RK_PERSIST_STAGES caps the ring depth,
 // RK_PERSIST_L2PF_KB sets the per-CTA L2 prefetch of the next GEMV (KB, 0 = off).
 int EngineImpl::setup_executor() {
-    // Single GPU: one kernel per op replayed from CUDA graphs (measured faster than the persistent kernel on
-    // B200: 2.45 vs 2.66 ms per token, 3.50 vs 3.66 ms per MTP round). Tensor parallelism: the persistent
-    // kernel (its row-parallel exchanges run inside it). RK_ENGINE_MODE=graph|persistent overrides.
+    // One kernel per op replayed from CUDA graphs by default (measured faster than the persistent kernel on
+    // B200: on one GPU 2.45 vs 2.66 ms per token and 3.50 vs 3.66 ms per MTP round; under 2-way tensor
+    // parallelism 302 vs 230 tok/s with exact MTP). RK_ENGINE_MODE=graph|persistent overrides.
     const char* mode = std::getenv("RK_ENGINE_MODE");
-    persistent = mode ? std::strcmp(mode, "graph") != 0 : tp_size > 1;
+    persistent = mode != nullptr && std::strcmp(mode, "persistent") == 0;
     int sms = 0, optin = 0;
     if ((err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return RK_ECUDA;
     p_grid = sms;  // also the exchange's flag slots in graph mode (one GEMV CTA per SM)
@@ -1220,9 +1221,9 @@ static int create_engine(const rk_model_config* cfg, int device, int tp_rank, in
     }
     if (rc == RK_OK) rc = E.setup_executor();
     if (rc == RK_OK && tp_size > 1) {
-        // this rank's exchange memory: partials [2][8][2][H] floats | flags [grid + 1][8] | keys [2][8][2] |
-        // the graph executor's epoch per flag slot [grid + 1] (local only; the peers write flags and keys)
-        E.xoff_flags = (size_t) 2 * kMaxRanks * 2 * E.H * sizeof(float);
+        // this rank's exchange memory: partial words [2][8][2][H] | argmax flags [grid + 1][8] | keys [2][8][2]
+        // | the graph executor's epoch per slot [grid + 1] (local only; the peers write words, flags and keys)
+        E.xoff_flags = (size_t) 2 * kMaxRanks * 2 * E.H * sizeof(unsigned long long);
         E.xoff_keys = E.xoff_flags + (size_t) (E.p_grid + 1) * kMaxRanks * 8;
         E.xoff_ep = E.xoff_keys + (size_t) 2 * kMaxRanks * 2 * 8;
         E.xmem_bytes = E.xoff_ep + (size_t) (E.p_grid + 1) * 8;
@@ -1349,7 +1350,7 @@ int rk_engine_tp_connect(rk_engine* e, const void* handles, size_t bytes_per_ran
             E.peer_maps[q] = p;
             base = static_cast<uint8_t*>(p);
         }
-        d.buf[q] = reinterpret_cast<float*>(base);
+        d.buf[q] = reinterpret_cast<unsigned long long*>(base);
         d.flags[q] = reinterpret_cast<unsigned long long*>(base + E.xoff_flags);
         d.keys[q] = reinterpret_cast<unsigned long long*>(base + E.xoff_keys);
     }
@@ -1361,8 +1362,9 @@ int rk_engine_tp_connect(rk_engine* e, const void* handles, size_t bytes_per_ran
     return RK_OK;
 }
 
-// After a failed step (a peer that never signalled), the ranks' exchange epochs and flags disagree; every
-// rank clears its own (the peers write only into this rank's flag and key arrays, and none of them runs).
+// After a failed step (a peer that never signalled), the ranks' exchange epochs disagree; every rank clears
+// its own exchange memory (partial words, flags, keys, epoch counters: the epochs restart from zero, so no
+// word from before may stay) while none of the group's kernels runs.
 int rk_engine_tp_resync(rk_engine* e) {
     const char* what = "rk_engine_tp_resync";
     if (!e) return set_error(RK_EINVAL, "%s: null engine", what);
@@ -1370,7 +1372,7 @@ int rk_engine_tp_resync(rk_engine* e) {
     if (E.tp_size < 2 || !E.tp_connected) return set_error(RK_EINVAL, "%s: not a connected tensor-parallel engine", what);
     cudaError_t ce = cudaSetDevice(E.dev);
     if (ce == cudaSuccess) ce = cudaStreamSynchronize(E.s);
-    if (ce == cudaSuccess) ce = cudaMemset(E.xmem + E.xoff_flags, 0, E.xmem_bytes - E.xoff_flags);
+    if (ce == cudaSuccess) ce = cudaMemset(E.xmem, 0, E.xmem_bytes);  // words, flags, keys and epochs
     if (ce == cudaSuccess) ce = cudaMemset(E.psync, 0, sizeof(PSync));
     if (ce == cudaSuccess) ce = cudaDeviceSynchronize();
     if (ce != cudaSuccess) return set_error(RK_ECUDA, "%s: %s", what, cudaGetErrorString(ce));
@@ -1562,10 +1564,14 @@ int rk_engine_generate(rk_engine* e, const int* prompt, int n_prompt, int n_gen,
                 ++launches;
             }
         } else {
+            // A round emits one or two tokens, so (n_gen - emitted) / 2 rounds can be queued without reading
+            // the count back (no end-of-sequence stop here): ~log2(n_gen) host round trips per generation
+            // instead of one per round.
             while (ce == cudaSuccess && emitted >= 0 && emitted < n_gen) {
-                const bool single = emitted >= n_gen - 1;
-                ce = E.run(E.progs[single ? P_SINGLE : P_ROUND], 0);
-                ++launches;
+                const int rounds = emitted >= n_gen - 1 ? 0 : (n_gen - emitted) / 2;
+                for (int k = 0; k < rounds && ce == cudaSuccess; ++k) ce = E.run(E.progs[P_ROUND], 0);
+                if (rounds == 0 && ce == cudaSuccess) ce = E.run(E.progs[P_SINGLE], 0);
+                launches += rounds > 0 ? rounds : 1;
                 emitted = read_emitted();
             }
         }
@@ -1714,9 +1720,12 @@ int rk_engine_session_run(rk_engine* e, const int* tokens, int n_tokens, int n_g
             ++launches;
             read_ctrl(back);
         }
+        // graph mode: without an end-of-sequence id nothing stops a generation early, so the remaining
+        // passes are queued at once (one host round trip); with one, the count is read after every pass
         while (!E.persistent && !back.stop && back.n_emitted < n_gen && ce == cudaSuccess) {
-            ce = E.run(E.progs[P_SINGLE], 0);
-            ++launches;
+            const int passes = eos_id < 0 ? n_gen - back.n_emitted : 1;
+            for (int k = 0; k < passes && ce == cudaSuccess; ++k) ce = E.run(E.progs[P_SINGLE], 0);
+            launches += passes;
             read_ctrl(back);
         }
     } else if (!back.stop && back.n_emitted < n_gen && ce == cudaSuccess) {
@@ -1729,9 +1738,12 @@ int rk_engine_session_run(rk_engine* e, const int* tokens, int n_tokens, int n_g
             }
             read_ctrl(back);
         } else {
+            // a round emits one or two tokens: without an end-of-sequence id (n_gen - emitted) / 2 rounds are
+            // queued before the count is read back
             while (!back.stop && back.n_emitted < n_gen - 1 && ce == cudaSuccess) {
-                ce = E.run(E.progs[P_ROUND], 0);
-                ++launches;
+                const int rounds = eos_id < 0 ? (n_gen - back.n_emitted) / 2 : 1;
+                for (int k = 0; k < rounds && ce == cudaSuccess; ++k) ce = E.run(E.progs[P_ROUND], 0);
+                launches += rounds;
                 read_ctrl(back);
             }
         }

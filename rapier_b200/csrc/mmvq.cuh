@@ -448,13 +448,14 @@ __device__ __forceinline__ void mmvq_res_prefetch(const MmvqParams& p, int unit,
 }
 
 // EPI_XRES (tensor parallelism, both executors): a unit's 4 x NC row sums of this rank's share of the input
-// (the xor butterfly per value) go into this rank's slot of every rank's partial buffer (posted peer
-// stores); `yoff` (xres_offset) selects the slot and the epoch's parity half.
+// (the xor butterfly per value) go as epoch-tagged words (xch.cuh) into this rank's source slot of every
+// rank's partial buffer; `yoff` (xres_offset) selects the slot and the epoch's parity half.
 __device__ __forceinline__ size_t xres_offset(const XchDesc* x, unsigned long long ep) {
     return (((size_t) (ep & 1ull) * kMaxRanks + x->rank) * 2) * x->rows;
 }
 template <int NC>
-__device__ __forceinline__ void xres_push(const XchDesc* x, size_t yoff, int unit, int lane, float (&acc)[NC][4]) {
+__device__ __forceinline__ void xres_push(const XchDesc* x, size_t yoff, unsigned long long ep, int unit, int lane,
+                                          float (&acc)[NC][4]) {
 #pragma unroll
     for (int c = 0; c < NC; ++c)
 #pragma unroll
@@ -467,45 +468,41 @@ __device__ __forceinline__ void xres_push(const XchDesc* x, size_t yoff, int uni
             if (lane == c * 4 + r) out = acc[c][r];
     if (lane < NC * 4) {
         const size_t o = yoff + (size_t) (lane >> 2) * x->rows + (size_t) unit * 4 + (lane & 3);
-        for (int q = 0; q < x->n; ++q) x->buf[q][o] = out;
+        const unsigned long long w = xch_word(ep, out);
+        for (int q = 0; q < x->n; ++q) st_volatile_u64(x->buf[q] + o, w);
     }
 }
-// After a CTA's units (all threads call it): signal flag slot `slot` of every peer and wait for theirs, then
-// sum the CTA's rows [4 ubeg, 4 uend) over the ranks in rank order (every rank gets the same bits), add the
-// residual and write y and the 4-row partials as EPI_RES does (EPI_STORE_P without a residual). A CTA with
-// a failed part (`ok` false in any thread) does not signal, so its peers' waits give up too.
+// After a CTA's units: for each of the CTA's rows [4 ubeg, 4 uend) and columns, wait for every rank's word
+// of this exchange and sum them in rank order (every rank gets the same bits), add the residual and write y
+// and the 4-row partials as EPI_RES does (EPI_STORE_P without a residual). Returns false (this thread) when
+// a wait gave up; a rank whose warp failed before pushing leaves its peers' waits to give up too.
 template <int NC>
-__device__ __forceinline__ bool xres_finish(const MmvqParams& p, int ubeg, int uend, int slot, unsigned long long ep,
-                                            PSync* sync, int* sflag, bool ok) {
-    __threadfence_system();  // this thread's pushed partials, before the CTA's signal
-    const int all_ok = __syncthreads_and(ok ? 1 : 0);
-    if (threadIdx.x == 0) *sflag = all_ok && xch_signal_wait(p.xch, slot, ep, sync);
-    __syncthreads();
-    if (!*sflag) return false;
+__device__ __forceinline__ bool xres_finish(const MmvqParams& p, int ubeg, int uend, unsigned long long ep,
+                                            PSync* sync) {
     const XchDesc* x = p.xch;
     const int n = x->n;
-    const float* mine = x->buf[x->rank] + (size_t) (ep & 1ull) * kMaxRanks * 2 * x->rows;
+    const unsigned long long* mine = x->buf[x->rank] + (size_t) (ep & 1ull) * kMaxRanks * 2 * x->rows;
     const size_t src_stride = (size_t) 2 * x->rows;
-    for (int idx = (int) threadIdx.x; idx < (uend - ubeg) * NC; idx += (int) blockDim.x) {
+    bool ok = true;
+    for (int idx = (int) threadIdx.x; idx < (uend - ubeg) * NC && ok; idx += (int) blockDim.x) {
         const int u = ubeg + idx / NC, c = idx % NC;
         float part = 0.0f;
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
             const size_t off = (size_t) c * x->rows + (size_t) u * 4 + r;
-            float pq[kMaxRanks];
-#pragma unroll
-            for (int q = 0; q < kMaxRanks; ++q) pq[q] = q < n ? __ldcg(mine + q * src_stride + off) : 0.0f;
-            float v = pq[0];
-#pragma unroll
-            for (int q = 1; q < kMaxRanks; ++q)
-                if (q < n) v = __fadd_rn(v, pq[q]);
+            float v = 0.0f;
+            for (int q = 0; q < n && ok; ++q) {
+                float pq = 0.0f;
+                ok = xch_poll(mine + q * src_stride + off, ep, x, sync, pq);
+                v = q == 0 ? pq : __fadd_rn(v, pq);
+            }
             if (p.res != nullptr) v = __fadd_rn(v, __ldcg(p.res + (size_t) c * p.res_stride + (size_t) u * 4 + r));
             p.y[(size_t) c * p.y_stride + (size_t) u * 4 + r] = v;
             part = __fmaf_rn(v, v, part);
         }
         p.pout[(size_t) c * p.pout_stride + u] = part;
     }
-    return true;
+    return ok;
 }
 
 // EPI_SWIGLU, after a warp's units [first, end) (stride `stride`) are written: one fence, then one arrival
@@ -643,7 +640,6 @@ __global__ void __launch_bounds__(W * 32, 16 / W) mmvq_packed_kernel(const MmvqP
     // EPI_XRES (the graph executor under tensor parallelism): this CTA's exchange epoch, from the counter
     // of its flag slot (the previous exchange on this slot was written back by a launch now complete)
     __shared__ unsigned long long xep_sh;
-    __shared__ int xflag_sh;
     if constexpr (EPI == EPI_XRES)
         if (threadIdx.x == 0) xep_sh = xch_epoch_next(p.xch, (int) blockIdx.x);
 
@@ -706,7 +702,7 @@ __global__ void __launch_bounds__(W * 32, 16 / W) mmvq_packed_kernel(const MmvqP
         if (++kc == KT) {
             if (!paired) {
                 if (split < KC) mmvq_join_halves<NC>(acc, lo);
-                if constexpr (EPI == EPI_XRES) xres_push<NC>(p.xch, yoff, unit, lane, acc);
+                if constexpr (EPI == EPI_XRES) xres_push<NC>(p.xch, yoff, xep, unit, lane, acc);
                 else mmvq_epilogue<NC, EPI>(p, unit, lane, acc, best, resv);
             } else {
                 float* slot = pslots + ((size_t) (ul * 2 + (seq & 1)) * NC * 4) * 32;
@@ -753,7 +749,7 @@ __global__ void __launch_bounds__(W * 32, 16 / W) mmvq_packed_kernel(const MmvqP
     }
     if constexpr (EPI == EPI_XRES) {
         PSync* sync = p.xch->sync;
-        if (!xres_finish<NC>(p, ubeg, uend, (int) blockIdx.x, xep, sync, &xflag_sh, ok) && threadIdx.x == 0)
+        if (!ok || !xres_finish<NC>(p, ubeg, uend, xep, sync))
             atomicExch(&sync->abort, 1u);  // for the host, and so that later waits of this rank end at once
         if (threadIdx.x == 0) xch_epoch_done(p.xch, (int) blockIdx.x, xep);
     }

@@ -218,7 +218,7 @@ struct L2Pf {
 
 template <int NC, int PRO, int EPI>
 __device__ __forceinline__ bool p_gemv(const MmvqParams& p, uint8_t* xsm, float* red, WarpPipe& w,
-                                       unsigned long long* tp, unsigned long long& xep, PSync* sync, int* sflag,
+                                       unsigned long long* tp, unsigned long long& xep, PSync* sync,
                                        const L2Pf& pf) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // EPI_XRES: this exchange's epoch and this rank's partial buffer (by epoch parity)
@@ -274,12 +274,12 @@ __device__ __forceinline__ bool p_gemv(const MmvqParams& p, uint8_t* xsm, float*
         if (!ok) break;
         if (split < KC) mmvq_join_halves<NC>(acc, lo);
         if constexpr (EPI == EPI_XRES) {  // this rank's partial rows, pushed to every rank
-            xres_push<NC>(p.xch, yoff, unit, lane, acc);
+            xres_push<NC>(p.xch, yoff, ep, unit, lane, acc);
         } else {
             mmvq_epilogue<NC, EPI>(p, unit, lane, acc, best, resv);
         }
     }
-    if constexpr (EPI == EPI_XRES) return xres_finish<NC>(p, ubeg, uend, (int) blockIdx.x, ep, sync, sflag, ok);
+    if constexpr (EPI == EPI_XRES) return xres_finish<NC>(p, ubeg, uend, ep, sync) && ok;
     if constexpr (EPI == EPI_SWIGLU) mmvq_swiglu_finish<NC>(p, ubeg + warp, kPWarps, unit, lane);
     if constexpr (EPI == EPI_ARGMAX) mmvq_argmax_flush<NC>(p, lane, best);
     return ok;
@@ -294,17 +294,17 @@ __host__ __device__ __forceinline__ bool gemv_combo_supported(int pro, int epi) 
 template <int NC>
 __device__ __forceinline__ bool p_gemv_dispatch(const POp& op, uint8_t* xsm, float* red, WarpPipe& w,
                                                 unsigned long long* tp, unsigned long long& xep, PSync* sync,
-                                                int* sflag, const L2Pf& pf) {
+                                                const L2Pf& pf) {
     const MmvqParams& p = op.g;
     if (op.pro == PRO_RMS) {
-        if (op.epi == EPI_STORE) return p_gemv<NC, PRO_RMS, EPI_STORE>(p, xsm, red, w, tp, xep, sync, sflag, pf);
-        if (op.epi == EPI_SWIGLU) return p_gemv<NC, PRO_RMS, EPI_SWIGLU>(p, xsm, red, w, tp, xep, sync, sflag, pf);
-        return p_gemv<NC, PRO_RMS, EPI_ARGMAX>(p, xsm, red, w, tp, xep, sync, sflag, pf);
+        if (op.epi == EPI_STORE) return p_gemv<NC, PRO_RMS, EPI_STORE>(p, xsm, red, w, tp, xep, sync, pf);
+        if (op.epi == EPI_SWIGLU) return p_gemv<NC, PRO_RMS, EPI_SWIGLU>(p, xsm, red, w, tp, xep, sync, pf);
+        return p_gemv<NC, PRO_RMS, EPI_ARGMAX>(p, xsm, red, w, tp, xep, sync, pf);
     }
-    if (op.epi == EPI_RES) return p_gemv<NC, PRO_Q8, EPI_RES>(p, xsm, red, w, tp, xep, sync, sflag, pf);
+    if (op.epi == EPI_RES) return p_gemv<NC, PRO_Q8, EPI_RES>(p, xsm, red, w, tp, xep, sync, pf);
     if constexpr (NC <= 2)  // the exchange buffers hold two columns (tensor parallelism has no prefill program)
-        if (op.epi == EPI_XRES) return p_gemv<NC, PRO_Q8, EPI_XRES>(p, xsm, red, w, tp, xep, sync, sflag, pf);
-    return p_gemv<NC, PRO_Q8, EPI_STORE_P>(p, xsm, red, w, tp, xep, sync, sflag, pf);
+        if (op.epi == EPI_XRES) return p_gemv<NC, PRO_Q8, EPI_XRES>(p, xsm, red, w, tp, xep, sync, pf);
+    return p_gemv<NC, PRO_Q8, EPI_STORE_P>(p, xsm, red, w, tp, xep, sync, pf);
 }
 
 // Asynchronous copy of op record j into shared memory (16-byte cp.async chunks, one per thread), so the
@@ -366,7 +366,6 @@ __global__ void __launch_bounds__(kPWarps * 32, 1)
     __syncthreads();
     unsigned long long target = 0ull;
     unsigned long long xep = *reinterpret_cast<volatile unsigned long long*>(&sync->xepoch);
-    __shared__ int xflag;
     bool alive = ld_volatile_u32(&sync->abort) == 0u;
     if (alive) pipe_start(w, warp, lane);
     int k = 0;  // ops started; op_sm[k & 1] holds the running op
@@ -397,7 +396,7 @@ __global__ void __launch_bounds__(kPWarps * 32, 1)
             }
             bool ok = true;
             if (op.kind == POP_GEMV) {
-                ok = p_gemv_dispatch<NC>(op, region, red, w, tr != nullptr ? tr + 1 : nullptr, xep, sync, &xflag, pf);
+                ok = p_gemv_dispatch<NC>(op, region, red, w, tr != nullptr ? tr + 1 : nullptr, xep, sync, pf);
             } else if (op.kind == POP_XARGMAX) {
                 const unsigned long long ep = ++xep;
                 if constexpr (NC <= 2)

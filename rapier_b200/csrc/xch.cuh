@@ -2,19 +2,25 @@
 // persistent kernel (persistent.cuh) and the one-kernel-per-op graph executor (mmvq_packed_kernel's
 // EPI_XRES epilogue, xargmax_kernel).
 //
-// Every rank's exchange memory is mapped into this rank's address space (CUDA IPC over NVLink). A rank
-// pushes its row-parallel partial sums into its own slot of every rank's buffer (posted peer stores), then
-// signals each peer by a system-scope release store of the exchange's epoch into the peer's flag slot; a
-// rank that has acquired all the signals of a slot sums the partials from its own memory. Epochs only grow,
-// the flag words of a slot only grow, so no flag is ever cleared; buffers alternate by epoch parity, and a
-// rank starts an exchange only after every peer has signalled the previous one (which a peer does after
-// reading), so no buffer is rewritten while read. A flag slot belongs to one CTA index (the same CTA of
-// every rank covers the same rows: same grid, same split) plus one slot for the argmax exchange.
+// Every rank's exchange memory is mapped into this rank's address space (CUDA IPC over NVLink).
+//
+// Row-parallel partial sums travel as self-validating 8-byte words, (exchange epoch << 32) | fp32 bits: a
+// CTA stores each of its rows' partials into its own source slot of every rank's buffer with one 64-bit
+// store, and the same CTA of every rank (same grid, same split: the same rows) polls the words of its rows
+// in its own memory until each carries the exchange's epoch. A 64-bit store is seen whole, so a word with
+// the right epoch holds that exchange's value: no fence and no separate flag. Epochs only grow (a resync
+// clears them together with the buffers), and the buffers alternate by epoch parity: a rank writes epoch
+// e + 2 into a slot only after it has read the peers' epoch e + 1 words of the same rows, which the peers'
+// same CTA wrote after it had read epoch e, so no word is overwritten before it is read.
+//
+// The argmax exchange (one per lm_head) keeps a flag protocol: each rank writes its keys into every rank's
+// key array, fences at system scope and release-stores the epoch into every peer's flag slot, then acquires
+// all the peers' flags before it reads the keys.
 //
 // Epochs: the persistent kernel counts all of a launch's exchanges in one register (carried between
-// launches in PSync::xepoch); the graph executor keeps one counter per flag slot in this rank's own
-// exchange memory (`ep`), which the CTA owning the slot reads at its start and writes back at its end.
-// Either way the same slot of every rank sees the same epoch sequence.
+// launches in PSync::xepoch); the graph executor keeps one counter per slot (a GEMV CTA index, or the
+// argmax) in this rank's own exchange memory (`ep`), which the CTA owning the slot reads at its start and
+// writes back at its end. Either way the same slot of every rank sees the same epoch sequence.
 #pragma once
 
 #include "common.cuh"
@@ -32,9 +38,9 @@ constexpr int kMaxRanks = 8;
 struct XchDesc {
     int rank, n;  // this rank, number of ranks
     int rows;     // rows of a partial column (the hidden size)
-    int slots;    // flag slots: one per GEMV CTA + one for the argmax exchange
+    int slots;    // epoch slots: one per GEMV CTA (its rows' exchanges) + one for the argmax exchange
     unsigned long long wait_ns;            // a cross-rank wait gives up after this long
-    float* buf[kMaxRanks];                 // per rank: partials [2 parity][kMaxRanks source][2 columns][rows]
+    unsigned long long* buf[kMaxRanks];    // per rank: partial words [2 parity][kMaxRanks source][2 columns][rows]
     unsigned long long* flags[kMaxRanks];  // per rank: [slots][kMaxRanks] epochs, written by the peers
     unsigned long long* keys[kMaxRanks];   // per rank: argmax keys [2 parity][kMaxRanks][2 columns]
     unsigned long long* ep;                // graph executor: this rank's epoch counter per flag slot
@@ -64,6 +70,42 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned 
     unsigned long long v;
     asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
+}
+
+__device__ __forceinline__ unsigned long long ld_volatile_u64(const unsigned long long* p) {
+    return *reinterpret_cast<const volatile unsigned long long*>(p);
+}
+__device__ __forceinline__ void st_volatile_u64(unsigned long long* p, unsigned long long v) {
+    *reinterpret_cast<volatile unsigned long long*>(p) = v;
+}
+__device__ __forceinline__ unsigned long long xch_word(unsigned long long epoch, float v) {
+    return ((unsigned long long) (uint32_t) epoch << 32) | (unsigned long long) __float_as_uint(v);
+}
+
+// One partial word: waits until the word at `p` carries epoch `epoch` and returns its value in `v`. The wait
+// gives up after x->wait_ns (status bit, abort), or at once once the abort word is set.
+__device__ __forceinline__ bool xch_poll(const unsigned long long* p, unsigned long long epoch, const XchDesc* x,
+                                         PSync* sync, float& v) {
+    const uint32_t e32 = (uint32_t) epoch;
+    unsigned long long w = ld_volatile_u64(p);
+    if ((uint32_t) (w >> 32) != e32) {
+        const unsigned long long t0 = globaltimer_ns();
+        for (uint32_t it = 1;; ++it) {
+            if (it >= 64u) __nanosleep(32);
+            w = ld_volatile_u64(p);
+            if ((uint32_t) (w >> 32) == e32) break;
+            if ((it & 63u) == 0u) {
+                if (ld_volatile_u32(&sync->abort)) return false;
+                if (globaltimer_ns() - t0 > x->wait_ns) {
+                    atomicOr(&g_rk_status, kStatusGridTimeout);
+                    atomicExch(&sync->abort, 1u);
+                    return false;
+                }
+            }
+        }
+    }
+    v = __uint_as_float((uint32_t) w);
+    return true;
 }
 
 // One thread: signal flag slot `slot` of every peer with `epoch` (after a system-scope fence that makes

@@ -69,9 +69,8 @@ class _engine_mode:
 
 
 class Engine:
-    """mode: None (the library default: graph on one GPU, persistent under tensor parallelism), "persistent"
-    or "graph"; the executor is chosen when
-    the engine is created (the library reads RK_ENGINE_MODE then). tp_rank / tp_size: this process's shard
+    """mode: None (the library default, RK_ENGINE_MODE or graph), "persistent" or "graph"; the executor is
+    chosen when the engine is created (the library reads RK_ENGINE_MODE then). tp_rank / tp_size: this process's shard
     under tensor parallelism (rk_engine_create_tp); connect the ranks with connect_tp() before use."""
 
     def __init__(self, cfg: ModelConfig, device: int = 0, mode: str | None = None, tp_rank: int = 0,
