@@ -950,7 +950,9 @@ template <int NC>
 cudaError_t EngineImpl::launch_op(const POp& op) {
     if (op.kind == POP_GEMV) {
         const MmvqParams& p = op.g;
-        const int w = NC == 2 ? 16 : kMmvqWarps;  // the 2-column GEMVs with 16 warps per CTA (mmvq_launch)
+        int w = NC == 2 ? 16 : kMmvqWarps;  // the 2-column GEMVs with 16 warps per CTA (mmvq_launch)
+        static const int res16 = std::getenv("RK_MMVQ_RES16") ? std::atoi(std::getenv("RK_MMVQ_RES16")) : 0;
+        if (NC == 1 && op.pro == PRO_Q8 && res16 > 0) w = 16;
         if (op.pro == PRO_RMS) {
             if (op.epi == EPI_STORE) return mmvq_launch<RK_TYPE_Q6_K, NC, PRO_RMS, EPI_STORE>(p, s, true, w);
             if (op.epi == EPI_SWIGLU) return mmvq_launch<RK_TYPE_Q6_K, NC, PRO_RMS, EPI_SWIGLU>(p, s, true, w);

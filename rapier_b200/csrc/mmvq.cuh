@@ -590,7 +590,7 @@ __global__ void __launch_bounds__(W * 32, 16 / W) mmvq_packed_kernel(const MmvqP
     // chains to the even one through a shared-memory slot, and the even warp adds them (lo + hi) and runs
     // the epilogue. Measured on the decode's 2-column GEMVs: 4 % slower than 16 unpaired warps (the slots
     // cost a ring slot per warp and the handoff waits), so off by default.
-    const bool paired = EPI != EPI_XRES && W == 16 && split < KC && p.pair != 0;
+    const bool paired = W == 16 && split < KC && p.pair != 0;
     const int PW = paired ? W / 2 : W;           // units in flight per CTA
     const int ul = paired ? warp >> 1 : warp;    // this warp's unit lane
     const int half = paired ? warp & 1 : 0;      // which half of each unit this warp consumes
@@ -725,7 +725,8 @@ __global__ void __launch_bounds__(W * 32, 16 / W) mmvq_packed_kernel(const MmvqP
                     __syncwarp();
                     __threadfence_block();  // the slot is read before the odd warp may refill it
                     if (lane == 0) *reinterpret_cast<volatile int*>(&pair_ack[ul][seq & 1]) = seq + 1;
-                    mmvq_epilogue<NC, EPI>(p, unit, lane, acc, best, resv);
+                    if constexpr (EPI == EPI_XRES) xres_push<NC>(p.xch, yoff, xep, unit, lane, acc);
+                    else mmvq_epilogue<NC, EPI>(p, unit, lane, acc, best, resv);
                 }
             }
 #pragma unroll
@@ -775,18 +776,26 @@ cudaError_t mmvq_launch_w(MmvqParams p, cudaStream_t s, bool pdl) {
         if (max_optin <= 0) max_optin = 227 * 1024;
     }
     const size_t tile = TYPE == RK_TYPE_Q6_K ? kQ6Tile : kQ80Tile;
-    p.pair = mmvq_env_pair() > 0 ? 1 : 0;
+    int ctas = 1;
+    if (mmvq_env_ctas() > 0 && EPI != EPI_XRES) ctas = mmvq_env_ctas();  // an exchange CTA owns a flag slot per SM
+    const int units = p.n_out / 4;
+    int grid = num_sms() * ctas;
+    if (grid > units) grid = units;
+    // Warp pairs (16 warps, an even chunk count): the two halves of each unit's chunks go to two warps. By
+    // default only where whole units would leave warps idle: at most one unit per pair and CTA (the 4096-row
+    // residual GEMVs, 7 units per CTA). RK_MMVQ_PAIR=1 pairs every 16-warp launch, -1 none.
+    const int per_cta = (units + grid - 1) / grid;
+    const bool can_pair = W == 16 && mmvq_split(p.n_in >> 10) < (p.n_in >> 10);
+    p.pair = can_pair && (mmvq_env_pair() > 0 || (mmvq_env_pair() == 0 && 2 * per_cta <= W)) ? 1 : 0;
     const size_t fixed = mmvq_smem_bytes(TYPE, p.n_in, NC, 0, W) + (p.pair ? mmvq_pair_bytes(NC, W) : 0);
     // One CTA per SM (8 warps) with a ring of up to 5 slots: measured best on B200 for config 1 (12288 x
     // 4096, 2 columns: 2.8 vs 2.4-2.6 TB/s) and for a decode step of one GEMV launch per op (2.45 vs
     // 2.59 ms). Two 3-slot CTAs per SM leave the busiest warp 8 tiles where the average is 5 (units are
     // dealt to warps whole), with 16 warps sharing the SM's issue slots, and let the next op's CTAs become
     // resident and start their weight prefetch while this one still runs.
-    int ctas = 1;
     int stages = (int) (((long long) max_optin - 2048 - (long long) fixed) / (long long) (W * tile));
     if (stages > 5) stages = 5;
     if (mmvq_env_stages() > 0) stages = mmvq_env_stages();
-    if (mmvq_env_ctas() > 0 && EPI != EPI_XRES) ctas = mmvq_env_ctas();  // an exchange CTA owns a flag slot per SM
     if (stages < 2 || stages > kMmvqMaxStages) return cudaErrorInvalidValue;
     p.stages = stages;
     const size_t smem = mmvq_smem_bytes(TYPE, p.n_in, NC, stages, W) + (p.pair ? mmvq_pair_bytes(NC, W) : 0);
@@ -796,9 +805,6 @@ cudaError_t mmvq_launch_w(MmvqParams p, cudaStream_t s, bool pdl) {
         if (e != cudaSuccess) return e;
         configured_smem = (int) smem;
     }
-    const int units = p.n_out / 4;
-    int grid = num_sms() * ctas;
-    if (grid > units) grid = units;
     return launch_pdl(mmvq_packed_kernel<TYPE, NC, PRO, EPI, W>, dim3(grid), dim3(W * 32), smem, s, pdl, p);
 }
 // warps: consumer warps per CTA, 8 (256 threads, 5-slot rings) or 16 (512 threads, 3-4 slots).
