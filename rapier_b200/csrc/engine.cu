@@ -950,9 +950,10 @@ template <int NC>
 cudaError_t EngineImpl::launch_op(const POp& op) {
     if (op.kind == POP_GEMV) {
         const MmvqParams& p = op.g;
-        int w = NC == 2 ? 16 : kMmvqWarps;  // the 2-column GEMVs with 16 warps per CTA (mmvq_launch)
-        static const int res16 = std::getenv("RK_MMVQ_RES16") ? std::atoi(std::getenv("RK_MMVQ_RES16")) : 0;
-        if (NC == 1 && op.pro == PRO_Q8 && res16 > 0) w = 16;
+        // 16 warps per CTA for the 2-column GEMVs and for the single-column residual GEMVs (7 units per CTA:
+        // with 16 warps they run in warp pairs, mmvq_launch_w); 8 for the rest. Measured on one box against
+        // 8 warps there: the no-MTP decode +1.1 %.
+        const int w = NC == 2 || (NC == 1 && op.pro == PRO_Q8) ? 16 : kMmvqWarps;
         if (op.pro == PRO_RMS) {
             if (op.epi == EPI_STORE) return mmvq_launch<RK_TYPE_Q6_K, NC, PRO_RMS, EPI_STORE>(p, s, true, w);
             if (op.epi == EPI_SWIGLU) return mmvq_launch<RK_TYPE_Q6_K, NC, PRO_RMS, EPI_SWIGLU>(p, s, true, w);

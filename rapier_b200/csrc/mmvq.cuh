@@ -585,11 +585,13 @@ __global__ void __launch_bounds__(W * 32, 16 / W) mmvq_packed_kernel(const MmvqP
     const int ng = p.n_in >> 5;
     const int stages = p.stages;
     const int split = mmvq_split(KC);
-    // Warp pairs (16 warps, an even chunk count, RK_MMVQ_PAIR=1): warps 2m and 2m + 1 take the two halves of
-    // the same units, so a unit's tiles are consumed by two warps at once; the odd warp hands its half's
-    // chains to the even one through a shared-memory slot, and the even warp adds them (lo + hi) and runs
-    // the epilogue. Measured on the decode's 2-column GEMVs: 4 % slower than 16 unpaired warps (the slots
-    // cost a ring slot per warp and the handoff waits), so off by default.
+    // Warp pairs (16 warps, an even chunk count, p.pair set by the launcher): warps 2m and 2m + 1 take the
+    // two halves of the same units, so a unit's tiles are consumed by two warps at once; the odd warp hands
+    // its half's chains to the even one through a shared-memory slot, and the even warp adds them (lo + hi)
+    // and runs the epilogue. Measured on the decode (same box, alternating): pairs in every 2-column launch
+    // 4 % slower than 16 unpaired warps (the slots cost ring depth and the handoff waits); pairs only where a
+    // CTA has at most one unit per pair (the residual GEMVs, 7 units per CTA, where unpaired warps idle) 2 %
+    // faster with exact MTP.
     const bool paired = W == 16 && split < KC && p.pair != 0;
     const int PW = paired ? W / 2 : W;           // units in flight per CTA
     const int ul = paired ? warp >> 1 : warp;    // this warp's unit lane
@@ -810,8 +812,9 @@ cudaError_t mmvq_launch_w(MmvqParams p, cudaStream_t s, bool pdl) {
 // warps: consumer warps per CTA, 8 (256 threads, 5-slot rings) or 16 (512 threads, 3-4 slots).
 // Measured on B200 (same box, alternating): the decode engine's 2-column GEMVs (the MTP verify and draft)
 // run 9 % faster with 16 warps (the integer chains of two columns per tile leave 2 warps per scheduler
-// idle on dependencies; the MTP decode +5.4 %), single-column ones 6 % slower (the no-MTP decode -5 %), and
-// a lone repeated 41 MB GEMV 10 % slower. RK_MMVQ_WARPS=8|16 overrides.
+// idle on dependencies; the MTP decode +5.4 %), single-column ones 6 % slower unpaired (the no-MTP decode
+// -5 %; the single-column residual GEMVs gain with 16 paired warps), and a lone repeated 41 MB GEMV 10 %
+// slower. RK_MMVQ_WARPS=8|16 overrides.
 template <int TYPE, int NC, int PRO, int EPI>
 cudaError_t mmvq_launch(MmvqParams p, cudaStream_t s, bool pdl, int warps = kMmvqWarps) {
     if (mmvq_env_warps() == 8 || mmvq_env_warps() == 16) warps = mmvq_env_warps();
