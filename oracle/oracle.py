@@ -21,11 +21,18 @@ TYPE_Q6_K = 14
 _lib = None
 
 
+REF_TREE = "/root/reference"  # the reference checkout of the build container (absent on the GPU box)
+REF_GDN_LIB = os.path.join(_HERE, "_ref", "libref_gdn.so")
+
+
 def build() -> None:
-    """Compile liboracle.so with the committed Makefile."""
+    """Compile liboracle.so with the committed Makefile; where the reference tree is present, also the
+    reference's own fused GDN kernels into _ref/libref_gdn.so (the GPU box only uses the prebuilt file)."""
     import subprocess
 
     subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    if os.path.exists(os.path.join(REF_TREE, "src", "fused_gdn.cu")):
+        subprocess.run(["make", "-s", "-C", _HERE, "ref", f"REF={REF_TREE}"], check=True)
 
 
 def lib():
