@@ -10,8 +10,6 @@
 // kernel another SM may have rewritten a line this SM still holds in L1.
 #pragma once
 
-#include <cooperative_groups.h>
-
 #include "mmvq.cuh"
 
 namespace rk {
@@ -246,14 +244,10 @@ __device__ __noinline__ void embed_body(const EmbedArgs& a, Ctrl* ctrl, int draf
 //    row group = warp), the state after column 0 kept in `snap` when NC == 2 (the verify's rollback);
 //  * the gated RMSNorm over the head's 128 outputs and the Q8_1 epilogue by the head's last quarter
 //    to finish (a per-head arrival counter).
-// CL (the graph executor's gdn_kernel, a cluster of 4 CTAs per v-head, one per quarter): instead of the
-// arrival counter, each quarter's sum of squares goes to its shared memory, the cluster meets at a barrier,
-// and every quarter reads the four sums (in quarter order) through distributed shared memory and normalizes
-// its own 32 channels: the same operations on the same values, so the same bits.
 // Reduction order of the reference kernel: 32-row fma chains per row group, groups added 0..3, per-32
 // channel xor trees added in order. History: 8 slots per channel; this launch writes slots pos, pos+1
 // and reads pos-3 .. pos-1 (mod 8), so no write of any block can meet a read of another.
-template <int NC, bool CL = false>
+template <int NC>
 __device__ __forceinline__ void gdn_quarter_impl(const GdnArgs& a, int head, int quarter, int pos, bool from_snap,
                                                  float* sm) {
     constexpr int S = kSsm;
@@ -286,9 +280,7 @@ __device__ __forceinline__ void gdn_quarter_impl(const GdnArgs& a, int head, int
             const float* pc = a.proj + (size_t) c * a.proj_stride;
             beta_in[c] = ld_cg(pc + off_beta + head);
             alpha_in[c] = ld_cg(pc + off_alpha + head);
-            // the channel this thread normalizes: as the last quarter to finish (wid * 32 + lane), or in a
-            // cluster its own quarter's (warp 0)
-            z_in[c] = ld_cg(pc + off_z + head * S + (CL ? quarter : wid) * 32 + lane);
+            z_in[c] = ld_cg(pc + off_z + head * S + wid * 32 + lane);  // column this thread normalizes if last
         }
     }
     auto conv = [&](int ch, float (&x)[NC], float (&yv)[NC]) {
@@ -387,34 +379,6 @@ __device__ __forceinline__ void gdn_quarter_impl(const GdnArgs& a, int head, int
     if (stepper) {
 #pragma unroll
         for (int r = 0; r < 32; ++r) sbase[r * rs] = s[r];
-    }
-    if constexpr (CL) {  // ---- the head's norm through the cluster: every quarter normalizes its own ----
-        namespace cg = cooperative_groups;
-        cg::cluster_group cluster = cg::this_cluster();
-        float* ss_sm = qk_part;  // [NC]: this quarter's sums of squares (qk_part is free again)
-        float sq[NC];
-#pragma unroll
-        for (int c = 0; c < NC; ++c) sq[c] = warp_sum(__fmul_rn(oc[c], oc[c]));  // warp 0's values are used
-        if (tid == 0)
-#pragma unroll
-            for (int c = 0; c < NC; ++c) ss_sm[c] = sq[c];
-        cluster.sync();
-        if (wid == 0) {
-            const int j = quarter * 32 + lane;
-#pragma unroll
-            for (int c = 0; c < NC; ++c) {
-                float q4[4];
-#pragma unroll
-                for (int r = 0; r < 4; ++r) q4[r] = *cluster.map_shared_rank(ss_sm + c, r);
-                const float ss = __fadd_rn(__fadd_rn(__fadd_rn(q4[0], q4[1]), q4[2]), q4[3]);
-                const float scale = rk_rsqrtf(__fadd_rn(__fdiv_rn(ss, (float) S), a.eps));
-                const float yv = __fmul_rn(__fmul_rn(__fmul_rn(oc[c], scale), a.gamma[j]), silu_dev(z_in[c]));
-                if (a.y) a.y[(size_t) c * hv * S + head * S + j] = yv;
-                q8_1_warp_store(yv, a.q8 + ((size_t) c * hv * 4 + head * 4 + quarter) * 36, lane);
-            }
-        }
-        cluster.sync();  // no quarter leaves while another still reads its shared memory
-        return;
     }
     // ---- read-outs and sums of squares to the head's scratch; the last quarter normalizes ----
     if (wid == 0) {

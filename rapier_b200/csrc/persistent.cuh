@@ -476,10 +476,8 @@ __global__ void __launch_bounds__(256, kAttnCtas<NC>) attn_kernel(const POp op, 
 
 // The GDN op as its own launch (graph mode): a kernel of its own instead of the generic op kernel, whose
 // code covers every op body (instruction-cache misses) and whose register allocation is the largest body's.
-// One cluster of 4 CTAs per v-head (its quarters), one item per CTA (grid = hv * 4, a whole number of
-// clusters): the head's gated norm meets in distributed shared memory (gdn_quarter_impl<NC, true>).
 template <int NC>
-__global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(256) gdn_kernel(const POp op, Ctrl* ctrl) {
+__global__ void __launch_bounds__(256) gdn_kernel(const POp op, Ctrl* ctrl) {
     extern __shared__ __align__(128) uint8_t smem[];
     pdl_trigger();
     // The state slice this block steps was written by the same layer's GDN op one step earlier, long
@@ -497,10 +495,9 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(256) gdn_kernel(cons
     pdl_wait();
     const int pos = ld_cg(op.draft ? &ctrl->dpos : &ctrl->pos);
     const int rb = ld_cg(&ctrl->rollback);
-    const int items = pop_items<NC>(op, pos);  // hv * 4: the 4 CTAs of a cluster all take the item or none
-    if ((int) blockIdx.x < items)
-        gdn_quarter_impl<NC, true>(op.gd, (int) blockIdx.x >> 2, (int) blockIdx.x & 3, pos, rb != 0,
-                                   reinterpret_cast<float*>(smem));
+    const int items = pop_items<NC>(op, pos);
+    for (int it = (int) blockIdx.x; it < items; it += (int) gridDim.x)  // uniform over the block
+        gdn_quarter_impl<NC>(op.gd, it >> 2, it & 3, pos, rb != 0, reinterpret_cast<float*>(smem));
 }
 
 // The attention combine as its own launch (graph mode): n_head x NC x 8 items of 32 dims, small enough per
