@@ -105,6 +105,10 @@ def test_tp2_graph_executor_replicated_kv(tmp_path_factory):
     _check_executors(_run(tmp_path_factory, 2, "exec", "tiny", 29524))
 
 
+def test_tp4_graph_executor_bitwise_persistent(tmp_path_factory):
+    _check_executors(_run(tmp_path_factory, 4, "exec", "9b4", 29527))
+
+
 def test_tp8_graph_executor_bitwise_persistent(tmp_path_factory):
     _check_executors(_run(tmp_path_factory, 8, "exec", "9b4", 29525))
 
