@@ -589,9 +589,8 @@ __global__ void __launch_bounds__(W * 32, 16 / W) mmvq_packed_kernel(const MmvqP
     // two halves of the same units, so a unit's tiles are consumed by two warps at once; the odd warp hands
     // its half's chains to the even one through a shared-memory slot, and the even warp adds them (lo + hi)
     // and runs the epilogue. Measured on the decode (same box, alternating): pairs in every 2-column launch
-    // 4 % slower than 16 unpaired warps (the slots cost ring depth and the handoff waits); pairs only where a
-    // CTA has at most one unit per pair (the residual GEMVs, 7 units per CTA, where unpaired warps idle) 2 %
-    // faster with exact MTP.
+    // 3-4 % slower than 16 unpaired warps (the slots cost ring depth and the handoff waits); pairs where they
+    // shorten the busiest warp's tile chain (mmvq_launch_w) 4.4 % faster with exact MTP.
     const bool paired = W == 16 && split < KC && p.pair != 0;
     const int PW = paired ? W / 2 : W;           // units in flight per CTA
     const int ul = paired ? warp >> 1 : warp;    // this warp's unit lane
@@ -784,11 +783,15 @@ cudaError_t mmvq_launch_w(MmvqParams p, cudaStream_t s, bool pdl) {
     int grid = num_sms() * ctas;
     if (grid > units) grid = units;
     // Warp pairs (16 warps, an even chunk count): the two halves of each unit's chunks go to two warps. By
-    // default only where whole units would leave warps idle: at most one unit per pair and CTA (the 4096-row
-    // residual GEMVs, 7 units per CTA). RK_MMVQ_PAIR=1 pairs every 16-warp launch, -1 none.
+    // default where that shortens the busiest warp's tile chain by a quarter or more: a CTA's u units give
+    // it ceil(u / 16) whole units unpaired and ceil(u / 8) half units paired (the residual GEMVs, 7 units per
+    // CTA: 4 tiles -> 2; in_proj, 21: 8 -> 6; not up||gate, 42: 12 -> 12, nor the lm_head). Measured with
+    // exact MTP (same box): residual GEMVs paired +2.0 %, in_proj and qkv too +2.4 % more, up||gate too
+    // -5 %. RK_MMVQ_PAIR=1 pairs every 16-warp launch, -1 none.
     const int per_cta = (units + grid - 1) / grid;
     const bool can_pair = W == 16 && mmvq_split(p.n_in >> 10) < (p.n_in >> 10);
-    p.pair = can_pair && (mmvq_env_pair() > 0 || (mmvq_env_pair() == 0 && 2 * per_cta <= W)) ? 1 : 0;
+    const bool shorter = 2 * ((per_cta + W / 2 - 1) / (W / 2)) <= 3 * ((per_cta + W - 1) / W);
+    p.pair = can_pair && (mmvq_env_pair() > 0 || (mmvq_env_pair() == 0 && shorter)) ? 1 : 0;
     const size_t fixed = mmvq_smem_bytes(TYPE, p.n_in, NC, 0, W) + (p.pair ? mmvq_pair_bytes(NC, W) : 0);
     // One CTA per SM (8 warps) with a ring of up to 5 slots: measured best on B200 for config 1 (12288 x
     // 4096, 2 columns: 2.8 vs 2.4-2.6 TB/s) and for a decode step of one GEMV launch per op (2.45 vs
