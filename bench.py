@@ -257,8 +257,8 @@ def cpu_baseline_gemv(sample_rows=4096):
 N_PROMPT, N_GEN = 32, 400
 # DRAM bytes per GEMV launch of one 2-column (verify) trunk step, 32 layers + lm_head, from an ncu capture of
 # the 4-layer 2-column pass (profiles/mmvq_packed_decode_2col_pass.md): 24 x GDN layer + 8 x attention layer
-# + lm_head, / 129 launches (the engine's 2-column launches: 16 warps per CTA, residual GEMVs paired).
-DECODE_2COL_NCU_TRAFFIC = 50_607_078
+# + lm_head, / 129 launches (the engine's 2-column launches: 16 warps per CTA, paired where that helps).
+DECODE_2COL_NCU_TRAFFIC = 50_690_401
 
 
 def tp_layout(world: int) -> tuple:
